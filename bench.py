@@ -1,0 +1,518 @@
+#!/usr/bin/env python3
+"""Benchmark of the tadma_b200 hot path (achieved HBM GB/s), one JSON line.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2|3|4|5] [--impl ours|reference]
+
+Metric: achieved HBM GB/s = algorithmic bytes (every input
+read once, every output written once; gathered rows counted per use) / time.
+Default workload: config 2, y = gelu(x * 0.5 +
+bias), x[8192, 8192] bf16, bias[8192] bf16 -> y bf16, one fused kernel.
+Configs 3-5 are selectable for their own lines.
+
+Multi-GPU (torchrun, one process per GPU): every rank processes its own
+batch of the config's shape (a shard of an N-times larger global batch,
+generated at its global offset), no collective on the data path -> weak
+scaling.  Timing: W warm-up steps, then K steps, each bracketed by CUDA events
+on the launching stream with an L2 flush (256 MB write) between steps; barrier
++ synchronize around the timed region; the max over ranks is reported.
+
+--impl reference times the reference's algorithm on the host cores: the
+reference itself cannot be built here (it needs clang >= 19 / C++23), so this
+is the oracle's straightforward host loop (oracle/), all threads, on a
+bounded sample of the same workload; only rank 0 runs it.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+GB = 1e9
+L2_FLUSH_BYTES = 256 << 20
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4, 5])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="budget of the CPU-baseline sample")
+    ap.add_argument("--e2e-steps", type=int, default=20)
+    return ap.parse_args()
+
+
+def measured_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+# Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of the
+# dominant kernel from one ncu capture of the same command (see profiles/).
+NCU_TRAFFIC = {}
+
+
+# ----------------------------------------------------------------- clocks --
+
+class ClockSampler:
+    """Polls NVML (SM clock, clock-event reasons) in a thread during the timed region."""
+
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x2: "applications_clocks_setting"}
+
+    def __init__(self, device_index: int):
+        self.samples, self.reasons, self.max_mhz, self.ok = [], 0, None, False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            import torch
+            h = None
+            try:
+                props = torch.cuda.get_device_properties(device_index)
+                bus = "%08x:%02x:%02x.0" % (props.pci_domain_id, props.pci_bus_id, props.pci_device_id)
+                h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            except Exception:
+                h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.nvml, self.h = pynvml, h
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception as e:  # NVML unavailable: report it, do not fail the bench
+            self.err = str(e)
+        self._stop = threading.Event()
+
+    def _reasons(self):
+        n = self.nvml
+        f = getattr(n, "nvmlDeviceGetCurrentClocksEventReasons", None) or n.nvmlDeviceGetCurrentClocksThrottleReasons
+        return f(self.h)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nvml.nvmlDeviceGetClockInfo(self.h, self.nvml.NVML_CLOCK_SM))
+                self.reasons |= int(self._reasons())
+            except Exception:
+                pass
+            time.sleep(0.001)
+
+    def __enter__(self):
+        if self.ok:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        if self.ok:
+            self._stop.set()
+            self.t.join()
+
+    def result(self):
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0,
+                    "note": getattr(self, "err", "no samples")}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": [v for k, v in self.REASONS.items() if self.reasons & k], "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------- configs --
+
+class Config2:
+    """y = gelu(x * 0.5 + bias), x[8192, 8192] bf16, bias[8192] bf16, y bf16."""
+    name = "cfg2: y = gelu(x*0.5 + bias), x[8192,8192] bf16, bias[8192] bf16 -> bf16"
+    ROWS, COLS = 8192, 8192
+    dtype = "bf16"
+    kernel = "chain_vec_kernel"
+
+    def __init__(self, rank):
+        import torch
+        import tadma_b200 as tb
+        from tadma_b200.abi import Dist, DType, make_tensor
+        self.tb = tb
+        R, C = self.ROWS, self.COLS
+        self.x = torch.empty((R, C), dtype=torch.bfloat16, device="cuda")
+        self.bias = torch.empty((C,), dtype=torch.bfloat16, device="cuda")
+        self.y = torch.empty((R, C), dtype=torch.bfloat16, device="cuda")
+        tb.fill(self.x, Dist.NORMAL, 0.0, 1.0, seed=0, stream_id=1, offset=rank * R * C)
+        tb.fill(self.bias, Dist.NORMAL, 0.0, 0.1, seed=0, stream_id=2)
+        self.bview = make_tensor(self.bias.data_ptr(), DType.BF16, [R, C], [0, 1])
+        self.prog = self.program()
+        self.bytes = 2 * R * C * 2 + C * 2
+        self.launches = 1
+        self.units = R * C
+
+    @staticmethod
+    def program():
+        from tadma_b200.abi import SRC_IMM, DType, Op, instr
+        return [instr(Op.MUL, b=SRC_IMM, imm=0.5, round_dtype=DType.F32), instr(Op.ADD, b=1, round_dtype=DType.F32),
+                instr(Op.GELU, round_dtype=DType.F32)]
+
+    def step(self):
+        from tadma_b200.abi import Compute
+        self.tb.eltwise(self.y, [self.x, self.bview], self.prog, Compute.F32)
+
+    def e2e(self, steps, stream):
+        """Same op through the public C-ABI call, inputs from pinned host memory
+        and the result back to pinned host memory inside the timed region."""
+        import torch
+        xh = torch.empty_like(self.x, device="cpu").pin_memory()
+        bh = torch.empty_like(self.bias, device="cpu").pin_memory()
+        yh = torch.empty_like(self.y, device="cpu").pin_memory()
+        xh.copy_(self.x)
+        bh.copy_(self.bias)
+        times = []
+        for _ in range(steps):
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record(stream)
+            self.x.copy_(xh, non_blocking=True)
+            self.bias.copy_(bh, non_blocking=True)
+            self.step()
+            yh.copy_(self.y, non_blocking=True)
+            e.record(stream)
+            e.synchronize()
+            times.append(s.elapsed_time(e) / 1e3)
+        h2d = xh.numel() * 2 + bh.numel() * 2
+        d2h = yh.numel() * 2
+        return statistics.mean(times), h2d, d2h
+
+    # CPU legs (oracle host loop: test infrastructure, timed as the baseline only)
+    def cpu_sample(self, budget_s):
+        import numpy as np
+        from oracle import oracle as O
+        rows = 1024
+        x = self.x[:rows].contiguous().view(torch_int16()).cpu().numpy().view(np.uint16)
+        b = self.bias.view(torch_int16()).cpu().numpy().view(np.uint16)
+        y = np.zeros_like(x)
+        L = O.lib()
+        done, t0 = 0, time.perf_counter()
+        while True:
+            L.or_cfg2_gelu_affine_bf16(O.ptr(x), O.ptr(b), 0.5, O.ptr(y), rows, self.COLS)
+            done += 1
+            el = time.perf_counter() - t0
+            if el >= budget_s:
+                break
+        bytes_ = done * (2 * rows * self.COLS * 2 + self.COLS * 2)
+        return bytes_ / el / GB, L.or_num_threads(), f"{done} x {rows} rows of [8192, 8192] ({rows * self.COLS} elements per call)"
+
+    def reference_step(self, state):
+        from oracle import oracle as O
+        x, b, y, rows = state
+        O.lib().or_cfg2_gelu_affine_bf16(O.ptr(x), O.ptr(b), 0.5, O.ptr(y), rows, self.COLS)
+        return 2 * rows * self.COLS * 2 + self.COLS * 2
+
+    def reference_state(self):
+        import numpy as np
+        rows = 512
+        x = self.x[:rows].contiguous().view(torch_int16()).cpu().numpy().view(np.uint16)
+        b = self.bias.view(torch_int16()).cpu().numpy().view(np.uint16)
+        return (x, b, np.zeros_like(x), rows), f"512 rows of x[8192, 8192] per step"
+
+
+def torch_int16():
+    import torch
+    return torch.int16
+
+
+class Config3:
+    """sum / max / argmax over the last axis and mean over the middle axis of X[32, 4096, 4096] fp32."""
+    name = "cfg3: sum/max/argmax over axis -1 + mean over axis 1 of X[32,4096,4096] fp32"
+    dtype = "f32"
+    kernel = "reduce_row_kernel"
+
+    def __init__(self, rank):
+        import torch
+        import tadma_b200 as tb
+        from tadma_b200.abi import Dist
+        self.tb = tb
+        B, R, C = 32, 4096, 4096
+        self.x = torch.empty((B, R, C), dtype=torch.float32, device="cuda")
+        tb.fill(self.x, Dist.UNIFORM, -1.0, 1.0, seed=0, stream_id=1, offset=rank * B * R * C)
+        self.s = torch.empty((B, R, 1), dtype=torch.float32, device="cuda")
+        self.m = torch.empty((B, R, 1), dtype=torch.float32, device="cuda")
+        self.a = torch.empty((B, R), dtype=torch.int64, device="cuda")
+        self.mean = torch.empty((B, 1, C), dtype=torch.float32, device="cuda")
+        xin = B * R * C * 4
+        self.bytes = 4 * xin + B * R * 4 * 2 + B * R * 8 + B * C * 4
+        self.launches = 4
+        self.units = 4 * B * R * C
+
+    def step(self):
+        from tadma_b200.abi import Reduce
+        tb = self.tb
+        tb.reduce(Reduce.SUM, self.x, -1, self.s)
+        tb.reduce(Reduce.MAX, self.x, -1, self.m)
+        tb.reduce(Reduce.ARGMAX, self.x, -1, self.a)
+        tb.reduce(Reduce.MEAN, self.x, 1, self.mean)
+
+    def cpu_sample(self, budget_s):
+        import numpy as np
+        from oracle import oracle as O
+        x = self.x[0, :1024].contiguous().cpu().numpy()
+        L = O.lib()
+        s, a = np.zeros(1024, np.float32), np.zeros(1024, np.int64)
+        mean = np.zeros(4096, np.float32)
+        done, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < budget_s:
+            L.or_cfg3_sum_lastaxis_f32(O.ptr(x), O.ptr(s), 1024, 4096)
+            L.or_cfg3_max_lastaxis_f32(O.ptr(x), O.ptr(s), 1024, 4096)
+            L.or_cfg3_argmax_lastaxis_f32(O.ptr(x), O.ptr(a), 1024, 4096)
+            L.or_cfg3_mean_midaxis_f32(O.ptr(x), O.ptr(mean), 1, 1024, 4096)
+            done += 1
+        el = time.perf_counter() - t0
+        return done * 4 * x.nbytes / el / GB, L.or_num_threads(), f"{done} x X[0, :1024, :] for all four ops"
+
+
+class Config4:
+    """LayerNorm over the last axis of [64, 2048, 1024] fp16 + softmax over the last axis of [32, 16, 2048, 2048] fp16."""
+    name = "cfg4: LayerNorm [64,2048,1024] fp16 + softmax [32,16,2048,2048] fp16 (last axis)"
+    dtype = "f16"
+    kernel = "rownorm_warp_kernel"
+
+    def __init__(self, rank):
+        import torch
+        import tadma_b200 as tb
+        from tadma_b200.abi import Dist
+        self.tb = tb
+        self.x = torch.empty((64, 2048, 1024), dtype=torch.float16, device="cuda")
+        self.g = torch.empty((1024,), dtype=torch.float16, device="cuda")
+        self.b = torch.empty((1024,), dtype=torch.float16, device="cuda")
+        tb.fill(self.x, Dist.NORMAL, 0.0, 1.0, 0, 1, offset=rank * self.x.numel())
+        tb.fill(self.g, Dist.NORMAL, 1.0, 0.02, 0, 2)
+        tb.fill(self.b, Dist.NORMAL, 0.0, 0.02, 0, 3)
+        self.y = torch.empty_like(self.x)
+        self.s = torch.empty((32, 16, 2048, 2048), dtype=torch.float16, device="cuda")
+        tb.fill(self.s, Dist.NORMAL, 0.0, 3.0, 0, 4, offset=rank * self.s.numel())
+        self.sy = torch.empty_like(self.s)
+        self.bytes = (2 * self.x.numel() * 2 + 2 * 1024 * 2) + 2 * self.s.numel() * 2
+        self.launches = 2
+        self.units = self.x.numel() + self.s.numel()
+
+    def step(self):
+        from tadma_b200.abi import LNMode
+        self.tb.layer_norm(self.x, -1, self.g, self.b, 1e-5, self.y, LNMode.ONNX)
+        self.tb.softmax(self.s, -1, self.sy)
+
+    def cpu_sample(self, budget_s):
+        import numpy as np
+        from oracle import oracle as O
+        L = O.lib()
+        xs = self.x.view(-1, 1024)[:4096].contiguous().view(torch_int16()).cpu().numpy().view(np.uint16)
+        g = self.g.view(torch_int16()).cpu().numpy().view(np.uint16)
+        b = self.b.view(torch_int16()).cpu().numpy().view(np.uint16)
+        ss = self.s.view(-1, 2048)[:2048].contiguous().view(torch_int16()).cpu().numpy().view(np.uint16)
+        y1, y2 = np.zeros_like(xs), np.zeros_like(ss)
+        done, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < budget_s:
+            L.or_cfg4_layer_norm_f16(O.ptr(xs), O.ptr(g), O.ptr(b), 1e-5, O.ptr(y1), 4096, 1024)
+            L.or_cfg4_softmax_f16(O.ptr(ss), O.ptr(y2), 2048, 2048)
+            done += 1
+        el = time.perf_counter() - t0
+        return done * 2 * (xs.nbytes + ss.nbytes) / el / GB, L.or_num_threads(), f"{done} x (4096 LN rows + 2048 softmax rows)"
+
+
+class Config5:
+    """Embedding gather: table [50257, 4096] fp16, ids [2048, 4096] int64, + pos [4096, 4096] bf16 -> bf16."""
+    name = "cfg5: gather table[50257,4096] fp16 by ids[2048,4096] int64 + pos[4096,4096] bf16 -> bf16"
+    dtype = "f16/bf16"
+    kernel = "gather_rows_kernel"
+    V, B, S, D = 50257, 2048, 4096, 4096
+
+    def __init__(self, rank):
+        import torch
+        import tadma_b200 as tb
+        from tadma_b200.abi import Dist, DType, make_tensor
+        self.tb = tb
+        V, B, S, D = self.V, self.B, self.S, self.D
+        self.table = torch.empty((V, D), dtype=torch.float16, device="cuda")
+        self.ids = torch.empty((B, S), dtype=torch.int64, device="cuda")
+        self.pos = torch.empty((S, D), dtype=torch.bfloat16, device="cuda")
+        tb.fill(self.table, Dist.NORMAL, 0.0, 0.02, 0, 1)
+        tb.fill(self.ids, Dist.INDEX, 0, V, 0, 2, offset=rank * B * S)
+        tb.fill(self.pos, Dist.NORMAL, 0.0, 0.02, 0, 3)
+        self.out = torch.empty((B, S, D), dtype=torch.bfloat16, device="cuda")
+        self.addv = make_tensor(self.pos.data_ptr(), DType.BF16, [B, S, D], [0, D, 1])
+        n_out = B * S * D
+        self.bytes = B * S * 8 + n_out * 2 + S * D * 2 + n_out * 2
+        self.compulsory = B * S * 8 + V * D * 2 + S * D * 2 + n_out * 2
+        self.launches = 1
+        self.units = n_out
+
+    def step(self):
+        self.tb.gather(self.table, 0, self.ids, self.out, add=self.addv)
+
+    def cpu_sample(self, budget_s):
+        import numpy as np
+        from oracle import oracle as O
+        L = O.lib()
+        rows = 16
+        table = self.table.view(torch_int16()).cpu().numpy().view(np.uint16)
+        ids = self.ids[:rows].contiguous().cpu().numpy()
+        pos = self.pos.view(torch_int16()).cpu().numpy().view(np.uint16)
+        out = np.zeros((rows, self.S, self.D), np.uint16)
+        done, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < budget_s:
+            L.or_cfg5_gather_add(O.ptr(table), self.V, O.ptr(ids), O.ptr(pos), O.ptr(out), rows, self.S, self.D)
+            done += 1
+        el = time.perf_counter() - t0
+        per = rows * self.S * 8 + rows * self.S * self.D * 2 * 2 + self.S * self.D * 2
+        return done * per / el / GB, L.or_num_threads(), f"{done} x {rows} batch rows of ids[2048, 4096]"
+
+
+CONFIGS = {2: Config2, 3: Config3, 4: Config4, 5: Config5}
+
+
+# --------------------------------------------------------------- reference --
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    cfg = CONFIGS[args.config]
+    if args.config != 2:
+        print(json.dumps({"impl": "reference", "unavailable": "reference arm implemented for the default workload (config 2)"}))
+        return
+    import numpy as np
+    from oracle import oracle as O
+    from tadma_b200.abi import Dist, DType
+    # The inputs come from the oracle's own generator (same values as the GPU arm).
+    rows = 512
+    x = O.fill((rows, Config2.COLS), DType.BF16, Dist.NORMAL, 0.0, 1.0, 0, 1)
+    b = O.fill((Config2.COLS,), DType.BF16, Dist.NORMAL, 0.0, 0.1, 0, 2)
+    y = np.zeros_like(x)
+    L = O.lib()
+    per = 2 * rows * Config2.COLS * 2 + Config2.COLS * 2
+    for _ in range(args.warmup):
+        L.or_cfg2_gelu_affine_bf16(O.ptr(x), O.ptr(b), 0.5, O.ptr(y), rows, Config2.COLS)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        L.or_cfg2_gelu_affine_bf16(O.ptr(x), O.ptr(b), 0.5, O.ptr(y), rows, Config2.COLS)
+    el = time.perf_counter() - t0
+    v = per * args.steps / el / GB
+    cores = L.or_num_threads()
+    print(json.dumps({
+        "impl": "reference", "metric": "achieved HBM GB/s", "value": round(v, 3), "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": cfg.name, "sample": f"{rows} rows of x[8192, 8192] per step"},
+        "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": cores, "kind": "port",
+                         "sample": f"{rows} rows of x[8192, 8192] per step, {args.steps} steps"},
+        "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "reference (OgnianM/TADMA) needs clang>=19/C++23 and cannot be built here; its algorithm runs as the "
+                "oracle's host C loop (oracle/tadma_oracle.c, OpenMP)",
+    }))
+
+
+# -------------------------------------------------------------------- main --
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    try:
+        run(args, rank, world, local)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+
+
+def barrier(world):
+    import torch
+    import torch.distributed as dist
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def run(args, rank, world, local):
+    import torch
+    import torch.distributed as dist
+    cfg = CONFIGS[args.config](rank)
+    stream = torch.cuda.current_stream()
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+    for _ in range(max(args.warmup, 3)):
+        flush.zero_()
+        cfg.step()
+    barrier(world)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    sampler = ClockSampler(local)
+    t_region = time.perf_counter()
+    with sampler:
+        for i in range(args.steps):
+            flush.zero_()
+            starts[i].record(stream)
+            cfg.step()
+            ends[i].record(stream)
+        barrier(world)
+    region_s = time.perf_counter() - t_region
+    step_s = statistics.mean(s.elapsed_time(e) for s, e in zip(starts, ends)) / 1e3
+    t = torch.tensor([step_s], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    step_max = float(t.item())
+    value = cfg.bytes * world / step_max / GB
+
+    e2e = None
+    if hasattr(cfg, "e2e"):
+        e2e_steps = max(1, min(args.e2e_steps, args.steps))
+        e_s, h2d, d2h = cfg.e2e(e2e_steps, stream)
+        te = torch.tensor([e_s], dtype=torch.float64, device="cuda")
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        e2e = {"value": round(cfg.bytes * world / float(te.item()) / GB, 3), "unit": "GB/s",
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(float(te.item()) * 1e3, 4),
+               "steps": e2e_steps}
+    barrier(world)
+    if rank != 0:
+        return
+    peak, peak_kind = measured_peak()
+    achieved = cfg.bytes / step_s / GB
+    roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+            "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs, burst copy)",
+            "kernel": cfg.kernel, "algorithmic_bytes_per_step": cfg.bytes,
+            "traffic": NCU_TRAFFIC.get(args.config)}
+    cpu = None
+    if world == 1 and args.cpu_seconds > 0:
+        v, cores, sample = cfg.cpu_sample(args.cpu_seconds)
+        cpu = {"value": round(v, 3), "unit": "GB/s", "cores": cores, "kind": "port", "sample": sample}
+    line = {
+        "metric": "achieved HBM GB/s", "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": round(step_max * 1e3, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": cfg.dtype,
+        "data": "synthetic (seeded counter-based generator, BASELINE.json distributions)",
+        "config": {"workload": cfg.name, "per_gpu_batch": "one full config batch per GPU (global batch = N x)",
+                   "l2": "flushed between steps (256 MB write outside the step events)",
+                   "parallelism": f"dp{world} (leading-axis shards, no data-path collective)"},
+        "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
+        "gpu_launches": cfg.launches * args.steps,
+        "clocks": sampler.result(),
+        "elements_per_s": round(cfg.units * world / step_max, 1),
+        "region_s": round(region_s, 4),
+    }
+    if hasattr(cfg, "compulsory"):
+        line["compulsory_bytes_gbs"] = round(cfg.compulsory * world / step_max / GB, 3)
+    print(json.dumps(line))
+
+
+if __name__ == "__main__":
+    main()

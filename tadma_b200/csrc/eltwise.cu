@@ -1,0 +1,462 @@
+// eltwise.cu - fused element-wise / broadcast engine (sm_100a).
+//
+// Replaces the reference's lazy-node executor: EltwiseNode / CombineToNode /
+// CombineNode / InplaceNode (Kernels.hpp:16-53) run through CUDAHIPExecutor
+// (Node.hpp:25-48): one scalar element per thread, 512-thread blocks, a 32-bit
+// index and an int64 div/mod per dimension per element.  MergeNodes
+// (Node.hpp:189-224) composes node lambdas into one kernel; here a fused
+// chain is a short instruction list (tadma_instr) evaluated in registers.
+//
+// Design:
+// * the joint layout of out and inputs is folded (layout.hpp); typical
+//   launches become rank 1 (streaming) or rank 2 (row broadcast);
+// * vector path: each thread step handles V = 8 consecutive elements with
+//   16-byte loads/stores (2 x 16 B for fp32, 1 x 16 B for 16-bit types); an
+//   operand whose innermost stride is 0 is loaded once and splatted;
+//   operands with no broadcast stream through with evict-first hints;
+// * grid-stride persistent grid (SMs x resident blocks), U = 2 vector steps
+//   in flight per thread before any compute, so each SM keeps >= 32 KB of
+//   loads outstanding;
+// * any other layout takes the scalar path (one element per thread step,
+//   DivMod index decomposition, still 64-bit safe);
+// * the chain is uniform across the grid (kernel parameters), so the
+//   per-instruction switch is a uniform branch amortised over 8 elements.
+#include <mutex>
+#include <unordered_map>
+
+#include "common.cuh"
+#include "layout.hpp"
+#include "ops.cuh"
+
+namespace tadma_b200 {
+namespace {
+
+constexpr int V = 8;        // elements per vector step
+constexpr int U = 2;        // vector steps in flight per thread
+constexpr int THREADS = 256;
+
+struct Operand {
+    const char* base;
+    int32_t dtype;
+    int32_t inner_bcast;  // innermost folded stride is 0
+    int32_t streaming;    // no stride-0 dim: evict-first loads
+    int32_t pad;
+    int64_t stride[TADMA_MAX_RANK];
+};
+
+struct ChainParams {
+    int32_t rank;
+    int32_t n_instr;
+    int32_t out_dtype;
+    int32_t pad;
+    int64_t start;  // first element (scalar tail launch)
+    int64_t n;      // element count (scalar path) / vector count (vector path)
+    int64_t dims[TADMA_MAX_RANK];
+    DivMod dm[TADMA_MAX_RANK];
+    char* out;
+    int64_t out_stride[TADMA_MAX_RANK];
+    Operand in[TADMA_MAX_INPUTS];
+    tadma_instr prog[TADMA_MAX_INSTR];
+};
+
+template <typename C>
+__device__ __forceinline__ C imm_as(double v);
+template <>
+__device__ __forceinline__ float imm_as<float>(double v) { return __double2float_rn(v); }
+template <>
+__device__ __forceinline__ double imm_as<double>(double v) { return v; }
+template <>
+__device__ __forceinline__ int64_t imm_as<int64_t>(double v) { return f2i(v); }
+
+// Operand selection: static indices only, so `val` stays in registers.
+template <typename C, int NIN, int W>
+__device__ __forceinline__ void select(int sel, double imm, const C (&val)[NIN > 0 ? NIN : 1][W], C (&dst)[W]) {
+    if (sel < 0 || sel >= NIN) {
+        C s = imm_as<C>(imm);
+#pragma unroll
+        for (int j = 0; j < W; j++) dst[j] = s;
+        return;
+    }
+#pragma unroll
+    for (int k = 0; k < NIN; k++) {
+        if (sel == k) {
+#pragma unroll
+            for (int j = 0; j < W; j++) dst[j] = val[k][j];
+        }
+    }
+}
+
+template <typename C, int NIN, int W>
+__device__ __forceinline__ void run_chain(const ChainParams& p, C (&acc)[W], const C (&val)[NIN > 0 ? NIN : 1][W]) {
+    for (int i = 0; i < p.n_instr; i++) {
+        const tadma_instr& I = p.prog[i];
+        const int op = I.op;
+        if (op < 32) {
+            if (op == TADMA_OP_COPY && I.b == TADMA_SRC_IMM) {
+                C s = imm_as<C>(I.imm);
+#pragma unroll
+                for (int j = 0; j < W; j++) acc[j] = s;
+            } else if (op != TADMA_OP_COPY) {
+#pragma unroll
+                for (int j = 0; j < W; j++) acc[j] = unary(op, acc[j]);
+            }
+        } else {
+            C b[W], c[W];
+            select<C, NIN, W>(I.b, I.imm, val, b);
+            if (op == TADMA_OP_WHERE) {
+                select<C, NIN, W>(I.c, I.imm, val, c);
+            } else {
+#pragma unroll
+                for (int j = 0; j < W; j++) c[j] = b[j];
+            }
+#pragma unroll
+            for (int j = 0; j < W; j++) acc[j] = binary(op, acc[j], b[j], c[j]);
+        }
+        if (I.round_dtype >= 0) {
+#pragma unroll
+            for (int j = 0; j < W; j++) acc[j] = round_to(acc[j], I.round_dtype);
+        }
+    }
+}
+
+// ------------------------------------------------------- vector load/store --
+
+template <typename C>
+__device__ __forceinline__ C from_f(float f);
+template <>
+__device__ __forceinline__ float from_f<float>(float f) { return f; }
+template <>
+__device__ __forceinline__ double from_f<double>(float f) { return (double)f; }
+template <>
+__device__ __forceinline__ int64_t from_f<int64_t>(float f) { return f2i(f); }
+
+template <typename C>
+__device__ __forceinline__ void load_vec(const Operand& o, int64_t off, C (&v)[V]) {
+    if (o.inner_bcast) {
+        C s = load_as<C>(o.base, o.dtype, off);
+#pragma unroll
+        for (int j = 0; j < V; j++) v[j] = s;
+        return;
+    }
+    const char* p = o.base + off * dtype_size(o.dtype);
+    switch (o.dtype) {
+    case TADMA_F32: {
+        uint4 a = o.streaming ? ld_stream_v4(p) : ld_v4(p);
+        uint4 b = o.streaming ? ld_stream_v4(p + 16) : ld_v4(p + 16);
+        const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int j = 0; j < V; j++) v[j] = from_f<C>(__uint_as_float(w[j]));
+        break;
+    }
+    case TADMA_F16:
+    case TADMA_BF16: {
+        uint4 a = o.streaming ? ld_stream_v4(p) : ld_v4(p);
+        float f[8];
+        unpack8(a, o.dtype, f);
+#pragma unroll
+        for (int j = 0; j < V; j++) v[j] = from_f<C>(f[j]);
+        break;
+    }
+    default: {
+#pragma unroll
+        for (int j = 0; j < V; j++) v[j] = load_as<C>(o.base, o.dtype, off + j);
+        break;
+    }
+    }
+}
+
+template <typename C>
+__device__ __forceinline__ float to_f(C v);
+template <>
+__device__ __forceinline__ float to_f<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float to_f<double>(double v) { return __double2float_rn(v); }
+template <>
+__device__ __forceinline__ float to_f<int64_t>(int64_t v) { return __ll2float_rn(v); }
+
+template <typename C>
+__device__ __forceinline__ void store_vec(char* base, int dt, int64_t off, const C (&v)[V]) {
+    char* p = base + off * dtype_size(dt);
+    switch (dt) {
+    case TADMA_F32: {
+        if constexpr (sizeof(C) == 4) {
+            uint4 a = make_uint4(__float_as_uint(to_f(v[0])), __float_as_uint(to_f(v[1])), __float_as_uint(to_f(v[2])), __float_as_uint(to_f(v[3])));
+            uint4 b = make_uint4(__float_as_uint(to_f(v[4])), __float_as_uint(to_f(v[5])), __float_as_uint(to_f(v[6])), __float_as_uint(to_f(v[7])));
+            st_stream_v4(p, a);
+            st_stream_v4(p + 16, b);
+            break;
+        }
+    }
+        [[fallthrough]];
+    default:
+        if (dt == TADMA_F16 || dt == TADMA_BF16) {
+            float f[8];
+#pragma unroll
+            for (int j = 0; j < V; j++) f[j] = to_f(v[j]);
+            st_stream_v4(p, pack8(f, dt));
+        } else {
+#pragma unroll
+            for (int j = 0; j < V; j++) store_from(base, dt, off + j, v[j]);
+        }
+        break;
+    }
+}
+
+// ----------------------------------------------------------------- kernels --
+
+template <int NIN>
+__device__ __forceinline__ void offsets(const ChainParams& p, uint64_t e, int64_t& oo, int64_t (&io)[NIN > 0 ? NIN : 1]) {
+    oo = 0;
+#pragma unroll
+    for (int k = 0; k < NIN; k++) io[k] = 0;
+    for (int d = p.rank - 1; d >= 1; d--) {
+        uint64_t q, r;
+        p.dm[d].divmod(e, q, r);
+        oo += (int64_t)r * p.out_stride[d];
+#pragma unroll
+        for (int k = 0; k < NIN; k++) io[k] += (int64_t)r * p.in[k].stride[d];
+        e = q;
+    }
+    oo += (int64_t)e * p.out_stride[0];
+#pragma unroll
+    for (int k = 0; k < NIN; k++) io[k] += (int64_t)e * p.in[k].stride[0];
+}
+
+template <typename C, int NIN>
+__global__ void __launch_bounds__(THREADS) chain_vec_kernel(const __grid_constant__ ChainParams p) {
+    constexpr int NI = NIN > 0 ? NIN : 1;
+    const int64_t gstride = (int64_t)gridDim.x * THREADS;
+    for (int64_t base = (int64_t)blockIdx.x * THREADS + threadIdx.x; base < p.n; base += gstride * U) {
+        C val[U][NI][V];
+        int64_t oo[U];
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int64_t vi = base + u * gstride;
+            if (vi < p.n) {
+                int64_t io[NI];
+                offsets<NIN>(p, (uint64_t)vi * V, oo[u], io);
+#pragma unroll
+                for (int k = 0; k < NIN; k++) load_vec<C>(p.in[k], io[k], val[u][k]);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int64_t vi = base + u * gstride;
+            if (vi < p.n) {
+                C acc[V];
+#pragma unroll
+                for (int j = 0; j < V; j++) acc[j] = NIN > 0 ? val[u][0][j] : C(0);
+                run_chain<C, NIN, V>(p, acc, val[u]);
+                store_vec<C>(p.out, p.out_dtype, oo[u], acc);
+            }
+        }
+    }
+}
+
+template <typename C, int NIN>
+__global__ void __launch_bounds__(THREADS) chain_scalar_kernel(const __grid_constant__ ChainParams p) {
+    constexpr int NI = NIN > 0 ? NIN : 1;
+    const int64_t gstride = (int64_t)gridDim.x * THREADS;
+    for (int64_t e = p.start + (int64_t)blockIdx.x * THREADS + threadIdx.x; e < p.n; e += gstride) {
+        int64_t oo, io[NI];
+        offsets<NIN>(p, (uint64_t)e, oo, io);
+        C val[NI][1];
+#pragma unroll
+        for (int k = 0; k < NIN; k++) val[k][0] = load_as<C>(p.in[k].base, p.in[k].dtype, io[k]);
+        C acc[1] = {NIN > 0 ? val[0][0] : C(0)};
+        run_chain<C, NIN, 1>(p, acc, val);
+        store_from(p.out, p.out_dtype, oo, acc[0]);
+    }
+}
+
+// ------------------------------------------------------------ host side --
+
+int blocks_per_sm(const void* fn) {
+    static std::mutex mu;
+    static std::unordered_map<const void*, int> cache;
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(fn);
+    if (it != cache.end()) return it->second;
+    int nb = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, fn, THREADS, 0) != cudaSuccess || nb <= 0) nb = 1;
+    cache[fn] = nb;
+    return nb;
+}
+
+template <typename C, int NIN>
+int launch(const ChainParams& p, bool vec, int64_t work, cudaStream_t s) {
+    const void* fn = vec ? (const void*)chain_vec_kernel<C, NIN> : (const void*)chain_scalar_kernel<C, NIN>;
+    int64_t per_block = (int64_t)THREADS * (vec ? U : 1);
+    int64_t want = (work + per_block - 1) / per_block;
+    int64_t cap = (int64_t)sm_count() * blocks_per_sm(fn);
+    int grid = (int)(want < cap ? (want > 0 ? want : 1) : cap);
+    if (vec) chain_vec_kernel<C, NIN><<<grid, THREADS, 0, s>>>(p);
+    else chain_scalar_kernel<C, NIN><<<grid, THREADS, 0, s>>>(p);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? TADMA_OK : cuda_fail(e, "tadma_b200_eltwise launch");
+}
+
+template <typename C>
+int launch_nin(int nin, const ChainParams& p, bool vec, int64_t work, cudaStream_t s) {
+    switch (nin) {
+    case 0: return launch<C, 0>(p, vec, work, s);
+    case 1: return launch<C, 1>(p, vec, work, s);
+    case 2: return launch<C, 2>(p, vec, work, s);
+    case 3: return launch<C, 3>(p, vec, work, s);
+    default: return launch<C, 4>(p, vec, work, s);
+    }
+}
+
+bool is_transcendental(int op) { return op >= TADMA_OP_EXP && op <= TADMA_OP_GELU && op != TADMA_OP_RELU; }
+
+bool valid_op(int op) {
+    return (op >= 0 && op <= TADMA_OP_NOT) || (op >= TADMA_OP_ADD && op <= TADMA_OP_LOR) || op == TADMA_OP_WHERE;
+}
+
+}  // namespace
+
+// Same rule as the oracle: integer-only chains compute in int64, anything
+// touching f64/i64 in f64, the rest in f32.
+int resolve_compute(const tadma_tensor* out, const tadma_tensor* ins, int n_ins, const tadma_instr* prog, int n_instr,
+                    int compute) {
+    if (compute != TADMA_COMPUTE_AUTO) return compute;
+    bool all_int = !dtype_is_float(out->dtype);
+    bool any_wide = out->dtype == TADMA_F64 || out->dtype == TADMA_I64;
+    for (int k = 0; k < n_ins; k++) {
+        if (dtype_is_float(ins[k].dtype)) all_int = false;
+        if (ins[k].dtype == TADMA_F64 || ins[k].dtype == TADMA_I64) any_wide = true;
+    }
+    for (int i = 0; i < n_instr; i++) {
+        if (is_transcendental(prog[i].op) || prog[i].op == TADMA_OP_POW) all_int = false;
+        if ((prog[i].b == TADMA_SRC_IMM || prog[i].c == TADMA_SRC_IMM) && prog[i].imm != (double)(int64_t)prog[i].imm)
+            all_int = false;
+    }
+    if (all_int) return TADMA_COMPUTE_I64;
+    return any_wide ? TADMA_COMPUTE_F64 : TADMA_COMPUTE_F32;
+}
+
+}  // namespace tadma_b200
+
+using namespace tadma_b200;
+
+extern "C" int tadma_b200_eltwise(const tadma_tensor* out, const tadma_tensor* ins, int32_t n_ins,
+                                  const tadma_instr* prog, int32_t n_instr, int32_t compute, void* stream) {
+    std::string err = check_tensor(out, "out");
+    if (!err.empty()) return fail(TADMA_ERR_INVALID, err);
+    if (n_ins < 0 || n_ins > TADMA_MAX_INPUTS) return fail(TADMA_ERR_INVALID, "n_ins out of range [0, 4]");
+    if (n_instr < 0 || n_instr > TADMA_MAX_INSTR) return fail(TADMA_ERR_INVALID, "n_instr out of range [0, 16]");
+    if (n_ins > 0 && !ins) return fail(TADMA_ERR_INVALID, "ins is NULL");
+    if (n_instr > 0 && !prog) return fail(TADMA_ERR_INVALID, "prog is NULL");
+    for (int k = 0; k < n_ins; k++) {
+        err = check_tensor(&ins[k], "ins[k]");
+        if (!err.empty()) return fail(TADMA_ERR_INVALID, err);
+        if (ins[k].rank != out->rank) return fail(TADMA_ERR_INVALID, "ins[k] rank differs from out rank");
+        for (int d = 0; d < out->rank; d++)
+            if (ins[k].dims[d] != out->dims[d] && ins[k].dims[d] != 1)
+                return fail(TADMA_ERR_INVALID, "ins[k] dims not broadcastable to out dims");
+    }
+    for (int i = 0; i < n_instr; i++) {
+        const tadma_instr& I = prog[i];
+        if (!valid_op(I.op)) return fail(TADMA_ERR_INVALID, "unknown op code");
+        bool needs_b = I.op >= 32 || (I.op == TADMA_OP_COPY && I.b == TADMA_SRC_IMM);
+        if (needs_b && !(I.b == TADMA_SRC_IMM || (I.b >= 0 && I.b < n_ins)))
+            return fail(TADMA_ERR_INVALID, "operand selector b out of range");
+        if (I.op == TADMA_OP_WHERE && !(I.c == TADMA_SRC_IMM || (I.c >= 0 && I.c < n_ins)))
+            return fail(TADMA_ERR_INVALID, "operand selector c out of range");
+        if (I.round_dtype >= 0 && dtype_size(I.round_dtype) == 0) return fail(TADMA_ERR_INVALID, "bad round_dtype");
+    }
+    int cm = resolve_compute(out, ins, n_ins, prog, n_instr, compute);
+    if (cm < TADMA_COMPUTE_F32 || cm > TADMA_COMPUTE_I64) return fail(TADMA_ERR_INVALID, "bad compute mode");
+    if (cm == TADMA_COMPUTE_I64)
+        for (int i = 0; i < n_instr; i++)
+            if (is_transcendental(prog[i].op) || prog[i].op == TADMA_OP_POW)
+                return fail(TADMA_ERR_UNSUPPORTED, "transcendental op in int64 compute");
+    const int64_t n = numel(out);
+    if (n == 0) return TADMA_OK;
+
+    // Joint fold of out + inputs.
+    int64_t strides[1 + TADMA_MAX_INPUTS][TADMA_MAX_RANK];
+    for (int d = 0; d < out->rank; d++) {
+        strides[0][d] = out->strides[d];
+        for (int k = 0; k < n_ins; k++) strides[1 + k][d] = (ins[k].dims[d] == 1) ? 0 : ins[k].strides[d];
+    }
+    Folded f = fold(out->rank, out->dims, strides, 1 + n_ins);
+
+    ChainParams p{};
+    p.rank = f.rank;
+    p.n_instr = n_instr;
+    p.out_dtype = out->dtype;
+    p.out = (char*)out->data;
+    for (int d = 0; d < f.rank; d++) {
+        p.dims[d] = f.dims[d];
+        p.out_stride[d] = f.strides[0][d];
+    }
+    for (int k = 0; k < n_ins; k++) {
+        Operand& o = p.in[k];
+        o.base = (const char*)ins[k].data;
+        o.dtype = ins[k].dtype;
+        o.streaming = 1;
+        for (int d = 0; d < f.rank; d++) {
+            o.stride[d] = f.strides[1 + k][d];
+            if (o.stride[d] == 0 && f.dims[d] > 1) o.streaming = 0;
+        }
+        if (ins[k].data == out->data) o.streaming = 0;  // in-place: keep coherent loads
+    }
+    for (int i = 0; i < n_instr; i++) p.prog[i] = prog[i];
+
+    // Vector-path eligibility.
+    const int last = f.rank - 1;
+    const int64_t inner = f.dims[last];
+    auto aligned = [&](const void* ptr, int dt, const int64_t* st) {
+        int64_t a = 8 * dtype_size(dt);
+        if (a > 16) a = 16;
+        if ((uintptr_t)ptr % (uintptr_t)a) return false;
+        for (int d = 0; d < last; d++)
+            if ((st[d] * dtype_size(dt)) % a) return false;
+        return true;
+    };
+    bool vec = f.strides[0][last] == 1 && aligned(out->data, out->dtype, f.strides[0]);
+    for (int k = 0; k < n_ins && vec; k++) {
+        int64_t s = f.strides[1 + k][last];
+        if (s == 1) vec = aligned(ins[k].data, ins[k].dtype, f.strides[1 + k]);
+        else if (s == 0) p.in[k].inner_bcast = 1;
+        else vec = false;
+    }
+    if (f.rank > 1 && inner % V) vec = false;
+    if (n < V) vec = false;
+    // Both paths decompose ELEMENT indices; a vector (V elements, inner % V
+    // == 0 when rank > 1) never straddles a row.
+    for (int d = 1; d < f.rank; d++) p.dm[d] = DivMod((uint64_t)f.dims[d]);
+
+    cudaStream_t s = (cudaStream_t)stream;
+    auto go = [&](bool v, int64_t work) {
+        switch (cm) {
+        case TADMA_COMPUTE_F32: return launch_nin<float>(n_ins, p, v, work, s);
+        case TADMA_COMPUTE_F64: return launch_nin<double>(n_ins, p, v, work, s);
+        default: return launch_nin<int64_t>(n_ins, p, v, work, s);
+        }
+    };
+    if (!vec) {
+        p.start = 0;
+        p.n = n;
+        return go(false, n);
+    }
+    // Vector path: vector vi covers elements [vi * V, vi * V + V); a rank-1
+    // tail of n % V elements goes to the scalar kernel afterwards.
+    const int64_t nvec = n / V;
+    ChainParams pv = p;
+    pv.n = nvec;
+    int rc;
+    switch (cm) {
+    case TADMA_COMPUTE_F32: rc = launch_nin<float>(n_ins, pv, true, nvec, s); break;
+    case TADMA_COMPUTE_F64: rc = launch_nin<double>(n_ins, pv, true, nvec, s); break;
+    default: rc = launch_nin<int64_t>(n_ins, pv, true, nvec, s); break;
+    }
+    if (rc != TADMA_OK) return rc;
+    if (nvec * V < n) {
+        p.start = nvec * V;
+        p.n = n;
+        return go(false, n - nvec * V);
+    }
+    return TADMA_OK;
+}

@@ -1,0 +1,128 @@
+// fill.cu - counter-based seeded generator (sm_100a).
+//
+// Element i of a tensor (global index g = offset + i) is a pure function of
+// (seed, stream_id, g): the splitmix64 finaliser of a Weyl sequence keyed by
+// (seed, stream_id).  Any shard therefore generates bit-identically on any
+// GPU count, and the host oracle regenerates any element.  Floating values
+// are built in double with explicitly rounded operations (no contraction),
+// then rounded to fp32 and, for 16-bit types, from fp32 to the target.
+//   UNIFORM: p0 + (p1 - p0) * (k * 2^-24),        k = top 24 bits of draw 0
+//   NORMAL : p0 + p1 * (sqrt(3)/2 * sum_{j<4} (k_j * 2^-23 - 1))
+//            (Irwin-Hall(4) of U(-1,1), rescaled to unit variance)
+//   INDEX  : floor(draw0 * n / 2^64)  (multiply-shift, bias < n / 2^64)
+// The reference's randn (Operations.hpp:290-297) is host-only and seeded
+// from std::random_device, so it cannot reproduce runs.
+#include "common.cuh"
+#include "layout.hpp"
+
+namespace tadma_b200 {
+namespace {
+
+constexpr int THREADS = 256;
+
+__host__ __device__ __forceinline__ uint64_t mix64(uint64_t z) {
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ULL;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBULL;
+    return z ^ (z >> 31);
+}
+
+__device__ __forceinline__ uint64_t draw(uint64_t key, uint64_t g, uint64_t j) {
+    return mix64(key + (4 * g + j + 1) * 0x9E3779B97F4A7C15ULL);
+}
+
+struct FillParams {
+    char* out;
+    int32_t dtype, dist;
+    double p0, p1, span;
+    uint64_t key;
+    uint64_t n_ids;
+    int64_t offset, n;
+    int32_t rank, contiguous;
+    DivMod dm[TADMA_MAX_RANK];
+    int64_t strides[TADMA_MAX_RANK];
+};
+
+__global__ void __launch_bounds__(THREADS) fill_kernel(const __grid_constant__ FillParams p) {
+    const int64_t stride = (int64_t)gridDim.x * THREADS;
+    for (int64_t i = (int64_t)blockIdx.x * THREADS + threadIdx.x; i < p.n; i += stride) {
+        int64_t off = i;
+        if (!p.contiguous) {
+            uint64_t e = (uint64_t)i;
+            off = 0;
+            for (int d = p.rank - 1; d >= 1; d--) {
+                uint64_t q, r;
+                p.dm[d].divmod(e, q, r);
+                off += (int64_t)r * p.strides[d];
+                e = q;
+            }
+            off += (int64_t)e * p.strides[0];
+        }
+        const uint64_t g = (uint64_t)(p.offset + i);
+        if (p.dist == TADMA_DIST_INDEX) {
+            const uint64_t id = __umul64hi(draw(p.key, g, 0), p.n_ids);
+            store_from(p.out, p.dtype, off, (int64_t)id);
+        } else if (p.dist == TADMA_DIST_UNIFORM) {
+            const double u = __dmul_rn(__ull2double_rn(draw(p.key, g, 0) >> 40), 0x1p-24);
+            store_from(p.out, p.dtype, off, __dadd_rn(p.p0, __dmul_rn(p.span, u)));
+        } else {
+            double s = 0.0;
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+                s = __dadd_rn(s, __dsub_rn(__dmul_rn(__ull2double_rn(draw(p.key, g, (uint64_t)j) >> 40), 0x1p-23), 1.0));
+            const double z = __dmul_rn(s, 0.8660254037844386);
+            store_from(p.out, p.dtype, off, __dadd_rn(p.p0, __dmul_rn(p.p1, z)));
+        }
+    }
+}
+
+}  // namespace
+}  // namespace tadma_b200
+
+using namespace tadma_b200;
+
+extern "C" int tadma_b200_fill(const tadma_tensor* out, int32_t dist, double p0, double p1, uint64_t seed,
+                               uint64_t stream_id, int64_t offset, void* stream) {
+    std::string err = check_tensor(out, "out");
+    if (!err.empty()) return fail(TADMA_ERR_INVALID, err);
+    if (dist < TADMA_DIST_UNIFORM || dist > TADMA_DIST_INDEX) return fail(TADMA_ERR_INVALID, "unknown distribution");
+    if (dist == TADMA_DIST_INDEX && (dtype_is_float(out->dtype) || !(p1 >= 1.0)))
+        return fail(TADMA_ERR_INVALID, "INDEX fills an integer tensor with n = p1 >= 1");
+    if (dist != TADMA_DIST_INDEX && !dtype_is_float(out->dtype))
+        return fail(TADMA_ERR_INVALID, "UNIFORM / NORMAL fill float tensors");
+    if (offset < 0) return fail(TADMA_ERR_INVALID, "negative offset");
+    const int64_t n = numel(out);
+    if (n == 0) return TADMA_OK;
+    FillParams p{};
+    p.out = (char*)out->data;
+    p.dtype = out->dtype;
+    p.dist = dist;
+    p.p0 = p0;
+    p.p1 = p1;
+    p.span = p1 - p0;
+    p.key = mix64(seed ^ mix64(stream_id + 0x632BE59BD9B4E019ULL));
+    p.n_ids = dist == TADMA_DIST_INDEX ? (uint64_t)p1 : 0;
+    p.offset = offset;
+    p.n = n;
+    p.rank = out->rank > 0 ? out->rank : 1;
+    // contiguous row-major?
+    int64_t expect = 1;
+    p.contiguous = 1;
+    for (int d = out->rank - 1; d >= 0; d--) {
+        if (out->dims[d] != 1 && out->strides[d] != expect) p.contiguous = 0;
+        expect *= out->dims[d];
+    }
+    if (out->rank == 0) {
+        p.dm[0] = DivMod(1);
+        p.strides[0] = 0;
+    }
+    for (int d = 0; d < out->rank; d++) {
+        p.dm[d] = DivMod((uint64_t)out->dims[d]);
+        p.strides[d] = out->strides[d];
+    }
+    int64_t want = (n + THREADS - 1) / THREADS;
+    int64_t cap = (int64_t)sm_count() * 8;
+    int grid = (int)(want < cap ? want : cap);
+    fill_kernel<<<grid, THREADS, 0, (cudaStream_t)stream>>>(p);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? TADMA_OK : cuda_fail(e, "tadma_b200_fill launch");
+}

@@ -1,0 +1,444 @@
+// norm.cu - fused reduce-then-broadcast row kernels (sm_100a): softmax,
+// LayerNorm (ONNX and TADMA eps placement) and RMSNorm.
+//
+// The reference composes these from separate kernels, every intermediate a
+// full tensor in HBM:
+// * softmax (Operations.hpp:190-193): exp node, sum ReduceKernel, in-place
+//   divide node -> 3 reads + 2 writes of the data, and no max subtraction
+//   (fp16 exp overflows for x > ~11);
+// * layer_norm (Operations.hpp:195-220): mean reduce, squared-difference
+//   node, sqrt-post reduce, normalise node -> ~5 passes;
+// * rms_norm (Operations.hpp:222-233): square-pre reduce, divide node.
+//
+// Here a row of up to 32 lanes x 8 chunks x 16 bytes (2048 fp16/bf16 or
+// 1024 fp32 elements) lives in one warp's registers: one 16-byte-vector
+// read, the statistics by shuffle butterflies, one write.  Softmax subtracts
+// the row max (same value in exact arithmetic, no overflow).  Longer or
+// strided rows take a block-per-row kernel that re-reads the row (L2-hot).
+#include <mutex>
+#include <unordered_map>
+
+#include "common.cuh"
+#include "layout.hpp"
+
+namespace tadma_b200 {
+namespace {
+
+enum Mode { M_SOFTMAX = 0, M_LN_ONNX = 1, M_LN_TADMA = 2, M_RMS = 3 };
+
+constexpr int THREADS = 256;
+
+struct NormParams {
+    const char* in;
+    char* out;
+    const char* gamma;
+    const char* beta;
+    int32_t dtype, out_dtype, g_dtype, b_dtype;
+    int32_t gb_vec;  // gamma/beta have x's dtype, stride 1, 16-byte aligned
+    int32_t mode;
+    float eps;
+    int32_t pad;
+    int64_t nrows, L;
+    int64_t in_row_stride, out_row_stride;
+    int64_t in_ax_stride, out_ax_stride;
+    int64_t g_stride, b_stride;
+    // folded row dims (block kernel)
+    int32_t krank, pad2;
+    DivMod kdm[TADMA_MAX_RANK];
+    int64_t kin[TADMA_MAX_RANK];
+    int64_t kout[TADMA_MAX_RANK];
+};
+
+template <typename T>
+struct VecT;
+template <>
+struct VecT<float> {
+    static constexpr int N = 4;
+    static constexpr int DT = TADMA_F32;
+};
+template <>
+struct VecT<__half> {
+    static constexpr int N = 8;
+    static constexpr int DT = TADMA_F16;
+};
+template <>
+struct VecT<__nv_bfloat16> {
+    static constexpr int N = 8;
+    static constexpr int DT = TADMA_BF16;
+};
+
+template <typename T>
+__device__ __forceinline__ void cvt_in(uint4 r, float* f) {
+    if constexpr (sizeof(T) == 4) {
+        f[0] = __uint_as_float(r.x);
+        f[1] = __uint_as_float(r.y);
+        f[2] = __uint_as_float(r.z);
+        f[3] = __uint_as_float(r.w);
+    } else {
+        unpack8(r, VecT<T>::DT, f);
+    }
+}
+
+template <typename T>
+__device__ __forceinline__ uint4 cvt_out(const float* f) {
+    if constexpr (sizeof(T) == 4) {
+        return make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]), __float_as_uint(f[3]));
+    } else {
+        return pack8(f, VecT<T>::DT);
+    }
+}
+
+template <typename T>
+__device__ __forceinline__ float fast_exp(float x) {
+    // 16-bit outputs: the fast exponential's few-ulp fp32 error is far below
+    // half an fp16/bf16 ulp; fp32 outputs use the accurate expf.
+    if constexpr (sizeof(T) == 4) return expf(x);
+    else return __expf(x);
+}
+
+// ----------------------------------------------------------- warp kernel --
+
+template <typename T, int CH, int MODE>
+__global__ void __launch_bounds__(THREADS) rownorm_warp_kernel(const __grid_constant__ NormParams p) {
+    constexpr int N = VecT<T>::N;
+    const int lane = threadIdx.x & 31;
+    const int64_t gw = ((int64_t)blockIdx.x * THREADS + threadIdx.x) >> 5;
+    const int64_t nw = ((int64_t)gridDim.x * THREADS) >> 5;
+    const float fL = (float)p.L;
+    for (int64_t row = gw; row < p.nrows; row += nw) {
+        const T* x = reinterpret_cast<const T*>(p.in) + row * p.in_row_stride;
+        T* y = reinterpret_cast<T*>(p.out) + row * p.out_row_stride;
+        float v[CH][N];
+#pragma unroll
+        for (int c = 0; c < CH; c++) {
+            const int64_t col = ((int64_t)c * 32 + lane) * N;
+            if (col < p.L) {
+                cvt_in<T>(ld_stream_v4(x + col), v[c]);
+            } else {
+#pragma unroll
+                for (int j = 0; j < N; j++) v[c][j] = (MODE == M_SOFTMAX) ? -INFINITY : 0.0f;
+            }
+        }
+        if constexpr (MODE == M_SOFTMAX) {
+            float m = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < CH; c++)
+#pragma unroll
+                for (int j = 0; j < N; j++) m = fmaxf(m, v[c][j]);
+            m = warp_max(m);
+            float s = 0.0f;
+#pragma unroll
+            for (int c = 0; c < CH; c++)
+#pragma unroll
+                for (int j = 0; j < N; j++) {
+                    v[c][j] = fast_exp<T>(v[c][j] - m);
+                    s += v[c][j];
+                }
+            s = warp_sum(s);
+            const float inv = 1.0f / s;
+#pragma unroll
+            for (int c = 0; c < CH; c++)
+#pragma unroll
+                for (int j = 0; j < N; j++) v[c][j] *= inv;
+        } else if constexpr (MODE == M_RMS) {
+            float ss = 0.0f;
+#pragma unroll
+            for (int c = 0; c < CH; c++)
+#pragma unroll
+                for (int j = 0; j < N; j++) ss += v[c][j] * v[c][j];
+            ss = warp_sum(ss);
+            const float r = 1.0f / sqrtf(ss / fL + p.eps);
+#pragma unroll
+            for (int c = 0; c < CH; c++)
+#pragma unroll
+                for (int j = 0; j < N; j++) v[c][j] *= r;
+        } else {
+            float sum = 0.0f;
+#pragma unroll
+            for (int c = 0; c < CH; c++)
+#pragma unroll
+                for (int j = 0; j < N; j++) sum += v[c][j];
+            const float mean = warp_sum(sum) / fL;
+            float sq = 0.0f;
+#pragma unroll
+            for (int c = 0; c < CH; c++) {
+                const int64_t col = ((int64_t)c * 32 + lane) * N;
+                if (col < p.L) {
+#pragma unroll
+                    for (int j = 0; j < N; j++) {
+                        const float d = v[c][j] - mean;
+                        sq += d * d;
+                    }
+                }
+            }
+            const float var = warp_sum(sq) / fL;
+            const float rstd = (MODE == M_LN_ONNX) ? 1.0f / sqrtf(var + p.eps) : 1.0f / (sqrtf(var) + p.eps);
+#pragma unroll
+            for (int c = 0; c < CH; c++) {
+                const int64_t col = ((int64_t)c * 32 + lane) * N;
+                if (col < p.L) {
+                    float g[N], b[N];
+                    if (p.gb_vec) {
+                        if (p.gamma) cvt_in<T>(ld_v4(reinterpret_cast<const T*>(p.gamma) + col), g);
+                        if (p.beta) cvt_in<T>(ld_v4(reinterpret_cast<const T*>(p.beta) + col), b);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < N; j++) {
+                            if (p.gamma) g[j] = load_as<float>(p.gamma, p.g_dtype, (col + j) * p.g_stride);
+                            if (p.beta) b[j] = load_as<float>(p.beta, p.b_dtype, (col + j) * p.b_stride);
+                        }
+                    }
+#pragma unroll
+                    for (int j = 0; j < N; j++) {
+                        float t = (v[c][j] - mean) * rstd;
+                        if (p.gamma) t = t * g[j];
+                        if (p.beta) t = t + b[j];
+                        v[c][j] = t;
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int c = 0; c < CH; c++) {
+            const int64_t col = ((int64_t)c * 32 + lane) * N;
+            if (col < p.L) st_stream_v4(y + col, cvt_out<T>(v[c]));
+        }
+    }
+}
+
+// ---------------------------------------------------------- block kernel --
+// One CTA per row, any axis stride and dtype; re-reads the row per pass.
+
+__device__ __forceinline__ float block_reduce(float v, bool is_max, float* sh) {
+    v = is_max ? warp_max(v) : warp_sum(v);
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    __syncthreads();
+    if (lane == 0) sh[w] = v;
+    __syncthreads();
+    float r = sh[0];
+    for (int i = 1; i < THREADS / 32; i++) r = is_max ? fmaxf(r, sh[i]) : r + sh[i];
+    return r;
+}
+
+__global__ void __launch_bounds__(THREADS) rownorm_block_kernel(const __grid_constant__ NormParams p) {
+    __shared__ float sh[THREADS / 32];
+    for (int64_t row = blockIdx.x; row < p.nrows; row += gridDim.x) {
+        uint64_t e = (uint64_t)row;
+        int64_t ib = 0, ob = 0;
+        for (int d = p.krank - 1; d >= 1; d--) {
+            uint64_t q, r;
+            p.kdm[d].divmod(e, q, r);
+            ib += (int64_t)r * p.kin[d];
+            ob += (int64_t)r * p.kout[d];
+            e = q;
+        }
+        ib += (int64_t)e * p.kin[0];
+        ob += (int64_t)e * p.kout[0];
+        const float fL = (float)p.L;
+        float a = 0.0f, b = 0.0f;
+        if (p.mode == M_SOFTMAX) {
+            float m = -INFINITY;
+            for (int64_t i = threadIdx.x; i < p.L; i += THREADS) m = fmaxf(m, load_as<float>(p.in, p.dtype, ib + i * p.in_ax_stride));
+            a = block_reduce(m, true, sh);
+            float s = 0.0f;
+            for (int64_t i = threadIdx.x; i < p.L; i += THREADS) s += expf(load_as<float>(p.in, p.dtype, ib + i * p.in_ax_stride) - a);
+            b = 1.0f / block_reduce(s, false, sh);
+        } else if (p.mode == M_RMS) {
+            float ss = 0.0f;
+            for (int64_t i = threadIdx.x; i < p.L; i += THREADS) {
+                float v = load_as<float>(p.in, p.dtype, ib + i * p.in_ax_stride);
+                ss += v * v;
+            }
+            b = 1.0f / sqrtf(block_reduce(ss, false, sh) / fL + p.eps);
+        } else {
+            float s = 0.0f;
+            for (int64_t i = threadIdx.x; i < p.L; i += THREADS) s += load_as<float>(p.in, p.dtype, ib + i * p.in_ax_stride);
+            a = block_reduce(s, false, sh) / fL;
+            float sq = 0.0f;
+            for (int64_t i = threadIdx.x; i < p.L; i += THREADS) {
+                float d = load_as<float>(p.in, p.dtype, ib + i * p.in_ax_stride) - a;
+                sq += d * d;
+            }
+            const float var = block_reduce(sq, false, sh) / fL;
+            b = (p.mode == M_LN_ONNX) ? 1.0f / sqrtf(var + p.eps) : 1.0f / (sqrtf(var) + p.eps);
+        }
+        for (int64_t i = threadIdx.x; i < p.L; i += THREADS) {
+            float v = load_as<float>(p.in, p.dtype, ib + i * p.in_ax_stride);
+            float r;
+            if (p.mode == M_SOFTMAX) r = expf(v - a) * b;
+            else if (p.mode == M_RMS) r = v * b;
+            else {
+                r = (v - a) * b;
+                if (p.gamma) r = r * load_as<float>(p.gamma, p.g_dtype, i * p.g_stride);
+                if (p.beta) r = r + load_as<float>(p.beta, p.b_dtype, i * p.b_stride);
+            }
+            store_from(p.out, p.out_dtype, ob + i * p.out_ax_stride, r);
+        }
+        __syncthreads();  // all reads of this row done before a possible in-place next row
+    }
+}
+
+// ------------------------------------------------------------- host side --
+
+int blocks_per_sm(const void* fn) {
+    static std::mutex mu;
+    static std::unordered_map<const void*, int> cache;
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(fn);
+    if (it != cache.end()) return it->second;
+    int nb = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, fn, THREADS, 0) != cudaSuccess || nb <= 0) nb = 1;
+    cache[fn] = nb;
+    return nb;
+}
+
+template <typename T, int CH, int MODE>
+int launch_warp(const NormParams& p, cudaStream_t s) {
+    const void* fn = (const void*)rownorm_warp_kernel<T, CH, MODE>;
+    int64_t want = (p.nrows + (THREADS / 32) - 1) / (THREADS / 32);
+    int64_t cap = (int64_t)sm_count() * blocks_per_sm(fn);
+    int grid = (int)(want < cap ? (want > 0 ? want : 1) : cap);
+    rownorm_warp_kernel<T, CH, MODE><<<grid, THREADS, 0, s>>>(p);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? TADMA_OK : cuda_fail(e, "row-norm launch");
+}
+
+template <typename T, int MODE>
+int launch_ch(int ch, const NormParams& p, cudaStream_t s) {
+    switch (ch) {
+    case 1: return launch_warp<T, 1, MODE>(p, s);
+    case 2: return launch_warp<T, 2, MODE>(p, s);
+    case 4: return launch_warp<T, 4, MODE>(p, s);
+    default: return launch_warp<T, 8, MODE>(p, s);
+    }
+}
+
+template <typename T>
+int launch_mode(int mode, int ch, const NormParams& p, cudaStream_t s) {
+    switch (mode) {
+    case M_SOFTMAX: return launch_ch<T, M_SOFTMAX>(ch, p, s);
+    case M_LN_ONNX: return launch_ch<T, M_LN_ONNX>(ch, p, s);
+    case M_LN_TADMA: return launch_ch<T, M_LN_TADMA>(ch, p, s);
+    default: return launch_ch<T, M_RMS>(ch, p, s);
+    }
+}
+
+int run_rownorm(int mode, const tadma_tensor* in, int32_t axis, const tadma_tensor* gamma, const tadma_tensor* beta,
+                double eps, const tadma_tensor* out, cudaStream_t s) {
+    std::string err = check_tensor(in, "in");
+    if (err.empty()) err = check_tensor(out, "out");
+    if (!err.empty()) return fail(TADMA_ERR_INVALID, err);
+    if (in->rank < 1) return fail(TADMA_ERR_INVALID, "rank must be >= 1");
+    if (out->rank != in->rank) return fail(TADMA_ERR_INVALID, "out rank differs from in rank");
+    for (int d = 0; d < in->rank; d++)
+        if (out->dims[d] != in->dims[d]) return fail(TADMA_ERR_INVALID, "out dims differ from in dims");
+    if (!dtype_is_float(in->dtype) || !dtype_is_float(out->dtype)) return fail(TADMA_ERR_INVALID, "float dtypes only");
+    const int ax = axis < 0 ? axis + in->rank : axis;
+    if (ax < 0 || ax >= in->rank) return fail(TADMA_ERR_INVALID, "axis out of range");
+    const int64_t L = in->dims[ax];
+    NormParams p{};
+    p.in = (const char*)in->data;
+    p.out = (char*)out->data;
+    p.dtype = in->dtype;
+    p.out_dtype = out->dtype;
+    p.mode = mode;
+    p.eps = (float)eps;
+    p.L = L;
+    p.in_ax_stride = in->strides[ax];
+    p.out_ax_stride = out->strides[ax];
+    for (int k = 0; k < 2; k++) {
+        const tadma_tensor* t = k == 0 ? gamma : beta;
+        if (!t || !t->data) continue;
+        err = check_tensor(t, k == 0 ? "gamma" : "beta");
+        if (!err.empty()) return fail(TADMA_ERR_INVALID, err);
+        if (t->rank != 1 || t->dims[0] != L) return fail(TADMA_ERR_INVALID, "gamma/beta must be 1-D of the normalised length");
+        if (k == 0) {
+            p.gamma = (const char*)t->data;
+            p.g_dtype = t->dtype;
+            p.g_stride = t->strides[0];
+        } else {
+            p.beta = (const char*)t->data;
+            p.b_dtype = t->dtype;
+            p.b_stride = t->strides[0];
+        }
+    }
+    if (numel(in) == 0) return TADMA_OK;
+
+    int64_t kd[TADMA_MAX_RANK], ks[2][TADMA_MAX_RANK];
+    int kr = 0;
+    for (int d = 0; d < in->rank; d++) {
+        if (d == ax) continue;
+        kd[kr] = in->dims[d];
+        ks[0][kr] = in->strides[d];
+        ks[1][kr] = out->strides[d];
+        kr++;
+    }
+    Folded f = fold(kr, kd, ks, 2);
+    p.nrows = 1;
+    for (int d = 0; d < f.rank; d++) p.nrows *= f.dims[d];
+
+    const int dt = in->dtype;
+    const int es = dtype_size(dt);
+    const int N = 16 / es;
+    const bool fast_dt = (dt == TADMA_F32 || dt == TADMA_F16 || dt == TADMA_BF16) && out->dtype == dt;
+    const int64_t cap = 32LL * N * 8;
+    if (fast_dt && f.rank == 1 && p.in_ax_stride == 1 && p.out_ax_stride == 1 && L % N == 0 && L <= cap &&
+        (uintptr_t)in->data % 16 == 0 && (uintptr_t)out->data % 16 == 0 &&
+        (f.strides[0][0] * es) % 16 == 0 && (f.strides[1][0] * es) % 16 == 0) {
+        p.in_row_stride = f.strides[0][0];
+        p.out_row_stride = f.strides[1][0];
+        p.gb_vec = 1;
+        for (int k = 0; k < 2; k++) {
+            const char* ptr = k == 0 ? p.gamma : p.beta;
+            if (!ptr) continue;
+            int gdt = k == 0 ? p.g_dtype : p.b_dtype;
+            int64_t gs = k == 0 ? p.g_stride : p.b_stride;
+            if (gdt != dt || gs != 1 || (uintptr_t)ptr % 16) p.gb_vec = 0;
+        }
+        const int64_t per = 32LL * N;
+        int ch = (int)((L + per - 1) / per);
+        ch = ch <= 1 ? 1 : ch <= 2 ? 2 : ch <= 4 ? 4 : 8;
+        switch (dt) {
+        case TADMA_F32: return launch_mode<float>(mode, ch, p, s);
+        case TADMA_F16: return launch_mode<__half>(mode, ch, p, s);
+        default: return launch_mode<__nv_bfloat16>(mode, ch, p, s);
+        }
+    }
+    p.krank = f.rank;
+    for (int d = 0; d < f.rank; d++) {
+        p.kdm[d] = DivMod((uint64_t)f.dims[d]);
+        p.kin[d] = f.strides[0][d];
+        p.kout[d] = f.strides[1][d];
+    }
+    int64_t cap_blocks = (int64_t)sm_count() * blocks_per_sm((const void*)rownorm_block_kernel);
+    int grid = (int)(p.nrows < cap_blocks ? p.nrows : cap_blocks);
+    rownorm_block_kernel<<<grid, THREADS, 0, s>>>(p);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? TADMA_OK : cuda_fail(e, "row-norm launch");
+}
+
+}  // namespace
+}  // namespace tadma_b200
+
+using namespace tadma_b200;
+
+extern "C" int tadma_b200_softmax(const tadma_tensor* in, int32_t axis, const tadma_tensor* out, void* stream) {
+    return run_rownorm(M_SOFTMAX, in, axis, nullptr, nullptr, 0.0, out, (cudaStream_t)stream);
+}
+
+extern "C" int tadma_b200_layer_norm(const tadma_tensor* in, int32_t axis, const tadma_tensor* gamma,
+                                     const tadma_tensor* beta, double eps, int32_t mode, const tadma_tensor* out,
+                                     void* stream) {
+    if (mode != TADMA_LN_ONNX && mode != TADMA_LN_TADMA) return fail(TADMA_ERR_INVALID, "unknown layer-norm mode");
+    if (in) {
+        const int ax = axis < 0 ? axis + in->rank : axis;
+        if (ax != in->rank - 1) return fail(TADMA_ERR_UNSUPPORTED, "layer_norm: only the last axis");
+    }
+    return run_rownorm(mode == TADMA_LN_ONNX ? M_LN_ONNX : M_LN_TADMA, in, axis, gamma, beta, eps, out,
+                       (cudaStream_t)stream);
+}
+
+extern "C" int tadma_b200_rms_norm(const tadma_tensor* in, int32_t axis, double eps, const tadma_tensor* out,
+                                   void* stream) {
+    return run_rownorm(M_RMS, in, axis, nullptr, nullptr, eps, out, (cudaStream_t)stream);
+}

@@ -1,0 +1,504 @@
+// reduce.cu - reduction engine (sm_100a): sum / mean / max / min / argmax /
+// argmin / sum-of-squares / rms along one axis.
+//
+// Replaces ReduceNode + ReduceKernel (kernels/Reduce.hpp:10-71), which moves
+// the reduced axis to dim 0 with transpose<D,0> and runs one block per output
+// element: a strided per-thread fold, then a shared-memory tree with a
+// __syncthreads per level.  For a middle axis the lanes of a warp read
+// addresses one row-stride apart (uncoalesced), and fp16 accumulates in fp16.
+//
+// Here the input is folded to [outer, R, inner] (layout.hpp) and:
+// * ROW path (reduced axis contiguous, e.g. sum<-1>): one warp per output
+//   row, 16-byte loads (4 x fp32 / 8 x 16-bit) with 4 loads in flight per
+//   lane, fp32 accumulation, a 5-step shuffle butterfly;
+// * COL path (reduced axis strided, inner contiguous, e.g. mean<1> of
+//   [32,4096,4096]): a CTA owns 32 x VEC adjacent output columns; its 8 warps
+//   split R (rows w, w+8, ...), each lane reading 16 contiguous bytes per row
+//   so every warp load is a fully used 512-byte run; partials combine through
+//   shared memory in warp order;
+// * GENERIC path: any other layout / dtype, one warp per output element.
+// Every path assigns elements to lanes and combines partials in a fixed
+// order, so results are deterministic run to run.
+#include <mutex>
+#include <type_traits>
+#include <unordered_map>
+
+#include "common.cuh"
+#include "layout.hpp"
+#include "ops.cuh"
+
+namespace tadma_b200 {
+namespace {
+
+enum Kind { K_SUM = 0, K_MAX = 1, K_MIN = 2, K_ARGMAX = 3, K_ARGMIN = 4 };
+enum Post { P_NONE = 0, P_MEAN = 1, P_RMS = 2 };
+
+constexpr int THREADS = 256;
+constexpr int WARPS = THREADS / 32;
+
+struct RedParams {
+    const char* in;
+    char* out;
+    int32_t in_dtype, out_dtype;
+    int32_t pre_op, square, post, kind;
+    int64_t R;               // reduced extent
+    int64_t r_stride;        // input stride along the reduced axis
+    int64_t nrows;           // ROW: output count; COL: outer extent
+    int64_t inner;           // COL: inner extent
+    int64_t in_row_stride;   // ROW: input stride between outputs; COL: outer stride
+    int64_t out_row_stride;  // ROW: output stride; COL: outer stride
+    // GENERIC: folded kept dims
+    int32_t krank, pad;
+    int64_t kdims[TADMA_MAX_RANK];
+    DivMod kdm[TADMA_MAX_RANK];
+    int64_t kin[TADMA_MAX_RANK];
+    int64_t kout[TADMA_MAX_RANK];
+};
+
+// ------------------------------------------------------------ state ops --
+
+template <typename A>
+struct State {
+    A v;
+    int64_t i;  // argument index (ARG kinds), -1 = empty
+};
+
+template <int K, typename A>
+__device__ __forceinline__ State<A> init_state() {
+    State<A> s;
+    s.i = -1;
+    s.v = A(0);
+    if constexpr (std::is_floating_point<A>::value) {
+        if (K == K_MAX) s.v = -INFINITY;
+        if (K == K_MIN) s.v = INFINITY;
+    } else {
+        if (K == K_MAX) s.v = INT64_MIN;
+        if (K == K_MIN) s.v = INT64_MAX;
+    }
+    return s;
+}
+
+// Fold element v (index idx, visited in increasing order within a lane).
+template <int K, typename A>
+__device__ __forceinline__ void update(State<A>& s, A v, int64_t idx) {
+    if (K == K_SUM) {
+        s.v = s.v + v;
+    } else if (K == K_MAX) {
+        s.v = (v > s.v || v != v) ? v : s.v;  // NaN sticks once seen
+    } else if (K == K_MIN) {
+        s.v = (v < s.v || v != v) ? v : s.v;
+    } else {
+        const bool better = (K == K_ARGMAX) ? (v > s.v) : (v < s.v);
+        const bool take = s.i < 0 || (s.v == s.v && (better || v != v));
+        if (take) {
+            s.v = v;
+            s.i = idx;
+        }
+    }
+}
+
+// Combine two partial states; ties and NaN resolve to the lower index.
+template <int K, typename A>
+__device__ __forceinline__ State<A> combine(State<A> a, State<A> b) {
+    if (K == K_SUM) {
+        a.v = a.v + b.v;
+        return a;
+    } else if (K == K_MAX) {
+        a.v = (b.v > a.v || b.v != b.v) ? b.v : a.v;
+        return a;
+    } else if (K == K_MIN) {
+        a.v = (b.v < a.v || b.v != b.v) ? b.v : a.v;
+        return a;
+    } else {
+        if (b.i < 0) return a;
+        if (a.i < 0) return b;
+        const bool an = a.v != a.v, bn = b.v != b.v;
+        if (an || bn) {
+            if (an && bn) return a.i < b.i ? a : b;
+            return an ? a : b;
+        }
+        const bool b_better = (K == K_ARGMAX) ? (b.v > a.v) : (b.v < a.v);
+        if (b_better || (b.v == a.v && b.i < a.i)) return b;
+        return a;
+    }
+}
+
+template <int K, typename A>
+__device__ __forceinline__ State<A> warp_combine(State<A> s) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        State<A> t;
+        t.v = __shfl_xor_sync(0xffffffffu, s.v, o);
+        t.i = __shfl_xor_sync(0xffffffffu, s.i, o);
+        // Keep the combine order fixed: lower lane is the left operand.
+        s = ((threadIdx.x & 31) & o) ? combine<K, A>(t, s) : combine<K, A>(s, t);
+    }
+    return s;
+}
+
+template <typename A>
+__device__ __forceinline__ A prep(const RedParams& p, A v) {
+    if (p.pre_op != TADMA_OP_COPY) v = unary(p.pre_op, v);
+    if (p.square) v = v * v;
+    return v;
+}
+
+template <int K, typename A>
+__device__ __forceinline__ void finish(const RedParams& p, const State<A>& s, int64_t off) {
+    if (K == K_ARGMAX || K == K_ARGMIN) {
+        store_from(p.out, p.out_dtype, off, (int64_t)(s.i < 0 ? 0 : s.i));
+        return;
+    }
+    A v = s.v;
+    if constexpr (std::is_floating_point<A>::value) {
+        if (p.post == P_MEAN) v = v / (A)p.R;
+        else if (p.post == P_RMS) v = sqrt(v / (A)p.R);
+    } else {
+        if (p.post == P_MEAN) v = p.R ? v / p.R : 0;  // integer mean (x / Dim(D), Tensor.hpp:448)
+    }
+    store_from(p.out, p.out_dtype, off, v);
+}
+
+// 16-byte vector of T -> VEC floats
+template <typename T>
+struct Vec;
+template <>
+struct Vec<float> {
+    static constexpr int N = 4;
+    static __device__ __forceinline__ void cvt(uint4 r, float* f) {
+        f[0] = __uint_as_float(r.x);
+        f[1] = __uint_as_float(r.y);
+        f[2] = __uint_as_float(r.z);
+        f[3] = __uint_as_float(r.w);
+    }
+};
+template <>
+struct Vec<__half> {
+    static constexpr int N = 8;
+    static __device__ __forceinline__ void cvt(uint4 r, float* f) { unpack8(r, TADMA_F16, f); }
+};
+template <>
+struct Vec<__nv_bfloat16> {
+    static constexpr int N = 8;
+    static __device__ __forceinline__ void cvt(uint4 r, float* f) { unpack8(r, TADMA_BF16, f); }
+};
+
+template <typename T>
+__device__ __forceinline__ float ld1(const T* p) {
+    if constexpr (sizeof(T) == 4) return *reinterpret_cast<const float*>(p);
+    else if constexpr (std::is_same<T, __half>::value) return __half2float(*p);
+    else return __bfloat162float(*p);
+}
+
+// -------------------------------------------------------------- ROW path --
+
+template <typename T, int K>
+__global__ void __launch_bounds__(THREADS) reduce_row_kernel(const __grid_constant__ RedParams p, int vec) {
+    constexpr int N = Vec<T>::N;
+    constexpr int UNR = 4;
+    const int lane = threadIdx.x & 31;
+    const int64_t gw = ((int64_t)blockIdx.x * THREADS + threadIdx.x) >> 5;
+    const int64_t nw = ((int64_t)gridDim.x * THREADS) >> 5;
+    for (int64_t row = gw; row < p.nrows; row += nw) {
+        const T* x = reinterpret_cast<const T*>(p.in) + row * p.in_row_stride;
+        State<float> s = init_state<K, float>();
+        int64_t done = 0;
+        if (vec) {
+            const int64_t nv = p.R / N;
+            for (int64_t i0 = lane; i0 < nv; i0 += 32 * UNR) {
+                uint4 r[UNR];
+#pragma unroll
+                for (int u = 0; u < UNR; u++)
+                    if (i0 + 32 * u < nv) r[u] = ld_stream_v4(x + (i0 + 32 * u) * N);
+#pragma unroll
+                for (int u = 0; u < UNR; u++) {
+                    if (i0 + 32 * u < nv) {
+                        float f[N];
+                        Vec<T>::cvt(r[u], f);
+#pragma unroll
+                        for (int j = 0; j < N; j++) update<K, float>(s, prep(p, f[j]), (i0 + 32 * u) * N + j);
+                    }
+                }
+            }
+            done = nv * N;
+        }
+        for (int64_t i = done + lane; i < p.R; i += 32) update<K, float>(s, prep(p, ld1(x + i * p.r_stride)), i);
+        s = warp_combine<K, float>(s);
+        if (lane == 0) finish<K, float>(p, s, row * p.out_row_stride);
+    }
+}
+
+// -------------------------------------------------------------- COL path --
+
+template <typename T, int K, int VEC>
+__global__ void __launch_bounds__(THREADS) reduce_col_kernel(const __grid_constant__ RedParams p) {
+    constexpr int COLS = 32 * VEC;
+    __shared__ State<float> part[WARPS][COLS];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int64_t col0 = (int64_t)blockIdx.x * COLS + lane * VEC;
+    for (int64_t o = blockIdx.y; o < p.nrows; o += gridDim.y) {
+        const T* base = reinterpret_cast<const T*>(p.in) + o * p.in_row_stride;
+        State<float> s[VEC];
+#pragma unroll
+        for (int j = 0; j < VEC; j++) s[j] = init_state<K, float>();
+        if (col0 < p.inner) {
+            constexpr int UNR = 4;
+            for (int64_t r0 = w; r0 < p.R; r0 += WARPS * UNR) {
+                if constexpr (VEC > 1) {
+                    uint4 v[UNR];
+#pragma unroll
+                    for (int u = 0; u < UNR; u++)
+                        if (r0 + WARPS * u < p.R) v[u] = ld_stream_v4(base + (r0 + WARPS * u) * p.r_stride + col0);
+#pragma unroll
+                    for (int u = 0; u < UNR; u++) {
+                        if (r0 + WARPS * u < p.R) {
+                            float f[Vec<T>::N];
+                            Vec<T>::cvt(v[u], f);
+#pragma unroll
+                            for (int j = 0; j < VEC; j++) update<K, float>(s[j], prep(p, f[j]), r0 + WARPS * u);
+                        }
+                    }
+                } else {
+                    float v[UNR];
+#pragma unroll
+                    for (int u = 0; u < UNR; u++)
+                        if (r0 + WARPS * u < p.R) v[u] = ld1(base + (r0 + WARPS * u) * p.r_stride + col0);
+#pragma unroll
+                    for (int u = 0; u < UNR; u++)
+                        if (r0 + WARPS * u < p.R) update<K, float>(s[0], prep(p, v[u]), r0 + WARPS * u);
+                }
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < VEC; j++) part[w][lane * VEC + j] = s[j];
+        __syncthreads();
+        for (int c = threadIdx.x; c < COLS; c += THREADS) {
+            const int64_t col = (int64_t)blockIdx.x * COLS + c;
+            if (col < p.inner) {
+                State<float> t = part[0][c];
+#pragma unroll
+                for (int ww = 1; ww < WARPS; ww++) t = combine<K, float>(t, part[ww][c]);
+                finish<K, float>(p, t, o * p.out_row_stride + col);
+            }
+        }
+        __syncthreads();
+    }
+}
+
+// ---------------------------------------------------------- GENERIC path --
+
+template <typename A, int K>
+__global__ void __launch_bounds__(THREADS) reduce_generic_kernel(const __grid_constant__ RedParams p) {
+    const int lane = threadIdx.x & 31;
+    const int64_t gw = ((int64_t)blockIdx.x * THREADS + threadIdx.x) >> 5;
+    const int64_t nw = ((int64_t)gridDim.x * THREADS) >> 5;
+    for (int64_t o = gw; o < p.nrows; o += nw) {
+        uint64_t e = (uint64_t)o;
+        int64_t ioff = 0, ooff = 0;
+        for (int d = p.krank - 1; d >= 1; d--) {
+            uint64_t q, r;
+            p.kdm[d].divmod(e, q, r);
+            ioff += (int64_t)r * p.kin[d];
+            ooff += (int64_t)r * p.kout[d];
+            e = q;
+        }
+        ioff += (int64_t)e * p.kin[0];
+        ooff += (int64_t)e * p.kout[0];
+        State<A> s = init_state<K, A>();
+        for (int64_t r = lane; r < p.R; r += 32) {
+            A v = load_as<A>(p.in, p.in_dtype, ioff + r * p.r_stride);
+            update<K, A>(s, prep(p, v), r);
+        }
+        s = warp_combine<K, A>(s);
+        if (lane == 0) {
+            finish<K, A>(p, s, ooff);
+        }
+    }
+}
+
+// ------------------------------------------------------------- host side --
+
+int blocks_per_sm(const void* fn) {
+    static std::mutex mu;
+    static std::unordered_map<const void*, int> cache;
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(fn);
+    if (it != cache.end()) return it->second;
+    int nb = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, fn, THREADS, 0) != cudaSuccess || nb <= 0) nb = 1;
+    cache[fn] = nb;
+    return nb;
+}
+
+int grid_for(const void* fn, int64_t want) {
+    int64_t cap = (int64_t)sm_count() * blocks_per_sm(fn);
+    if (want < 1) want = 1;
+    return (int)(want < cap ? want : cap);
+}
+
+template <typename T, int K>
+int launch_fast(int path, const RedParams& p, bool vec, cudaStream_t s) {
+    if (path == 0) {
+        const void* fn = (const void*)reduce_row_kernel<T, K>;
+        int grid = grid_for(fn, (p.nrows + WARPS - 1) / WARPS);
+        reduce_row_kernel<T, K><<<grid, THREADS, 0, s>>>(p, vec ? 1 : 0);
+    } else {
+        constexpr int VEC = Vec<T>::N;
+        int64_t tiles = vec ? (p.inner + 32 * VEC - 1) / (32 * VEC) : (p.inner + 31) / 32;
+        if (tiles > 0x7fffffff) return fail(TADMA_ERR_UNSUPPORTED, "reduce: too many column tiles");
+        dim3 grid((unsigned)tiles, (unsigned)(p.nrows < 65535 ? p.nrows : 65535));
+        if (vec) reduce_col_kernel<T, K, VEC><<<grid, THREADS, 0, s>>>(p);
+        else reduce_col_kernel<T, K, 1><<<grid, THREADS, 0, s>>>(p);
+    }
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? TADMA_OK : cuda_fail(e, "tadma_b200_reduce launch");
+}
+
+template <typename T>
+int launch_fast_kind(int kind, int path, const RedParams& p, bool vec, cudaStream_t s) {
+    switch (kind) {
+    case K_SUM: return launch_fast<T, K_SUM>(path, p, vec, s);
+    case K_MAX: return launch_fast<T, K_MAX>(path, p, vec, s);
+    case K_MIN: return launch_fast<T, K_MIN>(path, p, vec, s);
+    case K_ARGMAX: return launch_fast<T, K_ARGMAX>(path, p, vec, s);
+    default: return launch_fast<T, K_ARGMIN>(path, p, vec, s);
+    }
+}
+
+template <typename A>
+int launch_generic(int kind, const RedParams& p, cudaStream_t s) {
+    const void* fn;
+    switch (kind) {
+    case K_SUM: fn = (const void*)reduce_generic_kernel<A, K_SUM>; break;
+    case K_MAX: fn = (const void*)reduce_generic_kernel<A, K_MAX>; break;
+    case K_MIN: fn = (const void*)reduce_generic_kernel<A, K_MIN>; break;
+    case K_ARGMAX: fn = (const void*)reduce_generic_kernel<A, K_ARGMAX>; break;
+    default: fn = (const void*)reduce_generic_kernel<A, K_ARGMIN>; break;
+    }
+    int grid = grid_for(fn, (p.nrows + WARPS - 1) / WARPS);
+    switch (kind) {
+    case K_SUM: reduce_generic_kernel<A, K_SUM><<<grid, THREADS, 0, s>>>(p); break;
+    case K_MAX: reduce_generic_kernel<A, K_MAX><<<grid, THREADS, 0, s>>>(p); break;
+    case K_MIN: reduce_generic_kernel<A, K_MIN><<<grid, THREADS, 0, s>>>(p); break;
+    case K_ARGMAX: reduce_generic_kernel<A, K_ARGMAX><<<grid, THREADS, 0, s>>>(p); break;
+    default: reduce_generic_kernel<A, K_ARGMIN><<<grid, THREADS, 0, s>>>(p); break;
+    }
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? TADMA_OK : cuda_fail(e, "tadma_b200_reduce launch");
+}
+
+}  // namespace
+}  // namespace tadma_b200
+
+using namespace tadma_b200;
+
+extern "C" int tadma_b200_reduce(int32_t op, const tadma_tensor* in, int32_t axis, int32_t pre_op,
+                                 const tadma_tensor* out, void* stream) {
+    std::string err = check_tensor(in, "in");
+    if (err.empty()) err = check_tensor(out, "out");
+    if (!err.empty()) return fail(TADMA_ERR_INVALID, err);
+    if (op < TADMA_REDUCE_SUM || op > TADMA_REDUCE_RMS) return fail(TADMA_ERR_INVALID, "unknown reduce op");
+    if (in->rank < 1) return fail(TADMA_ERR_INVALID, "reduce needs rank >= 1");
+    const int ax = axis < 0 ? axis + in->rank : axis;
+    if (ax < 0 || ax >= in->rank) return fail(TADMA_ERR_INVALID, "axis out of range");
+    const bool keep = out->rank == in->rank;
+    if (!keep && out->rank != in->rank - 1) return fail(TADMA_ERR_INVALID, "out rank must be in rank or in rank - 1");
+    for (int d = 0, k = 0; d < in->rank; d++) {
+        if (d == ax) {
+            if (keep && out->dims[d] != 1) return fail(TADMA_ERR_INVALID, "out dims[axis] must be 1");
+            if (keep) k++;
+            continue;
+        }
+        if (out->dims[k] != in->dims[d]) return fail(TADMA_ERR_INVALID, "out dims do not match in dims");
+        k++;
+    }
+    const bool arg = op == TADMA_REDUCE_ARGMAX || op == TADMA_REDUCE_ARGMIN;
+    if (arg && out->dtype != TADMA_I64 && out->dtype != TADMA_I32)
+        return fail(TADMA_ERR_INVALID, "argmax/argmin output must be int64 or int32");
+    if (pre_op != TADMA_OP_COPY && !(pre_op > 0 && pre_op <= TADMA_OP_NOT))
+        return fail(TADMA_ERR_INVALID, "pre_op must be a unary op code");
+    const int64_t R = in->dims[ax];
+    if (R == 0 && op != TADMA_REDUCE_SUM && op != TADMA_REDUCE_SUMSQ)
+        return fail(TADMA_ERR_INVALID, "empty reduction has no identity for this op");
+    if (numel(out) == 0) return TADMA_OK;
+
+    // Kept dims, folded jointly for in and out.
+    int64_t kd[TADMA_MAX_RANK], ks[2][TADMA_MAX_RANK];
+    int kr = 0;
+    for (int d = 0; d < in->rank; d++) {
+        if (d == ax) continue;
+        kd[kr] = in->dims[d];
+        ks[0][kr] = in->strides[d];
+        ks[1][kr] = out->strides[keep ? d : (d < ax ? d : d - 1)];
+        kr++;
+    }
+    Folded f = fold(kr, kd, ks, 2);
+
+    RedParams p{};
+    p.in = (const char*)in->data;
+    p.out = (char*)out->data;
+    p.in_dtype = in->dtype;
+    p.out_dtype = out->dtype;
+    p.pre_op = pre_op;
+    p.square = (op == TADMA_REDUCE_SUMSQ || op == TADMA_REDUCE_RMS);
+    p.post = op == TADMA_REDUCE_MEAN ? P_MEAN : (op == TADMA_REDUCE_RMS ? P_RMS : P_NONE);
+    int kind;
+    switch (op) {
+    case TADMA_REDUCE_MAX: kind = K_MAX; break;
+    case TADMA_REDUCE_MIN: kind = K_MIN; break;
+    case TADMA_REDUCE_ARGMAX: kind = K_ARGMAX; break;
+    case TADMA_REDUCE_ARGMIN: kind = K_ARGMIN; break;
+    default: kind = K_SUM; break;
+    }
+    p.kind = kind;
+    p.R = R;
+    p.r_stride = in->strides[ax];
+    cudaStream_t s = (cudaStream_t)stream;
+
+    const int dt = in->dtype;
+    const bool fast_dt = dt == TADMA_F32 || dt == TADMA_F16 || dt == TADMA_BF16;
+    const int es = dtype_size(dt);
+    const int last = f.rank - 1;
+    const bool in_aligned = ((uintptr_t)in->data % 16) == 0;
+    if (fast_dt && R > 1 && p.r_stride == 1 && f.rank == 1) {
+        // ROW
+        p.nrows = f.dims[0];
+        p.in_row_stride = f.strides[0][0];
+        p.out_row_stride = f.strides[1][0];
+        const int N = 16 / es;
+        bool vec = in_aligned && R >= N && (p.nrows == 1 || (p.in_row_stride * es) % 16 == 0);
+        switch (dt) {
+        case TADMA_F32: return launch_fast_kind<float>(kind, 0, p, vec, s);
+        case TADMA_F16: return launch_fast_kind<__half>(kind, 0, p, vec, s);
+        default: return launch_fast_kind<__nv_bfloat16>(kind, 0, p, vec, s);
+        }
+    }
+    if (fast_dt && R > 1 && p.r_stride != 1 && f.rank <= 2 && f.strides[0][last] == 1 && f.strides[1][last] == 1 &&
+        f.dims[last] > 1) {
+        // COL
+        p.inner = f.dims[last];
+        p.nrows = f.rank == 2 ? f.dims[0] : 1;
+        p.in_row_stride = f.rank == 2 ? f.strides[0][0] : 0;
+        p.out_row_stride = f.rank == 2 ? f.strides[1][0] : 0;
+        const int N = 16 / es;
+        bool vec = in_aligned && p.inner % N == 0 && (p.r_stride * es) % 16 == 0 && (p.in_row_stride * es) % 16 == 0;
+        switch (dt) {
+        case TADMA_F32: return launch_fast_kind<float>(kind, 1, p, vec, s);
+        case TADMA_F16: return launch_fast_kind<__half>(kind, 1, p, vec, s);
+        default: return launch_fast_kind<__nv_bfloat16>(kind, 1, p, vec, s);
+        }
+    }
+    // GENERIC
+    p.krank = f.rank;
+    p.nrows = 1;
+    for (int d = 0; d < f.rank; d++) {
+        p.kdims[d] = f.dims[d];
+        p.kdm[d] = DivMod((uint64_t)f.dims[d]);
+        p.kin[d] = f.strides[0][d];
+        p.kout[d] = f.strides[1][d];
+        p.nrows *= f.dims[d];
+    }
+    const bool int_acc = !dtype_is_float(dt) && pre_op == TADMA_OP_COPY && op != TADMA_REDUCE_RMS;
+    if (int_acc) return launch_generic<int64_t>(kind, p, s);
+    return launch_generic<double>(kind, p, s);
+}
