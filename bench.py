@@ -47,6 +47,9 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="budget of the CPU-baseline sample")
     ap.add_argument("--e2e-steps", type=int, default=20)
+    ap.add_argument("--batch", type=int, default=0,
+                    help="leading-axis size per GPU (0 = the BASELINE size); smaller values give the small cases "
+                         "used for ncu captures")
     return ap.parse_args()
 
 
@@ -130,12 +133,13 @@ class ClockSampler:
 
 class Config2:
     """y = gelu(x * 0.5 + bias), x[8192, 8192] bf16, bias[8192] bf16, y bf16."""
-    name = "cfg2: y = gelu(x*0.5 + bias), x[8192,8192] bf16, bias[8192] bf16 -> bf16"
     ROWS, COLS = 8192, 8192
     dtype = "bf16"
     kernel = "chain_vec_kernel"
 
-    def __init__(self, rank):
+    def __init__(self, rank, batch=0):
+        self.ROWS = batch or Config2.ROWS
+        self.name = f"cfg2: y = gelu(x*0.5 + bias), x[{self.ROWS},8192] bf16, bias[8192] bf16 -> bf16"
         import torch
         import tadma_b200 as tb
         from tadma_b200.abi import Dist, DType, make_tensor
@@ -148,6 +152,8 @@ class Config2:
         tb.fill(self.bias, Dist.NORMAL, 0.0, 0.1, seed=0, stream_id=2)
         self.bview = make_tensor(self.bias.data_ptr(), DType.BF16, [R, C], [0, 1])
         self.prog = self.program()
+        from tadma_b200.abi import Compute
+        self.call = tb.prepare_eltwise(self.y, [self.x, self.bview], self.prog, Compute.F32)
         self.bytes = 2 * R * C * 2 + C * 2
         self.launches = 1
         self.units = R * C
@@ -159,8 +165,7 @@ class Config2:
                 instr(Op.GELU, round_dtype=DType.F32)]
 
     def step(self):
-        from tadma_b200.abi import Compute
-        self.tb.eltwise(self.y, [self.x, self.bview], self.prog, Compute.F32)
+        self.call()
 
     def e2e(self, steps, stream):
         """Same op through the public C-ABI call, inputs from pinned host memory
@@ -226,16 +231,16 @@ def torch_int16():
 
 class Config3:
     """sum / max / argmax over the last axis and mean over the middle axis of X[32, 4096, 4096] fp32."""
-    name = "cfg3: sum/max/argmax over axis -1 + mean over axis 1 of X[32,4096,4096] fp32"
     dtype = "f32"
     kernel = "reduce_row_kernel"
 
-    def __init__(self, rank):
+    def __init__(self, rank, batch=0):
         import torch
         import tadma_b200 as tb
-        from tadma_b200.abi import Dist
+        from tadma_b200.abi import Dist, Reduce
         self.tb = tb
-        B, R, C = 32, 4096, 4096
+        B, R, C = batch or 32, 4096, 4096
+        self.name = f"cfg3: sum/max/argmax over axis -1 + mean over axis 1 of X[{B},4096,4096] fp32"
         self.x = torch.empty((B, R, C), dtype=torch.float32, device="cuda")
         tb.fill(self.x, Dist.UNIFORM, -1.0, 1.0, seed=0, stream_id=1, offset=rank * B * R * C)
         self.s = torch.empty((B, R, 1), dtype=torch.float32, device="cuda")
@@ -246,14 +251,13 @@ class Config3:
         self.bytes = 4 * xin + B * R * 4 * 2 + B * R * 8 + B * C * 4
         self.launches = 4
         self.units = 4 * B * R * C
+        self.calls = [tb.prepare_reduce(Reduce.SUM, self.x, -1, self.s), tb.prepare_reduce(Reduce.MAX, self.x, -1, self.m),
+                      tb.prepare_reduce(Reduce.ARGMAX, self.x, -1, self.a),
+                      tb.prepare_reduce(Reduce.MEAN, self.x, 1, self.mean)]
 
     def step(self):
-        from tadma_b200.abi import Reduce
-        tb = self.tb
-        tb.reduce(Reduce.SUM, self.x, -1, self.s)
-        tb.reduce(Reduce.MAX, self.x, -1, self.m)
-        tb.reduce(Reduce.ARGMAX, self.x, -1, self.a)
-        tb.reduce(Reduce.MEAN, self.x, 1, self.mean)
+        for c in self.calls:
+            c()
 
     def cpu_sample(self, budget_s):
         import numpy as np
@@ -275,33 +279,36 @@ class Config3:
 
 class Config4:
     """LayerNorm over the last axis of [64, 2048, 1024] fp16 + softmax over the last axis of [32, 16, 2048, 2048] fp16."""
-    name = "cfg4: LayerNorm [64,2048,1024] fp16 + softmax [32,16,2048,2048] fp16 (last axis)"
     dtype = "f16"
     kernel = "rownorm_warp_kernel"
 
-    def __init__(self, rank):
+    def __init__(self, rank, batch=0):
         import torch
         import tadma_b200 as tb
-        from tadma_b200.abi import Dist
+        from tadma_b200.abi import Dist, LNMode
         self.tb = tb
-        self.x = torch.empty((64, 2048, 1024), dtype=torch.float16, device="cuda")
+        lb = batch or 64
+        sb = max(1, lb // 2)
+        self.name = f"cfg4: LayerNorm [{lb},2048,1024] fp16 + softmax [{sb},16,2048,2048] fp16 (last axis)"
+        self.x = torch.empty((lb, 2048, 1024), dtype=torch.float16, device="cuda")
         self.g = torch.empty((1024,), dtype=torch.float16, device="cuda")
         self.b = torch.empty((1024,), dtype=torch.float16, device="cuda")
         tb.fill(self.x, Dist.NORMAL, 0.0, 1.0, 0, 1, offset=rank * self.x.numel())
         tb.fill(self.g, Dist.NORMAL, 1.0, 0.02, 0, 2)
         tb.fill(self.b, Dist.NORMAL, 0.0, 0.02, 0, 3)
         self.y = torch.empty_like(self.x)
-        self.s = torch.empty((32, 16, 2048, 2048), dtype=torch.float16, device="cuda")
+        self.s = torch.empty((sb, 16, 2048, 2048), dtype=torch.float16, device="cuda")
         tb.fill(self.s, Dist.NORMAL, 0.0, 3.0, 0, 4, offset=rank * self.s.numel())
         self.sy = torch.empty_like(self.s)
         self.bytes = (2 * self.x.numel() * 2 + 2 * 1024 * 2) + 2 * self.s.numel() * 2
         self.launches = 2
         self.units = self.x.numel() + self.s.numel()
+        self.calls = [tb.prepare_layer_norm(self.x, -1, self.g, self.b, 1e-5, self.y, LNMode.ONNX),
+                      tb.prepare_softmax(self.s, -1, self.sy)]
 
     def step(self):
-        from tadma_b200.abi import LNMode
-        self.tb.layer_norm(self.x, -1, self.g, self.b, 1e-5, self.y, LNMode.ONNX)
-        self.tb.softmax(self.s, -1, self.sy)
+        for c in self.calls:
+            c()
 
     def cpu_sample(self, budget_s):
         import numpy as np
@@ -323,17 +330,18 @@ class Config4:
 
 class Config5:
     """Embedding gather: table [50257, 4096] fp16, ids [2048, 4096] int64, + pos [4096, 4096] bf16 -> bf16."""
-    name = "cfg5: gather table[50257,4096] fp16 by ids[2048,4096] int64 + pos[4096,4096] bf16 -> bf16"
     dtype = "f16/bf16"
     kernel = "gather_rows_kernel"
     V, B, S, D = 50257, 2048, 4096, 4096
 
-    def __init__(self, rank):
+    def __init__(self, rank, batch=0):
         import torch
         import tadma_b200 as tb
         from tadma_b200.abi import Dist, DType, make_tensor
         self.tb = tb
+        self.B = batch or Config5.B
         V, B, S, D = self.V, self.B, self.S, self.D
+        self.name = f"cfg5: gather table[50257,4096] fp16 by ids[{B},4096] int64 + pos[4096,4096] bf16 -> bf16"
         self.table = torch.empty((V, D), dtype=torch.float16, device="cuda")
         self.ids = torch.empty((B, S), dtype=torch.int64, device="cuda")
         self.pos = torch.empty((S, D), dtype=torch.bfloat16, device="cuda")
@@ -347,9 +355,10 @@ class Config5:
         self.compulsory = B * S * 8 + V * D * 2 + S * D * 2 + n_out * 2
         self.launches = 1
         self.units = n_out
+        self.call = tb.prepare_gather(self.table, 0, self.ids, self.out, add=self.addv)
 
     def step(self):
-        self.tb.gather(self.table, 0, self.ids, self.out, add=self.addv)
+        self.call()
 
     def cpu_sample(self, budget_s):
         import numpy as np
@@ -377,7 +386,6 @@ CONFIGS = {2: Config2, 3: Config3, 4: Config4, 5: Config5}
 def run_reference(args, rank, world):
     if rank != 0:
         return
-    cfg = CONFIGS[args.config]
     if args.config != 2:
         print(json.dumps({"impl": "reference", "unavailable": "reference arm implemented for the default workload (config 2)"}))
         return
@@ -403,7 +411,8 @@ def run_reference(args, rank, world):
         "impl": "reference", "metric": "achieved HBM GB/s", "value": round(v, 3), "unit": "GB/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": cfg.name, "sample": f"{rows} rows of x[8192, 8192] per step"},
+        "config": {"workload": "cfg2: y = gelu(x*0.5 + bias), x[8192,8192] bf16, bias[8192] bf16 -> bf16",
+                   "sample": f"{rows} rows of x[8192, 8192] per step"},
         "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": cores, "kind": "port",
                          "sample": f"{rows} rows of x[8192, 8192] per step, {args.steps} steps"},
         "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -446,7 +455,7 @@ def barrier(world):
 def run(args, rank, world, local):
     import torch
     import torch.distributed as dist
-    cfg = CONFIGS[args.config](rank)
+    cfg = CONFIGS[args.config](rank, args.batch)
     stream = torch.cuda.current_stream()
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
     for _ in range(max(args.warmup, 3)):

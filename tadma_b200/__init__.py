@@ -116,54 +116,96 @@ def _stream(stream):
     return ctypes.c_void_p(stream.cuda_stream)
 
 
+class Prepared:
+    """A C-ABI call with its ctypes arguments built once (descriptors, program,
+    stream): calling it costs one foreign call, for launch-bound loops."""
+
+    def __init__(self, fn, args, keep=()):
+        self._fn, self._args, self._keep = fn, args, keep
+
+    def __call__(self) -> None:
+        rc = self._fn(*self._args)
+        if rc != 0:
+            check(rc)
+
+
+def _d(t):
+    return t if isinstance(t, TadmaTensor) else desc(t)
+
+
+def prepare_eltwise(out, ins, prog, compute=Compute.AUTO, stream=None) -> Prepared:
+    o = _d(out)
+    arr = (TadmaTensor * max(1, len(ins)))(*[_d(x) for x in ins])
+    p, n = program(prog)
+    return Prepared(lib().tadma_b200_eltwise, (ctypes.byref(o), arr, len(ins), p, n, int(compute), _stream(stream)),
+                    (o, arr, p))
+
+
+def prepare_reduce(op, x, axis, out, pre_op=Op.COPY, stream=None) -> Prepared:
+    i, o = _d(x), _d(out)
+    return Prepared(lib().tadma_b200_reduce, (int(op), ctypes.byref(i), int(axis), int(pre_op), ctypes.byref(o),
+                                              _stream(stream)), (i, o))
+
+
+def prepare_softmax(x, axis, out, stream=None) -> Prepared:
+    i, o = _d(x), _d(out)
+    return Prepared(lib().tadma_b200_softmax, (ctypes.byref(i), int(axis), ctypes.byref(o), _stream(stream)), (i, o))
+
+
+def prepare_layer_norm(x, axis, gamma, beta, eps, out, mode=LNMode.ONNX, stream=None) -> Prepared:
+    i, o = _d(x), _d(out)
+    g = none_tensor() if gamma is None else _d(gamma)
+    b = none_tensor() if beta is None else _d(beta)
+    return Prepared(lib().tadma_b200_layer_norm, (ctypes.byref(i), int(axis), ctypes.byref(g), ctypes.byref(b),
+                                                  float(eps), int(mode), ctypes.byref(o), _stream(stream)), (i, o, g, b))
+
+
+def prepare_rms_norm(x, axis, eps, out, stream=None) -> Prepared:
+    i, o = _d(x), _d(out)
+    return Prepared(lib().tadma_b200_rms_norm, (ctypes.byref(i), int(axis), float(eps), ctypes.byref(o),
+                                                _stream(stream)), (i, o))
+
+
+def prepare_gather(table, axis, ids, out, add=None, stream=None) -> Prepared:
+    t, i, o = _d(table), _d(ids), _d(out)
+    a = none_tensor() if add is None else _d(add)
+    return Prepared(lib().tadma_b200_gather, (ctypes.byref(t), int(axis), ctypes.byref(i), ctypes.byref(a),
+                                              ctypes.byref(o), _stream(stream)), (t, i, o, a))
+
+
+def prepare_fill(out, dist, p0, p1, seed, stream_id, offset=0, stream=None) -> Prepared:
+    o = _d(out)
+    return Prepared(lib().tadma_b200_fill, (ctypes.byref(o), int(dist), float(p0), float(p1), int(seed),
+                                            int(stream_id), int(offset), _stream(stream)), (o,))
+
+
 def eltwise(out, ins, prog, compute=Compute.AUTO, stream=None) -> None:
     """out = chain(ins...) (tadma_b200_eltwise).  `out`/`ins` are torch tensors or descriptors."""
-    o = out if isinstance(out, TadmaTensor) else desc(out)
-    arr = (TadmaTensor * max(1, len(ins)))(*[x if isinstance(x, TadmaTensor) else desc(x) for x in ins])
-    p, n = program(prog)
-    check(lib().tadma_b200_eltwise(ctypes.byref(o), arr, len(ins), p, n, int(compute), _stream(stream)))
+    prepare_eltwise(out, ins, prog, compute, stream)()
 
 
 def reduce(op, x, axis, out, pre_op=Op.COPY, stream=None) -> None:
-    i = x if isinstance(x, TadmaTensor) else desc(x)
-    o = out if isinstance(out, TadmaTensor) else desc(out)
-    check(lib().tadma_b200_reduce(int(op), ctypes.byref(i), int(axis), int(pre_op), ctypes.byref(o), _stream(stream)))
+    prepare_reduce(op, x, axis, out, pre_op, stream)()
 
 
 def softmax(x, axis, out, stream=None) -> None:
-    i = x if isinstance(x, TadmaTensor) else desc(x)
-    o = out if isinstance(out, TadmaTensor) else desc(out)
-    check(lib().tadma_b200_softmax(ctypes.byref(i), int(axis), ctypes.byref(o), _stream(stream)))
+    prepare_softmax(x, axis, out, stream)()
 
 
 def layer_norm(x, axis, gamma, beta, eps, out, mode=LNMode.ONNX, stream=None) -> None:
-    i = x if isinstance(x, TadmaTensor) else desc(x)
-    o = out if isinstance(out, TadmaTensor) else desc(out)
-    g = none_tensor() if gamma is None else (gamma if isinstance(gamma, TadmaTensor) else desc(gamma))
-    b = none_tensor() if beta is None else (beta if isinstance(beta, TadmaTensor) else desc(beta))
-    check(lib().tadma_b200_layer_norm(ctypes.byref(i), int(axis), ctypes.byref(g), ctypes.byref(b), float(eps),
-                                      int(mode), ctypes.byref(o), _stream(stream)))
+    prepare_layer_norm(x, axis, gamma, beta, eps, out, mode, stream)()
 
 
 def rms_norm(x, axis, eps, out, stream=None) -> None:
-    i = x if isinstance(x, TadmaTensor) else desc(x)
-    o = out if isinstance(out, TadmaTensor) else desc(out)
-    check(lib().tadma_b200_rms_norm(ctypes.byref(i), int(axis), float(eps), ctypes.byref(o), _stream(stream)))
+    prepare_rms_norm(x, axis, eps, out, stream)()
 
 
 def gather(table, axis, ids, out, add=None, stream=None) -> None:
-    t = table if isinstance(table, TadmaTensor) else desc(table)
-    i = ids if isinstance(ids, TadmaTensor) else desc(ids)
-    o = out if isinstance(out, TadmaTensor) else desc(out)
-    a = none_tensor() if add is None else (add if isinstance(add, TadmaTensor) else desc(add))
-    check(lib().tadma_b200_gather(ctypes.byref(t), int(axis), ctypes.byref(i), ctypes.byref(a), ctypes.byref(o),
-                                  _stream(stream)))
+    prepare_gather(table, axis, ids, out, add, stream)()
 
 
 def fill(out, dist, p0, p1, seed, stream_id, offset=0, stream=None) -> None:
-    o = out if isinstance(out, TadmaTensor) else desc(out)
-    check(lib().tadma_b200_fill(ctypes.byref(o), int(dist), float(p0), float(p1), int(seed), int(stream_id),
-                                int(offset), _stream(stream)))
+    prepare_fill(out, dist, p0, p1, seed, stream_id, offset, stream)()
 
 
 def error_flags(clear: bool = True) -> int:

@@ -86,6 +86,86 @@ __device__ __forceinline__ void select(int sel, double imm, const C (&val)[NIN >
     }
 }
 
+// One dispatch per instruction per vector: every case carries its own
+// unrolled W-element loop with the op code as a compile-time constant, so the
+// scalar op bodies (ops.cuh) constant-fold their switch.
+#define TADMA_UCASE(OPC)                                        \
+    case OPC: {                                                 \
+        _Pragma("unroll") for (int j = 0; j < W; j++) acc[j] = unary(OPC, acc[j]); \
+    } break;
+#define TADMA_BCASE(OPC)                                        \
+    case OPC: {                                                 \
+        _Pragma("unroll") for (int j = 0; j < W; j++) acc[j] = binary(OPC, acc[j], b[j], c[j]); \
+    } break;
+#define TADMA_RCASE(DT)                                         \
+    case DT: {                                                  \
+        _Pragma("unroll") for (int j = 0; j < W; j++) acc[j] = round_to(acc[j], DT); \
+    } break;
+
+template <typename C, int W>
+__device__ __forceinline__ void unary_vec(int op, C (&acc)[W]) {
+    switch (op) {
+        TADMA_UCASE(TADMA_OP_NEG)
+        TADMA_UCASE(TADMA_OP_ABS)
+        TADMA_UCASE(TADMA_OP_EXP)
+        TADMA_UCASE(TADMA_OP_SQRT)
+        TADMA_UCASE(TADMA_OP_RELU)
+        TADMA_UCASE(TADMA_OP_SIGMOID)
+        TADMA_UCASE(TADMA_OP_TANH)
+        TADMA_UCASE(TADMA_OP_GELU)
+        TADMA_UCASE(TADMA_OP_NOT)
+    default: {
+#pragma unroll
+        for (int j = 0; j < W; j++) acc[j] = unary(op, acc[j]);
+    } break;
+    }
+}
+
+template <typename C, int W>
+__device__ __forceinline__ void binary_vec(int op, C (&acc)[W], const C (&b)[W], const C (&c)[W]) {
+    switch (op) {
+        TADMA_BCASE(TADMA_OP_ADD)
+        TADMA_BCASE(TADMA_OP_SUB)
+        TADMA_BCASE(TADMA_OP_MUL)
+        TADMA_BCASE(TADMA_OP_DIV)
+        TADMA_BCASE(TADMA_OP_POW)
+        TADMA_BCASE(TADMA_OP_RSUB)
+        TADMA_BCASE(TADMA_OP_RDIV)
+        TADMA_BCASE(TADMA_OP_MAX)
+        TADMA_BCASE(TADMA_OP_MIN)
+        TADMA_BCASE(TADMA_OP_EQ)
+        TADMA_BCASE(TADMA_OP_NE)
+        TADMA_BCASE(TADMA_OP_LT)
+        TADMA_BCASE(TADMA_OP_GT)
+        TADMA_BCASE(TADMA_OP_LE)
+        TADMA_BCASE(TADMA_OP_GE)
+        TADMA_BCASE(TADMA_OP_AND)
+        TADMA_BCASE(TADMA_OP_OR)
+        TADMA_BCASE(TADMA_OP_XOR)
+        TADMA_BCASE(TADMA_OP_LAND)
+        TADMA_BCASE(TADMA_OP_LOR)
+        TADMA_BCASE(TADMA_OP_WHERE)
+    default:
+        break;
+    }
+}
+
+template <typename C, int W>
+__device__ __forceinline__ void round_vec(int dt, C (&acc)[W]) {
+    switch (dt) {
+        TADMA_RCASE(TADMA_F16)
+        TADMA_RCASE(TADMA_BF16)
+        TADMA_RCASE(TADMA_I64)
+        TADMA_RCASE(TADMA_I32)
+        TADMA_RCASE(TADMA_U8)
+        TADMA_RCASE(TADMA_BOOL)
+        TADMA_RCASE(TADMA_I8)
+        TADMA_RCASE(TADMA_F32)
+    default:
+        break;  // F64: nothing to round
+    }
+}
+
 template <typename C, int NIN, int W>
 __device__ __forceinline__ void run_chain(const ChainParams& p, C (&acc)[W], const C (&val)[NIN > 0 ? NIN : 1][W]) {
     for (int i = 0; i < p.n_instr; i++) {
@@ -97,8 +177,7 @@ __device__ __forceinline__ void run_chain(const ChainParams& p, C (&acc)[W], con
 #pragma unroll
                 for (int j = 0; j < W; j++) acc[j] = s;
             } else if (op != TADMA_OP_COPY) {
-#pragma unroll
-                for (int j = 0; j < W; j++) acc[j] = unary(op, acc[j]);
+                unary_vec<C, W>(op, acc);
             }
         } else {
             C b[W], c[W];
@@ -109,12 +188,14 @@ __device__ __forceinline__ void run_chain(const ChainParams& p, C (&acc)[W], con
 #pragma unroll
                 for (int j = 0; j < W; j++) c[j] = b[j];
             }
-#pragma unroll
-            for (int j = 0; j < W; j++) acc[j] = binary(op, acc[j], b[j], c[j]);
+            binary_vec<C, W>(op, acc, b, c);
         }
         if (I.round_dtype >= 0) {
-#pragma unroll
-            for (int j = 0; j < W; j++) acc[j] = round_to(acc[j], I.round_dtype);
+            if constexpr (sizeof(C) == 4) {
+                if (I.round_dtype != TADMA_F32 && I.round_dtype != TADMA_F64) round_vec<C, W>(I.round_dtype, acc);
+            } else {
+                round_vec<C, W>(I.round_dtype, acc);
+            }
         }
     }
 }

@@ -11,7 +11,7 @@
 //
 // Fast path (axis 0, table rows contiguous): one warp per output row; the id
 // is read once per row (one broadcast load), the row is copied in 8-element
-// chunks (16 B of fp16/bf16, 32 B of fp32) with 4 chunks in flight per lane,
+// chunks (16 B of fp16/bf16, 32 B of fp32) with 4 raw chunks in flight per lane,
 // the add operand's row (e.g. pos[s]) is fetched with a read-only load so it
 // stays L2-resident across the batch, and the output is written with
 // evict-first stores: the gather writes its output once and reads each
@@ -53,16 +53,29 @@ struct GatherParams {
     int64_t os[TADMA_MAX_RANK], as[TADMA_MAX_RANK], ts[TADMA_MAX_RANK], is[TADMA_MAX_RANK];
 };
 
+// Raw 8-element chunk: 1 x 16 B for 16-bit types, 2 x 16 B for fp32.  Loads
+// keep the raw bits (4 or 8 registers) so UNR chunks can be in flight with a
+// small register footprint; conversion happens at compute time.
 template <typename T>
-__device__ __forceinline__ void load8(const T* p, float* f, bool nc) {
+struct Raw8 {
+    uint4 w[sizeof(T) == 4 ? 2 : 1];
+};
+
+template <typename T>
+__device__ __forceinline__ void load_raw(const T* p, Raw8<T>& r) {
+    r.w[0] = ld_nc_v4(p);
+    if constexpr (sizeof(T) == 4) r.w[1] = ld_nc_v4(p + 4);
+}
+
+template <typename T>
+__device__ __forceinline__ void raw_to_f(const Raw8<T>& r, float* f) {
     if constexpr (sizeof(T) == 4) {
-        uint4 a = nc ? ld_nc_v4(p) : ld_v4(p);
-        uint4 b = nc ? ld_nc_v4(p + 4) : ld_v4(p + 4);
-        f[0] = __uint_as_float(a.x); f[1] = __uint_as_float(a.y); f[2] = __uint_as_float(a.z); f[3] = __uint_as_float(a.w);
-        f[4] = __uint_as_float(b.x); f[5] = __uint_as_float(b.y); f[6] = __uint_as_float(b.z); f[7] = __uint_as_float(b.w);
+        f[0] = __uint_as_float(r.w[0].x); f[1] = __uint_as_float(r.w[0].y);
+        f[2] = __uint_as_float(r.w[0].z); f[3] = __uint_as_float(r.w[0].w);
+        f[4] = __uint_as_float(r.w[1].x); f[5] = __uint_as_float(r.w[1].y);
+        f[6] = __uint_as_float(r.w[1].z); f[7] = __uint_as_float(r.w[1].w);
     } else {
-        uint4 a = nc ? ld_nc_v4(p) : ld_v4(p);
-        unpack8(a, std::is_same<T, __half>::value ? TADMA_F16 : TADMA_BF16, f);
+        unpack8(r.w[0], std::is_same<T, __half>::value ? TADMA_F16 : TADMA_BF16, f);
     }
 }
 
@@ -108,28 +121,34 @@ __global__ void __launch_bounds__(THREADS) gather_rows_kernel(const __grid_const
         }
         OT* orow = reinterpret_cast<OT*>(p.out) + row * p.o_row_stride;
         for (int64_t c0 = lane; c0 < nch; c0 += 32 * UNR) {
-            float t[UNR][CHUNK], a[UNR][CHUNK];
+            Raw8<TT> tr[UNR];
+            Raw8<AT> ar[UNR];
 #pragma unroll
             for (int u = 0; u < UNR; u++) {
                 const int64_t c = c0 + 32 * u;
                 if (c < nch) {
-                    if (ok) load8<TT>(trow + c * CHUNK, t[u], true);
-                    else {
-#pragma unroll
-                        for (int j = 0; j < CHUNK; j++) t[u][j] = 0.0f;
-                    }
-                    if constexpr (ADD) load8<AT>(arow + c * CHUNK, a[u], true);
+                    if (ok) load_raw<TT>(trow + c * CHUNK, tr[u]);
+                    if constexpr (ADD) load_raw<AT>(arow + c * CHUNK, ar[u]);
                 }
             }
 #pragma unroll
             for (int u = 0; u < UNR; u++) {
                 const int64_t c = c0 + 32 * u;
                 if (c < nch) {
-                    if constexpr (ADD) {
+                    float t[CHUNK];
+                    if (ok) {
+                        raw_to_f<TT>(tr[u], t);
+                    } else {
 #pragma unroll
-                        for (int j = 0; j < CHUNK; j++) t[u][j] = __fadd_rn(t[u][j], a[u][j]);
+                        for (int j = 0; j < CHUNK; j++) t[j] = 0.0f;
                     }
-                    store8<OT>(orow + c * CHUNK, t[u]);
+                    if constexpr (ADD) {
+                        float a[CHUNK];
+                        raw_to_f<AT>(ar[u], a);
+#pragma unroll
+                        for (int j = 0; j < CHUNK; j++) t[j] = __fadd_rn(t[j], a[j]);
+                    }
+                    store8<OT>(orow + c * CHUNK, t);
                 }
             }
         }

@@ -103,7 +103,8 @@ def test_config5_full_size_sampled():
     th = from_dev(table[torch.as_tensor(idh, device="cuda")])
     ph = from_dev(pos[torch.as_tensor(ss, device="cuda")])
     ref = np.zeros_like(got)
-    O.lib().or_cfg5_gather_add(O.ptr(th), 128, O.ptr(np.arange(128, dtype=np.int64)), O.ptr(ph), O.ptr(ref), 1, 128, D)
+    rows = np.arange(128, dtype=np.int64)  # keep alive across the C call
+    O.lib().or_cfg5_gather_add(O.ptr(th), 128, O.ptr(rows), O.ptr(ph), O.ptr(ref), 1, 128, D)
     assert np.array_equal(got, ref)
     del out
     torch.cuda.empty_cache()
