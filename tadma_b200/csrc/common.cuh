@@ -222,6 +222,28 @@ __device__ __forceinline__ uint4 ld_stream_v4(const void* p) { return __ldcs(rei
 __device__ __forceinline__ uint4 ld_v4(const void* p) { return *reinterpret_cast<const uint4*>(p); }
 __device__ __forceinline__ uint4 ld_nc_v4(const void* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
 __device__ __forceinline__ void st_stream_v4(void* p, uint4 v) { __stcs(reinterpret_cast<uint4*>(p), v); }
+
+// L2 eviction-priority policies (PTX createpolicy) for loads whose reuse is
+// known: evict_last keeps a small operand that every row re-reads (e.g. a
+// position table) resident while a large stream passes through L2;
+// evict_first marks data read once.
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+__device__ __forceinline__ uint4 ld_nc_v4_policy(const void* p, uint64_t pol) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %5;"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p), "l"(pol));
+    return r;
+}
 __device__ __forceinline__ void st_v4(void* p, uint4 v) { *reinterpret_cast<uint4*>(p) = v; }
 
 // Unpack / pack 8 x 16-bit floats <-> 8 x fp32.

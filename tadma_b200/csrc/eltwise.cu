@@ -22,6 +22,7 @@
 // * the chain is uniform across the grid (kernel parameters), so the
 //   per-instruction switch is a uniform branch amortised over 8 elements.
 #include <mutex>
+#include <type_traits>
 #include <unordered_map>
 
 #include "common.cuh"
@@ -57,7 +58,17 @@ struct ChainParams {
     int64_t out_stride[TADMA_MAX_RANK];
     Operand in[TADMA_MAX_INPUTS];
     tadma_instr prog[TADMA_MAX_INSTR];
+    float scale;  // affine program: the MUL immediate, rounded to fp32
 };
+
+// Program selector of a kernel instance: the run-time interpreter (precise or
+// fast math) or a compile-time affine + activation chain act(x * s + b).
+constexpr int PROG_INTERP = 0;
+constexpr int PROG_INTERP_FAST = 1;
+constexpr int ACT_NONE = 0, ACT_GELU = 1, ACT_RELU = 2, ACT_SIGMOID = 3, ACT_TANH = 4;
+constexpr int affine_prog(int act, bool fast, bool mul, bool add) {
+    return 0x100 | (act << 4) | (fast ? 4 : 0) | (mul ? 2 : 0) | (add ? 1 : 0);
+}
 
 template <typename C>
 __device__ __forceinline__ C imm_as(double v);
@@ -91,7 +102,7 @@ __device__ __forceinline__ void select(int sel, double imm, const C (&val)[NIN >
 // scalar op bodies (ops.cuh) constant-fold their switch.
 #define TADMA_UCASE(OPC)                                        \
     case OPC: {                                                 \
-        _Pragma("unroll") for (int j = 0; j < W; j++) acc[j] = unary(OPC, acc[j]); \
+        _Pragma("unroll") for (int j = 0; j < W; j++) acc[j] = unary<FAST>(OPC, acc[j]); \
     } break;
 #define TADMA_BCASE(OPC)                                        \
     case OPC: {                                                 \
@@ -102,7 +113,7 @@ __device__ __forceinline__ void select(int sel, double imm, const C (&val)[NIN >
         _Pragma("unroll") for (int j = 0; j < W; j++) acc[j] = round_to(acc[j], DT); \
     } break;
 
-template <typename C, int W>
+template <typename C, int W, bool FAST>
 __device__ __forceinline__ void unary_vec(int op, C (&acc)[W]) {
     switch (op) {
         TADMA_UCASE(TADMA_OP_NEG)
@@ -116,7 +127,7 @@ __device__ __forceinline__ void unary_vec(int op, C (&acc)[W]) {
         TADMA_UCASE(TADMA_OP_NOT)
     default: {
 #pragma unroll
-        for (int j = 0; j < W; j++) acc[j] = unary(op, acc[j]);
+        for (int j = 0; j < W; j++) acc[j] = unary<FAST>(op, acc[j]);
     } break;
     }
 }
@@ -166,7 +177,7 @@ __device__ __forceinline__ void round_vec(int dt, C (&acc)[W]) {
     }
 }
 
-template <typename C, int NIN, int W>
+template <typename C, int NIN, int W, bool FAST>
 __device__ __forceinline__ void run_chain(const ChainParams& p, C (&acc)[W], const C (&val)[NIN > 0 ? NIN : 1][W]) {
     for (int i = 0; i < p.n_instr; i++) {
         const tadma_instr& I = p.prog[i];
@@ -177,7 +188,7 @@ __device__ __forceinline__ void run_chain(const ChainParams& p, C (&acc)[W], con
 #pragma unroll
                 for (int j = 0; j < W; j++) acc[j] = s;
             } else if (op != TADMA_OP_COPY) {
-                unary_vec<C, W>(op, acc);
+                unary_vec<C, W, FAST>(op, acc);
             }
         } else {
             C b[W], c[W];
@@ -196,6 +207,36 @@ __device__ __forceinline__ void run_chain(const ChainParams& p, C (&acc)[W], con
             } else {
                 round_vec<C, W>(I.round_dtype, acc);
             }
+        }
+    }
+}
+
+template <int ACT, bool FAST>
+__device__ __forceinline__ float activation(float v) {
+    if constexpr (ACT == ACT_GELU) return unary<FAST>(TADMA_OP_GELU, v);
+    else if constexpr (ACT == ACT_RELU) return unary<FAST>(TADMA_OP_RELU, v);
+    else if constexpr (ACT == ACT_SIGMOID) return unary<FAST>(TADMA_OP_SIGMOID, v);
+    else if constexpr (ACT == ACT_TANH) return unary<FAST>(TADMA_OP_TANH, v);
+    else return v;
+}
+
+// Runs the kernel's program on W elements.  The affine program uses the very
+// op bodies the interpreter uses (__fmul_rn, __fadd_rn, unary<FAST>), so both
+// paths give identical bits for the same chain.
+template <typename C, int NIN, int W, int PROG>
+__device__ __forceinline__ void program(const ChainParams& p, C (&acc)[W], const C (&val)[NIN > 0 ? NIN : 1][W]) {
+    if constexpr (PROG == PROG_INTERP || PROG == PROG_INTERP_FAST) {
+        run_chain<C, NIN, W, PROG == PROG_INTERP_FAST>(p, acc, val);
+    } else {
+        constexpr int ACT = (PROG >> 4) & 0xf;
+        constexpr bool FAST = (PROG & 4) != 0, MUL = (PROG & 2) != 0, ADD = (PROG & 1) != 0;
+        static_assert(std::is_same<C, float>::value && (!ADD || NIN == 2));
+#pragma unroll
+        for (int j = 0; j < W; j++) {
+            float v = acc[j];
+            if constexpr (MUL) v = __fmul_rn(v, p.scale);
+            if constexpr (ADD) v = __fadd_rn(v, val[NIN > 1 ? 1 : 0][j]);
+            acc[j] = activation<ACT, FAST>(v);
         }
     }
 }
@@ -303,7 +344,7 @@ __device__ __forceinline__ void offsets(const ChainParams& p, uint64_t e, int64_
     for (int k = 0; k < NIN; k++) io[k] += (int64_t)e * p.in[k].stride[0];
 }
 
-template <typename C, int NIN>
+template <typename C, int NIN, int PROG>
 __global__ void __launch_bounds__(THREADS) chain_vec_kernel(const __grid_constant__ ChainParams p) {
     constexpr int NI = NIN > 0 ? NIN : 1;
     const int64_t gstride = (int64_t)gridDim.x * THREADS;
@@ -327,14 +368,14 @@ __global__ void __launch_bounds__(THREADS) chain_vec_kernel(const __grid_constan
                 C acc[V];
 #pragma unroll
                 for (int j = 0; j < V; j++) acc[j] = NIN > 0 ? val[u][0][j] : C(0);
-                run_chain<C, NIN, V>(p, acc, val[u]);
+                program<C, NIN, V, PROG>(p, acc, val[u]);
                 store_vec<C>(p.out, p.out_dtype, oo[u], acc);
             }
         }
     }
 }
 
-template <typename C, int NIN>
+template <typename C, int NIN, int PROG>
 __global__ void __launch_bounds__(THREADS) chain_scalar_kernel(const __grid_constant__ ChainParams p) {
     constexpr int NI = NIN > 0 ? NIN : 1;
     const int64_t gstride = (int64_t)gridDim.x * THREADS;
@@ -345,7 +386,7 @@ __global__ void __launch_bounds__(THREADS) chain_scalar_kernel(const __grid_cons
 #pragma unroll
         for (int k = 0; k < NIN; k++) val[k][0] = load_as<C>(p.in[k].base, p.in[k].dtype, io[k]);
         C acc[1] = {NIN > 0 ? val[0][0] : C(0)};
-        run_chain<C, NIN, 1>(p, acc, val);
+        program<C, NIN, 1, PROG>(p, acc, val);
         store_from(p.out, p.out_dtype, oo, acc[0]);
     }
 }
@@ -364,28 +405,98 @@ int blocks_per_sm(const void* fn) {
     return nb;
 }
 
-template <typename C, int NIN>
+template <typename C, int NIN, int PROG>
 int launch(const ChainParams& p, bool vec, int64_t work, cudaStream_t s) {
-    const void* fn = vec ? (const void*)chain_vec_kernel<C, NIN> : (const void*)chain_scalar_kernel<C, NIN>;
+    const void* fn = vec ? (const void*)chain_vec_kernel<C, NIN, PROG> : (const void*)chain_scalar_kernel<C, NIN, PROG>;
     int64_t per_block = (int64_t)THREADS * (vec ? U : 1);
     int64_t want = (work + per_block - 1) / per_block;
     int64_t cap = (int64_t)sm_count() * blocks_per_sm(fn);
     int grid = (int)(want < cap ? (want > 0 ? want : 1) : cap);
-    if (vec) chain_vec_kernel<C, NIN><<<grid, THREADS, 0, s>>>(p);
-    else chain_scalar_kernel<C, NIN><<<grid, THREADS, 0, s>>>(p);
+    if (vec) chain_vec_kernel<C, NIN, PROG><<<grid, THREADS, 0, s>>>(p);
+    else chain_scalar_kernel<C, NIN, PROG><<<grid, THREADS, 0, s>>>(p);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? TADMA_OK : cuda_fail(e, "tadma_b200_eltwise launch");
 }
 
+// Interpreter launch; `fast` only exists for fp32 compute.
 template <typename C>
-int launch_nin(int nin, const ChainParams& p, bool vec, int64_t work, cudaStream_t s) {
-    switch (nin) {
-    case 0: return launch<C, 0>(p, vec, work, s);
-    case 1: return launch<C, 1>(p, vec, work, s);
-    case 2: return launch<C, 2>(p, vec, work, s);
-    case 3: return launch<C, 3>(p, vec, work, s);
-    default: return launch<C, 4>(p, vec, work, s);
+int launch_interp(int nin, bool fast, const ChainParams& p, bool vec, int64_t work, cudaStream_t s) {
+    if constexpr (std::is_same<C, float>::value) {
+        if (fast) {
+            switch (nin) {
+            case 0: return launch<C, 0, PROG_INTERP_FAST>(p, vec, work, s);
+            case 1: return launch<C, 1, PROG_INTERP_FAST>(p, vec, work, s);
+            case 2: return launch<C, 2, PROG_INTERP_FAST>(p, vec, work, s);
+            case 3: return launch<C, 3, PROG_INTERP_FAST>(p, vec, work, s);
+            default: return launch<C, 4, PROG_INTERP_FAST>(p, vec, work, s);
+            }
+        }
     }
+    switch (nin) {
+    case 0: return launch<C, 0, PROG_INTERP>(p, vec, work, s);
+    case 1: return launch<C, 1, PROG_INTERP>(p, vec, work, s);
+    case 2: return launch<C, 2, PROG_INTERP>(p, vec, work, s);
+    case 3: return launch<C, 3, PROG_INTERP>(p, vec, work, s);
+    default: return launch<C, 4, PROG_INTERP>(p, vec, work, s);
+    }
+}
+
+// Affine + activation vector kernels (fp32 compute).
+template <int ACT, bool FAST, bool MUL>
+int launch_affine_add(bool add, const ChainParams& p, int64_t work, cudaStream_t s) {
+    if (add) return launch<float, 2, affine_prog(ACT, FAST, MUL, true)>(p, true, work, s);
+    return launch<float, 1, affine_prog(ACT, FAST, MUL, false)>(p, true, work, s);
+}
+template <int ACT, bool FAST>
+int launch_affine_mul(bool mul, bool add, const ChainParams& p, int64_t work, cudaStream_t s) {
+    return mul ? launch_affine_add<ACT, FAST, true>(add, p, work, s) : launch_affine_add<ACT, FAST, false>(add, p, work, s);
+}
+template <int ACT>
+int launch_affine_fast(bool fast, bool mul, bool add, const ChainParams& p, int64_t work, cudaStream_t s) {
+    return fast ? launch_affine_mul<ACT, true>(mul, add, p, work, s) : launch_affine_mul<ACT, false>(mul, add, p, work, s);
+}
+int launch_affine(int act, bool fast, bool mul, bool add, const ChainParams& p, int64_t work, cudaStream_t s) {
+    switch (act) {
+    case ACT_GELU: return launch_affine_fast<ACT_GELU>(fast, mul, add, p, work, s);
+    case ACT_RELU: return launch_affine_fast<ACT_RELU>(fast, mul, add, p, work, s);
+    case ACT_SIGMOID: return launch_affine_fast<ACT_SIGMOID>(fast, mul, add, p, work, s);
+    case ACT_TANH: return launch_affine_fast<ACT_TANH>(fast, mul, add, p, work, s);
+    default: return launch_affine_fast<ACT_NONE>(fast, mul, add, p, work, s);
+    }
+}
+
+// Recognises [MUL imm]? [ADD ins[1]]? [GELU | RELU | SIGMOID | TANH]? in fp32
+// compute with only no-op roundings (fp32 / fp64): act(x * s + b).
+struct AffineMatch {
+    bool ok = false, mul = false, add = false;
+    int act = ACT_NONE;
+    float scale = 1.0f;
+};
+
+AffineMatch match_affine(const tadma_instr* prog, int n_instr, int n_ins) {
+    AffineMatch m;
+    auto noop_round = [](int rd) { return rd < 0 || rd == TADMA_F32 || rd == TADMA_F64; };
+    int i = 0;
+    if (i < n_instr && prog[i].op == TADMA_OP_MUL && prog[i].b == TADMA_SRC_IMM && noop_round(prog[i].round_dtype)) {
+        m.mul = true;
+        m.scale = (float)prog[i].imm;
+        i++;
+    }
+    if (i < n_instr && prog[i].op == TADMA_OP_ADD && prog[i].b == 1 && noop_round(prog[i].round_dtype)) {
+        m.add = true;
+        i++;
+    }
+    if (i < n_instr && noop_round(prog[i].round_dtype)) {
+        switch (prog[i].op) {
+        case TADMA_OP_GELU: m.act = ACT_GELU; i++; break;
+        case TADMA_OP_RELU: m.act = ACT_RELU; i++; break;
+        case TADMA_OP_SIGMOID: m.act = ACT_SIGMOID; i++; break;
+        case TADMA_OP_TANH: m.act = ACT_TANH; i++; break;
+        default: break;
+        }
+    }
+    m.ok = i == n_instr && n_instr > 0 && n_ins == (m.add ? 2 : 1);
+    return m;
 }
 
 bool is_transcendental(int op) { return op >= TADMA_OP_EXP && op <= TADMA_OP_GELU && op != TADMA_OP_RELU; }
@@ -509,18 +620,26 @@ extern "C" int tadma_b200_eltwise(const tadma_tensor* out, const tadma_tensor* i
     // == 0 when rank > 1) never straddles a row.
     for (int d = 1; d < f.rank; d++) p.dm[d] = DivMod((uint64_t)f.dims[d]);
 
+    // Fast math (SFU exp / reciprocal) when an fp32 chain ends in a 16-bit
+    // store and every intermediate rounding is to fp32 or coarser: the
+    // approximation error is far below the output's half-ulp.
+    bool fast = cm == TADMA_COMPUTE_F32 && (out->dtype == TADMA_F16 || out->dtype == TADMA_BF16);
+    for (int i = 0; i < n_instr && fast; i++) {
+        int rd = prog[i].round_dtype;
+        if (!(rd < 0 || rd == TADMA_F32 || rd == TADMA_F16 || rd == TADMA_BF16)) fast = false;
+    }
     cudaStream_t s = (cudaStream_t)stream;
-    auto go = [&](bool v, int64_t work) {
+    auto go = [&](const ChainParams& pp, bool v, int64_t work) {
         switch (cm) {
-        case TADMA_COMPUTE_F32: return launch_nin<float>(n_ins, p, v, work, s);
-        case TADMA_COMPUTE_F64: return launch_nin<double>(n_ins, p, v, work, s);
-        default: return launch_nin<int64_t>(n_ins, p, v, work, s);
+        case TADMA_COMPUTE_F32: return launch_interp<float>(n_ins, fast, pp, v, work, s);
+        case TADMA_COMPUTE_F64: return launch_interp<double>(n_ins, false, pp, v, work, s);
+        default: return launch_interp<int64_t>(n_ins, false, pp, v, work, s);
         }
     };
     if (!vec) {
         p.start = 0;
         p.n = n;
-        return go(false, n);
+        return go(p, false, n);
     }
     // Vector path: vector vi covers elements [vi * V, vi * V + V); a rank-1
     // tail of n % V elements goes to the scalar kernel afterwards.
@@ -528,16 +647,18 @@ extern "C" int tadma_b200_eltwise(const tadma_tensor* out, const tadma_tensor* i
     ChainParams pv = p;
     pv.n = nvec;
     int rc;
-    switch (cm) {
-    case TADMA_COMPUTE_F32: rc = launch_nin<float>(n_ins, pv, true, nvec, s); break;
-    case TADMA_COMPUTE_F64: rc = launch_nin<double>(n_ins, pv, true, nvec, s); break;
-    default: rc = launch_nin<int64_t>(n_ins, pv, true, nvec, s); break;
+    AffineMatch am = cm == TADMA_COMPUTE_F32 ? match_affine(prog, n_instr, n_ins) : AffineMatch{};
+    if (am.ok) {
+        pv.scale = am.scale;
+        rc = launch_affine(am.act, fast, am.mul, am.add, pv, nvec, s);
+    } else {
+        rc = go(pv, true, nvec);
     }
     if (rc != TADMA_OK) return rc;
     if (nvec * V < n) {
         p.start = nvec * V;
         p.n = n;
-        return go(false, n - nvec * V);
+        return go(p, false, n - nvec * V);
     }
     return TADMA_OK;
 }

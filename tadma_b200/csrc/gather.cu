@@ -12,10 +12,11 @@
 // Fast path (axis 0, table rows contiguous): one warp per output row; the id
 // is read once per row (one broadcast load), the row is copied in 8-element
 // chunks (16 B of fp16/bf16, 32 B of fp32) with 4 raw chunks in flight per lane,
-// the add operand's row (e.g. pos[s]) is fetched with a read-only load so it
-// stays L2-resident across the batch, and the output is written with
-// evict-first stores: the gather writes its output once and reads each
-// gathered row once, so at config 5 sizes it is an HBM-write-bound copy.
+// the add operand's row (e.g. pos[s]) is fetched with an L2 evict_last policy
+// so it stays resident across the batch while the gathered rows (evict_first
+// policy) and the output (evict-first stores) stream through: the gather
+// writes its output once and reads each gathered row once, so at config 5
+// sizes it is an HBM-bound copy.
 // Any other layout takes a per-element path with the same semantics.
 #include <mutex>
 #include <type_traits>
@@ -62,9 +63,9 @@ struct Raw8 {
 };
 
 template <typename T>
-__device__ __forceinline__ void load_raw(const T* p, Raw8<T>& r) {
-    r.w[0] = ld_nc_v4(p);
-    if constexpr (sizeof(T) == 4) r.w[1] = ld_nc_v4(p + 4);
+__device__ __forceinline__ void load_raw(const T* p, Raw8<T>& r, uint64_t pol) {
+    r.w[0] = ld_nc_v4_policy(p, pol);
+    if constexpr (sizeof(T) == 4) r.w[1] = ld_nc_v4_policy(p + 4, pol);
 }
 
 template <typename T>
@@ -100,6 +101,10 @@ __global__ void __launch_bounds__(THREADS) gather_rows_kernel(const __grid_const
     const int64_t gw = ((int64_t)blockIdx.x * THREADS + threadIdx.x) >> 5;
     const int64_t nw = ((int64_t)gridDim.x * THREADS) >> 5;
     const int64_t nch = p.D / CHUNK;
+    // Gathered rows stream through L2 once; the add operand (a table every
+    // batch row re-reads) is kept resident.
+    const uint64_t pol_stream = l2_policy_evict_first();
+    const uint64_t pol_keep = l2_policy_evict_last();
     for (int64_t row = gw; row < p.nrows; row += nw) {
         int64_t id = load_id(p.ids, p.i_dtype, row * p.ids_stride);
         if (id < 0) id += p.n;
@@ -127,8 +132,8 @@ __global__ void __launch_bounds__(THREADS) gather_rows_kernel(const __grid_const
             for (int u = 0; u < UNR; u++) {
                 const int64_t c = c0 + 32 * u;
                 if (c < nch) {
-                    if (ok) load_raw<TT>(trow + c * CHUNK, tr[u]);
-                    if constexpr (ADD) load_raw<AT>(arow + c * CHUNK, ar[u]);
+                    if (ok) load_raw<TT>(trow + c * CHUNK, tr[u], pol_stream);
+                    if constexpr (ADD) load_raw<AT>(arow + c * CHUNK, ar[u], pol_keep);
                 }
             }
 #pragma unroll

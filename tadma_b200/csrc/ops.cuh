@@ -19,6 +19,21 @@ __device__ __forceinline__ float gelu_f(float x) {
     return __fdiv_rn(x, __fadd_rn(1.0f, e));
 }
 
+// Fast forms, used when an fp32 chain writes a 16-bit output: the SFU
+// exponential and reciprocal (a few fp32 ulp) in a form that only ever
+// divides by a value in (1, 2]: sigmoid(y) = (y >= 0 ? 1 : t) / (1 + t) with
+// t = exp(-|y|).  Their error is orders of magnitude below half an fp16/bf16 ulp.
+__device__ __forceinline__ float sigmoid_fast(float y) {
+    const float t = __expf(-fabsf(y));
+    const float r = __fdividef(1.0f, 1.0f + t);
+    return y >= 0.0f ? r : t * r;
+}
+
+__device__ __forceinline__ float gelu_fast(float x) {
+    const float u = 0.7978845608f * (x + 0.044715f * x * x * x);
+    return x * sigmoid_fast(2.0f * u);
+}
+
 // Rarely fused, register-hungry functions (trig slow paths, erf, log, pow)
 // live out of line so they do not inflate the register budget of the chain.
 __device__ __noinline__ float unary_cold(int op, float a) {
@@ -40,17 +55,18 @@ __device__ __noinline__ float unary_cold(int op, float a) {
 
 __device__ __noinline__ float pow_cold(float a, float b) { return powf(a, b); }
 
+template <bool FAST = false>
 __device__ __forceinline__ float unary(int op, float a) {
     switch (op) {
     case TADMA_OP_COPY: return a;
     case TADMA_OP_NEG: return -a;
     case TADMA_OP_ABS: return fabsf(a);
-    case TADMA_OP_EXP: return expf(a);
+    case TADMA_OP_EXP: return FAST ? __expf(a) : expf(a);
     case TADMA_OP_SQRT: return __fsqrt_rn(a);
     case TADMA_OP_RELU: return a > 0.0f ? a : 0.0f;
-    case TADMA_OP_SIGMOID: return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-a)));
+    case TADMA_OP_SIGMOID: return FAST ? sigmoid_fast(a) : __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-a)));
     case TADMA_OP_TANH: return tanhf(a);
-    case TADMA_OP_GELU: return gelu_f(a);
+    case TADMA_OP_GELU: return FAST ? gelu_fast(a) : gelu_f(a);
     case TADMA_OP_NOT: return a == 0.0f ? 1.0f : 0.0f;
     }
     return unary_cold(op, a);
@@ -83,6 +99,7 @@ __device__ __noinline__ double gelu_d(double x) {
     return x / (1.0 + exp(-2.0 * u));
 }
 
+template <bool FAST = false>
 __device__ __forceinline__ double unary(int op, double a) {
     switch (op) {
     case TADMA_OP_COPY: return a;
@@ -97,6 +114,7 @@ __device__ __forceinline__ double unary(int op, double a) {
     return unary_cold(op, a);
 }
 
+template <bool FAST = false>
 __device__ __forceinline__ int64_t unary(int op, int64_t a) {
     switch (op) {
     case TADMA_OP_NEG: return (int64_t)(0ull - (uint64_t)a);

@@ -1,0 +1,141 @@
+// Conformance program for the header-only Tensor API (include/tadma/Tadma.hpp):
+// calls written the way TADMA's generated graph code writes them
+// (scripts/generated.cu style: operators, .template mean<...>(), pow<false>,
+// sqrt<true>, softmax<-1,false>, gather, concat, transpose, slice, unsqueeze,
+// reshape, where, to<T>), on seeded synthetic inputs.  Every result is written
+// as raw bytes to <outdir>/<name>.bin; tests/test_cpp_api_gpu.py regenerates
+// the inputs with the oracle and checks each file.
+//
+// Build: nvcc -std=c++20 -gencode arch=compute_100a,code=sm_100a -I include
+//        tests/cpp/conformance.cu -L tadma_b200 -ltadma_b200
+#include <cstdio>
+#include <string>
+
+#include "tadma/Tadma.hpp"
+
+using namespace tadma;
+using ALLOCATOR = Allocator<kCUDA>;
+
+static std::string g_dir;
+
+template <AnyTensor T>
+void fill(const T& t, int dist, double p0, double p1, uint64_t sid) {
+    tadma_tensor d = t.describe();
+    detail::check(tadma_b200_fill(&d, dist, p0, p1, 0, sid, 0, stream), "fill");
+}
+
+template <AnyTensor T>
+void save(const char* name, const T& t) {
+    auto h = t.contiguous().template to<kCPU>();
+    std::string path = g_dir + "/" + name + ".bin";
+    FILE* f = std::fopen(path.c_str(), "wb");
+    if (!f) throw std::runtime_error("cannot write " + path);
+    std::fwrite(h.data.view, sizeof(typename T::ValueType), T::Size, f);
+    std::fclose(f);
+}
+
+int main(int argc, char** argv) {
+    if (argc < 2) {
+        std::fprintf(stderr, "usage: %s <outdir>\n", argv[0]);
+        return 2;
+    }
+    g_dir = argv[1];
+    InitGuard guard;
+
+    // config 2 through the operators: x * 0.5f -> float, + bias -> float, gelu in place.
+    Tensor<__nv_bfloat16, ALLOCATOR, Sequence<64, 1024>> x;
+    Tensor<__nv_bfloat16, ALLOCATOR, Sequence<1024>> bias;
+    fill(x, TADMA_DIST_NORMAL, 0.0, 1.0, 1);
+    fill(bias, TADMA_DIST_NORMAL, 0.0, 0.1, 2);
+    auto y_ops = gelu(x * 0.5f + bias);
+    static_assert(std::is_same_v<decltype(y_ops)::ValueType, float>);
+    save("cfg2_ops_f32", y_ops);
+    // config 2 as one fused kernel with a bf16 result.
+    auto y_fused = fused<__nv_bfloat16>(x, fuse::mul(0.5), fuse::add(bias), fuse::gelu());
+    save("cfg2_fused_bf16", y_fused);
+
+    // config 1: y = sum_{last}(exp(A + b)), A[64,128], b[128] fp32.
+    Tensor<float, ALLOCATOR, Sequence<64, 128>> A;
+    Tensor<float, ALLOCATOR, Sequence<128>> b;
+    fill(A, TADMA_DIST_NORMAL, 0.0, 1.0, 1);
+    fill(b, TADMA_DIST_NORMAL, 0.0, 1.0, 2);
+    auto e = exp<false>(A + b);
+    auto s1 = e.template sum<-1, false>();
+    static_assert(decltype(s1)::Rank == 1 && decltype(s1)::Dim(0) == 64);
+    save("cfg1_sum", s1);
+
+    // config 3 (scaled): X[2, 64, 256] ~ U(-1, 1).
+    Tensor<float, ALLOCATOR, Sequence<2, 64, 256>> X;
+    fill(X, TADMA_DIST_UNIFORM, -1.0, 1.0, 3);
+    save("cfg3_sum", X.template sum<-1>());
+    save("cfg3_max", X.template max<-1>());
+    save("cfg3_argmax", X.template argmax<-1>());
+    save("cfg3_mean1", X.template mean<1>());
+
+    // config 4 (scaled): ONNX LayerNorm and softmax, fp16.
+    Tensor<__half, ALLOCATOR, Sequence<4, 16, 1024>> L;
+    Tensor<__half, ALLOCATOR, Sequence<1024>> g, be;
+    fill(L, TADMA_DIST_NORMAL, 0.0, 1.0, 4);
+    fill(g, TADMA_DIST_NORMAL, 1.0, 0.02, 5);
+    fill(be, TADMA_DIST_NORMAL, 0.0, 0.02, 6);
+    save("cfg4_ln", layer_norm_onnx<-1, false>(L, g, be, 1e-5f));
+    save("cfg4_ln_tadma", layer_norm<-1, false>(L, g, be, 1e-5f));
+    Tensor<__half, ALLOCATOR, Sequence<2, 4, 256, 2048>> S;
+    fill(S, TADMA_DIST_NORMAL, 0.0, 3.0, 7);
+    save("cfg4_softmax", softmax<-1, false>(S));
+
+    // config 5 (scaled): embedding gather + position table, fused and as two ops.
+    Tensor<__half, ALLOCATOR, Sequence<1000, 256>> table;
+    Tensor<int64_t, ALLOCATOR, Sequence<4, 64>> ids;
+    Tensor<__nv_bfloat16, ALLOCATOR, Sequence<64, 256>> pos;
+    fill(table, TADMA_DIST_NORMAL, 0.0, 0.02, 8);
+    fill(ids, TADMA_DIST_INDEX, 0.0, 1000.0, 9);
+    fill(pos, TADMA_DIST_NORMAL, 0.0, 0.02, 10);
+    auto emb = gather_add(table, ids, pos);
+    static_assert(std::is_same_v<decltype(emb)::ValueType, float>);
+    save("cfg5_gather_add_f32", emb);
+    auto gathered = gather(table, ids);
+    save("cfg5_gather", gathered);
+
+    // generated.cu's decomposed LayerNorm chain (ReduceMean, Sub, Pow 2,
+    // ReduceMean, Add eps, Sqrt, Div, Mul, Add) on [2, 8, 768] fp32.
+    Tensor<float, ALLOCATOR, Sequence<2, 8, 768>> h;
+    Tensor<float, ALLOCATOR, Sequence<768>> w, wb;
+    fill(h, TADMA_DIST_NORMAL, 0.0, 1.0, 11);
+    fill(w, TADMA_DIST_NORMAL, 1.0, 0.02, 12);
+    fill(wb, TADMA_DIST_NORMAL, 0.0, 0.02, 13);
+    auto m = h.template mean<-1>();
+    auto sub = h - m;
+    auto sq = pow<false>(sub, 2.0f);
+    auto var = sq.template mean<-1>();
+    auto ve = var + 9.999999960041972e-13;
+    auto sd = sqrt<true>(ve);
+    auto nrm = sub / sd;
+    auto mul = nrm * w;
+    auto ln = mul + wb;
+    save("gen_ln", ln);
+
+    // views and copies
+    auto tr = X.template transpose<0, 2, 1>().contiguous();
+    static_assert(decltype(tr)::Dim(1) == 256 && decltype(tr)::Dim(2) == 64);
+    save("view_transpose", tr);
+    auto sl = X.template slice<1, 9, 1, 2>().contiguous();  // rows 1, 3, 5, 7 of axis 1
+    static_assert(decltype(sl)::Dim(1) == 4);
+    save("view_slice", sl);
+    auto rs = X.template reshape<2, -1>();
+    static_assert(decltype(rs)::Dim(1) == 64 * 256);
+    save("view_reshape_sum", rs.template sum<1, false>());
+    auto cc = concat<1>(X, X.template slice<0, 8, 1>());
+    static_assert(decltype(cc)::Dim(1) == 72);
+    save("concat", cc);
+    auto cond = X > 0.25f;
+    auto wsel = where(cond, X, X * -1.0f);
+    save("where", wsel);
+    save("cast_f16", X.template to<__half>());
+    auto un = b.template unsqueeze<0>();  // [1, 128]
+    save("unsqueeze_bcast_add", A + un);
+
+    check_cuda(cudaStreamSynchronize(stream));
+    std::printf("conformance ok\n");
+    return 0;
+}

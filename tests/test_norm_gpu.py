@@ -1,7 +1,10 @@
 """Fused softmax / LayerNorm / RMSNorm vs the oracle (double-precision rows).
 
 Tolerance: fp16/bf16 outputs within 1 ulp of the double result rounded to the
-output type; fp32 outputs within 4 ulp (fp32 statistics of the row).
+output type; fp32 outputs (row statistics accumulated in fp32) within the
+north star's reduction bound, relative error <= 1e-5 * sqrt(L), measured
+against max(|exact|, 1) for LayerNorm / RMSNorm outputs (values near 0) and
+against |exact| for softmax (all outputs positive).
 LayerNorm's ONNX form sqrt(var + eps) and the reference's std + eps
 (Operations.hpp:205-220) are both checked; for var ~ 1 they differ by < 1e-5
 relative, inside the fp16 tolerance.
@@ -16,7 +19,17 @@ from tests.helpers import as_f64, dev_view, empty_dev, from_dev, gen, to_dev, ul
 
 pytestmark = pytest.mark.gpu
 
-TOL = {DType.F16: 1, DType.BF16: 1, DType.F32: 4}
+TOL = {DType.F16: 1, DType.BF16: 1}
+
+
+def assert_close(got, ref, dt, L, softmax=False):
+    if dt == DType.F32:
+        scale = np.abs(ref.astype(np.float64)) if softmax else np.maximum(np.abs(ref.astype(np.float64)), 1.0)
+        rel = np.abs(got.astype(np.float64) - ref) / scale
+        assert rel.max() <= 1e-5 * np.sqrt(L), rel.max()
+    else:
+        d = ulp_diff(got, ref, dt)
+        assert d.max() <= TOL[dt], d.max()
 
 
 def _softmax_both(x, dt, axis):
@@ -40,8 +53,7 @@ def _softmax_both(x, dt, axis):
 def test_softmax(dt, shape, axis):
     x = gen(shape, dt, Dist.NORMAL, 0.0, 3.0, 1)
     got, ref = _softmax_both(x, dt, axis)
-    d = ulp_diff(got, ref, dt)
-    assert d.max() <= TOL[dt], d.max()
+    assert_close(got, ref, dt, shape[axis], softmax=True)
 
 
 def test_softmax_inplace_and_extremes():
@@ -85,8 +97,7 @@ def test_layer_norm(mode, dt, gdt, shape):
     g = gen((L,), gdt, Dist.NORMAL, 1.0, 0.02, 2)
     b = gen((L,), gdt, Dist.NORMAL, 0.0, 0.02, 3)
     got, ref = _ln_both(x, dt, g, b, gdt, 1e-5, mode)
-    d = ulp_diff(got, ref, dt)
-    assert d.max() <= TOL[dt], d.max()
+    assert_close(got, ref, dt, L)
 
 
 def test_layer_norm_kat_alternating_rows():
@@ -105,7 +116,7 @@ def test_rms_norm(dt, shape):
     tb.rms_norm(xd, -1, 0.0, out)
     ref = np.zeros(shape, dtype=from_dev(out).dtype)
     assert O.rms_norm(x, -1, 0.0, ref, dtype=dt) == 0
-    assert ulp_diff(from_dev(out), ref, dt).max() <= TOL[dt]
+    assert_close(from_dev(out), ref, dt, shape[-1])
 
 
 def test_config4_reduced_size():
