@@ -391,6 +391,93 @@ __global__ void __launch_bounds__(THREADS) chain_scalar_kernel(const __grid_cons
     }
 }
 
+// ------------------------------------------------------ row-broadcast affine --
+//
+// y[r, c] = act(x[r, c] * s + b[c]) over a [rows, cols] layout (cols % 8 == 0)
+// with a row-broadcast b: the bias-plus-activation pattern of config 2 and of
+// every dense layer.  Each thread owns one 8-column vector for all of its rows,
+// so b is loaded and converted once and stays in registers, the row loop needs
+// no index division, and 4 rows are in flight per thread.  Same op bodies as
+// the interpreter (__fmul_rn, __fadd_rn, activation<ACT, FAST>, RN stores), so
+// the bits are identical to the generic path.
+
+struct AffineRowsParams {
+    const char* x;
+    const char* bias;
+    char* out;
+    int64_t rows, ncv;      // rows, 8-element column vectors
+    int64_t x_rs, out_rs;   // row strides (elements)
+    float scale;
+};
+
+template <typename T>
+struct Raw8x {
+    uint4 w[sizeof(T) == 4 ? 2 : 1];
+};
+
+template <typename T>
+__device__ __forceinline__ void raw8_load(const T* p, Raw8x<T>& r, bool stream) {
+    r.w[0] = stream ? ld_stream_v4(p) : ld_v4(p);
+    if constexpr (sizeof(T) == 4) r.w[1] = stream ? ld_stream_v4(p + 4) : ld_v4(p + 4);
+}
+
+template <typename T>
+__device__ __forceinline__ void raw8_cvt(const Raw8x<T>& r, float* f) {
+    if constexpr (sizeof(T) == 4) {
+        const uint32_t w[8] = {r.w[0].x, r.w[0].y, r.w[0].z, r.w[0].w, r.w[1].x, r.w[1].y, r.w[1].z, r.w[1].w};
+#pragma unroll
+        for (int j = 0; j < 8; j++) f[j] = __uint_as_float(w[j]);
+    } else {
+        unpack8(r.w[0], std::is_same<T, __half>::value ? TADMA_F16 : TADMA_BF16, f);
+    }
+}
+
+template <typename T>
+__device__ __forceinline__ void raw8_store(T* p, const float* f) {
+    if constexpr (sizeof(T) == 4) {
+        st_stream_v4(p, make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]), __float_as_uint(f[3])));
+        st_stream_v4(p + 4, make_uint4(__float_as_uint(f[4]), __float_as_uint(f[5]), __float_as_uint(f[6]), __float_as_uint(f[7])));
+    } else {
+        st_stream_v4(p, pack8(f, std::is_same<T, __half>::value ? TADMA_F16 : TADMA_BF16));
+    }
+}
+
+template <typename XT, typename OT, int ACT>
+__global__ void __launch_bounds__(THREADS) affine_rows_kernel(const __grid_constant__ AffineRowsParams p) {
+    constexpr bool FAST = sizeof(OT) == 2;  // same rule as the host: fp32 compute, 16-bit store
+    constexpr int UR = 4;
+    const int64_t cv = (int64_t)blockIdx.x * THREADS + threadIdx.x;
+    if (cv >= p.ncv) return;
+    float b[8];
+    {
+        Raw8x<XT> rb;
+        raw8_load<XT>(reinterpret_cast<const XT*>(p.bias) + cv * 8, rb, false);
+        raw8_cvt<XT>(rb, b);
+    }
+    const XT* xcol = reinterpret_cast<const XT*>(p.x) + cv * 8;
+    OT* ocol = reinterpret_cast<OT*>(p.out) + cv * 8;
+    const int64_t ystep = gridDim.y;
+    for (int64_t r0 = blockIdx.y; r0 < p.rows; r0 += ystep * UR) {
+        Raw8x<XT> raw[UR];
+#pragma unroll
+        for (int u = 0; u < UR; u++) {
+            const int64_t r = r0 + u * ystep;
+            if (r < p.rows) raw8_load<XT>(xcol + r * p.x_rs, raw[u], true);
+        }
+#pragma unroll
+        for (int u = 0; u < UR; u++) {
+            const int64_t r = r0 + u * ystep;
+            if (r < p.rows) {
+                float v[8];
+                raw8_cvt<XT>(raw[u], v);
+#pragma unroll
+                for (int j = 0; j < 8; j++) v[j] = activation<ACT, FAST>(__fadd_rn(__fmul_rn(v[j], p.scale), b[j]));
+                raw8_store<OT>(ocol + r * p.out_rs, v);
+            }
+        }
+    }
+}
+
 // ------------------------------------------------------------ host side --
 
 int blocks_per_sm(const void* fn) {
@@ -497,6 +584,41 @@ AffineMatch match_affine(const tadma_instr* prog, int n_instr, int n_ins) {
     }
     m.ok = i == n_instr && n_instr > 0 && n_ins == (m.add ? 2 : 1);
     return m;
+}
+
+template <typename XT, typename OT, int ACT>
+int launch_rows_t(const AffineRowsParams& p, cudaStream_t s) {
+    const void* fn = (const void*)affine_rows_kernel<XT, OT, ACT>;
+    const int64_t gx = (p.ncv + THREADS - 1) / THREADS;
+    int64_t target = (int64_t)sm_count() * blocks_per_sm(fn);
+    int64_t gy = (target + gx - 1) / gx;
+    if (gy > p.rows) gy = p.rows;
+    if (gy > 65535) gy = 65535;
+    if (gy < 1) gy = 1;
+    if (gx > 0x7fffffff) return fail(TADMA_ERR_UNSUPPORTED, "eltwise: too many column vectors");
+    affine_rows_kernel<XT, OT, ACT><<<dim3((unsigned)gx, (unsigned)gy), THREADS, 0, s>>>(p);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? TADMA_OK : cuda_fail(e, "tadma_b200_eltwise launch");
+}
+
+template <typename XT, typename OT>
+int launch_rows_act(int act, const AffineRowsParams& p, cudaStream_t s) {
+    switch (act) {
+    case ACT_GELU: return launch_rows_t<XT, OT, ACT_GELU>(p, s);
+    case ACT_RELU: return launch_rows_t<XT, OT, ACT_RELU>(p, s);
+    case ACT_SIGMOID: return launch_rows_t<XT, OT, ACT_SIGMOID>(p, s);
+    case ACT_TANH: return launch_rows_t<XT, OT, ACT_TANH>(p, s);
+    default: return launch_rows_t<XT, OT, ACT_NONE>(p, s);
+    }
+}
+
+// x dtype = bias dtype in {f32, f16, bf16}; out dtype = x dtype or f32.
+int launch_rows(int xdt, int odt, int act, const AffineRowsParams& p, cudaStream_t s) {
+    if (xdt == TADMA_F32) return launch_rows_act<float, float>(act, p, s);
+    if (xdt == TADMA_F16)
+        return odt == TADMA_F16 ? launch_rows_act<__half, __half>(act, p, s) : launch_rows_act<__half, float>(act, p, s);
+    return odt == TADMA_BF16 ? launch_rows_act<__nv_bfloat16, __nv_bfloat16>(act, p, s)
+                             : launch_rows_act<__nv_bfloat16, float>(act, p, s);
 }
 
 bool is_transcendental(int op) { return op >= TADMA_OP_EXP && op <= TADMA_OP_GELU && op != TADMA_OP_RELU; }
@@ -648,7 +770,25 @@ extern "C" int tadma_b200_eltwise(const tadma_tensor* out, const tadma_tensor* i
     pv.n = nvec;
     int rc;
     AffineMatch am = cm == TADMA_COMPUTE_F32 ? match_affine(prog, n_instr, n_ins) : AffineMatch{};
-    if (am.ok) {
+    const bool fdt = out->dtype == TADMA_F32 || out->dtype == TADMA_F16 || out->dtype == TADMA_BF16;
+    const bool rows_ok = am.ok && am.add && f.rank == 2 && fdt && ins[0].dtype == ins[1].dtype &&
+                         (ins[0].dtype == TADMA_F32 || ins[0].dtype == TADMA_F16 || ins[0].dtype == TADMA_BF16) &&
+                         (out->dtype == ins[0].dtype || out->dtype == TADMA_F32) && f.strides[2][0] == 0 &&
+                         f.strides[2][1] == 1 && f.strides[1][1] == 1 && f.strides[0][1] == 1 && !p.in[1].inner_bcast;
+    if (rows_ok) {
+        // vec eligibility (checked above) already guarantees 16-byte alignment of
+        // every row start and inner % 8 == 0.
+        AffineRowsParams ap{};
+        ap.x = (const char*)ins[0].data;
+        ap.bias = (const char*)ins[1].data;
+        ap.out = (char*)out->data;
+        ap.rows = f.dims[0];
+        ap.ncv = f.dims[1] / V;
+        ap.x_rs = f.strides[1][0];
+        ap.out_rs = f.strides[0][0];
+        ap.scale = am.mul ? am.scale : 1.0f;
+        rc = launch_rows(ins[0].dtype, out->dtype, am.act, ap, s);
+    } else if (am.ok) {
         pv.scale = am.scale;
         rc = launch_affine(am.act, fast, am.mul, am.add, pv, nvec, s);
     } else {
