@@ -98,8 +98,10 @@ __device__ __forceinline__ float fast_exp(float x) {
 
 // ----------------------------------------------------------- warp kernel --
 
+// Rows of <= 4 chunks per lane are latency-bound: cap registers so 3 CTAs
+// (24 warps) fit per SM; 8-chunk rows keep their registers (2 CTAs per SM).
 template <typename T, int CH, int MODE>
-__global__ void __launch_bounds__(THREADS) rownorm_warp_kernel(const __grid_constant__ NormParams p) {
+__global__ void __launch_bounds__(THREADS, (CH <= 4 ? 3 : 2)) rownorm_warp_kernel(const __grid_constant__ NormParams p) {
     constexpr int N = VecT<T>::N;
     const int lane = threadIdx.x & 31;
     const int64_t gw = ((int64_t)blockIdx.x * THREADS + threadIdx.x) >> 5;
@@ -179,8 +181,9 @@ __global__ void __launch_bounds__(THREADS) rownorm_warp_kernel(const __grid_cons
                 if (col < p.L) {
                     float g[N], b[N];
                     if (p.gb_vec) {
-                        if (p.gamma) cvt_in<T>(ld_v4(reinterpret_cast<const T*>(p.gamma) + col), g);
-                        if (p.beta) cvt_in<T>(ld_v4(reinterpret_cast<const T*>(p.beta) + col), b);
+                        // raw 16-byte loads converted at use keep few registers live
+                        if (p.gamma) cvt_in<T>(ld_nc_v4(reinterpret_cast<const T*>(p.gamma) + col), g);
+                        if (p.beta) cvt_in<T>(ld_nc_v4(reinterpret_cast<const T*>(p.beta) + col), b);
                     } else {
 #pragma unroll
                         for (int j = 0; j < N; j++) {

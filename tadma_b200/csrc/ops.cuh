@@ -20,18 +20,36 @@ __device__ __forceinline__ float gelu_f(float x) {
 }
 
 // Fast forms, used when an fp32 chain writes a 16-bit output: the SFU
-// exponential and reciprocal (a few fp32 ulp) in a form that only ever
-// divides by a value in (1, 2]: sigmoid(y) = (y >= 0 ? 1 : t) / (1 + t) with
-// t = exp(-|y|).  Their error is orders of magnitude below half an fp16/bf16 ulp.
-__device__ __forceinline__ float sigmoid_fast(float y) {
-    const float t = __expf(-fabsf(y));
-    const float r = __fdividef(1.0f, 1.0f + t);
-    return y >= 0.0f ? r : t * r;
+// base-2 exponential and reciprocal (ex2.approx / rcp.approx, a few fp32 ulp)
+// in a form whose reciprocal only ever sees (1, 2]:
+//   sigmoid(y) = (y >= 0 ? 1 : t) / (1 + t),  t = 2^(-|y| log2 e).
+// Their error is orders of magnitude below half an fp16/bf16 ulp.
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
 }
 
+// sigmoid of w / log2(e): callers fold log2(e) into their own constants.
+__device__ __forceinline__ float sigmoid_log2(float w) {
+    const float t = ex2_approx(-fabsf(w));
+    const float r = rcp_approx(1.0f + t);
+    return w >= 0.0f ? r : t * r;
+}
+
+__device__ __forceinline__ float sigmoid_fast(float y) { return sigmoid_log2(y * 1.4426950408889634f); }
+
 __device__ __forceinline__ float gelu_fast(float x) {
-    const float u = 0.7978845608f * (x + 0.044715f * x * x * x);
-    return x * sigmoid_fast(2.0f * u);
+    // gelu(x) = x * sigmoid(2u), u = 0.7978845608 (x + 0.044715 x^3)
+    // 2u log2(e) = x (K1 + K3 x^2) with the constants folded.
+    constexpr float K1 = 2.0f * 0.7978845608f * 1.4426950408889634f;
+    constexpr float K3 = K1 * 0.044715f;
+    return x * sigmoid_log2(x * fmaf(K3, x * x, K1));
 }
 
 // Rarely fused, register-hungry functions (trig slow paths, erf, log, pow)

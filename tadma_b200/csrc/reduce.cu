@@ -16,12 +16,17 @@
 //   split R (rows w, w+8, ...), each lane reading 16 contiguous bytes per row
 //   so every warp load is a fully used 512-byte run; partials combine through
 //   shared memory in warp order;
+// * SPLIT (ROW or COL) when few outputs share a long reduced axis: several
+//   CTAs per output reduce fixed chunks into a workspace, a second pass
+//   combines the chunk partials in order;
 // * GENERIC path: any other layout / dtype, one warp per output element.
 // Every path assigns elements to lanes and combines partials in a fixed
 // order, so results are deterministic run to run.
 #include <mutex>
+#include <string>
 #include <type_traits>
 #include <unordered_map>
+#include <vector>
 
 #include "common.cuh"
 #include "layout.hpp"
@@ -53,6 +58,10 @@ struct RedParams {
     DivMod kdm[TADMA_MAX_RANK];
     int64_t kin[TADMA_MAX_RANK];
     int64_t kout[TADMA_MAX_RANK];
+    // split-R (two-pass) reductions
+    int64_t splits;  // CTAs per row (ROW) / per column tile (COL)
+    int64_t chunk;   // reduced-axis elements per split
+    void* partials;  // State<float> workspace
 };
 
 // ------------------------------------------------------------ state ops --
@@ -94,6 +103,43 @@ __device__ __forceinline__ void update(State<A>& s, A v, int64_t idx) {
             s.v = v;
             s.i = idx;
         }
+    }
+}
+
+// Fold N consecutive elements f[0..N) with indices base..base+N-1.  For
+// arg-reductions the vector's extreme and NaN presence are found with N
+// compares; the first matching index is searched only when the vector beats
+// the running best, which becomes rare after the first few vectors.
+template <int K, int N>
+__device__ __forceinline__ void update_vec(State<float>& s, const float* f, int64_t base) {
+    if constexpr (K == K_ARGMAX || K == K_ARGMIN) {
+        if (s.i >= 0 && s.v != s.v) return;  // a NaN was already found: it stays
+        float m = f[0];
+        bool nan = f[0] != f[0];
+#pragma unroll
+        for (int j = 1; j < N; j++) {
+            m = (K == K_ARGMAX) ? fmaxf(m, f[j]) : fminf(m, f[j]);
+            nan |= f[j] != f[j];
+        }
+        if (nan) {
+#pragma unroll
+            for (int j = N - 1; j >= 0; j--)
+                if (f[j] != f[j]) s.i = base + j;
+            s.v = NAN;
+            return;
+        }
+        const bool better = s.i < 0 || ((K == K_ARGMAX) ? (m > s.v) : (m < s.v));
+        if (better) {
+            int64_t idx = base;
+#pragma unroll
+            for (int j = N - 1; j >= 0; j--)
+                if (f[j] == m) idx = base + j;
+            s.v = m;
+            s.i = idx;
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < N; j++) update<K, float>(s, f[j], base + j);
     }
 }
 
@@ -216,7 +262,8 @@ __global__ void __launch_bounds__(THREADS) reduce_row_kernel(const __grid_consta
                         float f[N];
                         Vec<T>::cvt(r[u], f);
 #pragma unroll
-                        for (int j = 0; j < N; j++) update<K, float>(s, prep(p, f[j]), (i0 + 32 * u) * N + j);
+                        for (int j = 0; j < N; j++) f[j] = prep(p, f[j]);
+                        update_vec<K, N>(s, f, (i0 + 32 * u) * N);
                     }
                 }
             }
@@ -230,12 +277,15 @@ __global__ void __launch_bounds__(THREADS) reduce_row_kernel(const __grid_consta
 
 // -------------------------------------------------------------- COL path --
 
-template <typename T, int K, int VEC>
+template <typename T, int K, int VEC, bool SPLIT>
 __global__ void __launch_bounds__(THREADS) reduce_col_kernel(const __grid_constant__ RedParams p) {
     constexpr int COLS = 32 * VEC;
     __shared__ State<float> part[WARPS][COLS];
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const int64_t col0 = (int64_t)blockIdx.x * COLS + lane * VEC;
+    // SPLIT: this CTA covers rows [rbeg, rend) of R and writes a partial state.
+    const int64_t rbeg = SPLIT ? (int64_t)blockIdx.z * p.chunk : 0;
+    const int64_t rend = SPLIT ? (rbeg + p.chunk < p.R ? rbeg + p.chunk : p.R) : p.R;
     for (int64_t o = blockIdx.y; o < p.nrows; o += gridDim.y) {
         const T* base = reinterpret_cast<const T*>(p.in) + o * p.in_row_stride;
         State<float> s[VEC];
@@ -243,15 +293,15 @@ __global__ void __launch_bounds__(THREADS) reduce_col_kernel(const __grid_consta
         for (int j = 0; j < VEC; j++) s[j] = init_state<K, float>();
         if (col0 < p.inner) {
             constexpr int UNR = 4;
-            for (int64_t r0 = w; r0 < p.R; r0 += WARPS * UNR) {
+            for (int64_t r0 = rbeg + w; r0 < rend; r0 += WARPS * UNR) {
                 if constexpr (VEC > 1) {
                     uint4 v[UNR];
 #pragma unroll
                     for (int u = 0; u < UNR; u++)
-                        if (r0 + WARPS * u < p.R) v[u] = ld_stream_v4(base + (r0 + WARPS * u) * p.r_stride + col0);
+                        if (r0 + WARPS * u < rend) v[u] = ld_stream_v4(base + (r0 + WARPS * u) * p.r_stride + col0);
 #pragma unroll
                     for (int u = 0; u < UNR; u++) {
-                        if (r0 + WARPS * u < p.R) {
+                        if (r0 + WARPS * u < rend) {
                             float f[Vec<T>::N];
                             Vec<T>::cvt(v[u], f);
 #pragma unroll
@@ -262,10 +312,10 @@ __global__ void __launch_bounds__(THREADS) reduce_col_kernel(const __grid_consta
                     float v[UNR];
 #pragma unroll
                     for (int u = 0; u < UNR; u++)
-                        if (r0 + WARPS * u < p.R) v[u] = ld1(base + (r0 + WARPS * u) * p.r_stride + col0);
+                        if (r0 + WARPS * u < rend) v[u] = ld1(base + (r0 + WARPS * u) * p.r_stride + col0);
 #pragma unroll
                     for (int u = 0; u < UNR; u++)
-                        if (r0 + WARPS * u < p.R) update<K, float>(s[0], prep(p, v[u]), r0 + WARPS * u);
+                        if (r0 + WARPS * u < rend) update<K, float>(s[0], prep(p, v[u]), r0 + WARPS * u);
                 }
             }
         }
@@ -278,10 +328,94 @@ __global__ void __launch_bounds__(THREADS) reduce_col_kernel(const __grid_consta
                 State<float> t = part[0][c];
 #pragma unroll
                 for (int ww = 1; ww < WARPS; ww++) t = combine<K, float>(t, part[ww][c]);
-                finish<K, float>(p, t, o * p.out_row_stride + col);
+                if constexpr (SPLIT) {
+                    reinterpret_cast<State<float>*>(p.partials)[(o * p.splits + blockIdx.z) * p.inner + col] = t;
+                } else {
+                    finish<K, float>(p, t, o * p.out_row_stride + col);
+                }
             }
         }
         __syncthreads();
+    }
+}
+
+// ----------------------------------------------------- split-R (two-pass) --
+//
+// Few output rows with a long reduced axis leave most SMs idle on the one-warp-
+// (or one-CTA-) per-output paths.  Pass 1 gives each output `splits` CTAs, each
+// reducing one fixed chunk of R into a State in a workspace; pass 2 combines
+// the partials of an output in chunk order.  Chunks and combine order depend
+// only on (R, splits), so results are deterministic.
+
+template <typename T, int K>
+__global__ void __launch_bounds__(THREADS) reduce_row_split_kernel(const __grid_constant__ RedParams p, int vec) {
+    constexpr int N = Vec<T>::N;
+    constexpr int UNR = 4;
+    __shared__ State<float> sh[WARPS];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int64_t row = blockIdx.y, g = blockIdx.x;
+    const int64_t r0 = g * p.chunk;
+    const int64_t r1 = r0 + p.chunk < p.R ? r0 + p.chunk : p.R;
+    const T* x = reinterpret_cast<const T*>(p.in) + row * p.in_row_stride;
+    State<float> s = init_state<K, float>();
+    int64_t done = r0;
+    if (vec) {  // chunk % N == 0, so every chunk starts 16-byte aligned
+        const int64_t v0 = r0 / N, v1 = r1 / N;
+        for (int64_t i0 = v0 + threadIdx.x; i0 < v1; i0 += THREADS * UNR) {
+            uint4 r[UNR];
+#pragma unroll
+            for (int u = 0; u < UNR; u++)
+                if (i0 + THREADS * u < v1) r[u] = ld_stream_v4(x + (i0 + THREADS * u) * N);
+#pragma unroll
+            for (int u = 0; u < UNR; u++) {
+                if (i0 + THREADS * u < v1) {
+                    float f[N];
+                    Vec<T>::cvt(r[u], f);
+#pragma unroll
+                    for (int j = 0; j < N; j++) f[j] = prep(p, f[j]);
+                    update_vec<K, N>(s, f, (i0 + THREADS * u) * N);
+                }
+            }
+        }
+        done = v1 * N;
+    }
+    for (int64_t i = done + threadIdx.x; i < r1; i += THREADS) update<K, float>(s, prep(p, ld1(x + i * p.r_stride)), i);
+    s = warp_combine<K, float>(s);
+    if (lane == 0) sh[w] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        State<float> t = sh[0];
+#pragma unroll
+        for (int ww = 1; ww < WARPS; ww++) t = combine<K, float>(t, sh[ww]);
+        reinterpret_cast<State<float>*>(p.partials)[row * p.splits + g] = t;
+    }
+}
+
+// Pass 2 of the ROW split: one warp per output row.
+template <int K>
+__global__ void __launch_bounds__(THREADS) reduce_row_finish_kernel(const __grid_constant__ RedParams p) {
+    const int lane = threadIdx.x & 31;
+    const int64_t gw = ((int64_t)blockIdx.x * THREADS + threadIdx.x) >> 5;
+    const int64_t nw = ((int64_t)gridDim.x * THREADS) >> 5;
+    const State<float>* part = reinterpret_cast<const State<float>*>(p.partials);
+    for (int64_t row = gw; row < p.nrows; row += nw) {
+        State<float> s = init_state<K, float>();
+        for (int64_t g = lane; g < p.splits; g += 32) s = combine<K, float>(s, part[row * p.splits + g]);
+        s = warp_combine<K, float>(s);
+        if (lane == 0) finish<K, float>(p, s, row * p.out_row_stride);
+    }
+}
+
+// Pass 2 of the COL split: one thread per output column of an outer index.
+template <int K>
+__global__ void __launch_bounds__(THREADS) reduce_col_finish_kernel(const __grid_constant__ RedParams p) {
+    const State<float>* part = reinterpret_cast<const State<float>*>(p.partials);
+    const int64_t total = p.nrows * p.inner;
+    for (int64_t idx = (int64_t)blockIdx.x * THREADS + threadIdx.x; idx < total; idx += (int64_t)gridDim.x * THREADS) {
+        const int64_t o = idx / p.inner, col = idx - o * p.inner;
+        State<float> t = init_state<K, float>();
+        for (int64_t g = 0; g < p.splits; g++) t = combine<K, float>(t, part[(o * p.splits + g) * p.inner + col]);
+        finish<K, float>(p, t, o * p.out_row_stride + col);
     }
 }
 
@@ -339,16 +473,29 @@ int grid_for(const void* fn, int64_t want) {
 template <typename T, int K>
 int launch_fast(int path, const RedParams& p, bool vec, cudaStream_t s) {
     if (path == 0) {
-        const void* fn = (const void*)reduce_row_kernel<T, K>;
-        int grid = grid_for(fn, (p.nrows + WARPS - 1) / WARPS);
-        reduce_row_kernel<T, K><<<grid, THREADS, 0, s>>>(p, vec ? 1 : 0);
+        if (p.splits > 1) {
+            reduce_row_split_kernel<T, K><<<dim3((unsigned)p.splits, (unsigned)p.nrows), THREADS, 0, s>>>(p, vec ? 1 : 0);
+            const void* fn = (const void*)reduce_row_finish_kernel<K>;
+            reduce_row_finish_kernel<K><<<grid_for(fn, (p.nrows + WARPS - 1) / WARPS), THREADS, 0, s>>>(p);
+        } else {
+            const void* fn = (const void*)reduce_row_kernel<T, K>;
+            int grid = grid_for(fn, (p.nrows + WARPS - 1) / WARPS);
+            reduce_row_kernel<T, K><<<grid, THREADS, 0, s>>>(p, vec ? 1 : 0);
+        }
     } else {
         constexpr int VEC = Vec<T>::N;
         int64_t tiles = vec ? (p.inner + 32 * VEC - 1) / (32 * VEC) : (p.inner + 31) / 32;
         if (tiles > 0x7fffffff) return fail(TADMA_ERR_UNSUPPORTED, "reduce: too many column tiles");
-        dim3 grid((unsigned)tiles, (unsigned)(p.nrows < 65535 ? p.nrows : 65535));
-        if (vec) reduce_col_kernel<T, K, VEC><<<grid, THREADS, 0, s>>>(p);
-        else reduce_col_kernel<T, K, 1><<<grid, THREADS, 0, s>>>(p);
+        dim3 grid((unsigned)tiles, (unsigned)(p.nrows < 65535 ? p.nrows : 65535), (unsigned)(p.splits > 1 ? p.splits : 1));
+        if (p.splits > 1) {
+            if (vec) reduce_col_kernel<T, K, VEC, true><<<grid, THREADS, 0, s>>>(p);
+            else reduce_col_kernel<T, K, 1, true><<<grid, THREADS, 0, s>>>(p);
+            const void* fn = (const void*)reduce_col_finish_kernel<K>;
+            reduce_col_finish_kernel<K><<<grid_for(fn, (p.nrows * p.inner + THREADS - 1) / THREADS), THREADS, 0, s>>>(p);
+        } else {
+            if (vec) reduce_col_kernel<T, K, VEC, false><<<grid, THREADS, 0, s>>>(p);
+            else reduce_col_kernel<T, K, 1, false><<<grid, THREADS, 0, s>>>(p);
+        }
     }
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? TADMA_OK : cuda_fail(e, "tadma_b200_reduce launch");
@@ -385,6 +532,67 @@ int launch_generic(int kind, const RedParams& p, cudaStream_t s) {
     }
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? TADMA_OK : cuda_fail(e, "tadma_b200_reduce launch");
+}
+
+// Split plans: how many CTAs share one output's reduced axis (1 = no split).
+// ROW: split when fewer than 16 warps per SM would be busy and R is long.
+void plan_row_split(RedParams& p, int64_t R, int64_t sm) {
+    p.splits = 1;
+    if (p.nrows >= 16 * sm || R < 16384 || p.nrows > 65535) return;
+    int64_t g = (4 * sm + p.nrows - 1) / p.nrows;
+    if (g > R / 4096) g = R / 4096;
+    if (g > 65535) g = 65535;
+    if (g < 2) return;
+    int64_t chunk = ((R + g - 1) / g + 7) / 8 * 8;  // multiple of every vector width
+    p.chunk = chunk;
+    p.splits = (R + chunk - 1) / chunk;
+}
+
+// COL: split when fewer than 2 CTAs per SM would be busy and R is long.
+void plan_col_split(RedParams& p, int64_t R, int64_t cols_per_cta, int64_t sm) {
+    p.splits = 1;
+    const int64_t tiles = (p.inner + cols_per_cta - 1) / cols_per_cta;
+    const int64_t ctas = tiles * p.nrows;
+    if (ctas >= 2 * sm || R < 2048 || p.nrows > 65535) return;
+    int64_t g = (4 * sm + ctas - 1) / ctas;
+    if (g > R / 256) g = R / 256;
+    if (g > 65535) g = 65535;
+    if (g < 2) return;
+    p.chunk = (R + g - 1) / g;
+    p.splits = (R + p.chunk - 1) / p.chunk;
+}
+
+int64_t split_workspace_bytes(const RedParams& p, int path) {
+    if (p.splits <= 1) return 0;
+    const int64_t states = path == 0 ? p.nrows * p.splits : p.nrows * p.splits * p.inner;
+    return states * (int64_t)sizeof(State<float>);
+}
+
+int dispatch_fast(int dt, int kind, int path, const RedParams& p, bool vec, cudaStream_t s) {
+    switch (dt) {
+    case TADMA_F32: return launch_fast_kind<float>(kind, path, p, vec, s);
+    case TADMA_F16: return launch_fast_kind<__half>(kind, path, p, vec, s);
+    default: return launch_fast_kind<__nv_bfloat16>(kind, path, p, vec, s);
+    }
+}
+
+// Runs a fast path; a split plan gets a stream-ordered workspace for its
+// partials (cudaMallocAsync / cudaFreeAsync on the call's stream, so calls on
+// different streams never share it).
+// Runs a fast path; a split plan gets a stream-ordered workspace for its
+// partials (cudaMallocAsync / cudaFreeAsync on the call's stream, so calls on
+// different streams never share it).
+int run_fast(int dt, int kind, int path, RedParams& p, bool vec, cudaStream_t s) {
+    const int64_t ws = split_workspace_bytes(p, path);
+    if (ws == 0) return dispatch_fast(dt, kind, path, p, vec, s);
+    void* buf = nullptr;
+    cudaError_t e = cudaMallocAsync(&buf, (size_t)ws, s);
+    if (e != cudaSuccess) return cuda_fail(e, "tadma_b200_reduce workspace");
+    p.partials = buf;
+    int rc = dispatch_fast(dt, kind, path, p, vec, s);
+    e = cudaFreeAsync(buf, s);
+    if (rc == TADMA_OK && e != cudaSuccess) return cuda_fail(e, "tadma_b200_reduce workspace free");
+    return rc;
 }
 
 }  // namespace
@@ -467,11 +675,8 @@ extern "C" int tadma_b200_reduce(int32_t op, const tadma_tensor* in, int32_t axi
         p.out_row_stride = f.strides[1][0];
         const int N = 16 / es;
         bool vec = in_aligned && R >= N && (p.nrows == 1 || (p.in_row_stride * es) % 16 == 0);
-        switch (dt) {
-        case TADMA_F32: return launch_fast_kind<float>(kind, 0, p, vec, s);
-        case TADMA_F16: return launch_fast_kind<__half>(kind, 0, p, vec, s);
-        default: return launch_fast_kind<__nv_bfloat16>(kind, 0, p, vec, s);
-        }
+        plan_row_split(p, R, sm_count());
+        return run_fast(dt, kind, 0, p, vec, s);
     }
     if (fast_dt && R > 1 && p.r_stride != 1 && f.rank <= 2 && f.strides[0][last] == 1 && f.strides[1][last] == 1 &&
         f.dims[last] > 1) {
@@ -482,11 +687,8 @@ extern "C" int tadma_b200_reduce(int32_t op, const tadma_tensor* in, int32_t axi
         p.out_row_stride = f.rank == 2 ? f.strides[1][0] : 0;
         const int N = 16 / es;
         bool vec = in_aligned && p.inner % N == 0 && (p.r_stride * es) % 16 == 0 && (p.in_row_stride * es) % 16 == 0;
-        switch (dt) {
-        case TADMA_F32: return launch_fast_kind<float>(kind, 1, p, vec, s);
-        case TADMA_F16: return launch_fast_kind<__half>(kind, 1, p, vec, s);
-        default: return launch_fast_kind<__nv_bfloat16>(kind, 1, p, vec, s);
-        }
+        plan_col_split(p, R, vec ? 32 * N : 32, sm_count());
+        return run_fast(dt, kind, 1, p, vec, s);
     }
     // GENERIC
     p.krank = f.rank;

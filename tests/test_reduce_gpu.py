@@ -177,3 +177,43 @@ def test_invalid():
         tb.reduce(Reduce.ARGMAX, x, 1, empty_dev((4, 1), DType.F32))
     with pytest.raises(tb.TadmaError):
         tb.reduce(Reduce.SUM, x, 1, empty_dev((4, 2), DType.F32))
+
+
+# ---- split-R (two-pass) paths: few outputs, long reduced axis ----------------
+
+@pytest.mark.parametrize("dt", [DType.F32, DType.BF16])
+@pytest.mark.parametrize("op", [Reduce.SUM, Reduce.MEAN, Reduce.MAX, Reduce.ARGMAX, Reduce.ARGMIN, Reduce.RMS])
+def test_row_split_long_rows(dt, op):
+    x = gen((3, 200003), dt, Dist.NORMAL, 0.0, 1.0, 21)  # odd length: vector body + scalar tail
+    got, ref = run_both(op, x, dt, -1, keep=False, out_dt=DType.I64 if op in (Reduce.ARGMAX, Reduce.ARGMIN) else DType.F32)
+    check_close(got, ref, x, dt, -1, op, DType.I64 if op in (Reduce.ARGMAX, Reduce.ARGMIN) else DType.F32)
+
+
+def test_row_split_full_reduction_and_ties():
+    n = 1 << 22
+    x = gen((1, n), DType.F32, Dist.UNIFORM, -1, 1, 22)
+    x[0, [123457, 2000001, 4000000]] = 7.0  # equal maxima in different chunks -> the first wins
+    got, ref = run_both(Reduce.ARGMAX, x, DType.F32, -1, keep=False)
+    assert got[0] == 123457 and ref[0] == 123457
+    got, ref = run_both(Reduce.SUM, x, DType.F32, -1, keep=False, out_dt=DType.F32)
+    check_close(got, ref, x, DType.F32, -1, Reduce.SUM, DType.F32)
+
+
+@pytest.mark.parametrize("op", [Reduce.SUM, Reduce.MAX, Reduce.ARGMAX, Reduce.MEAN])
+def test_col_split_long_axis(op):
+    x = gen((2, 100000, 64), DType.F32, Dist.NORMAL, 0.0, 1.0, 23)
+    out_dt = DType.I64 if op == Reduce.ARGMAX else DType.F32
+    got, ref = run_both(op, x, DType.F32, 1, keep=op != Reduce.ARGMAX, out_dt=out_dt)
+    check_close(got, ref, x, DType.F32, 1, op, out_dt)
+
+
+def test_split_results_are_deterministic():
+    import torch
+    x = empty_dev((2, 1 << 21), DType.F32)
+    tb.fill(x, Dist.NORMAL, 0, 1, 0, 24)
+    a = empty_dev((2,), DType.F32)
+    b = empty_dev((2,), DType.F32)
+    tb.reduce(Reduce.SUM, x, -1, a)
+    tb.reduce(Reduce.SUM, x, -1, b)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
