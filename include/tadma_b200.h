@@ -188,6 +188,28 @@ enum tadma_reduce_op {
 int tadma_b200_reduce(int32_t op, const tadma_tensor* in, int32_t axis, int32_t pre_op,
                       const tadma_tensor* out, void* stream);
 
+/*
+ * tadma_b200_reduce without any device allocation.  No counterpart in the
+ * reference.  For callers that cannot call cudaMalloc: a process whose memory
+ * pool has already claimed the device's HBM (so any further allocation
+ * fails), a latency-critical path that must not enter the allocator, or a
+ * host that only lends the library the buffers it passes in.
+ * Same arguments, results and errors as tadma_b200_reduce.  Reductions that
+ * split a long axis across CTAs keep their partial results in a 2 MiB static
+ * device buffer inside the library (every GPU that loads the library holds it
+ * until the process exits) instead of a per-call workspace; a reduction that
+ * would need more than 2 MiB of partials returns TADMA_ERR_INVALID with a
+ * message naming the size (tadma_b200_reduce handles it).
+ * - The first call on a device looks up the buffer's device address
+ *   (cudaGetSymbolAddress) and caches it; make that first call outside any
+ *   stream capture.
+ * - Every call shares the one buffer and overwrites what the previous call
+ *   left there (nothing in it needs to start at zero); calls whose executions
+ *   overlap on the GPU (different streams, no ordering) race on it.
+ */
+int tadma_b200_reduce_noalloc(int32_t op, const tadma_tensor* in, int32_t axis, int32_t pre_op,
+                              const tadma_tensor* out, void* stream);
+
 /* ---------------------------------------------- fused reduce + broadcast -- */
 /*
  * Softmax along `axis`: out = exp(x - max) / sum(exp(x - max)), one read and

@@ -25,7 +25,7 @@ _lib = None
 EXPORTS = (
     "tadma_b200_eltwise", "tadma_b200_reduce", "tadma_b200_softmax", "tadma_b200_layer_norm",
     "tadma_b200_rms_norm", "tadma_b200_gather", "tadma_b200_fill", "tadma_b200_last_error",
-    "tadma_b200_version", "tadma_b200_error_flags", "tadma_b200_dtype_size",
+    "tadma_b200_version", "tadma_b200_error_flags", "tadma_b200_dtype_size", "tadma_b200_reduce_noalloc",
 )
 
 
@@ -50,6 +50,7 @@ def lib() -> ctypes.CDLL:
     c_int, c_void, c_double = ctypes.c_int32, ctypes.c_void_p, ctypes.c_double
     L.tadma_b200_eltwise.argtypes = [P(T), P(T), c_int, P(I), c_int, c_int, c_void]
     L.tadma_b200_reduce.argtypes = [c_int, P(T), c_int, c_int, P(T), c_void]
+    L.tadma_b200_reduce_noalloc.argtypes = [c_int, P(T), c_int, c_int, P(T), c_void]
     L.tadma_b200_softmax.argtypes = [P(T), c_int, P(T), c_void]
     L.tadma_b200_layer_norm.argtypes = [P(T), c_int, P(T), P(T), c_double, c_int, P(T), c_void]
     L.tadma_b200_rms_norm.argtypes = [P(T), c_int, c_double, P(T), c_void]

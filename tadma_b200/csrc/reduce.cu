@@ -579,12 +579,24 @@ int dispatch_fast(int dt, int kind, int path, const RedParams& p, bool vec, cuda
 // Runs a fast path; a split plan gets a stream-ordered workspace for its
 // partials (cudaMallocAsync / cudaFreeAsync on the call's stream, so calls on
 // different streams never share it).
-// Runs a fast path; a split plan gets a stream-ordered workspace for its
-// partials (cudaMallocAsync / cudaFreeAsync on the call's stream, so calls on
-// different streams never share it).
-int run_fast(int dt, int kind, int path, RedParams& p, bool vec, cudaStream_t s) {
+// A fixed scratch buffer given by the no-allocation entry point (null for
+// tadma_b200_reduce, which allocates its workspace per call).
+struct FixedScratch {
+    void* ptr = nullptr;
+    int64_t bytes = 0;
+};
+
+int run_fast(int dt, int kind, int path, RedParams& p, bool vec, cudaStream_t s, const FixedScratch& fixed) {
     const int64_t ws = split_workspace_bytes(p, path);
     if (ws == 0) return dispatch_fast(dt, kind, path, p, vec, s);
+    if (fixed.ptr) {
+        if (ws > fixed.bytes)
+            return fail(TADMA_ERR_INVALID, "tadma_b200_reduce_noalloc: this reduction needs " + std::to_string(ws) +
+                                               " bytes of scratch, more than the " + std::to_string(fixed.bytes) +
+                                               "-byte static scratch; use tadma_b200_reduce");
+        p.partials = fixed.ptr;
+        return dispatch_fast(dt, kind, path, p, vec, s);
+    }
     void* buf = nullptr;
     cudaError_t e = cudaMallocAsync(&buf, (size_t)ws, s);
     if (e != cudaSuccess) return cuda_fail(e, "tadma_b200_reduce workspace");
@@ -595,13 +607,11 @@ int run_fast(int dt, int kind, int path, RedParams& p, bool vec, cudaStream_t s)
     return rc;
 }
 
-}  // namespace
-}  // namespace tadma_b200
+int reduce_impl(int32_t op, const tadma_tensor* in, int32_t axis, int32_t pre_op, const tadma_tensor* out,
+                void* stream, const FixedScratch& fixed);
 
-using namespace tadma_b200;
-
-extern "C" int tadma_b200_reduce(int32_t op, const tadma_tensor* in, int32_t axis, int32_t pre_op,
-                                 const tadma_tensor* out, void* stream) {
+int reduce_impl(int32_t op, const tadma_tensor* in, int32_t axis, int32_t pre_op, const tadma_tensor* out,
+                void* stream, const FixedScratch& fixed) {
     std::string err = check_tensor(in, "in");
     if (err.empty()) err = check_tensor(out, "out");
     if (!err.empty()) return fail(TADMA_ERR_INVALID, err);
@@ -676,7 +686,7 @@ extern "C" int tadma_b200_reduce(int32_t op, const tadma_tensor* in, int32_t axi
         const int N = 16 / es;
         bool vec = in_aligned && R >= N && (p.nrows == 1 || (p.in_row_stride * es) % 16 == 0);
         plan_row_split(p, R, sm_count());
-        return run_fast(dt, kind, 0, p, vec, s);
+        return run_fast(dt, kind, 0, p, vec, s, fixed);
     }
     if (fast_dt && R > 1 && p.r_stride != 1 && f.rank <= 2 && f.strides[0][last] == 1 && f.strides[1][last] == 1 &&
         f.dims[last] > 1) {
@@ -688,7 +698,7 @@ extern "C" int tadma_b200_reduce(int32_t op, const tadma_tensor* in, int32_t axi
         const int N = 16 / es;
         bool vec = in_aligned && p.inner % N == 0 && (p.r_stride * es) % 16 == 0 && (p.in_row_stride * es) % 16 == 0;
         plan_col_split(p, R, vec ? 32 * N : 32, sm_count());
-        return run_fast(dt, kind, 1, p, vec, s);
+        return run_fast(dt, kind, 1, p, vec, s, fixed);
     }
     // GENERIC
     p.krank = f.rank;
@@ -703,4 +713,57 @@ extern "C" int tadma_b200_reduce(int32_t op, const tadma_tensor* in, int32_t axi
     const bool int_acc = !dtype_is_float(dt) && pre_op == TADMA_OP_COPY && op != TADMA_REDUCE_RMS;
     if (int_acc) return launch_generic<int64_t>(kind, p, s);
     return launch_generic<double>(kind, p, s);
+}
+
+}  // namespace
+}  // namespace tadma_b200
+
+using namespace tadma_b200;
+
+extern "C" int tadma_b200_reduce(int32_t op, const tadma_tensor* in, int32_t axis, int32_t pre_op,
+                                 const tadma_tensor* out, void* stream) {
+    return reduce_impl(op, in, axis, pre_op, out, stream, FixedScratch{});
+}
+
+// ------------------------------------------------- no-allocation variant --
+//
+// Some callers cannot call cudaMalloc: a serving process whose memory pool
+// has claimed the device's HBM up front (any further allocation fails), a
+// real-time path that forbids the latency of an allocator call, or a host
+// that only lends this library the buffers it passes in.
+// tadma_b200_reduce_noalloc serves them: the partials of split reductions
+// live in this file-scope device array (every GPU that loads the library
+// holds it until the process exits) instead of a per-call workspace.
+
+constexpr int64_t NOALLOC_SCRATCH_BYTES = 2 << 20;  // 2 MiB
+static __device__ __align__(256) unsigned char g_reduce_scratch[NOALLOC_SCRATCH_BYTES];
+
+// Device address of g_reduce_scratch on the current device.  In host code the
+// array's name is only a host-side stand-in, so the address is looked up once
+// per device (with that device current) and cached.
+static int noalloc_scratch(void** ptr) {
+    static std::mutex mu;
+    static std::vector<void*> cache;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "tadma_b200_reduce_noalloc: cudaGetDevice");
+    std::lock_guard<std::mutex> lock(mu);
+    if ((int)cache.size() <= dev) cache.resize(dev + 1, nullptr);
+    if (!cache[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_reduce_scratch);
+        if (e != cudaSuccess || !p) return cuda_fail(e, "tadma_b200_reduce_noalloc: cudaGetSymbolAddress");
+        cache[dev] = p;
+    }
+    *ptr = cache[dev];
+    return TADMA_OK;
+}
+
+extern "C" int tadma_b200_reduce_noalloc(int32_t op, const tadma_tensor* in, int32_t axis, int32_t pre_op,
+                                         const tadma_tensor* out, void* stream) {
+    FixedScratch fixed;
+    int rc = noalloc_scratch(&fixed.ptr);
+    if (rc != TADMA_OK) return rc;
+    fixed.bytes = NOALLOC_SCRATCH_BYTES;
+    return reduce_impl(op, in, axis, pre_op, out, stream, fixed);
 }
