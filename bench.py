@@ -48,6 +48,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="budget of the CPU-baseline sample")
     ap.add_argument("--e2e-steps", type=int, default=20)
+    ap.add_argument("--no-ref-gpu", action="store_true",
+                    help="skip timing the reference's GPU algorithm (baseline/refalgo) beside ours")
     ap.add_argument("--batch", type=int, default=0,
                     help="leading-axis size per GPU (0 = the BASELINE size); smaller values give the small cases "
                          "used for ncu captures")
@@ -389,6 +391,90 @@ class Config5:
 
 CONFIGS = {2: Config2, 3: Config3, 4: Config4, 5: Config5}
 
+# ------------------------------------------------- reference GPU algorithm --
+
+REFALGO = os.path.join(ROOT, "baseline", "refalgo", "librefalgo.so")
+
+
+def time_steps(fn, steps, warmup, stream):
+    import torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    for _ in range(steps):
+        fn()
+    e.record(stream)
+    e.synchronize()
+    return s.elapsed_time(e) / 1e3 / steps
+
+
+def ref_gpu(cfg, args, stream):
+    """TADMA's own GPU kernels restated with their launch geometry
+    (baseline/refalgo/refalgo.cu) on the same device inputs, timed like ours
+    and reported against the same algorithmic bytes.  Returns the object for
+    the JSON line, or an `unavailable` note."""
+    import ctypes
+    import torch
+    if not os.path.exists(REFALGO):
+        return {"unavailable": "baseline/refalgo/librefalgo.so not built"}
+    L = ctypes.CDLL(REFALGO)
+    st = ctypes.c_void_p(stream.cuda_stream)
+    P = lambda t: ctypes.c_void_p(t.data_ptr())
+    steps = max(3, min(args.steps, 20))
+    if isinstance(cfg, Config2):
+        if cfg.ROWS != 8192:
+            return {"unavailable": "restated for the full [8192, 8192] workload only"}
+        t1 = torch.empty((8192, 8192), dtype=torch.float32, device="cuda")
+        t2 = torch.empty_like(t1)
+        sec = time_steps(lambda: L.ref_cfg2(P(cfg.x), P(cfg.bias), P(t1), P(t2), st), steps, 2, stream)
+        nbytes, launches = cfg.bytes, 3
+        note = "x*0.5f -> +bias -> gelu<true>: 3 executor launches with fp32 intermediates (the reference's result type)"
+    elif isinstance(cfg, Config3):
+        if cfg.x.shape[0] != 32:
+            return {"unavailable": "restated for the full X[32, 4096, 4096] workload only"}
+        o1 = torch.empty((32, 4096), dtype=torch.float32, device="cuda")
+        o2, o3 = torch.empty_like(o1), torch.empty_like(o1)
+        sec = time_steps(lambda: L.ref_cfg3(P(cfg.x), P(o1), P(o2), P(o3), st), steps, 2, stream)
+        nbytes = 3 * cfg.x.numel() * 4 + 3 * o1.numel() * 4
+        launches = 3
+        note = "sum<2>, max<2>, mean<1> through ReduceKernel<1024> (the reference has no argmax); bytes of those 3 ops"
+    elif isinstance(cfg, Config4):
+        if cfg.x.shape[0] != 64:
+            return {"unavailable": "restated for the full config-4 workload only"}
+        m = torch.empty((64 * 2048,), dtype=torch.float16, device="cuda")
+        sd = torch.empty_like(m)
+        sums = torch.empty((32 * 16 * 2048,), dtype=torch.float16, device="cuda")
+        sx = cfg.s.clone()
+
+        def step():
+            L.ref_cfg4_ln(P(cfg.x), P(cfg.g), P(cfg.b), P(m), P(sd), P(cfg.y), st)
+            L.ref_cfg4_softmax(P(sx), P(sums), ctypes.c_int64(32 * 16 * 2048), st)
+        sec = time_steps(step, steps, 2, stream)
+        nbytes, launches = cfg.bytes, 6
+        note = "LN: mean reduce, sq-diff reduce, normalise node; softmax: exp node, fp16 sum reduce, divide node"
+        del sx
+    else:
+        B = 64
+        if cfg.B < B:
+            return {"unavailable": "restated at batch 64; this run has fewer batch rows"}
+        ids = cfg.ids[:B].contiguous()
+        g = torch.empty((B, 4096, 4096), dtype=torch.float16, device="cuda")
+        out = torch.empty((B, 4096, 4096), dtype=torch.float32, device="cuda")
+        sec = time_steps(lambda: L.ref_cfg5_b64(P(cfg.table), P(ids), P(cfg.pos), P(g), P(out), st), steps, 2, stream)
+        n_out = B * 4096 * 4096
+        nbytes = B * 4096 * 8 + n_out * 2 + 4096 * 4096 * 2 + n_out * 2
+        launches = 2
+        note = ("gather node (256 threads, one element per thread) then + pos node, at batch 64: the reference's "
+                "32-bit index cannot address the batch-2048 output; GB/s over the batch-64 algorithmic bytes")
+        del g, out
+    torch.cuda.synchronize()
+    return {"value": round(nbytes / sec / GB, 3), "unit": "GB/s", "ms_per_step": round(sec * 1e3, 4),
+            "launches_per_step": launches, "kind": "reference algorithm, restated (baseline/refalgo/refalgo.cu)",
+            "note": note}
+
+
 
 # --------------------------------------------------------------- reference --
 
@@ -496,6 +582,9 @@ def run(args, rank, world, local):
         e2e = {"value": round(cfg.bytes * world / float(te.item()) / GB, 3), "unit": "GB/s",
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(float(te.item()) * 1e3, 4),
                "steps": e2e_steps}
+    refg = None
+    if world == 1 and not args.no_ref_gpu:
+        refg = ref_gpu(cfg, args, stream)
     barrier(world)
     if rank != 0:
         return
@@ -518,7 +607,7 @@ def run(args, rank, world, local):
                    "l2": "inputs larger than L2: every step reads > 126 MB of input not touched by the previous "
                          "step (config 2 rotates 4 x/y sets of 134 MB each); no flush; K steps timed back to back",
                    "parallelism": f"dp{world} (leading-axis shards, no data-path collective)"},
-        "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
+        "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "reference_gpu_restated": refg,
         "gpu_launches": cfg.launches * args.steps,
         "clocks": sampler.result(),
         "elements_per_s": round(cfg.units * world / step_max, 1),

@@ -397,9 +397,10 @@ __global__ void __launch_bounds__(THREADS) chain_scalar_kernel(const __grid_cons
 // with a row-broadcast b: the bias-plus-activation pattern of config 2 and of
 // every dense layer.  Each thread owns one 8-column vector for all of its rows,
 // so b is loaded and converted once and stays in registers, the row loop needs
-// no index division, and 4 rows are in flight per thread.  Same op bodies as
-// the interpreter (__fmul_rn, __fadd_rn, activation<ACT, FAST>, RN stores), so
-// the bits are identical to the generic path.
+// no index division, and the next 4 rows' loads are in flight while 4 rows
+// compute.  x * s + b and the fast GELU polynomial run as packed fp32x2
+// instructions (sm_100), every lane rounded as the scalar op would be, so the
+// bits equal the generic path's (__fmul_rn, __fadd_rn, activation<ACT, FAST>).
 
 struct AffineRowsParams {
     const char* x;
@@ -442,39 +443,108 @@ __device__ __forceinline__ void raw8_store(T* p, const float* f) {
     }
 }
 
+// Packed fp32x2 arithmetic (sm_100): two lanes per instruction, each lane
+// rounded exactly like the scalar op (__fmul_rn / __fadd_rn / fmaf).
+__device__ __forceinline__ unsigned long long f2_pack(float lo, float hi) {
+    unsigned long long r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void f2_unpack(unsigned long long v, float& lo, float& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ unsigned long long f2_mul(unsigned long long a, unsigned long long b) {
+    unsigned long long r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ unsigned long long f2_add(unsigned long long a, unsigned long long b) {
+    unsigned long long r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ unsigned long long f2_fma(unsigned long long a, unsigned long long b, unsigned long long c) {
+    unsigned long long r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+
+// gelu_fast on two lanes: the same operation sequence as gelu_fast (ops.cuh),
+// with the polynomial and the final products packed.
+__device__ __forceinline__ unsigned long long gelu_fast2(unsigned long long x) {
+    constexpr float K1 = 2.0f * 0.7978845608f * 1.4426950408889634f;
+    constexpr float K3 = K1 * 0.044715f;
+    const unsigned long long w = f2_mul(x, f2_fma(f2_pack(K3, K3), f2_mul(x, x), f2_pack(K1, K1)));
+    float w0, w1;
+    f2_unpack(w, w0, w1);
+    const float t0 = ex2_approx(-fabsf(w0)), t1 = ex2_approx(-fabsf(w1));
+    const unsigned long long t = f2_pack(t0, t1);
+    float d0, d1;
+    f2_unpack(f2_add(f2_pack(1.0f, 1.0f), t), d0, d1);
+    const unsigned long long r = f2_pack(rcp_approx(d0), rcp_approx(d1));
+    float tr0, tr1, r0, r1;
+    f2_unpack(f2_mul(t, r), tr0, tr1);
+    f2_unpack(r, r0, r1);
+    return f2_mul(x, f2_pack(w0 >= 0.0f ? r0 : tr0, w1 >= 0.0f ? r1 : tr1));
+}
+
+template <typename XT, typename OT, int ACT>
+__device__ __forceinline__ void affine_row_compute(const Raw8x<XT>& raw, const float (&b)[8],
+                                                   const unsigned long long (&b2)[4], float scale, OT* dst) {
+    constexpr bool FAST = sizeof(OT) == 2;  // same rule as the host: fp32 compute, 16-bit store
+    float v[8];
+    raw8_cvt<XT>(raw, v);
+    if constexpr (ACT == ACT_NONE || (ACT == ACT_GELU && FAST)) {
+        const unsigned long long s2 = f2_pack(scale, scale);
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            unsigned long long x = f2_add(f2_mul(f2_pack(v[2 * j], v[2 * j + 1]), s2), b2[j]);
+            if constexpr (ACT == ACT_GELU) x = gelu_fast2(x);
+            f2_unpack(x, v[2 * j], v[2 * j + 1]);
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 8; j++) v[j] = activation<ACT, FAST>(__fadd_rn(__fmul_rn(v[j], scale), b[j]));
+    }
+    raw8_store<OT>(dst, v);
+}
+
 template <typename XT, typename OT, int ACT>
 __global__ void __launch_bounds__(THREADS) affine_rows_kernel(const __grid_constant__ AffineRowsParams p) {
-    constexpr bool FAST = sizeof(OT) == 2;  // same rule as the host: fp32 compute, 16-bit store
+    // Double-buffered over rows: the next UR rows' loads are in flight while
+    // the current UR rows compute and store.
     constexpr int UR = 4;
     const int64_t cv = (int64_t)blockIdx.x * THREADS + threadIdx.x;
     if (cv >= p.ncv) return;
     float b[8];
+    unsigned long long b2[4];
     {
         Raw8x<XT> rb;
         raw8_load<XT>(reinterpret_cast<const XT*>(p.bias) + cv * 8, rb, false);
         raw8_cvt<XT>(rb, b);
+#pragma unroll
+        for (int j = 0; j < 4; j++) b2[j] = f2_pack(b[2 * j], b[2 * j + 1]);
     }
     const XT* xcol = reinterpret_cast<const XT*>(p.x) + cv * 8;
     OT* ocol = reinterpret_cast<OT*>(p.out) + cv * 8;
     const int64_t ystep = gridDim.y;
-    for (int64_t r0 = blockIdx.y; r0 < p.rows; r0 += ystep * UR) {
-        Raw8x<XT> raw[UR];
+    Raw8x<XT> cur[UR], nxt[UR];
+    int64_t r0 = blockIdx.y;
+#pragma unroll
+    for (int u = 0; u < UR; u++)
+        if (r0 + u * ystep < p.rows) raw8_load<XT>(xcol + (r0 + u * ystep) * p.x_rs, cur[u], true);
+    for (; r0 < p.rows; r0 += ystep * UR) {
+        const int64_t rn = r0 + ystep * UR;
+#pragma unroll
+        for (int u = 0; u < UR; u++)
+            if (rn + u * ystep < p.rows) raw8_load<XT>(xcol + (rn + u * ystep) * p.x_rs, nxt[u], true);
 #pragma unroll
         for (int u = 0; u < UR; u++) {
             const int64_t r = r0 + u * ystep;
-            if (r < p.rows) raw8_load<XT>(xcol + r * p.x_rs, raw[u], true);
+            if (r < p.rows) affine_row_compute<XT, OT, ACT>(cur[u], b, b2, p.scale, ocol + r * p.out_rs);
         }
 #pragma unroll
-        for (int u = 0; u < UR; u++) {
-            const int64_t r = r0 + u * ystep;
-            if (r < p.rows) {
-                float v[8];
-                raw8_cvt<XT>(raw[u], v);
-#pragma unroll
-                for (int j = 0; j < 8; j++) v[j] = activation<ACT, FAST>(__fadd_rn(__fmul_rn(v[j], p.scale), b[j]));
-                raw8_store<OT>(ocol + r * p.out_rs, v);
-            }
-        }
+        for (int u = 0; u < UR; u++) cur[u] = nxt[u];
     }
 }
 
