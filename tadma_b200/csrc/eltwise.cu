@@ -548,6 +548,68 @@ __global__ void __launch_bounds__(THREADS) affine_rows_kernel(const __grid_const
     }
 }
 
+// ---------------------------------------------------------- tiled transpose --
+//
+// One input whose unit-stride dim is not the output's: a copy through a
+// transpose (contiguous() after transpose<0,2,3,1>, a cast of a transposed
+// view).  Element-at-a-time, one side of the copy would be uncoalesced; here
+// a CTA stages a 32 x 32 tile in shared memory, reading along the input's
+// contiguous dim and writing along the output's, and runs the chain on each
+// element on the way out.  Remaining dims are batch dims (grid z).
+
+struct TransposeParams {
+    const char* in;
+    char* out;
+    int32_t in_dtype, out_dtype;
+    int64_t n_i, n_j;    // i: the input's unit-stride dim; j: the output's
+    int64_t in_sj;       // input stride along j
+    int64_t out_si;      // output stride along i
+    int32_t nb, pad;     // batch dims
+    int64_t nbatch;
+    DivMod bdm[TADMA_MAX_RANK];
+    int64_t b_in[TADMA_MAX_RANK], b_out[TADMA_MAX_RANK];
+    ChainParams chain;   // the program (n_instr, prog, scale)
+};
+
+template <int PROG>
+__global__ void __launch_bounds__(THREADS) transpose_chain_kernel(const __grid_constant__ TransposeParams tp) {
+    __shared__ float tile[32][33];
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8 threads
+    const int64_t i0 = (int64_t)blockIdx.y * 32, j0 = (int64_t)blockIdx.x * 32;
+    for (int64_t bz = blockIdx.z; bz < tp.nbatch; bz += gridDim.z) {
+        uint64_t e = (uint64_t)bz;
+        int64_t ib = 0, ob = 0;
+        for (int d = tp.nb - 1; d >= 1; d--) {
+            uint64_t q, r;
+            tp.bdm[d].divmod(e, q, r);
+            ib += (int64_t)r * tp.b_in[d];
+            ob += (int64_t)r * tp.b_out[d];
+            e = q;
+        }
+        if (tp.nb > 0) {
+            ib += (int64_t)e * tp.b_in[0];
+            ob += (int64_t)e * tp.b_out[0];
+        }
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const int64_t i = i0 + tx, j = j0 + ty + 8 * k;
+            if (i < tp.n_i && j < tp.n_j) tile[ty + 8 * k][tx] = load_as<float>(tp.in, tp.in_dtype, ib + i + j * tp.in_sj);
+        }
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const int64_t i = i0 + ty + 8 * k, j = j0 + tx;
+            if (i < tp.n_i && j < tp.n_j) {
+                float val[1][1] = {{tile[tx][ty + 8 * k]}};
+                float acc[1] = {val[0][0]};
+                program<float, 1, 1, PROG>(tp.chain, acc, val);
+                store_from(tp.out, tp.out_dtype, ob + i * tp.out_si + j, acc[0]);
+            }
+        }
+        __syncthreads();
+    }
+}
+
 // ------------------------------------------------------------ host side --
 
 int blocks_per_sm(const void* fn) {
@@ -691,6 +753,16 @@ int launch_rows(int xdt, int odt, int act, const AffineRowsParams& p, cudaStream
                              : launch_rows_act<__nv_bfloat16, float>(act, p, s);
 }
 
+int launch_transpose(bool fast, const TransposeParams& tp, cudaStream_t s) {
+    const int64_t gx = (tp.n_j + 31) / 32, gy = (tp.n_i + 31) / 32;
+    const int64_t gz = tp.nbatch < 65535 ? tp.nbatch : 65535;
+    dim3 grid((unsigned)gx, (unsigned)gy, (unsigned)(gz > 0 ? gz : 1));
+    if (fast) transpose_chain_kernel<PROG_INTERP_FAST><<<grid, THREADS, 0, s>>>(tp);
+    else transpose_chain_kernel<PROG_INTERP><<<grid, THREADS, 0, s>>>(tp);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? TADMA_OK : cuda_fail(e, "tadma_b200_eltwise launch");
+}
+
 bool is_transcendental(int op) { return op >= TADMA_OP_EXP && op <= TADMA_OP_GELU && op != TADMA_OP_RELU; }
 
 bool valid_op(int op) {
@@ -829,6 +901,35 @@ extern "C" int tadma_b200_eltwise(const tadma_tensor* out, const tadma_tensor* i
         }
     };
     if (!vec) {
+        // A single input whose contiguous dim differs from the output's: tiled transpose.
+        int dt_in = -1;
+        if (n_ins == 1 && cm == TADMA_COMPUTE_F32 && f.rank >= 2 && f.strides[0][last] == 1 &&
+            f.strides[1][last] != 1 && f.strides[1][last] != 0 && ins[0].data != out->data) {
+            for (int d = 0; d < last; d++)
+                if (f.strides[1][d] == 1) dt_in = d;
+        }
+        if (dt_in >= 0 && (f.dims[dt_in] + 31) / 32 <= 65535 && (f.dims[last] + 31) / 32 <= 0x7fffffff) {
+            TransposeParams tp{};
+            tp.in = (const char*)ins[0].data;
+            tp.out = (char*)out->data;
+            tp.in_dtype = ins[0].dtype;
+            tp.out_dtype = out->dtype;
+            tp.n_i = f.dims[dt_in];
+            tp.n_j = f.dims[last];
+            tp.in_sj = f.strides[1][last];
+            tp.out_si = f.strides[0][dt_in];
+            tp.nbatch = 1;
+            for (int d = 0; d < last; d++) {
+                if (d == dt_in) continue;
+                tp.bdm[tp.nb] = DivMod((uint64_t)f.dims[d]);
+                tp.b_in[tp.nb] = f.strides[1][d];
+                tp.b_out[tp.nb] = f.strides[0][d];
+                tp.nbatch *= f.dims[d];
+                tp.nb++;
+            }
+            tp.chain = p;
+            return launch_transpose(fast, tp, s);
+        }
         p.start = 0;
         p.n = n;
         return go(p, false, n);

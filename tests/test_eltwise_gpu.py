@@ -214,3 +214,37 @@ def test_invalid_arguments_raise():
         tb.eltwise(out, [out], [instr(Op.ADD, b=3)])
     with pytest.raises(tb.TadmaError):
         tb.eltwise(out, [out], [instr(99)])
+
+
+# ---- copies through a transpose (tiled shared-memory path) -------------------
+
+@pytest.mark.parametrize("shape,perm", [((70, 45), (1, 0)), ((3, 33, 100), (0, 2, 1)), ((2, 5, 37, 64), (0, 2, 3, 1)),
+                                        ((4, 8, 96, 64), (0, 1, 3, 2))])
+@pytest.mark.parametrize("dt,out_dt", [(DType.F32, DType.F32), (DType.BF16, DType.BF16), (DType.F16, DType.F32)])
+def test_transpose_copy_and_cast(shape, perm, dt, out_dt):
+    import torch
+    x = gen(shape, dt, Dist.NORMAL, 0.0, 1.0, 30)
+    xd = to_dev(x, dt)
+    out_shape = [shape[p] for p in perm]
+    strides = [xd.stride()[p] for p in perm]
+    view = make_tensor(xd.data_ptr(), dt, out_shape, strides)  # x.permute(perm) as a strided view
+    out = empty_dev(out_shape, out_dt)
+    tb.eltwise(out, [view], [instr(Op.COPY)])
+    torch.cuda.synchronize()
+    ref = np.zeros(out_shape, dtype=from_dev(out).dtype)
+    assert O.eltwise(ref, [np.transpose(x, perm)], [instr(Op.COPY)], out_dtype=out_dt, in_dtypes=[dt]) == 0
+    assert np.array_equal(from_dev(out).view(np.uint8), ref.view(np.uint8))
+
+
+def test_transpose_with_chain():
+    import torch
+    x = gen((6, 130, 66), DType.F32, Dist.NORMAL, 0.0, 1.0, 31)
+    xd = to_dev(x)
+    view = make_tensor(xd.data_ptr(), DType.F32, [6, 66, 130], [130 * 66, 1, 66])
+    out = empty_dev((6, 66, 130), DType.BF16)
+    prog = [instr(Op.MUL, b=SRC_IMM, imm=1.5), instr(Op.GELU)]
+    tb.eltwise(out, [view], prog, Compute.F32)
+    torch.cuda.synchronize()
+    ref = np.zeros((6, 66, 130), np.uint16)
+    assert O.eltwise(ref, [np.transpose(x, (0, 2, 1))], prog, Compute.F32, out_dtype=DType.BF16, in_dtypes=[DType.F32]) == 0
+    assert ulp_diff(from_dev(out), ref, DType.BF16).max() <= 1
