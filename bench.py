@@ -66,9 +66,20 @@ def measured_peak():
         return 6650.0, "fallback"
 
 
-# Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of the
-# dominant kernel from one ncu capture of the same command (see profiles/).
-NCU_TRAFFIC = {}
+# Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) per
+# (config, part label) from `ncu --set full` captures of this script, scaled
+# from the captured batch to the full workload by rows processed; the
+# summaries and commands are under profiles/.  Writes still dirty in L2 when a
+# launch ends are not in its figure (they reach DRAM during the next launch).
+NCU_TRAFFIC = {
+    (2, "act(x*s + b) rows"): {"bytes": 218389504, "captured": "full size"},
+    (3, "sum axis -1"): {"bytes": 8 * 272808960, "captured": "batch 4, x8"},
+    (3, "argmax axis -1"): {"bytes": 8 * 274656512, "captured": "batch 4, x8"},
+    (3, "mean axis 1 (+ finish kernel when split)"): {"bytes": 8 * 273631232, "captured": "batch 4, x8"},
+    (4, "LayerNorm (ONNX) rows of 1024"): {"bytes": 2 * 220624000, "captured": "batch 32, x2"},
+    (4, "softmax rows of 2048"): {"bytes": 2 * 4246966000, "captured": "batch 16, x2"},
+    (5, "gather + pos add"): {"bytes": 32 * 4479926000, "captured": "batch 64, x32"},
+}
 
 
 # ----------------------------------------------------------------- clocks --
@@ -138,7 +149,7 @@ class Config2:
     """y = gelu(x * 0.5 + bias), x[8192, 8192] bf16, bias[8192] bf16, y bf16."""
     ROWS, COLS = 8192, 8192
     dtype = "bf16"
-    kernel = "chain_vec_kernel"
+    kernel = "affine_rows_kernel"
 
     def __init__(self, rank, batch=0):
         self.ROWS = batch or Config2.ROWS
@@ -178,23 +189,38 @@ class Config2:
         self.calls[self.i % NBUF]()
         self.i += 1
 
+    def parts(self):
+        return [("affine_rows_kernel", "act(x*s + b) rows", self.bytes, self.step)]
+
     def e2e(self, steps, stream):
-        """Same op through the public C-ABI call, inputs from pinned host memory
-        and the result back to pinned host memory inside the timed region."""
+        """Same op through the public API with host buffers: every step uploads
+        x and bias from pinned host memory and downloads y, inside the timed
+        region; tadma_b200.pipeline.RowPipeline overlaps the upload, the
+        per-chunk C-ABI calls and the download across 8 row chunks."""
         import torch
+        import tadma_b200 as tb
+        from tadma_b200.abi import Compute, DType, make_tensor
+        from tadma_b200.pipeline import RowPipeline
         xh = torch.empty_like(self.x, device="cpu").pin_memory()
         bh = torch.empty_like(self.bias, device="cpu").pin_memory()
         yh = torch.empty_like(self.y, device="cpu").pin_memory()
         xh.copy_(self.x)
         bh.copy_(self.bias)
+        C = self.COLS
+
+        def make_call(lo, hi, st):
+            bv = make_tensor(self.bias.data_ptr(), DType.BF16, [hi - lo, C], [0, 1])
+            return tb.prepare_eltwise(self.y[lo:hi], [self.x[lo:hi], bv], self.prog, Compute.F32, stream=st)
+
+        pipe = RowPipeline(self.ROWS, 8, uploads=[(xh, self.x)], downloads=[(self.y, yh)], make_call=make_call,
+                           once=[(bh, self.bias)])
+        pipe(stream)
+        stream.synchronize()
         times = []
         for _ in range(steps):
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             s.record(stream)
-            self.x.copy_(xh, non_blocking=True)
-            self.bias.copy_(bh, non_blocking=True)
-            self.calls[0]()
-            yh.copy_(self.y, non_blocking=True)
+            pipe(stream)
             e.record(stream)
             e.synchronize()
             times.append(s.elapsed_time(e) / 1e3)
@@ -270,6 +296,14 @@ class Config3:
         for c in self.calls:
             c()
 
+    def parts(self):
+        B, R, C = self.x.shape
+        xin = self.x.numel() * 4
+        return [("reduce_row_kernel", "sum axis -1", xin + B * R * 4, self.calls[0]),
+                ("reduce_row_kernel", "max axis -1", xin + B * R * 4, self.calls[1]),
+                ("reduce_row_kernel", "argmax axis -1", xin + B * R * 8, self.calls[2]),
+                ("reduce_col_kernel", "mean axis 1 (+ finish kernel when split)", xin + B * C * 4, self.calls[3])]
+
     def cpu_sample(self, budget_s):
         import numpy as np
         from oracle import oracle as O
@@ -321,6 +355,11 @@ class Config4:
         for c in self.calls:
             c()
 
+    def parts(self):
+        return [("rownorm_warp_kernel", "LayerNorm (ONNX) rows of 1024", 2 * self.x.numel() * 2 + 2 * 1024 * 2,
+                 self.calls[0]),
+                ("rownorm_warp_kernel", "softmax rows of 2048", 2 * self.s.numel() * 2, self.calls[1])]
+
     def cpu_sample(self, budget_s):
         import numpy as np
         from oracle import oracle as O
@@ -370,6 +409,9 @@ class Config5:
 
     def step(self):
         self.call()
+
+    def parts(self):
+        return [("gather_rows_kernel", "gather + pos add", self.bytes, self.call)]
 
     def cpu_sample(self, budget_s):
         import numpy as np
@@ -547,6 +589,41 @@ def barrier(world):
     torch.cuda.synchronize()
 
 
+def time_parts(cfg, args, stream):
+    """Each launch of the step timed on its own: n back-to-back launches of
+    that call on the launching stream between CUDA events (inputs larger than
+    L2, so no launch finds its input cached).  Returns [(kernel, label, bytes,
+    seconds per launch)]."""
+    n = max(3, min(args.steps, 20))
+    out = []
+    for kernel, label, nbytes, fn in cfg.parts():
+        out.append((kernel, label, nbytes, time_steps(fn, n, 2, stream)))
+    return out
+
+
+def roofline(cfg, args, parts, peak, peak_kind, step_s):
+    """Roofline of the dominant launch (the part with the largest time per
+    step): achieved = its algorithmic bytes / its average launch duration."""
+    rows = []
+    for kernel, label, nbytes, sec in parts:
+        tr = NCU_TRAFFIC.get((args.config, label))
+        rows.append({"kernel": kernel, "part": label, "ms": round(sec * 1e3, 4),
+                     "achieved": round(nbytes / sec / GB, 1), "frac": round(nbytes / sec / GB / peak, 4),
+                     "algorithmic_bytes": nbytes, "traffic": tr["bytes"] if tr else None,
+                     "share": round(sec / sum(p[3] for p in parts), 4)})
+    top = max(rows, key=lambda r: r["ms"])
+    tr = NCU_TRAFFIC.get((args.config, top["part"]))
+    return {"bound": "hbm", "achieved": top["achieved"], "peak": peak, "unit": "GB/s", "frac": top["frac"],
+            "traffic": top["traffic"], "kernel": top["kernel"], "part": top["part"],
+            "algorithmic_bytes_per_launch": top["algorithmic_bytes"],
+            "traffic_note": (f"ncu dram__bytes_read.sum + dram__bytes_write.sum per launch, captured at "
+                             f"{tr['captured']}" if tr else "no capture for this part"),
+            "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs, burst copy)",
+            "step": {"achieved": round(cfg.bytes / step_s / GB, 1), "frac": round(cfg.bytes / step_s / GB / peak, 4),
+                     "algorithmic_bytes_per_step": cfg.bytes},
+            "parts": rows}
+
+
 def run(args, rank, world, local):
     import torch
     import torch.distributed as dist
@@ -585,15 +662,12 @@ def run(args, rank, world, local):
     refg = None
     if world == 1 and not args.no_ref_gpu:
         refg = ref_gpu(cfg, args, stream)
+    parts = time_parts(cfg, args, stream) if rank == 0 else None
     barrier(world)
     if rank != 0:
         return
     peak, peak_kind = measured_peak()
-    achieved = cfg.bytes / step_s / GB
-    roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-            "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs, burst copy)",
-            "kernel": cfg.kernel, "algorithmic_bytes_per_step": cfg.bytes,
-            "traffic": NCU_TRAFFIC.get(args.config)}
+    roof = roofline(cfg, args, parts, peak, peak_kind, step_s)
     cpu = None
     if world == 1 and args.cpu_seconds > 0:
         v, cores, sample = cfg.cpu_sample(args.cpu_seconds)

@@ -297,6 +297,19 @@ __device__ __forceinline__ T warp_max(T v) {
     return v;
 }
 
+// max / min that return NaN when either input is NaN (PTX max.NaN / min.NaN,
+// one ALU op): the "NaN sticks once seen" rule of the max/min reductions.
+__device__ __forceinline__ float fmax_nan(float a, float b) {
+    float r;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ float fmin_nan(float a, float b) {
+    float r;
+    asm("min.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+    return r;
+}
+
 // ------------------------------------------------------------- host side --
 
 // Per-thread last error message (tadma_b200_last_error).

@@ -470,22 +470,17 @@ __device__ __forceinline__ unsigned long long f2_fma(unsigned long long a, unsig
 }
 
 // gelu_fast on two lanes: the same operation sequence as gelu_fast (ops.cuh),
-// with the polynomial and the final products packed.
+// gelu(x) = x / (1 + 2^(-w)), w = x (K1 + K3 x^2), with the polynomial, the
+// sum and the final product packed (the sign of w folded into K1, K3).
 __device__ __forceinline__ unsigned long long gelu_fast2(unsigned long long x) {
     constexpr float K1 = 2.0f * 0.7978845608f * 1.4426950408889634f;
     constexpr float K3 = K1 * 0.044715f;
-    const unsigned long long w = f2_mul(x, f2_fma(f2_pack(K3, K3), f2_mul(x, x), f2_pack(K1, K1)));
-    float w0, w1;
-    f2_unpack(w, w0, w1);
-    const float t0 = ex2_approx(-fabsf(w0)), t1 = ex2_approx(-fabsf(w1));
-    const unsigned long long t = f2_pack(t0, t1);
+    const unsigned long long nw = f2_mul(x, f2_fma(f2_pack(-K3, -K3), f2_mul(x, x), f2_pack(-K1, -K1)));
+    float a, b;
+    f2_unpack(nw, a, b);
     float d0, d1;
-    f2_unpack(f2_add(f2_pack(1.0f, 1.0f), t), d0, d1);
-    const unsigned long long r = f2_pack(rcp_approx(d0), rcp_approx(d1));
-    float tr0, tr1, r0, r1;
-    f2_unpack(f2_mul(t, r), tr0, tr1);
-    f2_unpack(r, r0, r1);
-    return f2_mul(x, f2_pack(w0 >= 0.0f ? r0 : tr0, w1 >= 0.0f ? r1 : tr1));
+    f2_unpack(f2_add(f2_pack(ex2_approx(a), ex2_approx(b)), f2_pack(1.0f, 1.0f)), d0, d1);
+    return f2_mul(x, f2_pack(rcp_approx(d0), rcp_approx(d1)));
 }
 
 template <typename XT, typename OT, int ACT>
@@ -510,7 +505,7 @@ __device__ __forceinline__ void affine_row_compute(const Raw8x<XT>& raw, const f
 }
 
 template <typename XT, typename OT, int ACT>
-__global__ void __launch_bounds__(THREADS) affine_rows_kernel(const __grid_constant__ AffineRowsParams p) {
+__global__ void __launch_bounds__(THREADS, sizeof(XT) == 2 ? 3 : 2) affine_rows_kernel(const __grid_constant__ AffineRowsParams p) {
     // Double-buffered over rows: the next UR rows' loads are in flight while
     // the current UR rows compute and store.
     constexpr int UR = 4;

@@ -10,7 +10,7 @@
 // separate CombineToNode pass over the whole output (Kernels.hpp:33-45).
 //
 // Fast path (axis 0, table rows contiguous): one warp per output row; the id
-// is read once per row (one broadcast load), the row is copied in 8-element
+// is read once per row (one broadcast load, a row ahead), the row is copied in 8-element
 // chunks (16 B of fp16/bf16, 32 B of fp32) with 4 raw chunks in flight per lane,
 // the add operand's row (e.g. pos[s]) is fetched with an L2 evict_last policy
 // so it stays resident across the batch while the gathered rows (evict_first
@@ -27,7 +27,8 @@
 
 namespace tadma_b200 {
 
-// Per-device error word (bit 1 << TADMA_ERR_INDEX = an id was out of range).
+// Per-device error word of the gather kernels (bit 1 << TADMA_ERR_INDEX = an
+// id was out of range).
 static __device__ unsigned int g_error_word;
 
 namespace {
@@ -105,8 +106,12 @@ __global__ void __launch_bounds__(THREADS) gather_rows_kernel(const __grid_const
     // batch row re-reads) is kept resident.
     const uint64_t pol_stream = l2_policy_evict_first();
     const uint64_t pol_keep = l2_policy_evict_last();
+    // The id of the warp's next row is loaded while this row streams, so no
+    // dependent id load sits in front of a row's table loads.
+    int64_t id_next = gw < p.nrows ? load_id(p.ids, p.i_dtype, gw * p.ids_stride) : 0;
     for (int64_t row = gw; row < p.nrows; row += nw) {
-        int64_t id = load_id(p.ids, p.i_dtype, row * p.ids_stride);
+        int64_t id = id_next;
+        if (row + nw < p.nrows) id_next = load_id(p.ids, p.i_dtype, (row + nw) * p.ids_stride);
         if (id < 0) id += p.n;
         const bool ok = (uint64_t)id < (uint64_t)p.n;
         if (!ok && lane == 0) atomicOr(&g_error_word, 1u << TADMA_ERR_INDEX);
@@ -329,6 +334,7 @@ extern "C" int tadma_b200_gather(const tadma_tensor* table, int32_t axis, const 
                 p.idm[d] = DivMod((uint64_t)ids->dims[d]);
                 p.a_row[d] = astr[d];
             }
+
             switch (table->dtype) {
             case TADMA_F32: return launch_add<float>(p, has_add, s);
             case TADMA_F16: return launch_add<__half>(p, has_add, s);

@@ -22,6 +22,7 @@
 #include "layout.hpp"
 
 namespace tadma_b200 {
+
 namespace {
 
 enum Mode { M_SOFTMAX = 0, M_LN_ONNX = 1, M_LN_TADMA = 2, M_RMS = 3 };
@@ -96,20 +97,113 @@ __device__ __forceinline__ float fast_exp(float x) {
     else return __expf(x);
 }
 
-// ----------------------------------------------------------- warp kernel --
+// ----------------------------------------------------------- warp kernels --
 
-// Rows of <= 4 chunks per lane are latency-bound: cap registers so 3 CTAs
-// (24 warps) fit per SM; 8-chunk rows keep their registers (2 CTAs per SM).
+// Statistics, normalisation and store of one row held in a warp's registers
+// (lane l holds chunks c * 32 + l, N elements each; chunks past L hold the
+// neutral value of the mode).
 template <typename T, int CH, int MODE>
-__global__ void __launch_bounds__(THREADS, (CH <= 4 ? 3 : 2)) rownorm_warp_kernel(const __grid_constant__ NormParams p) {
+__device__ __forceinline__ void rownorm_finish(float (&v)[CH][VecT<T>::N], const NormParams& p, int lane, T* y) {
+    constexpr int N = VecT<T>::N;
+    const float fL = (float)p.L;
+    if constexpr (MODE == M_SOFTMAX) {
+        float m = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < CH; c++)
+#pragma unroll
+            for (int j = 0; j < N; j++) m = fmaxf(m, v[c][j]);
+        m = warp_max(m);
+        float s = 0.0f;
+#pragma unroll
+        for (int c = 0; c < CH; c++)
+#pragma unroll
+            for (int j = 0; j < N; j++) {
+                v[c][j] = fast_exp<T>(v[c][j] - m);
+                s += v[c][j];
+            }
+        s = warp_sum(s);
+        const float inv = 1.0f / s;
+#pragma unroll
+        for (int c = 0; c < CH; c++)
+#pragma unroll
+            for (int j = 0; j < N; j++) v[c][j] *= inv;
+    } else if constexpr (MODE == M_RMS) {
+        float ss = 0.0f;
+#pragma unroll
+        for (int c = 0; c < CH; c++)
+#pragma unroll
+            for (int j = 0; j < N; j++) ss += v[c][j] * v[c][j];
+        ss = warp_sum(ss);
+        const float r = 1.0f / sqrtf(ss / fL + p.eps);
+#pragma unroll
+        for (int c = 0; c < CH; c++)
+#pragma unroll
+            for (int j = 0; j < N; j++) v[c][j] *= r;
+    } else {
+        float sum = 0.0f;
+#pragma unroll
+        for (int c = 0; c < CH; c++)
+#pragma unroll
+            for (int j = 0; j < N; j++) sum += v[c][j];
+        const float mean = warp_sum(sum) / fL;
+        float sq = 0.0f;
+#pragma unroll
+        for (int c = 0; c < CH; c++) {
+            const int64_t col = ((int64_t)c * 32 + lane) * N;
+            if (col < p.L) {
+#pragma unroll
+                for (int j = 0; j < N; j++) {
+                    const float d = v[c][j] - mean;
+                    sq += d * d;
+                }
+            }
+        }
+        const float var = warp_sum(sq) / fL;
+        const float rstd = (MODE == M_LN_ONNX) ? 1.0f / sqrtf(var + p.eps) : 1.0f / (sqrtf(var) + p.eps);
+#pragma unroll
+        for (int c = 0; c < CH; c++) {
+            const int64_t col = ((int64_t)c * 32 + lane) * N;
+            if (col < p.L) {
+                float g[N], b[N];
+                if (p.gb_vec) {
+                    // raw 16-byte loads converted at use keep few registers live
+                    if (p.gamma) cvt_in<T>(ld_nc_v4(reinterpret_cast<const T*>(p.gamma) + col), g);
+                    if (p.beta) cvt_in<T>(ld_nc_v4(reinterpret_cast<const T*>(p.beta) + col), b);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < N; j++) {
+                        if (p.gamma) g[j] = load_as<float>(p.gamma, p.g_dtype, (col + j) * p.g_stride);
+                        if (p.beta) b[j] = load_as<float>(p.beta, p.b_dtype, (col + j) * p.b_stride);
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < N; j++) {
+                    float t = (v[c][j] - mean) * rstd;
+                    if (p.gamma) t = t * g[j];
+                    if (p.beta) t = t + b[j];
+                    v[c][j] = t;
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int c = 0; c < CH; c++) {
+        const int64_t col = ((int64_t)c * 32 + lane) * N;
+        if (col < p.L) st_stream_v4(y + col, cvt_out<T>(v[c]));
+    }
+}
+
+// 16-bit rows of <= 4 chunks per lane are latency-bound: cap registers so 3
+// CTAs (24 warps) fit per SM; 8-chunk and fp32 rows keep their registers
+// (2 CTAs per SM).
+template <typename T, int CH, int MODE>
+__global__ void __launch_bounds__(THREADS, (CH <= 4 && sizeof(T) == 2 ? 3 : 2)) rownorm_warp_kernel(const __grid_constant__ NormParams p) {
     constexpr int N = VecT<T>::N;
     const int lane = threadIdx.x & 31;
     const int64_t gw = ((int64_t)blockIdx.x * THREADS + threadIdx.x) >> 5;
     const int64_t nw = ((int64_t)gridDim.x * THREADS) >> 5;
-    const float fL = (float)p.L;
     for (int64_t row = gw; row < p.nrows; row += nw) {
         const T* x = reinterpret_cast<const T*>(p.in) + row * p.in_row_stride;
-        T* y = reinterpret_cast<T*>(p.out) + row * p.out_row_stride;
         float v[CH][N];
 #pragma unroll
         for (int c = 0; c < CH; c++) {
@@ -121,91 +215,7 @@ __global__ void __launch_bounds__(THREADS, (CH <= 4 ? 3 : 2)) rownorm_warp_kerne
                 for (int j = 0; j < N; j++) v[c][j] = (MODE == M_SOFTMAX) ? -INFINITY : 0.0f;
             }
         }
-        if constexpr (MODE == M_SOFTMAX) {
-            float m = -INFINITY;
-#pragma unroll
-            for (int c = 0; c < CH; c++)
-#pragma unroll
-                for (int j = 0; j < N; j++) m = fmaxf(m, v[c][j]);
-            m = warp_max(m);
-            float s = 0.0f;
-#pragma unroll
-            for (int c = 0; c < CH; c++)
-#pragma unroll
-                for (int j = 0; j < N; j++) {
-                    v[c][j] = fast_exp<T>(v[c][j] - m);
-                    s += v[c][j];
-                }
-            s = warp_sum(s);
-            const float inv = 1.0f / s;
-#pragma unroll
-            for (int c = 0; c < CH; c++)
-#pragma unroll
-                for (int j = 0; j < N; j++) v[c][j] *= inv;
-        } else if constexpr (MODE == M_RMS) {
-            float ss = 0.0f;
-#pragma unroll
-            for (int c = 0; c < CH; c++)
-#pragma unroll
-                for (int j = 0; j < N; j++) ss += v[c][j] * v[c][j];
-            ss = warp_sum(ss);
-            const float r = 1.0f / sqrtf(ss / fL + p.eps);
-#pragma unroll
-            for (int c = 0; c < CH; c++)
-#pragma unroll
-                for (int j = 0; j < N; j++) v[c][j] *= r;
-        } else {
-            float sum = 0.0f;
-#pragma unroll
-            for (int c = 0; c < CH; c++)
-#pragma unroll
-                for (int j = 0; j < N; j++) sum += v[c][j];
-            const float mean = warp_sum(sum) / fL;
-            float sq = 0.0f;
-#pragma unroll
-            for (int c = 0; c < CH; c++) {
-                const int64_t col = ((int64_t)c * 32 + lane) * N;
-                if (col < p.L) {
-#pragma unroll
-                    for (int j = 0; j < N; j++) {
-                        const float d = v[c][j] - mean;
-                        sq += d * d;
-                    }
-                }
-            }
-            const float var = warp_sum(sq) / fL;
-            const float rstd = (MODE == M_LN_ONNX) ? 1.0f / sqrtf(var + p.eps) : 1.0f / (sqrtf(var) + p.eps);
-#pragma unroll
-            for (int c = 0; c < CH; c++) {
-                const int64_t col = ((int64_t)c * 32 + lane) * N;
-                if (col < p.L) {
-                    float g[N], b[N];
-                    if (p.gb_vec) {
-                        // raw 16-byte loads converted at use keep few registers live
-                        if (p.gamma) cvt_in<T>(ld_nc_v4(reinterpret_cast<const T*>(p.gamma) + col), g);
-                        if (p.beta) cvt_in<T>(ld_nc_v4(reinterpret_cast<const T*>(p.beta) + col), b);
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < N; j++) {
-                            if (p.gamma) g[j] = load_as<float>(p.gamma, p.g_dtype, (col + j) * p.g_stride);
-                            if (p.beta) b[j] = load_as<float>(p.beta, p.b_dtype, (col + j) * p.b_stride);
-                        }
-                    }
-#pragma unroll
-                    for (int j = 0; j < N; j++) {
-                        float t = (v[c][j] - mean) * rstd;
-                        if (p.gamma) t = t * g[j];
-                        if (p.beta) t = t + b[j];
-                        v[c][j] = t;
-                    }
-                }
-            }
-        }
-#pragma unroll
-        for (int c = 0; c < CH; c++) {
-            const int64_t col = ((int64_t)c * 32 + lane) * N;
-            if (col < p.L) st_stream_v4(y + col, cvt_out<T>(v[c]));
-        }
+        rownorm_finish<T, CH, MODE>(v, p, lane, reinterpret_cast<T*>(p.out) + row * p.out_row_stride);
     }
 }
 
@@ -421,6 +431,7 @@ int run_rownorm(int mode, const tadma_tensor* in, int32_t axis, const tadma_tens
 }
 
 }  // namespace
+
 }  // namespace tadma_b200
 
 using namespace tadma_b200;

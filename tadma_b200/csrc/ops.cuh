@@ -20,10 +20,12 @@ __device__ __forceinline__ float gelu_f(float x) {
 }
 
 // Fast forms, used when an fp32 chain writes a 16-bit output: the SFU
-// base-2 exponential and reciprocal (ex2.approx / rcp.approx, a few fp32 ulp)
-// in a form whose reciprocal only ever sees (1, 2]:
-//   sigmoid(y) = (y >= 0 ? 1 : t) / (1 + t),  t = 2^(-|y| log2 e).
-// Their error is orders of magnitude below half an fp16/bf16 ulp.
+// base-2 exponential and reciprocal (ex2.approx, max relative error ~2^-22;
+// rcp.approx, max 1 ulp over the full range), with no branch or select:
+//   sigmoid(w / log2 e) = 1 / (1 + 2^(-w)).
+// For w << 0 the sum is huge or +inf and the reciprocal goes to 0 as the
+// function does; the error stays orders of magnitude below half an
+// fp16/bf16 ulp wherever the result is a normal number.
 __device__ __forceinline__ float ex2_approx(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -36,11 +38,7 @@ __device__ __forceinline__ float rcp_approx(float x) {
 }
 
 // sigmoid of w / log2(e): callers fold log2(e) into their own constants.
-__device__ __forceinline__ float sigmoid_log2(float w) {
-    const float t = ex2_approx(-fabsf(w));
-    const float r = rcp_approx(1.0f + t);
-    return w >= 0.0f ? r : t * r;
-}
+__device__ __forceinline__ float sigmoid_log2(float w) { return rcp_approx(1.0f + ex2_approx(-w)); }
 
 __device__ __forceinline__ float sigmoid_fast(float y) { return sigmoid_log2(y * 1.4426950408889634f); }
 

@@ -93,9 +93,11 @@ __device__ __forceinline__ void update(State<A>& s, A v, int64_t idx) {
     if (K == K_SUM) {
         s.v = s.v + v;
     } else if (K == K_MAX) {
-        s.v = (v > s.v || v != v) ? v : s.v;  // NaN sticks once seen
+        if constexpr (std::is_same<A, float>::value) s.v = fmax_nan(s.v, v);  // NaN sticks once seen
+        else s.v = (v > s.v || v != v) ? v : s.v;
     } else if (K == K_MIN) {
-        s.v = (v < s.v || v != v) ? v : s.v;
+        if constexpr (std::is_same<A, float>::value) s.v = fmin_nan(s.v, v);
+        else s.v = (v < s.v || v != v) ? v : s.v;
     } else {
         const bool better = (K == K_ARGMAX) ? (v > s.v) : (v < s.v);
         const bool take = s.i < 0 || (s.v == s.v && (better || v != v));
@@ -107,21 +109,18 @@ __device__ __forceinline__ void update(State<A>& s, A v, int64_t idx) {
 }
 
 // Fold N consecutive elements f[0..N) with indices base..base+N-1.  For
-// arg-reductions the vector's extreme and NaN presence are found with N
-// compares; the first matching index is searched only when the vector beats
-// the running best, which becomes rare after the first few vectors.
+// arg-reductions the vector's extreme is found with N - 1 NaN-propagating
+// max/min ops (a NaN anywhere makes it NaN); the first matching index is
+// searched only when the vector beats the running best, which becomes rare
+// after the first few vectors.
 template <int K, int N>
 __device__ __forceinline__ void update_vec(State<float>& s, const float* f, int64_t base) {
     if constexpr (K == K_ARGMAX || K == K_ARGMIN) {
         if (s.i >= 0 && s.v != s.v) return;  // a NaN was already found: it stays
         float m = f[0];
-        bool nan = f[0] != f[0];
 #pragma unroll
-        for (int j = 1; j < N; j++) {
-            m = (K == K_ARGMAX) ? fmaxf(m, f[j]) : fminf(m, f[j]);
-            nan |= f[j] != f[j];
-        }
-        if (nan) {
+        for (int j = 1; j < N; j++) m = (K == K_ARGMAX) ? fmax_nan(m, f[j]) : fmin_nan(m, f[j]);
+        if (m != m) {
 #pragma unroll
             for (int j = N - 1; j >= 0; j--)
                 if (f[j] != f[j]) s.i = base + j;
@@ -182,10 +181,14 @@ __device__ __forceinline__ State<A> warp_combine(State<A> s) {
     return s;
 }
 
-template <typename A>
+// Element pre-op (fused unary and/or square).  PRE = false: the call has
+// neither, and the fast kernels are instantiated without the per-element test.
+template <bool PRE = true, typename A>
 __device__ __forceinline__ A prep(const RedParams& p, A v) {
-    if (p.pre_op != TADMA_OP_COPY) v = unary(p.pre_op, v);
-    if (p.square) v = v * v;
+    if constexpr (PRE) {
+        if (p.pre_op != TADMA_OP_COPY) v = unary(p.pre_op, v);
+        if (p.square) v = v * v;
+    }
     return v;
 }
 
@@ -238,7 +241,7 @@ __device__ __forceinline__ float ld1(const T* p) {
 
 // -------------------------------------------------------------- ROW path --
 
-template <typename T, int K>
+template <typename T, int K, bool PRE>
 __global__ void __launch_bounds__(THREADS) reduce_row_kernel(const __grid_constant__ RedParams p, int vec) {
     constexpr int N = Vec<T>::N;
     constexpr int UNR = 4;
@@ -262,14 +265,14 @@ __global__ void __launch_bounds__(THREADS) reduce_row_kernel(const __grid_consta
                         float f[N];
                         Vec<T>::cvt(r[u], f);
 #pragma unroll
-                        for (int j = 0; j < N; j++) f[j] = prep(p, f[j]);
+                        for (int j = 0; j < N; j++) f[j] = prep<PRE>(p, f[j]);
                         update_vec<K, N>(s, f, (i0 + 32 * u) * N);
                     }
                 }
             }
             done = nv * N;
         }
-        for (int64_t i = done + lane; i < p.R; i += 32) update<K, float>(s, prep(p, ld1(x + i * p.r_stride)), i);
+        for (int64_t i = done + lane; i < p.R; i += 32) update<K, float>(s, prep<PRE>(p, ld1(x + i * p.r_stride)), i);
         s = warp_combine<K, float>(s);
         if (lane == 0) finish<K, float>(p, s, row * p.out_row_stride);
     }
@@ -277,7 +280,7 @@ __global__ void __launch_bounds__(THREADS) reduce_row_kernel(const __grid_consta
 
 // -------------------------------------------------------------- COL path --
 
-template <typename T, int K, int VEC, bool SPLIT>
+template <typename T, int K, int VEC, bool SPLIT, bool PRE>
 __global__ void __launch_bounds__(THREADS) reduce_col_kernel(const __grid_constant__ RedParams p) {
     constexpr int COLS = 32 * VEC;
     __shared__ State<float> part[WARPS][COLS];
@@ -305,7 +308,7 @@ __global__ void __launch_bounds__(THREADS) reduce_col_kernel(const __grid_consta
                             float f[Vec<T>::N];
                             Vec<T>::cvt(v[u], f);
 #pragma unroll
-                            for (int j = 0; j < VEC; j++) update<K, float>(s[j], prep(p, f[j]), r0 + WARPS * u);
+                            for (int j = 0; j < VEC; j++) update<K, float>(s[j], prep<PRE>(p, f[j]), r0 + WARPS * u);
                         }
                     }
                 } else {
@@ -315,7 +318,7 @@ __global__ void __launch_bounds__(THREADS) reduce_col_kernel(const __grid_consta
                         if (r0 + WARPS * u < rend) v[u] = ld1(base + (r0 + WARPS * u) * p.r_stride + col0);
 #pragma unroll
                     for (int u = 0; u < UNR; u++)
-                        if (r0 + WARPS * u < rend) update<K, float>(s[0], prep(p, v[u]), r0 + WARPS * u);
+                        if (r0 + WARPS * u < rend) update<K, float>(s[0], prep<PRE>(p, v[u]), r0 + WARPS * u);
                 }
             }
         }
@@ -347,7 +350,7 @@ __global__ void __launch_bounds__(THREADS) reduce_col_kernel(const __grid_consta
 // the partials of an output in chunk order.  Chunks and combine order depend
 // only on (R, splits), so results are deterministic.
 
-template <typename T, int K>
+template <typename T, int K, bool PRE>
 __global__ void __launch_bounds__(THREADS) reduce_row_split_kernel(const __grid_constant__ RedParams p, int vec) {
     constexpr int N = Vec<T>::N;
     constexpr int UNR = 4;
@@ -372,14 +375,14 @@ __global__ void __launch_bounds__(THREADS) reduce_row_split_kernel(const __grid_
                     float f[N];
                     Vec<T>::cvt(r[u], f);
 #pragma unroll
-                    for (int j = 0; j < N; j++) f[j] = prep(p, f[j]);
+                    for (int j = 0; j < N; j++) f[j] = prep<PRE>(p, f[j]);
                     update_vec<K, N>(s, f, (i0 + THREADS * u) * N);
                 }
             }
         }
         done = v1 * N;
     }
-    for (int64_t i = done + threadIdx.x; i < r1; i += THREADS) update<K, float>(s, prep(p, ld1(x + i * p.r_stride)), i);
+    for (int64_t i = done + threadIdx.x; i < r1; i += THREADS) update<K, float>(s, prep<PRE>(p, ld1(x + i * p.r_stride)), i);
     s = warp_combine<K, float>(s);
     if (lane == 0) sh[w] = s;
     __syncthreads();
@@ -470,17 +473,17 @@ int grid_for(const void* fn, int64_t want) {
     return (int)(want < cap ? want : cap);
 }
 
-template <typename T, int K>
+template <typename T, int K, bool PRE>
 int launch_fast(int path, const RedParams& p, bool vec, cudaStream_t s) {
     if (path == 0) {
         if (p.splits > 1) {
-            reduce_row_split_kernel<T, K><<<dim3((unsigned)p.splits, (unsigned)p.nrows), THREADS, 0, s>>>(p, vec ? 1 : 0);
+            reduce_row_split_kernel<T, K, PRE><<<dim3((unsigned)p.splits, (unsigned)p.nrows), THREADS, 0, s>>>(p, vec ? 1 : 0);
             const void* fn = (const void*)reduce_row_finish_kernel<K>;
             reduce_row_finish_kernel<K><<<grid_for(fn, (p.nrows + WARPS - 1) / WARPS), THREADS, 0, s>>>(p);
         } else {
-            const void* fn = (const void*)reduce_row_kernel<T, K>;
+            const void* fn = (const void*)reduce_row_kernel<T, K, PRE>;
             int grid = grid_for(fn, (p.nrows + WARPS - 1) / WARPS);
-            reduce_row_kernel<T, K><<<grid, THREADS, 0, s>>>(p, vec ? 1 : 0);
+            reduce_row_kernel<T, K, PRE><<<grid, THREADS, 0, s>>>(p, vec ? 1 : 0);
         }
     } else {
         constexpr int VEC = Vec<T>::N;
@@ -488,28 +491,34 @@ int launch_fast(int path, const RedParams& p, bool vec, cudaStream_t s) {
         if (tiles > 0x7fffffff) return fail(TADMA_ERR_UNSUPPORTED, "reduce: too many column tiles");
         dim3 grid((unsigned)tiles, (unsigned)(p.nrows < 65535 ? p.nrows : 65535), (unsigned)(p.splits > 1 ? p.splits : 1));
         if (p.splits > 1) {
-            if (vec) reduce_col_kernel<T, K, VEC, true><<<grid, THREADS, 0, s>>>(p);
-            else reduce_col_kernel<T, K, 1, true><<<grid, THREADS, 0, s>>>(p);
+            if (vec) reduce_col_kernel<T, K, VEC, true, PRE><<<grid, THREADS, 0, s>>>(p);
+            else reduce_col_kernel<T, K, 1, true, PRE><<<grid, THREADS, 0, s>>>(p);
             const void* fn = (const void*)reduce_col_finish_kernel<K>;
             reduce_col_finish_kernel<K><<<grid_for(fn, (p.nrows * p.inner + THREADS - 1) / THREADS), THREADS, 0, s>>>(p);
         } else {
-            if (vec) reduce_col_kernel<T, K, VEC, false><<<grid, THREADS, 0, s>>>(p);
-            else reduce_col_kernel<T, K, 1, false><<<grid, THREADS, 0, s>>>(p);
+            if (vec) reduce_col_kernel<T, K, VEC, false, PRE><<<grid, THREADS, 0, s>>>(p);
+            else reduce_col_kernel<T, K, 1, false, PRE><<<grid, THREADS, 0, s>>>(p);
         }
     }
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? TADMA_OK : cuda_fail(e, "tadma_b200_reduce launch");
 }
 
+template <typename T, bool PRE>
+int launch_fast_kind_pre(int kind, int path, const RedParams& p, bool vec, cudaStream_t s) {
+    switch (kind) {
+    case K_SUM: return launch_fast<T, K_SUM, PRE>(path, p, vec, s);
+    case K_MAX: return launch_fast<T, K_MAX, PRE>(path, p, vec, s);
+    case K_MIN: return launch_fast<T, K_MIN, PRE>(path, p, vec, s);
+    case K_ARGMAX: return launch_fast<T, K_ARGMAX, PRE>(path, p, vec, s);
+    default: return launch_fast<T, K_ARGMIN, PRE>(path, p, vec, s);
+    }
+}
+
 template <typename T>
 int launch_fast_kind(int kind, int path, const RedParams& p, bool vec, cudaStream_t s) {
-    switch (kind) {
-    case K_SUM: return launch_fast<T, K_SUM>(path, p, vec, s);
-    case K_MAX: return launch_fast<T, K_MAX>(path, p, vec, s);
-    case K_MIN: return launch_fast<T, K_MIN>(path, p, vec, s);
-    case K_ARGMAX: return launch_fast<T, K_ARGMAX>(path, p, vec, s);
-    default: return launch_fast<T, K_ARGMIN>(path, p, vec, s);
-    }
+    if (p.pre_op != TADMA_OP_COPY || p.square) return launch_fast_kind_pre<T, true>(kind, path, p, vec, s);
+    return launch_fast_kind_pre<T, false>(kind, path, p, vec, s);
 }
 
 template <typename A>

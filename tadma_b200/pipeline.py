@@ -1,0 +1,59 @@
+"""Host-buffer execution of row-wise ops with copies overlapped.
+
+A caller whose inputs and outputs live in (pinned) host memory pays a PCIe
+upload and download around every kernel.  PCIe is full duplex, and the
+element-wise / row ops are independent across rows, so RowPipeline splits a
+step into row chunks on three streams: chunk k+1 uploads while chunk k runs
+its C-ABI call and chunk k-1 downloads.  A step then costs about
+max(upload, download) instead of upload + compute + download.
+"""
+from __future__ import annotations
+
+
+class RowPipeline:
+    """One step = upload the `uploads` row chunks, run `make_call(lo, hi,
+    stream)` per chunk, download the `downloads` row chunks; `once` buffers
+    (e.g. a bias row) are uploaded whole at the start of each step.
+
+    uploads / downloads: lists of (src, dst) torch tensors whose leading axis
+    is the row axis (host -> device for uploads, device -> host for downloads).
+    make_call(lo, hi, stream) returns a callable that launches the op on rows
+    [lo, hi) on `stream` (e.g. a tadma_b200.prepare_* call built for views)."""
+
+    def __init__(self, rows, chunks, uploads, downloads, make_call, once=()):
+        import torch
+        self.rows, self.chunks = rows, max(1, chunks)
+        self.uploads, self.downloads, self.once = list(uploads), list(downloads), list(once)
+        self.s_in, self.s_run, self.s_out = torch.cuda.Stream(), torch.cuda.Stream(), torch.cuda.Stream()
+        step = (rows + self.chunks - 1) // self.chunks
+        self.bounds = [(lo, min(rows, lo + step)) for lo in range(0, rows, step)]
+        self.calls = [make_call(lo, hi, self.s_run) for lo, hi in self.bounds]
+        self.ev_in = [torch.cuda.Event() for _ in self.bounds]
+        self.ev_run = [torch.cuda.Event() for _ in self.bounds]
+        self.ev_done = torch.cuda.Event()
+
+    def __call__(self, stream):
+        """Enqueue one step after the work already queued on `stream`; `stream`
+        waits for the last download before anything queued after it runs."""
+        import torch
+        start = torch.cuda.Event()
+        start.record(stream)
+        for s in (self.s_in, self.s_run, self.s_out):
+            s.wait_event(start)
+        with torch.cuda.stream(self.s_in):
+            for src, dst in self.once:
+                dst.copy_(src, non_blocking=True)
+        for k, (lo, hi) in enumerate(self.bounds):
+            with torch.cuda.stream(self.s_in):
+                for src, dst in self.uploads:
+                    dst[lo:hi].copy_(src[lo:hi], non_blocking=True)
+                self.ev_in[k].record(self.s_in)
+            self.s_run.wait_event(self.ev_in[k])
+            self.calls[k]()
+            self.ev_run[k].record(self.s_run)
+            self.s_out.wait_event(self.ev_run[k])
+            with torch.cuda.stream(self.s_out):
+                for src, dst in self.downloads:
+                    dst[lo:hi].copy_(src[lo:hi], non_blocking=True)
+        self.ev_done.record(self.s_out)
+        stream.wait_event(self.ev_done)

@@ -108,3 +108,50 @@ def test_config5_full_size_sampled():
     assert np.array_equal(got, ref)
     del out
     torch.cuda.empty_cache()
+
+
+# --- row path edges: row lengths that are not a multiple of a warp's 256-element
+# step, fp32 operands, many rows per warp (the next id is loaded a row
+# ahead), invalid ids mid-stream, strided ids, padded output rows.
+
+@pytest.mark.parametrize("tdt,adt,odt,D", [(DType.F16, DType.BF16, DType.BF16, 1032),  # ragged last step
+                                           (DType.F32, DType.F32, DType.F32, 520),
+                                           (DType.BF16, None, DType.F32, 2056),        # no add
+                                           (DType.F16, DType.F32, DType.F16, 64)])     # one short row
+def test_row_lengths_and_dtypes(tdt, adt, odt, D):
+    V, B, S = 777, 3, 37
+    table = gen((V, D), tdt, Dist.NORMAL, 0, 1, 11)
+    ids = gen((B, S), DType.I64, Dist.INDEX, 0, V, 12)
+    add = np.broadcast_to(gen((S, D), adt, Dist.NORMAL, 0, 1, 13), (B, S, D)) if adt is not None else None
+    got, ref, flags, rc = run_both(table, tdt, 0, ids, add, adt, odt)
+    assert rc == 0 and flags == 0 and np.array_equal(got, ref)
+
+
+def test_many_rows_with_invalid_ids():
+    # 204800 rows: each warp walks tens of rows, loading each next id ahead.
+    V, B, S, D = 5000, 400, 512, 64
+    table = gen((V, D), DType.F16, Dist.NORMAL, 0, 1, 14)
+    ids = gen((B, S), DType.I64, Dist.INDEX, 0, V, 15)
+    ids[7, 100] = V          # out of range
+    ids[399, 511] = -V - 1   # out of range, last row
+    ids[200, 0] = -1         # valid (wraps to V-1)
+    pos = gen((S, D), DType.BF16, Dist.NORMAL, 0, 1, 16)
+    got, ref, flags, rc = run_both(table, DType.F16, 0, ids, np.broadcast_to(pos, (B, S, D)), DType.BF16, DType.BF16)
+    assert rc == 4 and flags & (1 << 4)
+    assert np.array_equal(got, ref)
+    assert np.array_equal(got[7, 100], pos[100])  # table part zero, pos still added
+
+
+def test_strided_ids_and_padded_out_rows():
+    import torch
+    V, R, D = 900, 300, 256
+    table = gen((V, D), DType.F16, Dist.NORMAL, 0, 1, 17)
+    ids_full = gen((R, 2), DType.I64, Dist.INDEX, 0, V, 18)
+    idd = to_dev(ids_full)[:, 1]                      # stride 2 ids
+    out_full = torch.zeros((R, D + 64), dtype=torch.float16, device="cuda")
+    out = out_full[:, 8:8 + D]                        # padded rows, 16-byte aligned start
+    tb.gather(to_dev(table), 0, idd, out)
+    assert tb.error_flags(clear=True) == 0
+    got = from_dev(out_full)
+    assert np.array_equal(got[:, 8:8 + D], table[ids_full[:, 1]])
+    assert not got[:, :8].any() and not got[:, 8 + D:].any()

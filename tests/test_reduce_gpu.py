@@ -217,3 +217,25 @@ def test_split_results_are_deterministic():
     tb.reduce(Reduce.SUM, x, -1, b)
     torch.cuda.synchronize()
     assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("shape", [(5, 4100), (3, 70000)])  # vector path with a tail; split-R path (few long rows)
+def test_nan_inf_extremes_vector_paths(shape):
+    R, L = shape
+    x = gen(shape, DType.F32, Dist.UNIFORM, -1, 1, 21)
+    x[0, 4000] = np.inf
+    x[0, 4001] = np.nan          # NaN after +inf: NaN wins max, first NaN wins argmax
+    x[1, :] = -np.inf
+    x[1, L - 1] = np.nan         # NaN in the tail
+    x[2, 3] = np.inf
+    x[2, L - 2] = np.inf         # inf ties: first index
+    if R > 3:
+        x[3, 1024:1028] = np.nan  # a whole 16-byte vector of NaN
+        x[4, 0] = -np.inf
+    for op in (Reduce.MAX, Reduce.MIN, Reduce.ARGMAX, Reduce.ARGMIN):
+        got, ref = run_both(op, x, DType.F32, -1, keep=False)
+        if op in (Reduce.ARGMAX, Reduce.ARGMIN):
+            assert np.array_equal(got, ref), (op.name, got, ref)
+        else:
+            assert np.array_equal(np.isnan(got), np.isnan(ref)), (op.name, got, ref)
+            assert np.array_equal(got[~np.isnan(got)], ref[~np.isnan(ref)]), (op.name, got, ref)
