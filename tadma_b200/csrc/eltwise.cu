@@ -443,32 +443,6 @@ __device__ __forceinline__ void raw8_store(T* p, const float* f) {
     }
 }
 
-// Packed fp32x2 arithmetic (sm_100): two lanes per instruction, each lane
-// rounded exactly like the scalar op (__fmul_rn / __fadd_rn / fmaf).
-__device__ __forceinline__ unsigned long long f2_pack(float lo, float hi) {
-    unsigned long long r;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
-    return r;
-}
-__device__ __forceinline__ void f2_unpack(unsigned long long v, float& lo, float& hi) {
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
-}
-__device__ __forceinline__ unsigned long long f2_mul(unsigned long long a, unsigned long long b) {
-    unsigned long long r;
-    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-    return r;
-}
-__device__ __forceinline__ unsigned long long f2_add(unsigned long long a, unsigned long long b) {
-    unsigned long long r;
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-    return r;
-}
-__device__ __forceinline__ unsigned long long f2_fma(unsigned long long a, unsigned long long b, unsigned long long c) {
-    unsigned long long r;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
-    return r;
-}
-
 // gelu_fast on two lanes: the same operation sequence as gelu_fast (ops.cuh),
 // gelu(x) = x / (1 + 2^(-w)), w = x (K1 + K3 x^2), with the polynomial, the
 // sum and the final product packed (the sign of w folded into K1, K3).

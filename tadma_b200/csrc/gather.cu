@@ -10,7 +10,8 @@
 // separate CombineToNode pass over the whole output (Kernels.hpp:33-45).
 //
 // Fast path (axis 0, table rows contiguous): one warp per output row; the id
-// is read once per row (one broadcast load, a row ahead), the row is copied in 8-element
+// is read once per row (one broadcast load, a row ahead), rows sharing an
+// add row are visited together (batch-fastest), the row is copied in 8-element
 // chunks (16 B of fp16/bf16, 32 B of fp32) with 4 raw chunks in flight per lane,
 // the add operand's row (e.g. pos[s]) is fetched with an L2 evict_last policy
 // so it stays resident across the batch while the gathered rows (evict_first
@@ -45,9 +46,14 @@ struct GatherParams {
     int64_t n;  // table extent along the gather axis
     // fast path
     int64_t nrows, D, t_row_stride, o_row_stride, ids_stride;
-    int32_t irank, pad;
+    int32_t irank, bperm;
     DivMod idm[TADMA_MAX_RANK];  // ids dims (row -> ids multi-index)
     int64_t a_row[TADMA_MAX_RANK];  // add strides over the ids dims
+    // bperm: rows are visited batch-fastest, task t -> row b * brest + q with
+    // (q, b) = divmod(t, ids.dims[0]), so warps running at the same time
+    // share the add operand's row (pos[s]) instead of sweeping all of it.
+    DivMod bdm;
+    int64_t brest;
     // generic path
     int32_t orank, ax;
     int64_t total;
@@ -106,12 +112,23 @@ __global__ void __launch_bounds__(THREADS) gather_rows_kernel(const __grid_const
     // batch row re-reads) is kept resident.
     const uint64_t pol_stream = l2_policy_evict_first();
     const uint64_t pol_keep = l2_policy_evict_last();
+    auto row_of = [&](int64_t t) -> int64_t {
+        if (!p.bperm) return t;
+        uint64_t q, b;
+        p.bdm.divmod((uint64_t)t, q, b);
+        return (int64_t)b * p.brest + (int64_t)q;
+    };
     // The id of the warp's next row is loaded while this row streams, so no
     // dependent id load sits in front of a row's table loads.
-    int64_t id_next = gw < p.nrows ? load_id(p.ids, p.i_dtype, gw * p.ids_stride) : 0;
-    for (int64_t row = gw; row < p.nrows; row += nw) {
+    int64_t row_next = row_of(gw);
+    int64_t id_next = gw < p.nrows ? load_id(p.ids, p.i_dtype, row_next * p.ids_stride) : 0;
+    for (int64_t t = gw; t < p.nrows; t += nw) {
+        const int64_t row = row_next;
         int64_t id = id_next;
-        if (row + nw < p.nrows) id_next = load_id(p.ids, p.i_dtype, (row + nw) * p.ids_stride);
+        if (t + nw < p.nrows) {
+            row_next = row_of(t + nw);
+            id_next = load_id(p.ids, p.i_dtype, row_next * p.ids_stride);
+        }
         if (id < 0) id += p.n;
         const bool ok = (uint64_t)id < (uint64_t)p.n;
         if (!ok && lane == 0) atomicOr(&g_error_word, 1u << TADMA_ERR_INDEX);
@@ -334,7 +351,13 @@ extern "C" int tadma_b200_gather(const tadma_tensor* table, int32_t axis, const 
                 p.idm[d] = DivMod((uint64_t)ids->dims[d]);
                 p.a_row[d] = astr[d];
             }
-
+            // An add broadcast over the leading ids dim (pos over the batch):
+            // visit rows batch-fastest so the add rows in use stay few.
+            if (has_add && irank >= 2 && astr[0] == 0 && ids->dims[0] > 1) {
+                p.bperm = 1;
+                p.bdm = DivMod((uint64_t)ids->dims[0]);
+                p.brest = p.nrows / ids->dims[0];
+            }
             switch (table->dtype) {
             case TADMA_F32: return launch_add<float>(p, has_add, s);
             case TADMA_F16: return launch_add<__half>(p, has_add, s);

@@ -16,6 +16,7 @@
 // the row max (same value in exact arithmetic, no overflow).  Longer or
 // strided rows take a block-per-row kernel that re-reads the row (L2-hot).
 #include <mutex>
+#include <type_traits>
 #include <unordered_map>
 
 #include "common.cuh"
@@ -102,11 +103,156 @@ __device__ __forceinline__ float fast_exp(float x) {
 // Statistics, normalisation and store of one row held in a warp's registers
 // (lane l holds chunks c * 32 + l, N elements each; chunks past L hold the
 // neutral value of the mode).
+// Two 16-bit values (one 32-bit word, low half first) widened to fp32x2.
+template <typename T>
+__device__ __forceinline__ unsigned long long widen2(uint32_t w) {
+    if constexpr (std::is_same<T, __half>::value) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w));
+        return f2_pack(f.x, f.y);
+    } else {
+        return f2_pack(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+    }
+}
+
+// 16-bit rows: the same statistics with the element arithmetic on packed
+// fp32x2 instructions (two elements per instruction, each rounded like the
+// scalar op), and the normalisation folded into fused multiply-adds:
+//   softmax   e = 2^(x log2e - m log2e),  y = e * (1 / sum e)
+//   LayerNorm y = (x rstd + (-mean rstd)) * gamma + beta
+//   RMSNorm   y = x * (1 / sqrt(mean(x^2) + eps))
+// Outputs are 16-bit, so the reassociation stays far inside half an ulp.
+template <typename T, int CH, int MODE>
+__device__ __forceinline__ void rownorm_finish_packed(float (&v)[CH][VecT<T>::N], const NormParams& p, int lane, T* y) {
+    constexpr int BM = MODE & 3;          // softmax / LN ONNX / LN TADMA / RMS
+    constexpr bool GBV = (MODE & 4) == 0;  // gamma/beta: x dtype, stride 1, 16-byte aligned
+    constexpr int N = VecT<T>::N;
+    constexpr int H = N / 2;
+    typedef unsigned long long u64;
+    const float fL = (float)p.L;
+    if constexpr (BM == M_SOFTMAX) {
+        float m = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < CH; c++)
+#pragma unroll
+            for (int j = 0; j < N; j++) m = fmaxf(m, v[c][j]);
+        m = warp_max(m);
+        constexpr float L2E = 1.4426950408889634f;
+        const u64 k2 = f2_pack(L2E, L2E), nm2 = f2_pack(-m * L2E, -m * L2E);
+        u64 s2 = f2_pack(0.0f, 0.0f);
+#pragma unroll
+        for (int c = 0; c < CH; c++)
+#pragma unroll
+            for (int h = 0; h < H; h++) {
+                float a, b;
+                f2_unpack(f2_fma(f2_pack(v[c][2 * h], v[c][2 * h + 1]), k2, nm2), a, b);
+                a = ex2_approx(a);
+                b = ex2_approx(b);
+                // chunks past L hold -inf: 2^-inf = 0 adds nothing
+                v[c][2 * h] = a;
+                v[c][2 * h + 1] = b;
+                s2 = f2_add(s2, f2_pack(a, b));
+            }
+        float s0, s1;
+        f2_unpack(s2, s0, s1);
+        const float inv = 1.0f / warp_sum(s0 + s1);
+        const u64 i2 = f2_pack(inv, inv);
+#pragma unroll
+        for (int c = 0; c < CH; c++)
+#pragma unroll
+            for (int h = 0; h < H; h++) f2_unpack(f2_mul(f2_pack(v[c][2 * h], v[c][2 * h + 1]), i2), v[c][2 * h], v[c][2 * h + 1]);
+    } else if constexpr (BM == M_RMS) {
+        u64 q2 = f2_pack(0.0f, 0.0f);
+#pragma unroll
+        for (int c = 0; c < CH; c++)
+#pragma unroll
+            for (int h = 0; h < H; h++) {
+                const u64 x = f2_pack(v[c][2 * h], v[c][2 * h + 1]);
+                q2 = f2_fma(x, x, q2);
+            }
+        float q0, q1;
+        f2_unpack(q2, q0, q1);
+        const float r = 1.0f / sqrtf(warp_sum(q0 + q1) / fL + p.eps);
+        const u64 r2 = f2_pack(r, r);
+#pragma unroll
+        for (int c = 0; c < CH; c++)
+#pragma unroll
+            for (int h = 0; h < H; h++) f2_unpack(f2_mul(f2_pack(v[c][2 * h], v[c][2 * h + 1]), r2), v[c][2 * h], v[c][2 * h + 1]);
+    } else {
+        u64 s2 = f2_pack(0.0f, 0.0f);
+#pragma unroll
+        for (int c = 0; c < CH; c++)
+#pragma unroll
+            for (int h = 0; h < H; h++) s2 = f2_add(s2, f2_pack(v[c][2 * h], v[c][2 * h + 1]));
+        float s0, s1;
+        f2_unpack(s2, s0, s1);
+        const float mean = warp_sum(s0 + s1) / fL;
+        const u64 nmean2 = f2_pack(-mean, -mean);
+        u64 q2 = f2_pack(0.0f, 0.0f);
+#pragma unroll
+        for (int c = 0; c < CH; c++) {
+            const int64_t col = ((int64_t)c * 32 + lane) * N;
+            if (col < p.L) {
+#pragma unroll
+                for (int h = 0; h < H; h++) {
+                    const u64 d = f2_add(f2_pack(v[c][2 * h], v[c][2 * h + 1]), nmean2);
+                    q2 = f2_fma(d, d, q2);
+                }
+            }
+        }
+        float q0, q1;
+        f2_unpack(q2, q0, q1);
+        const float var = warp_sum(q0 + q1) / fL;
+        const float rstd = (BM == M_LN_ONNX) ? 1.0f / sqrtf(var + p.eps) : 1.0f / (sqrtf(var) + p.eps);
+        const u64 r2 = f2_pack(rstd, rstd), c2 = f2_pack(-mean * rstd, -mean * rstd);
+#pragma unroll
+        for (int c = 0; c < CH; c++) {
+            const int64_t col = ((int64_t)c * 32 + lane) * N;
+            if (col < p.L) {
+                if constexpr (GBV) {
+                    // gamma / beta stay raw (4 registers each) and are widened
+                    // a pair at a time
+                    uint4 gr = make_uint4(0, 0, 0, 0), br = make_uint4(0, 0, 0, 0);
+                    if (p.gamma) gr = ld_nc_v4(reinterpret_cast<const T*>(p.gamma) + col);
+                    if (p.beta) br = ld_nc_v4(reinterpret_cast<const T*>(p.beta) + col);
+                    const uint32_t gw[4] = {gr.x, gr.y, gr.z, gr.w}, bw[4] = {br.x, br.y, br.z, br.w};
+#pragma unroll
+                    for (int h = 0; h < H; h++) {
+                        u64 t = f2_fma(f2_pack(v[c][2 * h], v[c][2 * h + 1]), r2, c2);
+                        if (p.gamma && p.beta) t = f2_fma(t, widen2<T>(gw[h]), widen2<T>(bw[h]));
+                        else if (p.gamma) t = f2_mul(t, widen2<T>(gw[h]));
+                        else if (p.beta) t = f2_add(t, widen2<T>(bw[h]));
+                        f2_unpack(t, v[c][2 * h], v[c][2 * h + 1]);
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < N; j++) {
+                        float t = fmaf(v[c][j], rstd, -mean * rstd);
+                        if (p.gamma) t = t * load_as<float>(p.gamma, p.g_dtype, (col + j) * p.g_stride);
+                        if (p.beta) t = t + load_as<float>(p.beta, p.b_dtype, (col + j) * p.b_stride);
+                        v[c][j] = t;
+                    }
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int c = 0; c < CH; c++) {
+        const int64_t col = ((int64_t)c * 32 + lane) * N;
+        if (col < p.L) st_stream_v4(y + col, cvt_out<T>(v[c]));
+    }
+}
+
 template <typename T, int CH, int MODE>
 __device__ __forceinline__ void rownorm_finish(float (&v)[CH][VecT<T>::N], const NormParams& p, int lane, T* y) {
+    constexpr int BM = MODE & 3;          // softmax / LN ONNX / LN TADMA / RMS
+    constexpr bool GBV = (MODE & 4) == 0;  // gamma/beta: x dtype, stride 1, 16-byte aligned
+    if constexpr (sizeof(T) == 2) {
+        rownorm_finish_packed<T, CH, MODE>(v, p, lane, y);
+        return;
+    }
     constexpr int N = VecT<T>::N;
     const float fL = (float)p.L;
-    if constexpr (MODE == M_SOFTMAX) {
+    if constexpr (BM == M_SOFTMAX) {
         float m = -INFINITY;
 #pragma unroll
         for (int c = 0; c < CH; c++)
@@ -127,7 +273,7 @@ __device__ __forceinline__ void rownorm_finish(float (&v)[CH][VecT<T>::N], const
         for (int c = 0; c < CH; c++)
 #pragma unroll
             for (int j = 0; j < N; j++) v[c][j] *= inv;
-    } else if constexpr (MODE == M_RMS) {
+    } else if constexpr (BM == M_RMS) {
         float ss = 0.0f;
 #pragma unroll
         for (int c = 0; c < CH; c++)
@@ -159,13 +305,13 @@ __device__ __forceinline__ void rownorm_finish(float (&v)[CH][VecT<T>::N], const
             }
         }
         const float var = warp_sum(sq) / fL;
-        const float rstd = (MODE == M_LN_ONNX) ? 1.0f / sqrtf(var + p.eps) : 1.0f / (sqrtf(var) + p.eps);
+        const float rstd = (BM == M_LN_ONNX) ? 1.0f / sqrtf(var + p.eps) : 1.0f / (sqrtf(var) + p.eps);
 #pragma unroll
         for (int c = 0; c < CH; c++) {
             const int64_t col = ((int64_t)c * 32 + lane) * N;
             if (col < p.L) {
                 float g[N], b[N];
-                if (p.gb_vec) {
+                if constexpr (GBV) {
                     // raw 16-byte loads converted at use keep few registers live
                     if (p.gamma) cvt_in<T>(ld_nc_v4(reinterpret_cast<const T*>(p.gamma) + col), g);
                     if (p.beta) cvt_in<T>(ld_nc_v4(reinterpret_cast<const T*>(p.beta) + col), b);
@@ -193,11 +339,17 @@ __device__ __forceinline__ void rownorm_finish(float (&v)[CH][VecT<T>::N], const
     }
 }
 
-// 16-bit rows of <= 4 chunks per lane are latency-bound: cap registers so 3
-// CTAs (24 warps) fit per SM; 8-chunk and fp32 rows keep their registers
-// (2 CTAs per SM).
+// Resident CTAs per SM the register cap aims for.  16-bit rows of <= 4 chunks
+// per lane are latency-bound: fp16 rows fit 4 CTAs (64 registers) without
+// spills, bf16 rows 3 (their widening keeps more values live); 8-chunk and
+// fp32 rows keep their registers (2 CTAs per SM).
+template <typename T, int CH>
+constexpr int norm_min_blocks() {
+    if (CH > 4 || sizeof(T) == 4) return 2;
+    return std::is_same<T, __half>::value ? 4 : 3;
+}
 template <typename T, int CH, int MODE>
-__global__ void __launch_bounds__(THREADS, (CH <= 4 && sizeof(T) == 2 ? 3 : 2)) rownorm_warp_kernel(const __grid_constant__ NormParams p) {
+__global__ void __launch_bounds__(THREADS, norm_min_blocks<T, CH>()) rownorm_warp_kernel(const __grid_constant__ NormParams p) {
     constexpr int N = VecT<T>::N;
     const int lane = threadIdx.x & 31;
     const int64_t gw = ((int64_t)blockIdx.x * THREADS + threadIdx.x) >> 5;
@@ -212,7 +364,7 @@ __global__ void __launch_bounds__(THREADS, (CH <= 4 && sizeof(T) == 2 ? 3 : 2)) 
                 cvt_in<T>(ld_stream_v4(x + col), v[c]);
             } else {
 #pragma unroll
-                for (int j = 0; j < N; j++) v[c][j] = (MODE == M_SOFTMAX) ? -INFINITY : 0.0f;
+                for (int j = 0; j < N; j++) v[c][j] = ((MODE & 3) == M_SOFTMAX) ? -INFINITY : 0.0f;
             }
         }
         rownorm_finish<T, CH, MODE>(v, p, lane, reinterpret_cast<T*>(p.out) + row * p.out_row_stride);
@@ -326,12 +478,14 @@ int launch_ch(int ch, const NormParams& p, cudaStream_t s) {
     }
 }
 
+// Kernel MODE = the row op, + 4 when gamma/beta take the per-element path.
 template <typename T>
 int launch_mode(int mode, int ch, const NormParams& p, cudaStream_t s) {
+    const bool gbv = p.gb_vec != 0;
     switch (mode) {
     case M_SOFTMAX: return launch_ch<T, M_SOFTMAX>(ch, p, s);
-    case M_LN_ONNX: return launch_ch<T, M_LN_ONNX>(ch, p, s);
-    case M_LN_TADMA: return launch_ch<T, M_LN_TADMA>(ch, p, s);
+    case M_LN_ONNX: return gbv ? launch_ch<T, M_LN_ONNX>(ch, p, s) : launch_ch<T, M_LN_ONNX | 4>(ch, p, s);
+    case M_LN_TADMA: return gbv ? launch_ch<T, M_LN_TADMA>(ch, p, s) : launch_ch<T, M_LN_TADMA | 4>(ch, p, s);
     default: return launch_ch<T, M_RMS>(ch, p, s);
     }
 }

@@ -26,11 +26,6 @@ __device__ __forceinline__ float gelu_f(float x) {
 // For w << 0 the sum is huge or +inf and the reciprocal goes to 0 as the
 // function does; the error stays orders of magnitude below half an
 // fp16/bf16 ulp wherever the result is a normal number.
-__device__ __forceinline__ float ex2_approx(float x) {
-    float y;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-    return y;
-}
 __device__ __forceinline__ float rcp_approx(float x) {
     float y;
     asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));

@@ -108,38 +108,12 @@ __device__ __forceinline__ void update(State<A>& s, A v, int64_t idx) {
     }
 }
 
-// Fold N consecutive elements f[0..N) with indices base..base+N-1.  For
-// arg-reductions the vector's extreme is found with N - 1 NaN-propagating
-// max/min ops (a NaN anywhere makes it NaN); the first matching index is
-// searched only when the vector beats the running best, which becomes rare
-// after the first few vectors.
+// Fold N consecutive elements f[0..N) with indices base..base+N-1 (sum,
+// max, min; arg kinds use ArgVec below).
 template <int K, int N>
 __device__ __forceinline__ void update_vec(State<float>& s, const float* f, int64_t base) {
-    if constexpr (K == K_ARGMAX || K == K_ARGMIN) {
-        if (s.i >= 0 && s.v != s.v) return;  // a NaN was already found: it stays
-        float m = f[0];
 #pragma unroll
-        for (int j = 1; j < N; j++) m = (K == K_ARGMAX) ? fmax_nan(m, f[j]) : fmin_nan(m, f[j]);
-        if (m != m) {
-#pragma unroll
-            for (int j = N - 1; j >= 0; j--)
-                if (f[j] != f[j]) s.i = base + j;
-            s.v = NAN;
-            return;
-        }
-        const bool better = s.i < 0 || ((K == K_ARGMAX) ? (m > s.v) : (m < s.v));
-        if (better) {
-            int64_t idx = base;
-#pragma unroll
-            for (int j = N - 1; j >= 0; j--)
-                if (f[j] == m) idx = base + j;
-            s.v = m;
-            s.i = idx;
-        }
-    } else {
-#pragma unroll
-        for (int j = 0; j < N; j++) update<K, float>(s, f[j], base + j);
-    }
+    for (int j = 0; j < N; j++) update<K, float>(s, f[j], base + j);
 }
 
 // Combine two partial states; ties and NaN resolve to the lower index.
@@ -239,6 +213,55 @@ __device__ __forceinline__ float ld1(const T* p) {
     else return __bfloat162float(*p);
 }
 
+// Per-lane arg-reduction over 16-byte vectors.  Each vector costs its N - 1
+// NaN-propagating max/min ops, one "beats the best" test and the selects
+// that keep the best vector's value, vector index and raw bits; the element
+// index inside the winning vector is found once, in resolve().  A vector
+// beats the best when its extreme is strictly better, or when it holds the
+// first NaN (NaN counts as the extreme and sticks), so ties keep the
+// earlier vector and, within it, the first matching element.
+template <int K, typename T, int N>
+struct ArgVec {
+    float v;
+    int64_t vi;  // vector index of the best, -1 = none yet
+    uint4 raw;
+
+    __device__ __forceinline__ void init() {
+        v = (K == K_ARGMAX) ? -INFINITY : INFINITY;
+        vi = -1;
+        raw = make_uint4(0, 0, 0, 0);
+    }
+    __device__ __forceinline__ void add(const uint4& r, const float* f, int64_t vidx) {
+        float m = f[0];
+#pragma unroll
+        for (int j = 1; j < N; j++) m = (K == K_ARGMAX) ? fmax_nan(m, f[j]) : fmin_nan(m, f[j]);
+        const bool take = ((K == K_ARGMAX) ? (m > v) : (m < v)) || (m != m && v == v);
+        v = take ? m : v;
+        vi = take ? vidx : vi;
+        raw.x = take ? r.x : raw.x;
+        raw.y = take ? r.y : raw.y;
+        raw.z = take ? r.z : raw.z;
+        raw.w = take ? r.w : raw.w;
+    }
+    template <bool PRE>
+    __device__ __forceinline__ State<float> resolve(const RedParams& p) const {
+        State<float> s;
+        s.v = v;
+        s.i = -1;
+        if (vi < 0) return s;
+        float f[N];
+        Vec<T>::cvt(raw, f);
+        int jj = 0;
+#pragma unroll
+        for (int j = N - 1; j >= 0; j--) {
+            const float x = prep<PRE>(p, f[j]);
+            if (v != v ? x != x : x == v) jj = j;
+        }
+        s.i = vi * N + jj;
+        return s;
+    }
+};
+
 // -------------------------------------------------------------- ROW path --
 
 template <typename T, int K, bool PRE>
@@ -253,6 +276,9 @@ __global__ void __launch_bounds__(THREADS) reduce_row_kernel(const __grid_consta
         State<float> s = init_state<K, float>();
         int64_t done = 0;
         if (vec) {
+            constexpr bool ARG = K == K_ARGMAX || K == K_ARGMIN;
+            ArgVec<K, T, N> av;
+            if constexpr (ARG) av.init();
             const int64_t nv = p.R / N;
             for (int64_t i0 = lane; i0 < nv; i0 += 32 * UNR) {
                 uint4 r[UNR];
@@ -266,10 +292,12 @@ __global__ void __launch_bounds__(THREADS) reduce_row_kernel(const __grid_consta
                         Vec<T>::cvt(r[u], f);
 #pragma unroll
                         for (int j = 0; j < N; j++) f[j] = prep<PRE>(p, f[j]);
-                        update_vec<K, N>(s, f, (i0 + 32 * u) * N);
+                        if constexpr (ARG) av.add(r[u], f, i0 + 32 * u);
+                        else update_vec<K, N>(s, f, (i0 + 32 * u) * N);
                     }
                 }
             }
+            if constexpr (ARG) s = av.template resolve<PRE>(p);
             done = nv * N;
         }
         for (int64_t i = done + lane; i < p.R; i += 32) update<K, float>(s, prep<PRE>(p, ld1(x + i * p.r_stride)), i);
@@ -363,6 +391,9 @@ __global__ void __launch_bounds__(THREADS) reduce_row_split_kernel(const __grid_
     State<float> s = init_state<K, float>();
     int64_t done = r0;
     if (vec) {  // chunk % N == 0, so every chunk starts 16-byte aligned
+        constexpr bool ARG = K == K_ARGMAX || K == K_ARGMIN;
+        ArgVec<K, T, N> av;
+        if constexpr (ARG) av.init();
         const int64_t v0 = r0 / N, v1 = r1 / N;
         for (int64_t i0 = v0 + threadIdx.x; i0 < v1; i0 += THREADS * UNR) {
             uint4 r[UNR];
@@ -376,10 +407,12 @@ __global__ void __launch_bounds__(THREADS) reduce_row_split_kernel(const __grid_
                     Vec<T>::cvt(r[u], f);
 #pragma unroll
                     for (int j = 0; j < N; j++) f[j] = prep<PRE>(p, f[j]);
-                    update_vec<K, N>(s, f, (i0 + THREADS * u) * N);
+                    if constexpr (ARG) av.add(r[u], f, i0 + THREADS * u);
+                    else update_vec<K, N>(s, f, (i0 + THREADS * u) * N);
                 }
             }
         }
+        if constexpr (ARG) s = av.template resolve<PRE>(p);
         done = v1 * N;
     }
     for (int64_t i = done + threadIdx.x; i < r1; i += THREADS) update<K, float>(s, prep<PRE>(p, ld1(x + i * p.r_stride)), i);

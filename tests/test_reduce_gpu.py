@@ -239,3 +239,24 @@ def test_nan_inf_extremes_vector_paths(shape):
         else:
             assert np.array_equal(np.isnan(got), np.isnan(ref)), (op.name, got, ref)
             assert np.array_equal(got[~np.isnan(got)], ref[~np.isnan(ref)]), (op.name, got, ref)
+
+
+@pytest.mark.parametrize("dt", [DType.F16, DType.BF16, DType.F32])
+@pytest.mark.parametrize("pre", [Op.COPY, Op.EXP])
+def test_arg_reductions_16bit_and_preop_vector_path(dt, pre):
+    # 8-element (16-bit) and 4-element (fp32) vectors; ties inside one vector,
+    # across vectors of one lane and across lanes; NaN; the pre-op applied in
+    # the final in-vector search too.
+    x = gen((6, 4096), dt, Dist.UNIFORM, -1, 1, 23)
+    v = {DType.F16: np.float16(4.0).view(np.uint16), DType.BF16: np.uint16(0x4080), DType.F32: np.float32(4.0)}[dt]
+    nan = {DType.F16: np.float16(np.nan).view(np.uint16), DType.BF16: np.uint16(0x7FC0), DType.F32: np.float32(np.nan)}[dt]
+    x[0, [3, 5]] = v            # tie inside one vector -> 3
+    x[1, [2000, 8, 300]] = v    # ties across lanes -> 8
+    x[2, [4095, 1024]] = v      # -> 1024
+    x[3, 77] = nan              # NaN -> 77
+    x[4, [10, 11]] = nan        # first NaN -> 10
+    for op in (Reduce.ARGMAX, Reduce.ARGMIN):
+        got, ref = run_both(op, x, dt, -1, keep=False, pre=pre)
+        assert np.array_equal(got, ref), (op.name, dt, pre, got, ref)
+    got, _ = run_both(Reduce.ARGMAX, x, dt, -1, keep=False, pre=pre)
+    assert list(got[:5]) == [3, 8, 1024, 77, 10]
