@@ -521,38 +521,91 @@ def ref_gpu(cfg, args, stream):
 
 # --------------------------------------------------------------- reference --
 
-def run_reference(args, rank, world):
-    if rank != 0:
-        return
-    if args.config != 2:
-        print(json.dumps({"impl": "reference", "unavailable": "reference arm implemented for the default workload (config 2)"}))
-        return
+def reference_workload(cfg_id):
+    """Host inputs and one step of the reference algorithm (the oracle's C
+    loops, OpenMP over rows) on a bounded sample of config `cfg_id`'s
+    workload, generated with the GPU arm's seeds.  Returns (name, sample
+    description, bytes per step, step function)."""
     import numpy as np
     from oracle import oracle as O
     from tadma_b200.abi import Dist, DType
-    # The inputs come from the oracle's own generator (same values as the GPU arm).
-    rows = 512
-    x = O.fill((rows, Config2.COLS), DType.BF16, Dist.NORMAL, 0.0, 1.0, 0, 1)
-    b = O.fill((Config2.COLS,), DType.BF16, Dist.NORMAL, 0.0, 0.1, 0, 2)
-    y = np.zeros_like(x)
     L = O.lib()
-    per = 2 * rows * Config2.COLS * 2 + Config2.COLS * 2
+    if cfg_id == 2:
+        rows, C = 512, Config2.COLS
+        x = O.fill((rows, C), DType.BF16, Dist.NORMAL, 0.0, 1.0, 0, 1)
+        b = O.fill((C,), DType.BF16, Dist.NORMAL, 0.0, 0.1, 0, 2)
+        y = np.zeros_like(x)
+        return ("cfg2: y = gelu(x*0.5 + bias), x[8192,8192] bf16, bias[8192] bf16 -> bf16",
+                f"{rows} rows of x[8192, 8192] per step", 2 * rows * C * 2 + C * 2,
+                lambda: L.or_cfg2_gelu_affine_bf16(O.ptr(x), O.ptr(b), 0.5, O.ptr(y), rows, C))
+    if cfg_id == 3:
+        rows, C = 1024, 4096
+        x = O.fill((rows, C), DType.F32, Dist.UNIFORM, -1.0, 1.0, 0, 1)
+        s_, a_, m_ = np.zeros(rows, np.float32), np.zeros(rows, np.int64), np.zeros(C, np.float32)
+
+        def step():
+            L.or_cfg3_sum_lastaxis_f32(O.ptr(x), O.ptr(s_), rows, C)
+            L.or_cfg3_max_lastaxis_f32(O.ptr(x), O.ptr(s_), rows, C)
+            L.or_cfg3_argmax_lastaxis_f32(O.ptr(x), O.ptr(a_), rows, C)
+            L.or_cfg3_mean_midaxis_f32(O.ptr(x), O.ptr(m_), 1, rows, C)
+        return ("cfg3: sum/max/argmax over axis -1 + mean over axis 1 of X[32,4096,4096] fp32",
+                f"X[0, :{rows}, :] for all four ops per step", 4 * x.nbytes, step)
+    if cfg_id == 4:
+        xs = O.fill((4096, 1024), DType.F16, Dist.NORMAL, 0.0, 1.0, 0, 1)
+        g = O.fill((1024,), DType.F16, Dist.NORMAL, 1.0, 0.02, 0, 2)
+        bb = O.fill((1024,), DType.F16, Dist.NORMAL, 0.0, 0.02, 0, 3)
+        ss = O.fill((2048, 2048), DType.F16, Dist.NORMAL, 0.0, 3.0, 0, 4)
+        y1, y2 = np.zeros_like(xs), np.zeros_like(ss)
+
+        def step():
+            L.or_cfg4_layer_norm_f16(O.ptr(xs), O.ptr(g), O.ptr(bb), 1e-5, O.ptr(y1), 4096, 1024)
+            L.or_cfg4_softmax_f16(O.ptr(ss), O.ptr(y2), 2048, 2048)
+        return ("cfg4: LayerNorm [64,2048,1024] fp16 + softmax [32,16,2048,2048] fp16 (last axis)",
+                "4096 LayerNorm rows + 2048 softmax rows per step", 2 * (xs.nbytes + ss.nbytes), step)
+    if cfg_id == 5:
+        V, S, D, rows = Config5.V, Config5.S, Config5.D, 4
+        table = O.fill((V, D), DType.F16, Dist.NORMAL, 0.0, 0.02, 0, 1)
+        ids = O.fill((rows, S), DType.I64, Dist.INDEX, 0, V, 0, 2)
+        pos = O.fill((S, D), DType.BF16, Dist.NORMAL, 0.0, 0.02, 0, 3)
+        out = np.zeros((rows, S, D), np.uint16)
+        return ("cfg5: gather table[50257,4096] fp16 by ids[2048,4096] int64 + pos[4096,4096] bf16 -> bf16",
+                f"{rows} batch rows of ids[2048, 4096] per step", rows * S * 8 + rows * S * D * 2 * 2 + S * D * 2,
+                lambda: L.or_cfg5_gather_add(O.ptr(table), V, O.ptr(ids), O.ptr(pos), O.ptr(out), rows, S, D))
+    return None
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the reference's algorithm on the host cores (the
+    reference itself needs clang >= 19 / C++23 and cannot be built here, so
+    its algorithm runs as the oracle's C loops), rank 0 only, on the same
+    metric and workload as the GPU arm, a bounded sample per step."""
+    if rank != 0:
+        return
+    from oracle import oracle as O
+    L = O.lib()
+    # torchrun sets OMP_NUM_THREADS=1 for every rank; this arm runs alone on
+    # rank 0 and may use every host thread it is allowed to run on.
+    L.or_set_num_threads(len(os.sched_getaffinity(0)))
+    wl = reference_workload(args.config)
+    if wl is None:
+        print(json.dumps({"impl": "reference", "unavailable": f"no reference workload for config {args.config}"}))
+        return
+    name, sample, per, step = wl
     for _ in range(args.warmup):
-        L.or_cfg2_gelu_affine_bf16(O.ptr(x), O.ptr(b), 0.5, O.ptr(y), rows, Config2.COLS)
+        step()
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        L.or_cfg2_gelu_affine_bf16(O.ptr(x), O.ptr(b), 0.5, O.ptr(y), rows, Config2.COLS)
+        step()
     el = time.perf_counter() - t0
     v = per * args.steps / el / GB
     cores = L.or_num_threads()
     print(json.dumps({
         "impl": "reference", "metric": "achieved HBM GB/s", "value": round(v, 3), "unit": "GB/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 4),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "cfg2: y = gelu(x*0.5 + bias), x[8192,8192] bf16, bias[8192] bf16 -> bf16",
-                   "sample": f"{rows} rows of x[8192, 8192] per step"},
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": CONFIGS[args.config].dtype,
+        "data": "synthetic", "config": {"workload": name, "sample": sample},
         "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": cores, "kind": "port",
-                         "sample": f"{rows} rows of x[8192, 8192] per step, {args.steps} steps"},
+                         "sample": f"{sample}, {args.steps} steps"},
         "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "reference (OgnianM/TADMA) needs clang>=19/C++23 and cannot be built here; its algorithm runs as the "
                 "oracle's host C loop (oracle/tadma_oracle.c, OpenMP)",
