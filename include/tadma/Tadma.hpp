@@ -3,6 +3,7 @@
 // Link with -L<repo>/tadma_b200 -ltadma_b200 (libtadma_b200.so, sm_100a).
 #pragma once
 
+#include "Constexpr.hpp"
 #include "Core.hpp"
 #include "Operations.hpp"
 #include "Sequence.hpp"

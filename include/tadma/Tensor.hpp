@@ -107,6 +107,20 @@ consteval auto broadcast_strides_arr() {
     return out;
 }
 
+// Values of one reshape<...> argument: an integer, or a compile-time shape
+// value whose type carries them (Vals::Arr of a ConstTensor, value of a holder).
+template <auto X>
+consteval auto shape_arg_values() {
+    using XT = std::remove_cvref_t<decltype(X)>;  // a class-type template argument is const
+    if constexpr (requires { XT::Vals::Arr; }) return XT::Vals::Arr;
+    else if constexpr (requires { XT::value; }) return std::array<int64_t, 1>{static_cast<int64_t>(XT::value)};
+    else return std::array<int64_t, 1>{static_cast<int64_t>(X)};
+}
+template <auto X>
+consteval std::size_t shape_arg_size() {
+    return shape_arg_values<X>().size();
+}
+
 template <typename Dims, int... P>
 consteval auto permute_arr(const std::array<int64_t, Dims::Size>& src) {
     std::array<int64_t, Dims::Size> out{};
@@ -310,6 +324,11 @@ struct Tensor {
     auto broadcastTo(const U&) const {
         return this->template broadcastTo<typename U::Dims>();
     }
+    // broadcastTo<TYPE(t)>(): the target given as a tensor type (generated code's Expand).
+    template <AnyTensor U>
+    auto broadcastTo() const {
+        return this->template broadcastTo<typename std::decay_t<U>::Dims>();
+    }
 
     // reshape<Sequence<...>> / reshape<d0, d1, ...> (Tensor.hpp:366-380); one
     // -1 is inferred; a non-contiguous view is materialised first (clone).
@@ -335,10 +354,25 @@ struct Tensor {
             return Tensor<T, Allocator, D>(data);
         }
     }
-    template <int64_t... NewDims>
+    // reshape<d0, d1, ...>, or reshape<shape> with one compile-time shape value
+    // (a ConstexprHolder or ConstTensor of Constexpr.hpp, as generated code
+    // passes the output of its shape arithmetic).  ONNX Reshape rules: 0
+    // copies the input dim at that position, one -1 is inferred.
+    template <auto... NewDims>
         requires(sizeof...(NewDims) > 0)
     auto reshape() const {
-        return this->template reshape<Sequence<NewDims...>>();
+        constexpr auto req = [] {
+            std::array<int64_t, (shape_arg_size<NewDims>() + ...)> r{};
+            std::size_t k = 0;
+            ((([&] {
+                 for (auto v : shape_arg_values<NewDims>()) r[k++] = v;
+             })()),
+             ...);
+            for (std::size_t i = 0; i < r.size(); i++)
+                if (r[i] == 0 && (int64_t)i < Rank) r[i] = Dims::Arr[i];
+            return r;
+        }();
+        return this->template reshape<SeqFromArray<req>>();
     }
 
     // index<Axis>(i): drop Axis at position i (Tensor.hpp:183-187).

@@ -18,6 +18,45 @@ using ALLOCATOR = Allocator<kCUDA>;
 
 static std::string g_dir;
 
+// The embedding prologue of a generated BERT-style graph, written the way the
+// generator writes it: constants are types (ConstexprHolder, a
+// ConstexprAllocator position table), the Shape / Gather / Unsqueeze / Concat
+// / Mul / Equal / Where arithmetic on shapes folds at compile time, and only
+// the tensor work launches kernels.
+struct GraphPrologue {
+    static constexpr ConstexprHolder<1> c_one = {};
+    static constexpr ConstexprHolder<0> c_zero = {};
+    static constexpr ConstexprHolder<-1> c_minus1 = {};
+    static constexpr ConstexprHolder<2.0> c_two = {};
+    using position_seq = Sequence<0, 1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12, 13, 14, 15>;
+    Tensor<TYPE(position_seq::Array()[0]), ConstexprAllocator<position_seq>, Sequence<16>> position_ids = {};
+    Tensor<float, Allocator<kCUDA>, Sequence<16, 32>> position_table;
+
+    template <int64_t B, int64_t S>
+    auto infer(const Tensor<int64_t, Allocator<kCUDA>, Sequence<B, S>>& input_ids,
+               const Tensor<float, Allocator<kCUDA>, Sequence<100, 32>>& word_table) {
+        auto shp = shape(input_ids);                      // [B, S]
+        auto seq = gather(shp, c_one);                    // S
+        auto seq1 = seq.template unsqueeze<c_zero>();     // [S]
+        constexpr int64_t seq_len = seq1;
+        static_assert(seq_len == S);
+        auto pid = position_ids.template slice<c_zero, seq1, 0, c_one>();  // the first S positions
+        auto word = gather(word_table, input_ids);        // [B, S, 32]
+        auto pos = gather(position_table, pid);           // [S, 32]
+        auto emb = word + pos;                            // [B, S, 32]
+        auto new_shape = concat<0>(gather(shp, c_zero), c_minus1);  // [B, -1]
+        auto flat = emb.template reshape<new_shape>();    // [B, S * 32]
+        static_assert(decltype(flat)::Dim(0) == B && decltype(flat)::Dim(1) == S * 32);
+        auto dims = shp * c_one;                          // [B, S]
+        auto is_unknown = dims == c_minus1;               // [false, false]
+        auto fixed = where(is_unknown, c_one, dims);      // [B, S]
+        static_assert(decltype(fixed)::at(0) == B && decltype(fixed)::at(1) == S);
+        static_assert(decltype(c_two * c_two)::value == 4.0);
+        auto expanded = pos.template broadcastTo<TYPE(emb)>().contiguous();  // Expand to [B, S, 32]
+        return std::make_tuple(pid.contiguous(), flat, expanded);
+    }
+};
+
 template <AnyTensor T>
 void fill(const T& t, int dist, double p0, double p1, uint64_t sid) {
     tadma_tensor d = t.describe();
@@ -134,6 +173,20 @@ int main(int argc, char** argv) {
     save("cast_f16", X.template to<__half>());
     auto un = b.template unsqueeze<0>();  // [1, 128]
     save("unsqueeze_bcast_add", A + un);
+
+    // generated-graph shape arithmetic (GraphPrologue above)
+    GraphPrologue graph;
+    fill(graph.position_table, TADMA_DIST_NORMAL, 0.0, 1.0, 15);
+    Tensor<float, ALLOCATOR, Sequence<100, 32>> word_table;
+    // infer() deduces <B, S> as int64_t, so the dims are spelled as int64_t values
+    Tensor<int64_t, ALLOCATOR, Sequence<int64_t(2), int64_t(12)>> input_ids;
+    fill(word_table, TADMA_DIST_NORMAL, 0.0, 1.0, 14);
+    fill(input_ids, TADMA_DIST_INDEX, 0.0, 100.0, 16);
+    auto [pid, flat, expanded] = graph.infer(input_ids, word_table);
+    save("gen_position_ids", pid);
+    save("gen_embed_flat", flat);
+    save("gen_expand", expanded);
+    std::cout << "shape " << shape(input_ids) << " seq " << gather(shape(input_ids), GraphPrologue::c_one) << "\n";
 
     check_cuda(cudaStreamSynchronize(stream));
     std::printf("conformance ok\n");

@@ -113,3 +113,16 @@ def test_views_and_copies(results):
     A = gen((64, 128), DType.F32, Dist.NORMAL, 0.0, 1.0, 1)
     b = gen((128,), DType.F32, Dist.NORMAL, 0.0, 1.0, 2)
     assert np.array_equal(results("unsqueeze_bcast_add", np.float32, (64, 128)), A + b[None, :])
+
+
+def test_generated_shape_arithmetic(results):
+    # GraphPrologue in tests/cpp/conformance.cu: position ids sliced from a
+    # ConstexprAllocator constant by a shape computed at compile time, word +
+    # position embeddings, Reshape by a concatenated shape, Expand by type.
+    word = gen((100, 32), DType.F32, Dist.NORMAL, 0.0, 1.0, 14)
+    pos = gen((16, 32), DType.F32, Dist.NORMAL, 0.0, 1.0, 15)
+    ids = gen((2, 12), DType.I64, Dist.INDEX, 0, 100, 16)
+    assert np.array_equal(results("gen_position_ids", np.int64, (12,)), np.arange(12))
+    emb = (word[ids] + pos[:12][None]).astype(np.float32)
+    assert np.array_equal(results("gen_embed_flat", np.float32, (2, 12 * 32)), emb.reshape(2, -1))
+    assert np.array_equal(results("gen_expand", np.float32, (2, 12, 32)), np.broadcast_to(pos[:12], (2, 12, 32)))
