@@ -150,7 +150,6 @@ class Config2:
     """y = gelu(x * 0.5 + bias), x[8192, 8192] bf16, bias[8192] bf16, y bf16."""
     ROWS, COLS = 8192, 8192
     dtype = "bf16"
-    kernel = "affine_rows_kernel"
 
     def __init__(self, rank, batch=0):
         self.ROWS = batch or Config2.ROWS
@@ -270,7 +269,6 @@ def torch_int16():
 class Config3:
     """sum / max / argmax over the last axis and mean over the middle axis of X[32, 4096, 4096] fp32."""
     dtype = "f32"
-    kernel = "reduce_row_kernel"
 
     def __init__(self, rank, batch=0):
         import torch
@@ -326,7 +324,6 @@ class Config3:
 class Config4:
     """LayerNorm over the last axis of [64, 2048, 1024] fp16 + softmax over the last axis of [32, 16, 2048, 2048] fp16."""
     dtype = "f16"
-    kernel = "rownorm_warp_kernel"
 
     def __init__(self, rank, batch=0):
         import torch
@@ -382,7 +379,6 @@ class Config4:
 class Config5:
     """Embedding gather: table [50257, 4096] fp16, ids [2048, 4096] int64, + pos [4096, 4096] bf16 -> bf16."""
     dtype = "f16/bf16"
-    kernel = "gather_rows_kernel"
     V, B, S, D = 50257, 2048, 4096, 4096
 
     def __init__(self, rank, batch=0):
