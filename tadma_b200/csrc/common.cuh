@@ -16,6 +16,7 @@
 #include <stdint.h>
 
 #include <string>
+#include <utility>
 
 #include "../../include/tadma_b200.h"
 
@@ -297,6 +298,17 @@ __device__ __forceinline__ T warp_max(T v) {
     return v;
 }
 
+// Programmatic dependent launch (sm_90+).  A kernel launched with
+// launch_pdl() may be scheduled while the previous kernel of its stream is
+// still running: it lets its own dependents launch at once
+// (griddepcontrol.launch_dependents) and waits for the previous grid to
+// complete and flush its writes (griddepcontrol.wait) before it touches
+// global memory.  Launched normally, both instructions are no-ops.
+__device__ __forceinline__ void pdl_begin() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 // 2^x on the SFU (ex2.approx.ftz: max relative error ~2^-22).
 __device__ __forceinline__ float ex2_approx(float x) {
     float y;
@@ -344,6 +356,25 @@ __device__ __forceinline__ float fmin_nan(float a, float b) {
 }
 
 // ------------------------------------------------------------- host side --
+
+// Launches kernel<<<grid, block, smem, stream>>>(args...) with programmatic
+// stream serialisation, so its CTAs can be scheduled during the previous
+// kernel's tail; the kernel must call pdl_begin() before any global access.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // Per-thread last error message (tadma_b200_last_error).
 void set_error(const std::string& msg);

@@ -346,6 +346,7 @@ __device__ __forceinline__ void offsets(const ChainParams& p, uint64_t e, int64_
 
 template <typename C, int NIN, int PROG>
 __global__ void __launch_bounds__(THREADS) chain_vec_kernel(const __grid_constant__ ChainParams p) {
+    pdl_begin();
     constexpr int NI = NIN > 0 ? NIN : 1;
     const int64_t gstride = (int64_t)gridDim.x * THREADS;
     for (int64_t base = (int64_t)blockIdx.x * THREADS + threadIdx.x; base < p.n; base += gstride * U) {
@@ -377,6 +378,7 @@ __global__ void __launch_bounds__(THREADS) chain_vec_kernel(const __grid_constan
 
 template <typename C, int NIN, int PROG>
 __global__ void __launch_bounds__(THREADS) chain_scalar_kernel(const __grid_constant__ ChainParams p) {
+    pdl_begin();
     constexpr int NI = NIN > 0 ? NIN : 1;
     const int64_t gstride = (int64_t)gridDim.x * THREADS;
     for (int64_t e = p.start + (int64_t)blockIdx.x * THREADS + threadIdx.x; e < p.n; e += gstride) {
@@ -480,6 +482,7 @@ __device__ __forceinline__ void affine_row_compute(const Raw8x<XT>& raw, const f
 
 template <typename XT, typename OT, int ACT>
 __global__ void __launch_bounds__(THREADS, sizeof(XT) == 2 ? 3 : 2) affine_rows_kernel(const __grid_constant__ AffineRowsParams p) {
+    pdl_begin();
     // Double-buffered over rows: the next UR rows' loads are in flight while
     // the current UR rows compute and store.
     constexpr int UR = 4;
@@ -542,6 +545,7 @@ struct TransposeParams {
 
 template <int PROG>
 __global__ void __launch_bounds__(THREADS) transpose_chain_kernel(const __grid_constant__ TransposeParams tp) {
+    pdl_begin();
     __shared__ float tile[32][33];
     const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8 threads
     const int64_t i0 = (int64_t)blockIdx.y * 32, j0 = (int64_t)blockIdx.x * 32;
@@ -600,8 +604,8 @@ int launch(const ChainParams& p, bool vec, int64_t work, cudaStream_t s) {
     int64_t want = (work + per_block - 1) / per_block;
     int64_t cap = (int64_t)sm_count() * blocks_per_sm(fn);
     int grid = (int)(want < cap ? (want > 0 ? want : 1) : cap);
-    if (vec) chain_vec_kernel<C, NIN, PROG><<<grid, THREADS, 0, s>>>(p);
-    else chain_scalar_kernel<C, NIN, PROG><<<grid, THREADS, 0, s>>>(p);
+    if (vec) (void)launch_pdl(chain_vec_kernel<C, NIN, PROG>, dim3(grid), dim3(THREADS), 0, s, p);
+    else (void)launch_pdl(chain_scalar_kernel<C, NIN, PROG>, dim3(grid), dim3(THREADS), 0, s, p);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? TADMA_OK : cuda_fail(e, "tadma_b200_eltwise launch");
 }
@@ -697,8 +701,8 @@ int launch_rows_t(const AffineRowsParams& p, cudaStream_t s) {
     if (gy > 65535) gy = 65535;
     if (gy < 1) gy = 1;
     if (gx > 0x7fffffff) return fail(TADMA_ERR_UNSUPPORTED, "eltwise: too many column vectors");
-    affine_rows_kernel<XT, OT, ACT><<<dim3((unsigned)gx, (unsigned)gy), THREADS, 0, s>>>(p);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_pdl(affine_rows_kernel<XT, OT, ACT>, dim3((unsigned)gx, (unsigned)gy), dim3(THREADS), 0, s, p);
+    if (e == cudaSuccess) e = cudaGetLastError();
     return e == cudaSuccess ? TADMA_OK : cuda_fail(e, "tadma_b200_eltwise launch");
 }
 
@@ -726,8 +730,8 @@ int launch_transpose(bool fast, const TransposeParams& tp, cudaStream_t s) {
     const int64_t gx = (tp.n_j + 31) / 32, gy = (tp.n_i + 31) / 32;
     const int64_t gz = tp.nbatch < 65535 ? tp.nbatch : 65535;
     dim3 grid((unsigned)gx, (unsigned)gy, (unsigned)(gz > 0 ? gz : 1));
-    if (fast) transpose_chain_kernel<PROG_INTERP_FAST><<<grid, THREADS, 0, s>>>(tp);
-    else transpose_chain_kernel<PROG_INTERP><<<grid, THREADS, 0, s>>>(tp);
+    if (fast) (void)launch_pdl(transpose_chain_kernel<PROG_INTERP_FAST>, dim3(grid), dim3(THREADS), 0, s, tp);
+    else (void)launch_pdl(transpose_chain_kernel<PROG_INTERP>, dim3(grid), dim3(THREADS), 0, s, tp);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? TADMA_OK : cuda_fail(e, "tadma_b200_eltwise launch");
 }

@@ -43,6 +43,7 @@ struct FillParams {
 };
 
 __global__ void __launch_bounds__(THREADS) fill_kernel(const __grid_constant__ FillParams p) {
+    pdl_begin();
     const int64_t stride = (int64_t)gridDim.x * THREADS;
     for (int64_t i = (int64_t)blockIdx.x * THREADS + threadIdx.x; i < p.n; i += stride) {
         int64_t off = i;
@@ -122,7 +123,7 @@ extern "C" int tadma_b200_fill(const tadma_tensor* out, int32_t dist, double p0,
     int64_t want = (n + THREADS - 1) / THREADS;
     int64_t cap = (int64_t)sm_count() * 8;
     int grid = (int)(want < cap ? want : cap);
-    fill_kernel<<<grid, THREADS, 0, (cudaStream_t)stream>>>(p);
+    (void)launch_pdl(fill_kernel, dim3(grid), dim3(THREADS), 0, (cudaStream_t)stream, p);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? TADMA_OK : cuda_fail(e, "tadma_b200_fill launch");
 }

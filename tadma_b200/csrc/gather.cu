@@ -103,6 +103,7 @@ __device__ __forceinline__ int64_t load_id(const char* ids, int dt, int64_t off)
 
 template <typename TT, typename AT, typename OT, bool ADD>
 __global__ void __launch_bounds__(THREADS) gather_rows_kernel(const __grid_constant__ GatherParams p) {
+    pdl_begin();
     constexpr int UNR = 4;
     const int lane = threadIdx.x & 31;
     const int64_t gw = ((int64_t)blockIdx.x * THREADS + threadIdx.x) >> 5;
@@ -183,6 +184,7 @@ __global__ void __launch_bounds__(THREADS) gather_rows_kernel(const __grid_const
 }
 
 __global__ void __launch_bounds__(THREADS) gather_generic_kernel(const __grid_constant__ GatherParams p) {
+    pdl_begin();
     const int64_t stride = (int64_t)gridDim.x * THREADS;
     for (int64_t e0 = (int64_t)blockIdx.x * THREADS + threadIdx.x; e0 < p.total; e0 += stride) {
         int64_t idx[TADMA_MAX_RANK];
@@ -236,7 +238,7 @@ int launch_rows(const GatherParams& p, cudaStream_t s) {
     int64_t want = (p.nrows + (THREADS / 32) - 1) / (THREADS / 32);
     int64_t cap = (int64_t)sm_count() * blocks_per_sm(fn);
     int grid = (int)(want < cap ? (want > 0 ? want : 1) : cap);
-    gather_rows_kernel<TT, AT, OT, ADD><<<grid, THREADS, 0, s>>>(p);
+    (void)launch_pdl(gather_rows_kernel<TT, AT, OT, ADD>, dim3(grid), dim3(THREADS), 0, s, p);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? TADMA_OK : cuda_fail(e, "tadma_b200_gather launch");
 }
@@ -380,7 +382,7 @@ extern "C" int tadma_b200_gather(const tadma_tensor* table, int32_t axis, const 
     int64_t cap = (int64_t)sm_count() * blocks_per_sm((const void*)gather_generic_kernel);
     int64_t want = (p.total + THREADS - 1) / THREADS;
     int grid = (int)(want < cap ? want : cap);
-    gather_generic_kernel<<<grid, THREADS, 0, s>>>(p);
+    (void)launch_pdl(gather_generic_kernel, dim3(grid), dim3(THREADS), 0, s, p);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? TADMA_OK : cuda_fail(e, "tadma_b200_gather launch");
 }

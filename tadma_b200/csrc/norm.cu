@@ -350,6 +350,7 @@ constexpr int norm_min_blocks() {
 }
 template <typename T, int CH, int MODE>
 __global__ void __launch_bounds__(THREADS, norm_min_blocks<T, CH>()) rownorm_warp_kernel(const __grid_constant__ NormParams p) {
+    pdl_begin();
     constexpr int N = VecT<T>::N;
     const int lane = threadIdx.x & 31;
     const int64_t gw = ((int64_t)blockIdx.x * THREADS + threadIdx.x) >> 5;
@@ -386,6 +387,7 @@ __device__ __forceinline__ float block_reduce(float v, bool is_max, float* sh) {
 }
 
 __global__ void __launch_bounds__(THREADS) rownorm_block_kernel(const __grid_constant__ NormParams p) {
+    pdl_begin();
     __shared__ float sh[THREADS / 32];
     for (int64_t row = blockIdx.x; row < p.nrows; row += gridDim.x) {
         uint64_t e = (uint64_t)row;
@@ -463,7 +465,7 @@ int launch_warp(const NormParams& p, cudaStream_t s) {
     int64_t want = (p.nrows + (THREADS / 32) - 1) / (THREADS / 32);
     int64_t cap = (int64_t)sm_count() * blocks_per_sm(fn);
     int grid = (int)(want < cap ? (want > 0 ? want : 1) : cap);
-    rownorm_warp_kernel<T, CH, MODE><<<grid, THREADS, 0, s>>>(p);
+    (void)launch_pdl(rownorm_warp_kernel<T, CH, MODE>, dim3(grid), dim3(THREADS), 0, s, p);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? TADMA_OK : cuda_fail(e, "row-norm launch");
 }
@@ -579,7 +581,7 @@ int run_rownorm(int mode, const tadma_tensor* in, int32_t axis, const tadma_tens
     }
     int64_t cap_blocks = (int64_t)sm_count() * blocks_per_sm((const void*)rownorm_block_kernel);
     int grid = (int)(p.nrows < cap_blocks ? p.nrows : cap_blocks);
-    rownorm_block_kernel<<<grid, THREADS, 0, s>>>(p);
+    (void)launch_pdl(rownorm_block_kernel, dim3(grid), dim3(THREADS), 0, s, p);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? TADMA_OK : cuda_fail(e, "row-norm launch");
 }

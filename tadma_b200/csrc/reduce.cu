@@ -266,6 +266,7 @@ struct ArgVec {
 
 template <typename T, int K, bool PRE>
 __global__ void __launch_bounds__(THREADS) reduce_row_kernel(const __grid_constant__ RedParams p, int vec) {
+    pdl_begin();
     constexpr int N = Vec<T>::N;
     constexpr int UNR = 4;
     const int lane = threadIdx.x & 31;
@@ -310,6 +311,7 @@ __global__ void __launch_bounds__(THREADS) reduce_row_kernel(const __grid_consta
 
 template <typename T, int K, int VEC, bool SPLIT, bool PRE>
 __global__ void __launch_bounds__(THREADS) reduce_col_kernel(const __grid_constant__ RedParams p) {
+    pdl_begin();
     constexpr int COLS = 32 * VEC;
     __shared__ State<float> part[WARPS][COLS];
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
@@ -380,6 +382,7 @@ __global__ void __launch_bounds__(THREADS) reduce_col_kernel(const __grid_consta
 
 template <typename T, int K, bool PRE>
 __global__ void __launch_bounds__(THREADS) reduce_row_split_kernel(const __grid_constant__ RedParams p, int vec) {
+    pdl_begin();
     constexpr int N = Vec<T>::N;
     constexpr int UNR = 4;
     __shared__ State<float> sh[WARPS];
@@ -430,6 +433,7 @@ __global__ void __launch_bounds__(THREADS) reduce_row_split_kernel(const __grid_
 // Pass 2 of the ROW split: one warp per output row.
 template <int K>
 __global__ void __launch_bounds__(THREADS) reduce_row_finish_kernel(const __grid_constant__ RedParams p) {
+    pdl_begin();
     const int lane = threadIdx.x & 31;
     const int64_t gw = ((int64_t)blockIdx.x * THREADS + threadIdx.x) >> 5;
     const int64_t nw = ((int64_t)gridDim.x * THREADS) >> 5;
@@ -445,6 +449,7 @@ __global__ void __launch_bounds__(THREADS) reduce_row_finish_kernel(const __grid
 // Pass 2 of the COL split: one thread per output column of an outer index.
 template <int K>
 __global__ void __launch_bounds__(THREADS) reduce_col_finish_kernel(const __grid_constant__ RedParams p) {
+    pdl_begin();
     const State<float>* part = reinterpret_cast<const State<float>*>(p.partials);
     const int64_t total = p.nrows * p.inner;
     for (int64_t idx = (int64_t)blockIdx.x * THREADS + threadIdx.x; idx < total; idx += (int64_t)gridDim.x * THREADS) {
@@ -459,6 +464,7 @@ __global__ void __launch_bounds__(THREADS) reduce_col_finish_kernel(const __grid
 
 template <typename A, int K>
 __global__ void __launch_bounds__(THREADS) reduce_generic_kernel(const __grid_constant__ RedParams p) {
+    pdl_begin();
     const int lane = threadIdx.x & 31;
     const int64_t gw = ((int64_t)blockIdx.x * THREADS + threadIdx.x) >> 5;
     const int64_t nw = ((int64_t)gridDim.x * THREADS) >> 5;
@@ -510,13 +516,13 @@ template <typename T, int K, bool PRE>
 int launch_fast(int path, const RedParams& p, bool vec, cudaStream_t s) {
     if (path == 0) {
         if (p.splits > 1) {
-            reduce_row_split_kernel<T, K, PRE><<<dim3((unsigned)p.splits, (unsigned)p.nrows), THREADS, 0, s>>>(p, vec ? 1 : 0);
+            (void)launch_pdl(reduce_row_split_kernel<T, K, PRE>, dim3(dim3((unsigned)p.splits, (unsigned)p.nrows)), dim3(THREADS), 0, s, p, vec ? 1 : 0);
             const void* fn = (const void*)reduce_row_finish_kernel<K>;
-            reduce_row_finish_kernel<K><<<grid_for(fn, (p.nrows + WARPS - 1) / WARPS), THREADS, 0, s>>>(p);
+            (void)launch_pdl(reduce_row_finish_kernel<K>, dim3(grid_for(fn, (p.nrows + WARPS - 1) / WARPS)), dim3(THREADS), 0, s, p);
         } else {
             const void* fn = (const void*)reduce_row_kernel<T, K, PRE>;
             int grid = grid_for(fn, (p.nrows + WARPS - 1) / WARPS);
-            reduce_row_kernel<T, K, PRE><<<grid, THREADS, 0, s>>>(p, vec ? 1 : 0);
+            (void)launch_pdl(reduce_row_kernel<T, K, PRE>, dim3(grid), dim3(THREADS), 0, s, p, vec ? 1 : 0);
         }
     } else {
         constexpr int VEC = Vec<T>::N;
@@ -524,13 +530,13 @@ int launch_fast(int path, const RedParams& p, bool vec, cudaStream_t s) {
         if (tiles > 0x7fffffff) return fail(TADMA_ERR_UNSUPPORTED, "reduce: too many column tiles");
         dim3 grid((unsigned)tiles, (unsigned)(p.nrows < 65535 ? p.nrows : 65535), (unsigned)(p.splits > 1 ? p.splits : 1));
         if (p.splits > 1) {
-            if (vec) reduce_col_kernel<T, K, VEC, true, PRE><<<grid, THREADS, 0, s>>>(p);
-            else reduce_col_kernel<T, K, 1, true, PRE><<<grid, THREADS, 0, s>>>(p);
+            if (vec) (void)launch_pdl(reduce_col_kernel<T, K, VEC, true, PRE>, dim3(grid), dim3(THREADS), 0, s, p);
+            else (void)launch_pdl(reduce_col_kernel<T, K, 1, true, PRE>, dim3(grid), dim3(THREADS), 0, s, p);
             const void* fn = (const void*)reduce_col_finish_kernel<K>;
-            reduce_col_finish_kernel<K><<<grid_for(fn, (p.nrows * p.inner + THREADS - 1) / THREADS), THREADS, 0, s>>>(p);
+            (void)launch_pdl(reduce_col_finish_kernel<K>, dim3(grid_for(fn, (p.nrows * p.inner + THREADS - 1) / THREADS)), dim3(THREADS), 0, s, p);
         } else {
-            if (vec) reduce_col_kernel<T, K, VEC, false, PRE><<<grid, THREADS, 0, s>>>(p);
-            else reduce_col_kernel<T, K, 1, false, PRE><<<grid, THREADS, 0, s>>>(p);
+            if (vec) (void)launch_pdl(reduce_col_kernel<T, K, VEC, false, PRE>, dim3(grid), dim3(THREADS), 0, s, p);
+            else (void)launch_pdl(reduce_col_kernel<T, K, 1, false, PRE>, dim3(grid), dim3(THREADS), 0, s, p);
         }
     }
     cudaError_t e = cudaGetLastError();
@@ -566,11 +572,11 @@ int launch_generic(int kind, const RedParams& p, cudaStream_t s) {
     }
     int grid = grid_for(fn, (p.nrows + WARPS - 1) / WARPS);
     switch (kind) {
-    case K_SUM: reduce_generic_kernel<A, K_SUM><<<grid, THREADS, 0, s>>>(p); break;
-    case K_MAX: reduce_generic_kernel<A, K_MAX><<<grid, THREADS, 0, s>>>(p); break;
-    case K_MIN: reduce_generic_kernel<A, K_MIN><<<grid, THREADS, 0, s>>>(p); break;
-    case K_ARGMAX: reduce_generic_kernel<A, K_ARGMAX><<<grid, THREADS, 0, s>>>(p); break;
-    default: reduce_generic_kernel<A, K_ARGMIN><<<grid, THREADS, 0, s>>>(p); break;
+    case K_SUM: (void)launch_pdl(reduce_generic_kernel<A, K_SUM>, dim3(grid), dim3(THREADS), 0, s, p); break;
+    case K_MAX: (void)launch_pdl(reduce_generic_kernel<A, K_MAX>, dim3(grid), dim3(THREADS), 0, s, p); break;
+    case K_MIN: (void)launch_pdl(reduce_generic_kernel<A, K_MIN>, dim3(grid), dim3(THREADS), 0, s, p); break;
+    case K_ARGMAX: (void)launch_pdl(reduce_generic_kernel<A, K_ARGMAX>, dim3(grid), dim3(THREADS), 0, s, p); break;
+    default: (void)launch_pdl(reduce_generic_kernel<A, K_ARGMIN>, dim3(grid), dim3(THREADS), 0, s, p); break;
     }
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? TADMA_OK : cuda_fail(e, "tadma_b200_reduce launch");
