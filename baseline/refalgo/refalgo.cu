@@ -136,6 +136,20 @@ __global__ void gather_kernel(const __half* table, const int64_t* ids, __half* o
 
 extern "C" {
 
+// config 1: t = A + b (float node), exp<true>(t) in place, sum<-1>(t) through
+// ReduceKernel<128>.  A [64, 128], b [128] fp32 -> y [64].
+int ref_cfg1(const void* A, const void* b, void* t, void* y, void* stream) {
+    constexpr int64_t R = 64, C = 128;
+    cudaStream_t s = (cudaStream_t)stream;
+    const float* ap = (const float*)A;
+    const float* bp = (const float*)b;
+    float* tp = (float*)t;
+    exec2<R, C>([=] __device__(int64_t i, int64_t j) { tp[i * C + j] = ap[i * C + j] + bp[j]; }, s);
+    exec2<R, C>([=] __device__(int64_t i, int64_t j) { tp[i * C + j] = expf(tp[i * C + j]); }, s);
+    reduce<float, float, 0>(tp, (float*)y, R, C, 1, R, C, 0, 1, 0, nullptr, 0, s);
+    return (int)cudaGetLastError();
+}
+
 // config 2: t1 = x * 0.5f; t2 = t1 + bias; gelu<true>(t2).  x, bias bf16; t1, t2 fp32 [8192, 8192].
 int ref_cfg2(const void* x, const void* bias, void* t1, void* t2, void* stream) {
     constexpr int64_t R = 8192, C = 8192;

@@ -44,7 +44,7 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4, 5])
+    ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4, 5])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="budget of the CPU-baseline sample")
     ap.add_argument("--e2e-steps", type=int, default=20)
@@ -145,6 +145,76 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------- configs --
+
+class Config1:
+    """y = sum_{last}(exp(A + b)), A[64, 128] fp32, b[128] fp32 -> y[64]: a
+    launch-bound correctness config.  One step = the element-wise chain
+    t = A + b and the row sum with exp as its pre-op, two prepared C-ABI calls
+    captured once into a CUDA graph and replayed (the eager two-launch step is
+    timed beside it as a part)."""
+    dtype = "f32"
+
+    def __init__(self, rank, batch=0):
+        import torch
+        import tadma_b200 as tb
+        from tadma_b200.abi import Compute, Dist, DType, Op, Reduce, instr, make_tensor
+        R = batch or 64
+        self.name = f"cfg1: y = sum_last(exp(A + b)), A[{R},128] fp32, b[128] fp32 -> [{R}] (CUDA graph of 2 calls)"
+        self.A = torch.empty((R, 128), dtype=torch.float32, device="cuda")
+        self.b = torch.empty((128,), dtype=torch.float32, device="cuda")
+        tb.fill(self.A, Dist.NORMAL, 0.0, 1.0, 0, 1, offset=rank * R * 128)
+        tb.fill(self.b, Dist.NORMAL, 0.0, 1.0, 0, 2)
+        self.t = torch.empty_like(self.A)
+        self.y = torch.empty((R,), dtype=torch.float32, device="cuda")
+        bv = make_tensor(self.b.data_ptr(), DType.F32, [R, 128], [0, 1])
+        self.side = torch.cuda.Stream()
+        prog = [instr(Op.ADD, b=1)]
+
+        def calls(st):
+            return [tb.prepare_eltwise(self.t, [self.A, bv], prog, Compute.F32, stream=st),
+                    tb.prepare_reduce(Reduce.SUM, self.t.view(R, 128), -1, self.y.view(R, 1), Op.EXP, stream=st)]
+        self.eager = calls(None)
+        cap = calls(self.side)
+        self.side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(self.side):
+            for c in cap:
+                c()
+        self.side.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=self.side):
+            for c in cap:
+                c()
+        torch.cuda.synchronize()
+        self.bytes = R * 128 * 4 + 128 * 4 + R * 4
+        self.launches = 2
+        self.units = R
+
+    def step(self):
+        self.graph.replay()
+
+    def eager_step(self):
+        for c in self.eager:
+            c()
+
+    def parts(self):
+        return [("chain_vec_kernel + reduce_row_kernel", "CUDA graph replay (2 kernels)", self.bytes, self.step),
+                ("chain_vec_kernel + reduce_row_kernel", "eager, 2 launches", self.bytes, self.eager_step)]
+
+    def cpu_sample(self, budget_s):
+        import numpy as np
+        from oracle import oracle as O
+        from tadma_b200.abi import Op, Reduce
+        A = self.A.cpu().numpy()
+        b = self.b.cpu().numpy()
+        y = np.zeros((A.shape[0], 1), np.float32)
+        done, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < budget_s:
+            t = (A + b).astype(np.float32)
+            O.reduce(Reduce.SUM, t, -1, y, Op.EXP)
+            done += 1
+        el = time.perf_counter() - t0
+        return done * self.bytes / el / GB, 1, f"{done} x the whole step (numpy add + oracle exp-sum, 1 thread)"
+
 
 class Config2:
     """y = gelu(x * 0.5 + bias), x[8192, 8192] bf16, bias[8192] bf16, y bf16."""
@@ -428,7 +498,7 @@ class Config5:
         return done * per / el / GB, L.or_num_threads(), f"{done} x {rows} batch rows of ids[2048, 4096]"
 
 
-CONFIGS = {2: Config2, 3: Config3, 4: Config4, 5: Config5}
+CONFIGS = {1: Config1, 2: Config2, 3: Config3, 4: Config4, 5: Config5}
 
 # ------------------------------------------------- reference GPU algorithm --
 
@@ -462,7 +532,15 @@ def ref_gpu(cfg, args, stream):
     st = ctypes.c_void_p(stream.cuda_stream)
     P = lambda t: ctypes.c_void_p(t.data_ptr())
     steps = max(3, min(args.steps, 20))
-    if isinstance(cfg, Config2):
+    if isinstance(cfg, Config1):
+        if cfg.A.shape[0] != 64:
+            return {"unavailable": "restated for the A[64, 128] workload only"}
+        t = torch.empty_like(cfg.A)
+        y = torch.empty((64,), dtype=torch.float32, device="cuda")
+        sec = time_steps(lambda: L.ref_cfg1(P(cfg.A), P(cfg.b), P(t), P(y), st), steps, 2, stream)
+        nbytes, launches = cfg.bytes, 3
+        note = "A + b node, exp<true> node, sum<-1> through ReduceKernel<128>: 3 launches"
+    elif isinstance(cfg, Config2):
         if cfg.ROWS != 8192:
             return {"unavailable": "restated for the full [8192, 8192] workload only"}
         t1 = torch.empty((8192, 8192), dtype=torch.float32, device="cuda")
@@ -526,6 +604,17 @@ def reference_workload(cfg_id):
     from oracle import oracle as O
     from tadma_b200.abi import Dist, DType
     L = O.lib()
+    if cfg_id == 1:
+        A = O.fill((64, 128), DType.F32, Dist.NORMAL, 0.0, 1.0, 0, 1)
+        b = O.fill((128,), DType.F32, Dist.NORMAL, 0.0, 1.0, 0, 2)
+        y = np.zeros((64, 1), np.float32)
+        from tadma_b200.abi import Op, Reduce
+
+        def step():
+            t = (A + b).astype(np.float32)
+            O.reduce(Reduce.SUM, t, -1, y, Op.EXP)
+        return ("cfg1: y = sum_last(exp(A + b)), A[64,128] fp32, b[128] fp32 -> [64]", "the whole workload per step",
+                64 * 128 * 4 + 128 * 4 + 64 * 4, step)
     if cfg_id == 2:
         rows, C = 512, Config2.COLS
         x = O.fill((rows, C), DType.BF16, Dist.NORMAL, 0.0, 1.0, 0, 1)

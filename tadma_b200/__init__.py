@@ -119,7 +119,9 @@ def _stream(stream):
 
 class Prepared:
     """A C-ABI call with its ctypes arguments built once (descriptors, program,
-    stream): calling it costs one foreign call, for launch-bound loops."""
+    stream): calling it costs one foreign call, for launch-bound loops.  The
+    stream is fixed when the call is prepared (the current torch stream when
+    none is given); prepare on the capture stream to record into a CUDA graph."""
 
     def __init__(self, fn, args, keep=()):
         self._fn, self._args, self._keep = fn, args, keep
