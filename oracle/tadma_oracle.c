@@ -441,6 +441,9 @@ int or_reduce(int32_t op, const tadma_tensor* in, int32_t axis, int32_t pre_op, 
     if (ax < 0) return TADMA_ERR_INVALID;
     int keep = out->rank == in->rank;
     int64_t R = in->dims[ax];
+    /* An empty reduction has an identity only for the sums; the C ABI
+     * rejects the others (there is no first element to return). */
+    if (R == 0 && op != TADMA_REDUCE_SUM && op != TADMA_REDUCE_SUMSQ) return TADMA_ERR_INVALID;
     int64_t n_out = numel(in) / (R ? R : 1);
     if (R == 0) n_out = numel(out);
     int64_t odims[TADMA_MAX_RANK];

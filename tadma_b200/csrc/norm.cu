@@ -116,9 +116,10 @@ __device__ __forceinline__ unsigned long long widen2(uint32_t w) {
 
 // 16-bit rows: the same statistics with the element arithmetic on packed
 // fp32x2 instructions (two elements per instruction, each rounded like the
-// scalar op), and the normalisation folded into fused multiply-adds:
+// scalar op), the softmax exponent folded into one fused multiply-add:
 //   softmax   e = 2^(x log2e - m log2e),  y = e * (1 / sum e)
-//   LayerNorm y = (x rstd + (-mean rstd)) * gamma + beta
+//   LayerNorm y = ((x - mean) * rstd) * gamma + beta  (x - mean first, so a
+//             value equal to the mean gives exactly 0, as the reference does)
 //   RMSNorm   y = x * (1 / sqrt(mean(x^2) + eps))
 // Outputs are 16-bit, so the reassociation stays far inside half an ulp.
 template <typename T, int CH, int MODE>
@@ -203,7 +204,7 @@ __device__ __forceinline__ void rownorm_finish_packed(float (&v)[CH][VecT<T>::N]
         f2_unpack(q2, q0, q1);
         const float var = warp_sum(q0 + q1) / fL;
         const float rstd = (BM == M_LN_ONNX) ? 1.0f / sqrtf(var + p.eps) : 1.0f / (sqrtf(var) + p.eps);
-        const u64 r2 = f2_pack(rstd, rstd), c2 = f2_pack(-mean * rstd, -mean * rstd);
+        const u64 r2 = f2_pack(rstd, rstd);
 #pragma unroll
         for (int c = 0; c < CH; c++) {
             const int64_t col = ((int64_t)c * 32 + lane) * N;
@@ -217,7 +218,7 @@ __device__ __forceinline__ void rownorm_finish_packed(float (&v)[CH][VecT<T>::N]
                     const uint32_t gw[4] = {gr.x, gr.y, gr.z, gr.w}, bw[4] = {br.x, br.y, br.z, br.w};
 #pragma unroll
                     for (int h = 0; h < H; h++) {
-                        u64 t = f2_fma(f2_pack(v[c][2 * h], v[c][2 * h + 1]), r2, c2);
+                        u64 t = f2_mul(f2_add(f2_pack(v[c][2 * h], v[c][2 * h + 1]), nmean2), r2);
                         if (p.gamma && p.beta) t = f2_fma(t, widen2<T>(gw[h]), widen2<T>(bw[h]));
                         else if (p.gamma) t = f2_mul(t, widen2<T>(gw[h]));
                         else if (p.beta) t = f2_add(t, widen2<T>(bw[h]));
@@ -226,7 +227,7 @@ __device__ __forceinline__ void rownorm_finish_packed(float (&v)[CH][VecT<T>::N]
                 } else {
 #pragma unroll
                     for (int j = 0; j < N; j++) {
-                        float t = fmaf(v[c][j], rstd, -mean * rstd);
+                        float t = (v[c][j] - mean) * rstd;
                         if (p.gamma) t = t * load_as<float>(p.gamma, p.g_dtype, (col + j) * p.g_stride);
                         if (p.beta) t = t + load_as<float>(p.beta, p.b_dtype, (col + j) * p.b_stride);
                         v[c][j] = t;
