@@ -148,10 +148,10 @@ class ClockSampler:
 
 class Config1:
     """y = sum_{last}(exp(A + b)), A[64, 128] fp32, b[128] fp32 -> y[64]: a
-    launch-bound correctness config.  One step = the element-wise chain
-    t = A + b and the row sum with exp as its pre-op, two prepared C-ABI calls
-    captured once into a CUDA graph and replayed (the eager two-launch step is
-    timed beside it as a part)."""
+    launch-bound correctness config.  One step = one tadma_b200_reduce_chain
+    call (the chain A + b -> exp reduced in the same kernel), captured once
+    into a CUDA graph and replayed; the eager call and the two-call
+    composition (eltwise, then reduce with an exp pre-op) are timed beside it."""
     dtype = "f32"
 
     def __init__(self, rank, batch=0):
@@ -159,7 +159,7 @@ class Config1:
         import tadma_b200 as tb
         from tadma_b200.abi import Compute, Dist, DType, Op, Reduce, instr, make_tensor
         R = batch or 64
-        self.name = f"cfg1: y = sum_last(exp(A + b)), A[{R},128] fp32, b[128] fp32 -> [{R}] (CUDA graph of 2 calls)"
+        self.name = f"cfg1: y = sum_last(exp(A + b)), A[{R},128] fp32, b[128] fp32 -> [{R}] (one fused kernel, CUDA graph)"
         self.A = torch.empty((R, 128), dtype=torch.float32, device="cuda")
         self.b = torch.empty((128,), dtype=torch.float32, device="cuda")
         tb.fill(self.A, Dist.NORMAL, 0.0, 1.0, 0, 1, offset=rank * R * 128)
@@ -168,37 +168,38 @@ class Config1:
         self.y = torch.empty((R,), dtype=torch.float32, device="cuda")
         bv = make_tensor(self.b.data_ptr(), DType.F32, [R, 128], [0, 1])
         self.side = torch.cuda.Stream()
-        prog = [instr(Op.ADD, b=1)]
 
-        def calls(st):
-            return [tb.prepare_eltwise(self.t, [self.A, bv], prog, Compute.F32, stream=st),
-                    tb.prepare_reduce(Reduce.SUM, self.t.view(R, 128), -1, self.y.view(R, 1), Op.EXP, stream=st)]
-        self.eager = calls(None)
-        cap = calls(self.side)
+        def fused(st):
+            return tb.prepare_reduce_chain(Reduce.SUM, [self.A, bv], [instr(Op.ADD, b=1), instr(Op.EXP)], -1, self.y,
+                                           Compute.F32, stream=st)
+        self.eager = fused(None)
+        self.two = [tb.prepare_eltwise(self.t, [self.A, bv], [instr(Op.ADD, b=1)], Compute.F32),
+                    tb.prepare_reduce(Reduce.SUM, self.t, -1, self.y.view(R, 1), Op.EXP)]
+        cap = fused(self.side)
         self.side.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(self.side):
-            for c in cap:
-                c()
+            cap()
         self.side.synchronize()
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph, stream=self.side):
-            for c in cap:
-                c()
+            cap()
         torch.cuda.synchronize()
         self.bytes = R * 128 * 4 + 128 * 4 + R * 4
-        self.launches = 2
+        self.launches = 1
         self.units = R
 
     def step(self):
         self.graph.replay()
 
-    def eager_step(self):
-        for c in self.eager:
+    def two_calls(self):
+        for c in self.two:
             c()
 
     def parts(self):
-        return [("chain_vec_kernel + reduce_row_kernel", "CUDA graph replay (2 kernels)", self.bytes, self.step),
-                ("chain_vec_kernel + reduce_row_kernel", "eager, 2 launches", self.bytes, self.eager_step)]
+        return [("chain_reduce_kernel", "one fused call, CUDA graph replay", self.bytes, self.step),
+                ("chain_reduce_kernel", "one fused call, eager", self.bytes, self.eager),
+                ("chain_vec_kernel + reduce_row_kernel", "two calls (eltwise, reduce), eager", self.bytes,
+                 self.two_calls)]
 
     def cpu_sample(self, budget_s):
         import numpy as np

@@ -479,4 +479,28 @@ auto fused(const X& x, const Steps&... steps) {
     return out;
 }
 
+
+// tadma::fused_reduce<OP, Axis, KeepDims>(x, steps...): the chain of
+// tadma::fused reduced along Axis in the same kernel (tadma_b200_reduce_chain),
+// e.g. fused_reduce<TADMA_REDUCE_SUM, -1, false>(A, fuse::add(b), fuse::exp())
+// for sum<-1>(exp(A + b)); the chain's values never reach HBM.  The result
+// is fp32 (int64 for ARGMAX / ARGMIN).
+template <int OP, int Axis, bool KeepDims = true, AnyTensor X, typename... Steps>
+auto fused_reduce(const X& x, const Steps&... steps) {
+    static_assert(sizeof...(Steps) <= TADMA_MAX_INSTR, "at most 16 fused ops");
+    constexpr int Ax = detail::real_dim<Axis, X::Rank>;
+    static_assert(Ax >= 0 && Ax < X::Rank, "reduction axis out of range");
+    detail::FuseBuilder<X> b;
+    b.ins[0] = x.describe();
+    (b.push(steps), ...);
+    using OutDims = std::conditional_t<KeepDims, typename X::Dims::template Set<Ax, 1>, typename X::Dims::template Remove<Ax>>;
+    using R = std::conditional_t<OP == TADMA_REDUCE_ARGMAX || OP == TADMA_REDUCE_ARGMIN, int64_t, float>;
+    Tensor<R, Allocator<kCUDA>, OutDims> out;
+    tadma_tensor o = out.describe();
+    detail::check(tadma_b200_reduce_chain(OP, b.ins.data(), b.n_ins, b.prog.data(), b.n_instr, TADMA_COMPUTE_F32, Ax,
+                                          &o, stream),
+                  "tadma fused_reduce");
+    return out;
+}
+
 }  // namespace tadma

@@ -189,6 +189,28 @@ int tadma_b200_reduce(int32_t op, const tadma_tensor* in, int32_t axis, int32_t 
                       const tadma_tensor* out, void* stream);
 
 /*
+ * Reduction of a fused element-wise chain, in one kernel:
+ *   out = reduce_op over `axis` of chain(ins[0][i], ins[1][i], ...)
+ * The chain (prog, n_instr, compute: as tadma_b200_eltwise) is evaluated per
+ * element on the way into the reduction and never materialised.  All ins have
+ * the same rank and dims S (broadcast operands carry stride 0); out has S
+ * with dims[axis] = 1 (KeepDims) or that dim removed.  op and the out dtype
+ * follow tadma_b200_reduce; float chains reduce in the compute type (fp32 for
+ * TADMA_COMPUTE_F32, fp64 for F64), integer chains in int64.  The result
+ * equals tadma_b200_eltwise into a compute-type temporary followed by
+ * tadma_b200_reduce (bit for bit for max / min / argmax / argmin; sums within
+ * the fp32 reduction tolerance, their order differing).
+ *
+ * Replaces: an EltwiseNode / CombineToNode chain feeding a ReduceNode
+ * (Kernels.hpp:20-45 -> kernels/Reduce.hpp:10-71), i.e. the ReduceKernel
+ * pre-functor (Reduce.hpp:29-56) generalised from one unary op to a chain
+ * over up to 4 broadcast operands; e.g. sum<-1>(exp(A + b)) in one launch.
+ */
+int tadma_b200_reduce_chain(int32_t op, const tadma_tensor* ins, int32_t n_ins, const tadma_instr* prog,
+                            int32_t n_instr, int32_t compute, int32_t axis, const tadma_tensor* out,
+                            void* stream);
+
+/*
  * tadma_b200_reduce without any device allocation.  No counterpart in the
  * reference.  For callers that cannot call cudaMalloc: a process whose memory
  * pool has already claimed the device's HBM (so any further allocation

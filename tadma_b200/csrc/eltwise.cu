@@ -28,6 +28,7 @@
 #include "common.cuh"
 #include "layout.hpp"
 #include "ops.cuh"
+#include "reduce_state.cuh"
 
 namespace tadma_b200 {
 namespace {
@@ -585,6 +586,154 @@ __global__ void __launch_bounds__(THREADS) transpose_chain_kernel(const __grid_c
 
 // ------------------------------------------------------------ host side --
 
+// ------------------------------------------------------ chain reduction --
+//
+// tadma_b200_reduce_chain: a reduction whose elements are a fused chain of
+// up to 4 broadcast operands, evaluated on the fly.  One warp per output
+// element (the kept dims, folded); its lanes walk the reduced axis.  With the
+// axis contiguous (stride 1) or broadcast (stride 0) in every operand and
+// fp32 compute, lanes take 8 elements per step with 16-byte loads (the
+// eltwise vector loader) and run the chain on the 8 at once; otherwise one
+// element per lane step.  Lanes fold their elements in increasing index
+// order and combine in a fixed butterfly, as the reduction kernels do.
+
+// Raw 16-byte words of one 8-element vector (fp32: 2 words, fp16 / bf16: 1),
+// converted to the compute type at use.
+struct RawV {
+    uint4 a, b;
+};
+__device__ __forceinline__ void load_raw_vec(const Operand& o, int64_t off, RawV& r) {
+    const char* p = o.base + off * dtype_size(o.dtype);
+    r.a = ld_stream_v4(p);
+    if (o.dtype == TADMA_F32) r.b = ld_stream_v4(p + 16);
+}
+template <typename C>
+__device__ __forceinline__ void cvt_raw_vec(int dt, const RawV& r, C (&v)[V]) {
+    if (dt == TADMA_F32) {
+        const uint32_t w[8] = {r.a.x, r.a.y, r.a.z, r.a.w, r.b.x, r.b.y, r.b.z, r.b.w};
+#pragma unroll
+        for (int j = 0; j < V; j++) v[j] = from_f<C>(__uint_as_float(w[j]));
+    } else {
+        float f[8];
+        unpack8(r.a, dt, f);
+#pragma unroll
+        for (int j = 0; j < V; j++) v[j] = from_f<C>(f[j]);
+    }
+}
+
+struct ChainReduceParams {
+    ChainParams chain;  // prog, n_instr and the operands (base, dtype, inner_bcast)
+    int32_t n_ins, square, post, out_dtype;
+    int64_t R;                        // reduced extent
+    int64_t ax[TADMA_MAX_INPUTS];     // operand strides along the reduced axis
+    int64_t nrows;                    // output elements
+    int32_t krank, pad;
+    DivMod kdm[TADMA_MAX_RANK];
+    int64_t kin[TADMA_MAX_INPUTS][TADMA_MAX_RANK];
+    int64_t kout[TADMA_MAX_RANK];
+    char* out;
+};
+
+constexpr int POST_NONE = 0, POST_MEAN = 1, POST_RMS = 2;
+
+template <typename C, int K, bool VEC, int NIN>
+__global__ void __launch_bounds__(THREADS, !VEC ? 2 : NIN == 1 ? 3 : 2) chain_reduce_kernel(const __grid_constant__ ChainReduceParams p) {
+    pdl_begin();
+    const int lane = threadIdx.x & 31;
+    const int64_t gw = ((int64_t)blockIdx.x * THREADS + threadIdx.x) >> 5;
+    const int64_t nw = ((int64_t)gridDim.x * THREADS) >> 5;
+    for (int64_t row = gw; row < p.nrows; row += nw) {
+        int64_t base[TADMA_MAX_INPUTS] = {0, 0, 0, 0};
+        int64_t ooff = 0;
+        {
+            uint64_t e = (uint64_t)row;
+            for (int d = p.krank - 1; d >= 0; d--) {
+                uint64_t q, r;
+                if (d > 0) {
+                    p.kdm[d].divmod(e, q, r);
+                } else {
+                    r = e;
+                    q = 0;
+                }
+                ooff += (int64_t)r * p.kout[d];
+#pragma unroll
+                for (int k = 0; k < TADMA_MAX_INPUTS; k++) base[k] += (int64_t)r * p.kin[k][d];
+                e = q;
+            }
+        }
+        State<C> s = init_state<K, C>();
+        int64_t done = 0;
+        if constexpr (VEC) {
+            // An operand broadcast along the axis is one value per output,
+            // loaded once.  The others are double-buffered as raw 16-byte
+            // words: the next vector step's loads are in flight while this
+            // step converts, runs the chain and folds.
+            const int64_t nv = p.R / V;
+            C bc[NIN];
+#pragma unroll
+            for (int k = 0; k < NIN; k++)
+                bc[k] = p.ax[k] == 0 ? load_as<C>(p.chain.in[k].base, p.chain.in[k].dtype, base[k]) : C(0);
+            RawV cur[NIN], nxt[NIN];
+            int64_t v = lane;
+            if (v < nv) {
+#pragma unroll
+                for (int k = 0; k < NIN; k++)
+                    if (p.ax[k] != 0) load_raw_vec(p.chain.in[k], base[k] + v * V, cur[k]);
+            }
+            for (; v < nv; v += 32) {
+                if (v + 32 < nv) {
+#pragma unroll
+                    for (int k = 0; k < NIN; k++)
+                        if (p.ax[k] != 0) load_raw_vec(p.chain.in[k], base[k] + (v + 32) * V, nxt[k]);
+                }
+                C val[NIN][V];
+#pragma unroll
+                for (int k = 0; k < NIN; k++) {
+                    if (p.ax[k] == 0) {
+#pragma unroll
+                        for (int j = 0; j < V; j++) val[k][j] = bc[k];
+                    } else {
+                        cvt_raw_vec<C>(p.chain.in[k].dtype, cur[k], val[k]);
+                    }
+                }
+                C acc[V];
+#pragma unroll
+                for (int j = 0; j < V; j++) acc[j] = val[0][j];
+                run_chain<C, NIN, V, false>(p.chain, acc, val);
+#pragma unroll
+                for (int j = 0; j < V; j++) update<K, C>(s, p.square ? acc[j] * acc[j] : acc[j], v * V + j);
+#pragma unroll
+                for (int k = 0; k < NIN; k++) cur[k] = nxt[k];
+            }
+            done = nv * V;
+        }
+        for (int64_t r = done + lane; r < p.R; r += 32) {
+            C val[TADMA_MAX_INPUTS][1];
+#pragma unroll
+            for (int k = 0; k < TADMA_MAX_INPUTS; k++)
+                if (k < p.n_ins) val[k][0] = load_as<C>(p.chain.in[k].base, p.chain.in[k].dtype, base[k] + r * p.ax[k]);
+            C acc[1] = {p.n_ins > 0 ? val[0][0] : C(0)};
+            run_chain<C, TADMA_MAX_INPUTS, 1, false>(p.chain, acc, val);
+            update<K, C>(s, p.square ? acc[0] * acc[0] : acc[0], r);
+        }
+        s = warp_combine<K, C>(s);
+        if (lane == 0) {
+            if constexpr (K == K_ARGMAX || K == K_ARGMIN) {
+                store_from(p.out, p.out_dtype, ooff, (int64_t)(s.i < 0 ? 0 : s.i));
+            } else {
+                C v = s.v;
+                if constexpr (std::is_floating_point<C>::value) {
+                    if (p.post == POST_MEAN) v = v / (C)p.R;
+                    else if (p.post == POST_RMS) v = sqrt(v / (C)p.R);
+                } else {
+                    if (p.post == POST_MEAN) v = v / p.R;
+                }
+                store_from(p.out, p.out_dtype, ooff, v);
+            }
+        }
+    }
+}
+
 int blocks_per_sm(const void* fn) {
     static std::mutex mu;
     static std::unordered_map<const void*, int> cache;
@@ -737,6 +886,44 @@ int launch_transpose(bool fast, const TransposeParams& tp, cudaStream_t s) {
 }
 
 bool is_transcendental(int op) { return op >= TADMA_OP_EXP && op <= TADMA_OP_GELU && op != TADMA_OP_RELU; }
+
+template <typename C, int K, bool VEC, int NIN>
+int launch_chain_reduce_k(const ChainReduceParams& p, cudaStream_t s) {
+    const void* fn = (const void*)chain_reduce_kernel<C, K, VEC, NIN>;
+    const int64_t want = (p.nrows + (THREADS / 32) - 1) / (THREADS / 32);
+    const int64_t cap = (int64_t)sm_count() * blocks_per_sm(fn);
+    const int grid = (int)(want < cap ? (want > 0 ? want : 1) : cap);
+    cudaError_t e = launch_pdl(chain_reduce_kernel<C, K, VEC, NIN>, dim3(grid), dim3(THREADS), 0, s, p);
+    if (e == cudaSuccess) e = cudaGetLastError();
+    return e == cudaSuccess ? TADMA_OK : cuda_fail(e, "tadma_b200_reduce_chain launch");
+}
+
+// The scalar path takes the operand count at run time (NIN = 4 arrays); the
+// vector path is instantiated per operand count to keep its registers.
+template <typename C, bool VEC, int NIN>
+int launch_chain_reduce_n(int kind, const ChainReduceParams& p, cudaStream_t s) {
+    switch (kind) {
+    case K_SUM: return launch_chain_reduce_k<C, K_SUM, VEC, NIN>(p, s);
+    case K_MAX: return launch_chain_reduce_k<C, K_MAX, VEC, NIN>(p, s);
+    case K_MIN: return launch_chain_reduce_k<C, K_MIN, VEC, NIN>(p, s);
+    case K_ARGMAX: return launch_chain_reduce_k<C, K_ARGMAX, VEC, NIN>(p, s);
+    default: return launch_chain_reduce_k<C, K_ARGMIN, VEC, NIN>(p, s);
+    }
+}
+
+template <typename C, bool VEC>
+int launch_chain_reduce(int kind, const ChainReduceParams& p, cudaStream_t s) {
+    if constexpr (!VEC) {
+        return launch_chain_reduce_n<C, false, TADMA_MAX_INPUTS>(kind, p, s);
+    } else {
+        switch (p.n_ins) {
+        case 1: return launch_chain_reduce_n<C, true, 1>(kind, p, s);
+        case 2: return launch_chain_reduce_n<C, true, 2>(kind, p, s);
+        case 3: return launch_chain_reduce_n<C, true, 3>(kind, p, s);
+        default: return launch_chain_reduce_n<C, true, 4>(kind, p, s);
+        }
+    }
+}
 
 bool valid_op(int op) {
     return (op >= 0 && op <= TADMA_OP_NOT) || (op >= TADMA_OP_ADD && op <= TADMA_OP_LOR) || op == TADMA_OP_WHERE;
@@ -945,4 +1132,124 @@ extern "C" int tadma_b200_eltwise(const tadma_tensor* out, const tadma_tensor* i
         return go(p, false, n - nvec * V);
     }
     return TADMA_OK;
+}
+
+extern "C" int tadma_b200_reduce_chain(int32_t op, const tadma_tensor* ins, int32_t n_ins, const tadma_instr* prog,
+                                       int32_t n_instr, int32_t compute, int32_t axis, const tadma_tensor* out,
+                                       void* stream) {
+    std::string err = check_tensor(out, "out");
+    if (!err.empty()) return fail(TADMA_ERR_INVALID, err);
+    if (n_ins < 1 || n_ins > TADMA_MAX_INPUTS) return fail(TADMA_ERR_INVALID, "n_ins out of range [1, 4]");
+    if (n_instr < 0 || n_instr > TADMA_MAX_INSTR) return fail(TADMA_ERR_INVALID, "n_instr out of range [0, 16]");
+    if (!ins) return fail(TADMA_ERR_INVALID, "ins is NULL");
+    if (n_instr > 0 && !prog) return fail(TADMA_ERR_INVALID, "prog is NULL");
+    if (op < TADMA_REDUCE_SUM || op > TADMA_REDUCE_RMS) return fail(TADMA_ERR_INVALID, "unknown reduce op");
+    const int rank = ins[0].rank;
+    if (rank < 1) return fail(TADMA_ERR_INVALID, "ins must have rank >= 1");
+    int64_t S[TADMA_MAX_RANK];
+    for (int d = 0; d < rank; d++) S[d] = 1;
+    for (int k = 0; k < n_ins; k++) {
+        err = check_tensor(&ins[k], "ins[k]");
+        if (!err.empty()) return fail(TADMA_ERR_INVALID, err);
+        if (ins[k].rank != rank) return fail(TADMA_ERR_INVALID, "ins must share one rank");
+        for (int d = 0; d < rank; d++) {
+            if (ins[k].dims[d] == 1) continue;
+            if (S[d] != 1 && S[d] != ins[k].dims[d]) return fail(TADMA_ERR_INVALID, "ins dims do not broadcast");
+            S[d] = ins[k].dims[d];
+        }
+    }
+    for (int i = 0; i < n_instr; i++) {
+        const tadma_instr& I = prog[i];
+        if (!valid_op(I.op)) return fail(TADMA_ERR_INVALID, "unknown op code");
+        bool needs_b = I.op >= 32 || (I.op == TADMA_OP_COPY && I.b == TADMA_SRC_IMM);
+        if (needs_b && !(I.b == TADMA_SRC_IMM || (I.b >= 0 && I.b < n_ins)))
+            return fail(TADMA_ERR_INVALID, "operand selector b out of range");
+        if (I.op == TADMA_OP_WHERE && !(I.c == TADMA_SRC_IMM || (I.c >= 0 && I.c < n_ins)))
+            return fail(TADMA_ERR_INVALID, "operand selector c out of range");
+        if (I.round_dtype >= 0 && dtype_size(I.round_dtype) == 0) return fail(TADMA_ERR_INVALID, "bad round_dtype");
+    }
+    const int ax = axis < 0 ? axis + rank : axis;
+    if (ax < 0 || ax >= rank) return fail(TADMA_ERR_INVALID, "axis out of range");
+    const bool keep = out->rank == rank;
+    if (!keep && out->rank != rank - 1) return fail(TADMA_ERR_INVALID, "out rank must be rank or rank - 1");
+    for (int d = 0, k = 0; d < rank; d++) {
+        if (d == ax) {
+            if (keep && out->dims[k++] != 1) return fail(TADMA_ERR_INVALID, "out dims[axis] must be 1");
+            continue;
+        }
+        if (out->dims[k++] != S[d]) return fail(TADMA_ERR_INVALID, "out dims do not match the reduced dims");
+    }
+    const bool arg = op == TADMA_REDUCE_ARGMAX || op == TADMA_REDUCE_ARGMIN;
+    if (arg && out->dtype != TADMA_I64 && out->dtype != TADMA_I32)
+        return fail(TADMA_ERR_INVALID, "argmax/argmin output must be int64 or int32");
+    // The chain's natural result type decides the compute type, as for a
+    // materialised chain (ins[0]'s dtype standing in for the temporary's).
+    tadma_tensor chain_out = ins[0];
+    int cm = resolve_compute(&chain_out, ins, n_ins, prog, n_instr, compute);
+    if (cm < TADMA_COMPUTE_F32 || cm > TADMA_COMPUTE_I64) return fail(TADMA_ERR_INVALID, "bad compute mode");
+    if (cm == TADMA_COMPUTE_I64)
+        for (int i = 0; i < n_instr; i++)
+            if (is_transcendental(prog[i].op) || prog[i].op == TADMA_OP_POW)
+                return fail(TADMA_ERR_UNSUPPORTED, "transcendental op in int64 compute");
+    const int64_t R = S[ax];
+    if (R == 0 && op != TADMA_REDUCE_SUM && op != TADMA_REDUCE_SUMSQ)
+        return fail(TADMA_ERR_INVALID, "empty reduction has no identity for this op");
+    if (numel(out) == 0) return TADMA_OK;
+
+    ChainReduceParams p{};
+    p.chain.n_instr = n_instr;
+    for (int i = 0; i < n_instr; i++) p.chain.prog[i] = prog[i];
+    p.n_ins = n_ins;
+    p.R = R;
+    p.out = (char*)out->data;
+    p.out_dtype = out->dtype;
+    p.square = (op == TADMA_REDUCE_SUMSQ || op == TADMA_REDUCE_RMS) ? 1 : 0;
+    p.post = op == TADMA_REDUCE_MEAN ? POST_MEAN : op == TADMA_REDUCE_RMS ? POST_RMS : POST_NONE;
+    const int kind = op == TADMA_REDUCE_MAX ? K_MAX : op == TADMA_REDUCE_MIN ? K_MIN
+                   : op == TADMA_REDUCE_ARGMAX ? K_ARGMAX : op == TADMA_REDUCE_ARGMIN ? K_ARGMIN : K_SUM;
+    // Kept dims, folded jointly for the operands and out.
+    int64_t kd[TADMA_MAX_RANK], ks[1 + TADMA_MAX_INPUTS][TADMA_MAX_RANK];
+    int kr = 0;
+    for (int d = 0; d < rank; d++) {
+        if (d == ax) continue;
+        kd[kr] = S[d];
+        ks[0][kr] = out->strides[keep ? d : (d < ax ? d : d - 1)];
+        for (int k = 0; k < n_ins; k++) ks[1 + k][kr] = ins[k].dims[d] == 1 ? 0 : ins[k].strides[d];
+        kr++;
+    }
+    int64_t nrows = 1;
+    Folded f{};
+    if (kr > 0) {
+        f = fold(kr, kd, ks, 1 + n_ins);
+        for (int d = 0; d < f.rank; d++) nrows *= f.dims[d];
+    }
+    p.nrows = nrows;
+    p.krank = kr > 0 ? f.rank : 0;
+    for (int d = 0; d < p.krank; d++) {
+        p.kdm[d] = DivMod((uint64_t)f.dims[d]);
+        p.kout[d] = f.strides[0][d];
+        for (int k = 0; k < n_ins; k++) p.kin[k][d] = f.strides[1 + k][d];
+    }
+    bool vec = cm == TADMA_COMPUTE_F32 && R >= V;
+    for (int k = 0; k < n_ins; k++) {
+        Operand& o = p.chain.in[k];
+        o.base = (const char*)ins[k].data;
+        o.dtype = ins[k].dtype;
+        o.streaming = 0;
+        p.ax[k] = ins[k].dims[ax] == 1 ? 0 : ins[k].strides[ax];
+        o.inner_bcast = p.ax[k] == 0 ? 1 : 0;
+        if (p.ax[k] == 0) continue;
+        const int es = dtype_size(o.dtype);
+        const bool vdt = o.dtype == TADMA_F32 || o.dtype == TADMA_F16 || o.dtype == TADMA_BF16;
+        bool ok = vdt && p.ax[k] == 1 && (uintptr_t)o.base % 16 == 0;
+        for (int d = 0; d < p.krank && ok; d++) ok = (p.kin[k][d] * es) % 16 == 0;
+        vec = vec && ok;
+    }
+    cudaStream_t s = (cudaStream_t)stream;
+    switch (cm) {
+    case TADMA_COMPUTE_F32:
+        return vec ? launch_chain_reduce<float, true>(kind, p, s) : launch_chain_reduce<float, false>(kind, p, s);
+    case TADMA_COMPUTE_F64: return launch_chain_reduce<double, false>(kind, p, s);
+    default: return launch_chain_reduce<int64_t, false>(kind, p, s);
+    }
 }

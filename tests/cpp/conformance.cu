@@ -102,6 +102,10 @@ int main(int argc, char** argv) {
     auto s1 = e.template sum<-1, false>();
     static_assert(decltype(s1)::Rank == 1 && decltype(s1)::Dim(0) == 64);
     save("cfg1_sum", s1);
+    // config 1 as one kernel: the chain add-then-exp reduced where it is computed
+    auto s1f = fused_reduce<TADMA_REDUCE_SUM, -1, false>(A, fuse::add(b), fuse::exp());
+    static_assert(std::is_same_v<decltype(s1f)::ValueType, float> && decltype(s1f)::Dim(0) == 64);
+    save("cfg1_fused_sum", s1f);
 
     // config 3 (scaled): X[2, 64, 256] ~ U(-1, 1).
     Tensor<float, ALLOCATOR, Sequence<2, 64, 256>> X;

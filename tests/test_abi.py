@@ -96,6 +96,22 @@ def test_host_validation_needs_no_gpu():
     assert L.tadma_b200_layer_norm(P(out), -1, None, None, ctypes.c_double(1e-5), 7, P(out), None) == abi.Status.ERR_INVALID
     gam = abi.make_tensor(fake, abi.DType.F32, [5])
     assert L.tadma_b200_layer_norm(P(out), -1, P(gam), None, ctypes.c_double(1e-5), 0, P(out), None) == abi.Status.ERR_INVALID
+    # reduce_chain: operand count, broadcast, axis, out shape, argmax dtype, empty max
+    rc_ins = (abi.TadmaTensor * 2)(abi.make_tensor(fake, abi.DType.F32, [4, 5]),
+                                   abi.make_tensor(fake, abi.DType.F32, [1, 5], [0, 1]))
+    add, na = abi.program([abi.instr(abi.Op.ADD, b=1)])
+    rc_out = abi.make_tensor(fake, abi.DType.F32, [4, 1])
+    RC = L.tadma_b200_reduce_chain
+    assert RC(0, rc_ins, 0, add, na, -1, -1, P(rc_out), None) == abi.Status.ERR_INVALID          # no operand
+    assert RC(0, rc_ins, 2, add, na, -1, 2, P(rc_out), None) == abi.Status.ERR_INVALID           # axis
+    assert RC(0, rc_ins, 2, add, na, -1, -1, P(abi.make_tensor(fake, abi.DType.F32, [4, 2])), None) == abi.Status.ERR_INVALID
+    assert RC(int(abi.Reduce.ARGMAX), rc_ins, 2, add, na, -1, -1, P(rc_out), None) == abi.Status.ERR_INVALID
+    bad_b = (abi.TadmaTensor * 2)(abi.make_tensor(fake, abi.DType.F32, [4, 5]), abi.make_tensor(fake, abi.DType.F32, [3, 5]))
+    assert RC(0, bad_b, 2, add, na, -1, -1, P(rc_out), None) == abi.Status.ERR_INVALID          # dims do not broadcast
+    sel2, ns = abi.program([abi.instr(abi.Op.ADD, b=2)])
+    assert RC(0, rc_ins, 2, sel2, ns, -1, -1, P(rc_out), None) == abi.Status.ERR_INVALID        # selector out of range
+    empty = (abi.TadmaTensor * 1)(abi.make_tensor(None, abi.DType.F32, [4, 0]))
+    assert RC(int(abi.Reduce.MAX), empty, 1, add, 0, -1, -1, P(rc_out), None) == abi.Status.ERR_INVALID
     # fill: distribution / dtype pairing
     assert L.tadma_b200_fill(P(out), 2, ctypes.c_double(0), ctypes.c_double(10), 0, 0, 0, None) == abi.Status.ERR_INVALID
     assert L.tadma_b200_fill(P(out), 9, ctypes.c_double(0), ctypes.c_double(1), 0, 0, 0, None) == abi.Status.ERR_INVALID

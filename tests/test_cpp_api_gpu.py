@@ -56,6 +56,8 @@ def test_config1(results):
     e = np.exp((A + b).astype(np.float64))
     got = results("cfg1_sum", np.float32, (64,))
     np.testing.assert_allclose(got, e.sum(axis=1), rtol=1e-5 * np.sqrt(128))
+    got = results("cfg1_fused_sum", np.float32, (64,))
+    np.testing.assert_allclose(got, e.sum(axis=1), rtol=1e-5 * np.sqrt(128))
 
 
 def test_config3(results):
