@@ -10,6 +10,14 @@ max(upload, download) instead of upload + compute + download.
 from __future__ import annotations
 
 
+def chunk_bounds(rows: int, chunks: int):
+    """[(lo, hi), ...]: `rows` split into at most `chunks` contiguous, non-empty
+    row ranges of equal size (the last may be shorter), covering [0, rows)."""
+    chunks = max(1, chunks)
+    step = max(1, (rows + chunks - 1) // chunks)
+    return [(lo, min(rows, lo + step)) for lo in range(0, rows, step)]
+
+
 class RowPipeline:
     """One step = upload the `uploads` row chunks, run `make_call(lo, hi,
     stream)` per chunk, download the `downloads` row chunks; `once` buffers
@@ -25,8 +33,7 @@ class RowPipeline:
         self.rows, self.chunks = rows, max(1, chunks)
         self.uploads, self.downloads, self.once = list(uploads), list(downloads), list(once)
         self.s_in, self.s_run, self.s_out = torch.cuda.Stream(), torch.cuda.Stream(), torch.cuda.Stream()
-        step = (rows + self.chunks - 1) // self.chunks
-        self.bounds = [(lo, min(rows, lo + step)) for lo in range(0, rows, step)]
+        self.bounds = chunk_bounds(rows, self.chunks)
         self.calls = [make_call(lo, hi, self.s_run) for lo, hi in self.bounds]
         self.ev_in = [torch.cuda.Event() for _ in self.bounds]
         self.ev_run = [torch.cuda.Event() for _ in self.bounds]
