@@ -14,8 +14,9 @@
 // add row are visited together (batch-fastest), the row is copied in 8-element
 // chunks (16 B of fp16/bf16, 32 B of fp32) with 4 raw chunks in flight per lane,
 // the add operand's row (e.g. pos[s]) is fetched with an L2 evict_last policy
-// so it stays resident across the batch while the gathered rows (evict_first
-// policy) and the output (evict-first stores) stream through: the gather
+// so it stays resident across the batch; the gathered rows keep the normal
+// policy, so repeated ids (a hot vocabulary subset) hit in L2, and the output
+// is written with evict-first stores: the gather
 // writes its output once and reads each gathered row once, so at config 5
 // sizes it is an HBM-bound copy.
 // Any other layout takes a per-element path with the same semantics.
@@ -109,9 +110,10 @@ __global__ void __launch_bounds__(THREADS) gather_rows_kernel(const __grid_const
     const int64_t gw = ((int64_t)blockIdx.x * THREADS + threadIdx.x) >> 5;
     const int64_t nw = ((int64_t)gridDim.x * THREADS) >> 5;
     const int64_t nch = p.D / CHUNK;
-    // Gathered rows stream through L2 once; the add operand (a table every
-    // batch row re-reads) is kept resident.
-    const uint64_t pol_stream = l2_policy_evict_first();
+    // The add operand (a table every batch row re-reads) is kept resident;
+    // gathered rows get the normal policy: repeated ids hit in L2.  (An
+    // evict_first policy here measured 4 % slower on config 5.)
+    const uint64_t pol_stream = l2_policy_evict_normal();
     const uint64_t pol_keep = l2_policy_evict_last();
     auto row_of = [&](int64_t t) -> int64_t {
         if (!p.bperm) return t;
