@@ -16,6 +16,13 @@
  * an async call: the kernel sets a bit in a per-device error word and writes
  * zeros for that row; tadma_b200_error_flags() reads (and optionally clears)
  * that word after synchronising.
+ *
+ * Every kernel is launched with programmatic stream serialisation: it may be
+ * scheduled while the previous kernel of its stream drains, and it waits for
+ * that kernel to complete before touching memory, so stream order is kept.
+ * Calls may be captured into a CUDA graph (prepare them on the capture
+ * stream); tadma_b200_reduce's split path allocates a stream-ordered
+ * workspace (cudaMallocAsync), tadma_b200_reduce_noalloc does not.
  */
 #ifndef TADMA_B200_H
 #define TADMA_B200_H
