@@ -79,7 +79,7 @@ NCU_TRAFFIC = {
     (3, "mean axis 1 (+ finish kernel when split)"): {"bytes": 8 * 273262592, "captured": "batch 4, x8"},
     (4, "LayerNorm (ONNX) rows of 1024"): {"bytes": 2 * 217847000, "captured": "batch 32, x2"},
     (4, "softmax rows of 2048"): {"bytes": 2 * 4245502000, "captured": "batch 16, x2"},
-    (5, "gather + pos add"): {"bytes": 32 * 4151773000, "captured": "batch 64, x32"},
+    (5, "gather + pos add"): {"bytes": 32 * 4088463616, "captured": "batch 64, x32"},
 }
 
 

@@ -5,6 +5,7 @@
 
 #include "Constexpr.hpp"
 #include "Core.hpp"
+#include "Lazy.hpp"
 #include "Operations.hpp"
 #include "Sequence.hpp"
 #include "Tensor.hpp"

@@ -178,6 +178,70 @@ int main(int argc, char** argv) {
     auto un = b.template unsqueeze<0>();  // [1, 128]
     save("unsqueeze_bcast_add", A + un);
 
+    // lazy chains (Lazy.hpp): each pair is the same computation made through
+    // lazy values (one kernel where consumed) and eagerly (one kernel per op);
+    // the test compares them bit for bit.
+    Tensor<float, ALLOCATOR, Sequence<64, 128>> A2, A3, A4, A5;
+    fill(A2, TADMA_DIST_NORMAL, 0.0, 1.0, 17);
+    fill(A3, TADMA_DIST_NORMAL, 0.0, 1.0, 18);
+    fill(A4, TADMA_DIST_NORMAL, 0.0, 1.0, 19);
+    fill(A5, TADMA_DIST_NORMAL, 0.0, 1.0, 20);
+    {
+        auto l2 = gelu(lazy(x) * 0.5f + bias);  // config 2: float chain, gelu in place
+        static_assert(LazyTensor<decltype(l2)> && std::is_same_v<decltype(l2)::ValueType, float>);
+        save("lazy_cfg2", l2);
+        save("eager_cfg2", gelu(x * 0.5f + bias));
+        auto l2d = gelu<false>(lazy(x) * 0.5f + bias);  // double result: the chain restarts at gelu
+        static_assert(std::is_same_v<decltype(l2d)::ValueType, double>);
+        save("lazy_cfg2_f64", l2d);
+        save("eager_cfg2_f64", gelu<false>(x * 0.5f + bias));
+
+        auto l1 = exp<false>(lazy(A) + b).template sum<-1, false>();  // config 1 in one kernel
+        static_assert(std::is_same_v<decltype(l1)::ValueType, float> && decltype(l1)::Rank == 1 && decltype(l1)::Dim(0) == 64);
+        save("lazy_cfg1_sum", l1);
+
+        auto lm = lazy(X) * 2.0f - 0.5f;
+        save("lazy_max", lm.template max<-1>());
+        save("eager_max", (X * 2.0f - 0.5f).template max<-1>());
+        save("lazy_argmin1", lm.template argmin<1>());
+        save("eager_argmin1", (X * 2.0f - 0.5f).template argmin<1>());
+
+        // every operator with a lazy operand extends a chain (no eager kernel)
+        static_assert(LazyTensor<decltype(lm)> && LazyTensor<decltype(-lazy(A))>);
+        static_assert(LazyTensor<decltype((A2 - lazy(A)) / (1.0f + lazy(A3)) + A4 / lazy(A))>);
+        static_assert(LazyTensor<decltype((A2 > lazy(A)) && (lazy(A3) < 0.5f))>);
+        static_assert(LazyTensor<decltype(lazy(A) + A2 - A3 * A4 + A5)>);
+        static_assert(LazyTensor<decltype(pow<false>(sqrt(lazy(A)), 2.0f))>);
+        static_assert(!LazyTensor<decltype(A + A2)>);
+        save("lazy_rev", (A2 - lazy(A)) / (1.0f + lazy(A3)) + A4 / lazy(A));
+        save("eager_rev", (A2 - A) / (1.0f + A3) + A4 / A);
+        save("lazy_cmp", (A2 > lazy(A)) && (lazy(A3) < 0.5f));
+        save("eager_cmp", (A2 > A) && (A3 < 0.5f));
+
+        auto li = lazy(ids) * 3 + 1;  // integer chain
+        static_assert(std::is_same_v<decltype(li)::ValueType, int64_t>);
+        save("lazy_int", (li > 1500) * 2.5);
+        save("eager_int", ((ids * 3 + 1) > 1500) * 2.5);
+
+        auto ll = lazy(A);  // 20 steps: more than one chain's 16 instructions
+        auto le = A.clone();
+        for (int i = 0; i < 10; i++) {
+            ll *= 1.0625f;
+            ll += A2;
+            le *= 1.0625f;
+            le += A2;
+        }
+        save("lazy_long", ll);
+        save("eager_long", le);
+        save("lazy_operands", lazy(A) + A2 - A3 * A4 + A5);  // 4 tensor operands: more than 3
+        save("eager_operands", A + A2 - A3 * A4 + A5);
+
+        save("lazy_softmax", softmax<-1, false>(lazy(S) * 0.5f));  // consumed by an eager API call
+        save("eager_softmax", softmax<-1, false>(S * 0.5f));
+        save("lazy_cast_sum", tanh(lazy(L).template to<float>()).template sum<-1>());
+        save("eager_cast_sum", tanh(L.template to<float>()).template sum<-1>());
+    }
+
     // generated-graph shape arithmetic (GraphPrologue above)
     GraphPrologue graph;
     fill(graph.position_table, TADMA_DIST_NORMAL, 0.0, 1.0, 15);
