@@ -72,6 +72,17 @@ struct LazyChain {
     int n_instr = 0, n_ins = 1, compute = TADMA_COMPUTE_AUTO;
 };
 
+// Index of the operand of `c` that is the same view as `t`, or -1.
+inline int find_operand(const LazyChain& c, const tadma_tensor& t) {
+    for (int k = 0; k < c.n_ins; k++) {
+        const tadma_tensor& u = c.ins[k];
+        bool same = u.data == t.data && u.dtype == t.dtype && u.rank == t.rank;
+        for (int d = 0; same && d < t.rank; d++) same = u.dims[d] == t.dims[d] && u.strides[d] == t.strides[d];
+        if (same) return k;
+    }
+    return -1;
+}
+
 // Swapped operand order for `tensor (op) lazy`: acc is the lazy value.
 constexpr int reversed_op(int op) {
     switch (op) {
@@ -109,8 +120,12 @@ struct Lazy {
 
     static consteval int64_t Dim(int i) { return Dims::Values(i < 0 ? i + Rank : i); }
 
-    // Runs the chain into a new tensor (one kernel).
+    // Runs the chain into a new tensor (one kernel).  After describe() has
+    // materialised the value, the value IS that tensor (an in-place call on it,
+    // e.g. softmax<D, true>, writes there): eval() returns it, and new steps
+    // and reductions start from it.
     Result eval() const {
+        if (cache) return *cache;
         Result out;
         tadma_tensor o = out.describe();
         detail::check(tadma_b200_eltwise(&o, chain.ins.data(), chain.n_ins, chain.prog.data(), chain.n_instr,
@@ -143,20 +158,26 @@ struct Lazy {
 
     // Appends `op` with result type R2; `b` is TADMA_SRC_IMM (imm), TADMA_SRC_NONE
     // or a new tensor operand (`operand`, already of this chain's dims).
+    // An operand the chain already reads (the same view) is not added twice.
     template <typename R2>
     Lazy<R2, Dims> then(int op, int b, double imm, const tadma_tensor* operand = nullptr,
                         std::shared_ptr<const void> keep = nullptr) const {
         const int cm = detail::eager_compute(dtype_v<R2>, dtype_v<R>, operand ? operand->dtype : -1, op,
                                              b == TADMA_SRC_IMM, imm);
-        const bool fits = chain.n_instr < TADMA_MAX_INSTR && (!operand || chain.n_ins < TADMA_MAX_INPUTS) &&
-                          (chain.compute == TADMA_COMPUTE_AUTO || chain.compute == cm);
+        const detail::LazyChain cur = current();
+        const bool room = !operand || detail::find_operand(cur, *operand) >= 0 || cur.n_ins < TADMA_MAX_INPUTS;
+        const bool fits = cur.n_instr < TADMA_MAX_INSTR && room &&
+                          (cur.compute == TADMA_COMPUTE_AUTO || cur.compute == cm);
         Lazy<R2, Dims> next;
-        next.chain = fits ? chain : restart().chain;
+        next.chain = fits ? cur : restart().chain;
         detail::LazyChain& c = next.chain;
         if (operand) {
-            b = c.n_ins++;
-            c.ins[b] = *operand;
-            c.keep[b] = std::move(keep);
+            b = detail::find_operand(c, *operand);
+            if (b < 0) {
+                b = c.n_ins++;
+                c.ins[b] = *operand;
+                c.keep[b] = std::move(keep);
+            }
         }
         c.prog[c.n_instr++] = detail::ins(op, b, imm, dtype_v<R2>);
         c.compute = cm;
@@ -171,6 +192,9 @@ struct Lazy {
 
     // A chain whose source is this chain's materialised value.
     Lazy restart() const;
+    // The chain that new steps extend: this one, or once materialised, a
+    // chain over the materialised tensor.
+    detail::LazyChain current() const;
 
     // -------------------------------------------------------- reductions --
     template <int OP, int D, bool KeepDims, typename Out>
@@ -180,8 +204,9 @@ struct Lazy {
         using OutDims = std::conditional_t<KeepDims, typename Dims::template Set<Ax, 1>, typename Dims::template Remove<Ax>>;
         Tensor<Out, Allocator, OutDims> out;
         tadma_tensor o = out.describe();
-        detail::check(tadma_b200_reduce_chain(OP, chain.ins.data(), chain.n_ins, chain.prog.data(), chain.n_instr,
-                                              chain.compute, Ax, &o, stream),
+        const detail::LazyChain c = current();
+        detail::check(tadma_b200_reduce_chain(OP, c.ins.data(), c.n_ins, c.prog.data(), c.n_instr, c.compute, Ax, &o,
+                                              stream),
                       "tadma lazy reduce");
         return out;
     }
@@ -222,6 +247,10 @@ auto lazy(const X& x) {
 template <typename R, AnySequence D>
 Lazy<R, D> Lazy<R, D>::restart() const {
     return lazy(eval());
+}
+template <typename R, AnySequence D>
+detail::LazyChain Lazy<R, D>::current() const {
+    return cache ? lazy(*cache).chain : chain;
 }
 
 namespace detail {

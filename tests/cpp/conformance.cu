@@ -210,7 +210,7 @@ int main(int argc, char** argv) {
         static_assert(LazyTensor<decltype(lm)> && LazyTensor<decltype(-lazy(A))>);
         static_assert(LazyTensor<decltype((A2 - lazy(A)) / (1.0f + lazy(A3)) + A4 / lazy(A))>);
         static_assert(LazyTensor<decltype((A2 > lazy(A)) && (lazy(A3) < 0.5f))>);
-        static_assert(LazyTensor<decltype(lazy(A) + A2 - A3 * A4 + A5)>);
+        static_assert(LazyTensor<decltype(lazy(A) + A2 - A3 + A4 - A5)>);
         static_assert(LazyTensor<decltype(pow<false>(sqrt(lazy(A)), 2.0f))>);
         static_assert(!LazyTensor<decltype(A + A2)>);
         save("lazy_rev", (A2 - lazy(A)) / (1.0f + lazy(A3)) + A4 / lazy(A));
@@ -233,11 +233,19 @@ int main(int argc, char** argv) {
         }
         save("lazy_long", ll);
         save("eager_long", le);
-        save("lazy_operands", lazy(A) + A2 - A3 * A4 + A5);  // 4 tensor operands: more than 3
-        save("eager_operands", A + A2 - A3 * A4 + A5);
+        save("lazy_operands", lazy(A) + A2 - A3 + A4 - A5);  // 4 tensor operands: more than 3
+        save("eager_operands", A + A2 - A3 + A4 - A5);
+        save("lazy_square", lazy(A) * A + A2 * lazy(A2));  // operands that are the source
+        save("eager_square", A * A + A2 * A2);
 
         save("lazy_softmax", softmax<-1, false>(lazy(S) * 0.5f));  // consumed by an eager API call
         save("eager_softmax", softmax<-1, false>(S * 0.5f));
+        // an in-place call materialises the lazy value and writes there; later
+        // steps and reductions start from that tensor
+        auto ls = softmax<-1, true>(lazy(S) * 0.5f);
+        save("lazy_softmax_then", (ls * 3.0f).template max<-1>());
+        auto es = softmax<-1, true>(S * 0.5f);
+        save("eager_softmax_then", (es * 3.0f).template max<-1>());
         save("lazy_cast_sum", tanh(lazy(L).template to<float>()).template sum<-1>());
         save("eager_cast_sum", tanh(L.template to<float>()).template sum<-1>());
     }

@@ -128,3 +128,44 @@ def test_generated_shape_arithmetic(results):
     emb = (word[ids] + pos[:12][None]).astype(np.float32)
     assert np.array_equal(results("gen_embed_flat", np.float32, (2, 12 * 32)), emb.reshape(2, -1))
     assert np.array_equal(results("gen_expand", np.float32, (2, 12, 32)), np.broadcast_to(pos[:12], (2, 12, 32)))
+
+
+# Lazy chains (include/tadma/Lazy.hpp): each lazy result is compared with the
+# same calls made eagerly, one kernel per op.  Element-wise chains and
+# max / argmin are bit-identical: every step rounds to the eager result type
+# and computes in the eager precision.  Sums differ only in their order.
+LAZY_PAIRS = [
+    ("cfg2", np.float32, (64, 1024)),
+    ("cfg2_f64", np.float64, (64, 1024)),
+    ("max", np.float32, (2, 64, 1)),
+    ("argmin1", np.int64, (2, 256)),
+    ("rev", np.float32, (64, 128)),
+    ("cmp", np.bool_, (64, 128)),
+    ("int", np.float64, (4, 64)),
+    ("long", np.float32, (64, 128)),
+    ("operands", np.float32, (64, 128)),
+    ("square", np.float32, (64, 128)),
+    ("softmax", np.float32, (2, 4, 256, 2048)),
+    ("softmax_then", np.float32, (2, 4, 256, 1)),
+]
+
+
+@pytest.mark.parametrize("name,dt,shape", LAZY_PAIRS)
+def test_lazy_chain_equals_eager_calls(results, name, dt, shape):
+    lazy, eager = results("lazy_" + name, dt, shape), results("eager_" + name, dt, shape)
+    assert np.array_equal(lazy.view(np.uint8), eager.view(np.uint8)), name
+
+
+def test_lazy_reductions(results):
+    # config 1 through lazy values: exp<false>(lazy(A) + b).sum<-1, false>()
+    # is the fused_reduce call (one kernel), bit for bit
+    A = gen((64, 128), DType.F32, Dist.NORMAL, 0.0, 1.0, 1)
+    b = gen((128,), DType.F32, Dist.NORMAL, 0.0, 1.0, 2)
+    got = results("lazy_cfg1_sum", np.float32, (64,))
+    assert np.array_equal(got, results("cfg1_fused_sum", np.float32, (64,)))
+    np.testing.assert_allclose(got, np.exp((A + b).astype(np.float64)).sum(axis=1), rtol=1e-5 * np.sqrt(128))
+    # tanh(lazy(L).to<float>()).sum<-1>() against the eager cast, tanh and row sum
+    lazy, eager = results("lazy_cast_sum", np.float32, (4, 16, 1)), results("eager_cast_sum", np.float32, (4, 16, 1))
+    L = gen((4, 16, 1024), DType.F16, Dist.NORMAL, 0.0, 1.0, 4).astype(np.float64)
+    np.testing.assert_allclose(lazy, eager, rtol=1e-5 * 32, atol=1e-5 * 32)
+    np.testing.assert_allclose(lazy, np.tanh(L).sum(-1, keepdims=True), rtol=1e-5 * 32, atol=1e-4)
