@@ -14,6 +14,7 @@
 
 #include <atomic>
 #include <cstdint>
+#include <cstdlib>
 #include <functional>
 #include <stdexcept>
 #include <string>
@@ -144,6 +145,10 @@ struct Allocator<kCUDA> {
         } else {
             T* ptr = nullptr;
             cudaStream_t s = stream;
+            // TADMA_B200_FAIL_ALLOC=1 fails every allocation as an exhausted
+            // device would, before any CUDA call (host-side fault injection).
+            if (const char* inject = std::getenv("TADMA_B200_FAIL_ALLOC"); inject && inject[0] == '1')
+                check_cuda(cudaErrorMemoryAllocation);
             check_cuda(cudaMallocAsync(reinterpret_cast<void**>(&ptr), sizeof(T) * Count, s));
             return HeapStorage<T>(ptr, [ptr, s]() { cudaFreeAsync(ptr, s); });
         }

@@ -385,6 +385,11 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
 void set_error(const std::string& msg);
 int fail(int code, const std::string& msg);
 int cuda_fail(cudaError_t e, const char* what);
+// Stream-ordered device workspace (cudaMallocAsync).  With TADMA_B200_FAIL_ALLOC=1
+// in the environment every call fails as on an exhausted device
+// (cudaErrorMemoryAllocation) without calling CUDA: host-side fault injection
+// for tests of the error path.
+cudaError_t workspace_alloc(void** p, size_t bytes, cudaStream_t s);
 // SM count of the current device (cached per device).
 int sm_count();
 // Validates a tensor descriptor; returns "" or a message.

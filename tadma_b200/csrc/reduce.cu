@@ -555,7 +555,7 @@ int run_fast(int dt, int kind, int path, RedParams& p, bool vec, cudaStream_t s,
         return dispatch_fast(dt, kind, path, p, vec, s);
     }
     void* buf = nullptr;
-    cudaError_t e = cudaMallocAsync(&buf, (size_t)ws, s);
+    cudaError_t e = workspace_alloc(&buf, (size_t)ws, s);
     if (e != cudaSuccess) return cuda_fail(e, "tadma_b200_reduce workspace");
     p.partials = buf;
     int rc = dispatch_fast(dt, kind, path, p, vec, s);

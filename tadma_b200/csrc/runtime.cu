@@ -1,5 +1,6 @@
 // runtime.cu - host-side plumbing of the C ABI: last-error text, version,
 // dtype sizes, SM-count cache and tensor-descriptor validation.
+#include <cstdlib>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -20,6 +21,15 @@ int fail(int code, const std::string& msg) {
 int cuda_fail(cudaError_t e, const char* what) {
     g_last_error = std::string(what) + ": " + cudaGetErrorString(e);
     return TADMA_ERR_CUDA;
+}
+
+cudaError_t workspace_alloc(void** p, size_t bytes, cudaStream_t s) {
+    const char* inject = std::getenv("TADMA_B200_FAIL_ALLOC");
+    if (inject && inject[0] == '1') {
+        *p = nullptr;
+        return cudaErrorMemoryAllocation;
+    }
+    return cudaMallocAsync(p, bytes, s);
 }
 
 int sm_count() {

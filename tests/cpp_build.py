@@ -5,13 +5,18 @@ import subprocess
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
-def build_conformance(out_dir: str) -> str:
-    exe = os.path.join(out_dir, "conformance")
+def build_program(name: str, out_dir: str) -> str:
+    """nvcc tests/cpp/<name>.cu -> <out_dir>/<name>, linked against libtadma_b200.so."""
+    exe = os.path.join(out_dir, name)
     lib_dir = os.path.join(ROOT, "tadma_b200")
     cmd = ["nvcc", "-std=c++20", "-O2", "-gencode", "arch=compute_100a,code=sm_100a",
-           "-I", os.path.join(ROOT, "include"), os.path.join(ROOT, "tests", "cpp", "conformance.cu"),
+           "-I", os.path.join(ROOT, "include"), os.path.join(ROOT, "tests", "cpp", name + ".cu"),
            "-L", lib_dir, "-ltadma_b200", "-Xlinker", f"-rpath={lib_dir}", "-o", exe]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
-        raise RuntimeError(f"conformance build failed:\n{r.stdout}\n{r.stderr}")
+        raise RuntimeError(f"{name} build failed:\n{r.stdout}\n{r.stderr}")
     return exe
+
+
+def build_conformance(out_dir: str) -> str:
+    return build_program("conformance", out_dir)
