@@ -52,13 +52,18 @@ inline bool op_transcendental(int op) {
 }
 
 // The precision tadma_b200_eltwise picks (TADMA_COMPUTE_AUTO) for the one-op
-// call y = op(a[, b | imm]) that the eager API makes.
-inline int eager_compute(int out_dt, int a_dt, int b_dt, int op, bool has_imm, double imm) {
-    bool all_int = !dtype_float(out_dt) && !dtype_float(a_dt) && (b_dt < 0 || !dtype_float(b_dt));
+// call y = op(a[, b | imm][, c]) that the eager API makes (-1: no operand).
+inline int eager_compute(int out_dt, int a_dt, int b_dt, int op, bool has_imm, double imm, int c_dt = -1) {
+    bool all_int = !dtype_float(out_dt) && !dtype_float(a_dt);
+    bool wide = dtype_wide(out_dt) || dtype_wide(a_dt);
+    for (int d : {b_dt, c_dt}) {
+        if (d < 0) continue;
+        all_int = all_int && !dtype_float(d);
+        wide = wide || dtype_wide(d);
+    }
     if (op_transcendental(op)) all_int = false;
     if (has_imm && imm != (double)(int64_t)imm) all_int = false;
     if (all_int) return TADMA_COMPUTE_I64;
-    const bool wide = dtype_wide(out_dt) || dtype_wide(a_dt) || (b_dt >= 0 && dtype_wide(b_dt));
     return wide ? TADMA_COMPUTE_F64 : TADMA_COMPUTE_F32;
 }
 
@@ -72,14 +77,15 @@ struct LazyChain {
     int n_instr = 0, n_ins = 1, compute = TADMA_COMPUTE_AUTO;
 };
 
+inline bool same_view(const tadma_tensor& u, const tadma_tensor& t) {
+    bool same = u.data == t.data && u.dtype == t.dtype && u.rank == t.rank;
+    for (int d = 0; same && d < t.rank; d++) same = u.dims[d] == t.dims[d] && u.strides[d] == t.strides[d];
+    return same;
+}
 // Index of the operand of `c` that is the same view as `t`, or -1.
 inline int find_operand(const LazyChain& c, const tadma_tensor& t) {
-    for (int k = 0; k < c.n_ins; k++) {
-        const tadma_tensor& u = c.ins[k];
-        bool same = u.data == t.data && u.dtype == t.dtype && u.rank == t.rank;
-        for (int d = 0; same && d < t.rank; d++) same = u.dims[d] == t.dims[d] && u.strides[d] == t.strides[d];
-        if (same) return k;
-    }
+    for (int k = 0; k < c.n_ins; k++)
+        if (same_view(c.ins[k], t)) return k;
     return -1;
 }
 
@@ -156,38 +162,56 @@ struct Lazy {
     template <auto... NewDims>
     auto reshape() const { return materialised().template reshape<NewDims...>(); }
 
-    // Appends `op` with result type R2; `b` is TADMA_SRC_IMM (imm), TADMA_SRC_NONE
-    // or a new tensor operand (`operand`, already of this chain's dims).
-    // An operand the chain already reads (the same view) is not added twice.
+    // Appends `op` with result type R2.  `b` is TADMA_SRC_IMM (imm) or
+    // TADMA_SRC_NONE; each given operand (a view of this chain's dims) takes
+    // the place of b, then c (TADMA_OP_WHERE reads both).  An operand the
+    // chain already reads (the same view) is not added twice.
+    struct Operand {
+        tadma_tensor desc;
+        std::shared_ptr<const void> keep;
+    };
     template <typename R2>
-    Lazy<R2, Dims> then(int op, int b, double imm, const tadma_tensor* operand = nullptr,
-                        std::shared_ptr<const void> keep = nullptr) const {
-        const int cm = detail::eager_compute(dtype_v<R2>, dtype_v<R>, operand ? operand->dtype : -1, op,
-                                             b == TADMA_SRC_IMM, imm);
-        const detail::LazyChain cur = current();
-        const bool room = !operand || detail::find_operand(cur, *operand) >= 0 || cur.n_ins < TADMA_MAX_INPUTS;
-        const bool fits = cur.n_instr < TADMA_MAX_INSTR && room &&
+    Lazy<R2, Dims> then(int op, int b, double imm, const Operand* ob = nullptr, const Operand* oc = nullptr) const {
+        detail::LazyChain cur = current();
+        const int cm = detail::eager_compute(dtype_v<R2>, dtype_v<R>, ob ? ob->desc.dtype : -1, op,
+                                             b == TADMA_SRC_IMM, imm, oc ? oc->desc.dtype : -1);
+        int fresh = 0;  // operand slots this step adds
+        if (ob && detail::find_operand(cur, ob->desc) < 0) fresh++;
+        if (oc && detail::find_operand(cur, oc->desc) < 0 && !(ob && detail::same_view(ob->desc, oc->desc))) fresh++;
+        const bool fits = cur.n_instr < TADMA_MAX_INSTR && cur.n_ins + fresh <= TADMA_MAX_INPUTS &&
                           (cur.compute == TADMA_COMPUTE_AUTO || cur.compute == cm);
         Lazy<R2, Dims> next;
-        next.chain = fits ? cur : restart().chain;
-        detail::LazyChain& c = next.chain;
-        if (operand) {
-            b = detail::find_operand(c, *operand);
-            if (b < 0) {
-                b = c.n_ins++;
-                c.ins[b] = *operand;
-                c.keep[b] = std::move(keep);
+        next.chain = fits ? std::move(cur) : restart().chain;
+        detail::LazyChain& ch = next.chain;
+        auto slot = [&ch](const Operand& o) {
+            int k = detail::find_operand(ch, o.desc);
+            if (k < 0) {
+                k = ch.n_ins++;
+                ch.ins[k] = o.desc;
+                ch.keep[k] = o.keep;
             }
-        }
-        c.prog[c.n_instr++] = detail::ins(op, b, imm, dtype_v<R2>);
-        c.compute = cm;
+            return k;
+        };
+        const int sb = ob ? slot(*ob) : b;
+        const int sc = oc ? slot(*oc) : TADMA_SRC_NONE;
+        ch.prog[ch.n_instr++] = detail::ins(op, sb, imm, dtype_v<R2>, sc);
+        ch.compute = cm;
         return next;
+    }
+    // The operand view of tensor y broadcast to this chain's dims.
+    template <AnyTensor B>
+    Operand operand(const B& y) const {
+        if constexpr (LazyTensor<B>) {
+            return operand(y.materialised());
+        } else {
+            auto yb = std::make_shared<const decltype(y.template broadcastTo<Dims>())>(y.template broadcastTo<Dims>());
+            return Operand{yb->describe(), std::move(yb)};
+        }
     }
     template <typename R2, AnyTensor B>
     Lazy<R2, Dims> then(int op, const B& y) const {
-        auto yb = std::make_shared<const decltype(y.template broadcastTo<Dims>())>(y.template broadcastTo<Dims>());
-        tadma_tensor d = yb->describe();
-        return then<R2>(op, TADMA_SRC_NONE, 0.0, &d, std::move(yb));
+        const Operand o = operand(y);
+        return then<R2>(op, TADMA_SRC_NONE, 0.0, &o);
     }
 
     // A chain whose source is this chain's materialised value.
@@ -326,8 +350,7 @@ template <AnyTensor T> requires LazyTensor<T> auto operator-(const T& t) { retur
     template <AnyTensor A, AnyTensor B>                                                              \
         requires LazyTensor<A>                                                                       \
     A& operator sym(A& a, const B& b) {                                                              \
-        if constexpr (LazyTensor<B>) a = a.template then<typename A::ValueType>(OPC, b.materialised()); \
-        else a = a.template then<typename A::ValueType>(OPC, b);                                     \
+        a = a.template then<typename A::ValueType>(OPC, b);                                          \
         return a;                                                                                    \
     }
 TADMA_LAZY_ASSIGN(+=, TADMA_OP_ADD)
@@ -367,6 +390,17 @@ TADMA_LAZY_MKOP(tanh, TADMA_OP_TANH, math_t<typename TT::ValueType>)
 TADMA_LAZY_MKOP(gelu, TADMA_OP_GELU, double)
 TADMA_LAZY_MKOP(negate, TADMA_OP_NEG, typename TT::ValueType)
 #undef TADMA_LAZY_MKOP
+
+// where(c, x, y) with a lazy condition (Operations.hpp:235-242): one
+// TADMA_OP_WHERE step reading x and y as operands; the result has the
+// condition's dims and the eager result type.
+template <AnyTensor Cond, AnyTensor X, AnyTensor Y>
+    requires LazyTensor<Cond>
+auto where(const Cond& c, const X& x, const Y& y) {
+    using R = arith_t<typename X::ValueType, typename Y::ValueType>;
+    const auto ox = c.operand(x), oy = c.operand(y);
+    return c.template then<R>(TADMA_OP_WHERE, TADMA_SRC_NONE, 0.0, &ox, &oy);
+}
 
 template <bool Inplace = true, AnyTensor T, Scalar S>
     requires LazyTensor<T>

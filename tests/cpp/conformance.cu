@@ -238,6 +238,13 @@ int main(int argc, char** argv) {
         save("lazy_square", lazy(A) * A + A2 * lazy(A2));  // operands that are the source
         save("eager_square", A * A + A2 * A2);
 
+        // where with a lazy condition: one step reading both branches
+        auto lw = where(lazy(A) > A2, A3, lazy(A4) * 2.0f);
+        static_assert(LazyTensor<decltype(lw)> && std::is_same_v<decltype(lw)::ValueType, float>);
+        save("lazy_where", lw + 1.0f);
+        save("eager_where", where(A > A2, A3, A4 * 2.0f) + 1.0f);
+        save("lazy_where_sum", where(lazy(X) < 0.0f, X * 0.5f, X).template sum<-1>());
+        save("eager_where_sum", where(X < 0.0f, X * 0.5f, X).template sum<-1>());
         save("lazy_softmax", softmax<-1, false>(lazy(S) * 0.5f));  // consumed by an eager API call
         save("eager_softmax", softmax<-1, false>(S * 0.5f));
         // an in-place call materialises the lazy value and writes there; later

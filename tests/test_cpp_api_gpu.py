@@ -145,6 +145,7 @@ LAZY_PAIRS = [
     ("long", np.float32, (64, 128)),
     ("operands", np.float32, (64, 128)),
     ("square", np.float32, (64, 128)),
+    ("where", np.float32, (64, 128)),
     ("softmax", np.float32, (2, 4, 256, 2048)),
     ("softmax_then", np.float32, (2, 4, 256, 1)),
 ]
@@ -169,3 +170,9 @@ def test_lazy_reductions(results):
     L = gen((4, 16, 1024), DType.F16, Dist.NORMAL, 0.0, 1.0, 4).astype(np.float64)
     np.testing.assert_allclose(lazy, eager, rtol=1e-5 * 32, atol=1e-5 * 32)
     np.testing.assert_allclose(lazy, np.tanh(L).sum(-1, keepdims=True), rtol=1e-5 * 32, atol=1e-4)
+    # where with a lazy condition, reduced in the same kernel
+    X = gen((2, 64, 256), DType.F32, Dist.UNIFORM, -1.0, 1.0, 3).astype(np.float64)
+    lazy, eager = results("lazy_where_sum", np.float32, (2, 64, 1)), results("eager_where_sum", np.float32, (2, 64, 1))
+    ref = np.where(X < 0, X * 0.5, X).sum(-1, keepdims=True)
+    np.testing.assert_allclose(lazy, eager, atol=1e-5 * 16)
+    np.testing.assert_allclose(lazy, ref, atol=1e-5 * 16)
