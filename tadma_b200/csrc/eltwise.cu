@@ -14,11 +14,11 @@
 //   16-byte loads/stores (2 x 16 B for fp32, 1 x 16 B for 16-bit types); an
 //   operand whose innermost stride is 0 is loaded once and splatted;
 //   operands with no broadcast stream through with evict-first hints;
-// * grid-stride persistent grid (SMs x resident blocks), U = 2 vector steps
-//   in flight per thread before any compute, so each SM keeps >= 32 KB of
-//   loads outstanding;
-// * any other layout takes the scalar path (one element per thread step,
-//   DivMod index decomposition, still 64-bit safe);
+// * one contiguous chunk per CTA (U = 2 vector steps per thread, 1 with 3-4
+//   operands, loaded before any compute) and as many CTAs as chunks, so the
+//   block scheduler balances the SMs;
+// * any other layout takes the scalar path (SU elements per thread, DivMod
+//   index decomposition, still 64-bit safe);
 // * the chain is uniform across the grid (kernel parameters), so the
 //   per-instruction switch is a uniform branch amortised over 8 elements.
 #include <mutex>
@@ -34,7 +34,10 @@ namespace tadma_b200 {
 namespace {
 
 constexpr int V = 8;        // elements per vector step
-constexpr int U = 2;        // vector steps in flight per thread
+// Vector steps in flight per thread: 2, or 1 with 3-4 operands (their
+// registers would otherwise halve the resident warps).
+template <int NIN>
+constexpr int vec_steps() { return NIN >= 3 ? 1 : 2; }
 constexpr int THREADS = 256;
 
 struct Operand {
@@ -280,12 +283,35 @@ __device__ __forceinline__ void load_vec(const Operand& o, int64_t off, C (&v)[V
         for (int j = 0; j < V; j++) v[j] = from_f<C>(f[j]);
         break;
     }
+    case TADMA_U8:
+    case TADMA_BOOL:
+    case TADMA_I8: {
+        // 8 one-byte elements in one 8-byte load; values as load_as gives them
+        const uint2 a = o.streaming ? __ldcs(reinterpret_cast<const uint2*>(p)) : *reinterpret_cast<const uint2*>(p);
+#pragma unroll
+        for (int j = 0; j < V; j++) {
+            const uint32_t byte = ((j < 4 ? a.x : a.y) >> (8 * (j & 3))) & 0xffu;
+            const int32_t iv = o.dtype == TADMA_I8 ? (int32_t)(int8_t)byte : o.dtype == TADMA_BOOL ? (byte != 0u) : (int32_t)byte;
+            v[j] = (C)iv;
+        }
+        break;
+    }
     default: {
 #pragma unroll
         for (int j = 0; j < V; j++) v[j] = load_as<C>(o.base, o.dtype, off + j);
         break;
     }
     }
+}
+
+// The byte store_from writes for a one-byte dtype.
+template <typename C>
+__device__ __forceinline__ uint32_t to_byte(C v, int dt) {
+    if (dt == TADMA_BOOL) return v != C(0) ? 1u : 0u;
+    int64_t i;
+    if constexpr (std::is_integral<C>::value) i = v;
+    else i = f2i(v);
+    return (uint32_t)(uint8_t)i;
 }
 
 template <typename C>
@@ -317,11 +343,70 @@ __device__ __forceinline__ void store_vec(char* base, int dt, int64_t off, const
 #pragma unroll
             for (int j = 0; j < V; j++) f[j] = to_f(v[j]);
             st_stream_v4(p, pack8(f, dt));
+        } else if (dt == TADMA_U8 || dt == TADMA_BOOL || dt == TADMA_I8) {
+            uint2 w = make_uint2(0u, 0u);
+#pragma unroll
+            for (int j = 0; j < V; j++) {
+                const uint32_t b = to_byte<C>(v[j], dt) << (8 * (j & 3));
+                if (j < 4) w.x |= b;
+                else w.y |= b;
+            }
+            __stcs(reinterpret_cast<uint2*>(p), w);
         } else {
 #pragma unroll
             for (int j = 0; j < V; j++) store_from(base, dt, off + j, v[j]);
         }
         break;
+    }
+}
+
+// Narrow operands (every input 1 or 2 bytes wide, or an innermost broadcast
+// of at most 4 bytes): one vector is kept as its raw 16-byte word and
+// converted to fp32 only when it is computed, so a thread can hold 4 vectors
+// of 2 operands in flight in 32 registers.
+__device__ __forceinline__ uint4 load_raw_narrow(const Operand& o, int64_t off) {
+    if (o.inner_bcast) {
+        // the element's raw bits (<= 4 bytes) in .x
+        const char* q = o.base + off * dtype_size(o.dtype);
+        const int es = dtype_size(o.dtype);
+        const uint32_t bits = es == 4 ? *reinterpret_cast<const uint32_t*>(q)
+                            : es == 2 ? (uint32_t)*reinterpret_cast<const uint16_t*>(q)
+                                      : (uint32_t)*reinterpret_cast<const uint8_t*>(q);
+        return make_uint4(bits, 0u, 0u, 0u);
+    }
+    const char* q = o.base + off * dtype_size(o.dtype);
+    if (dtype_size(o.dtype) == 2) return o.streaming ? ld_stream_v4(q) : ld_v4(q);
+    const uint2 a = o.streaming ? __ldcs(reinterpret_cast<const uint2*>(q)) : *reinterpret_cast<const uint2*>(q);
+    return make_uint4(a.x, a.y, 0u, 0u);
+}
+
+// fp32 value of one narrow element given its raw bits (as load_as<float>).
+__device__ __forceinline__ float narrow_value(uint32_t bits, int dt) {
+    switch (dt) {
+    case TADMA_F32: return __uint_as_float(bits);
+    case TADMA_F16: return __half2float(__ushort_as_half((unsigned short)bits));
+    case TADMA_BF16: return __uint_as_float(bits << 16);
+    case TADMA_I32: return __int2float_rn((int32_t)bits);
+    case TADMA_U8: return (float)(bits & 0xffu);
+    case TADMA_BOOL: return (bits & 0xffu) != 0u ? 1.0f : 0.0f;
+    case TADMA_I8: return (float)(int8_t)(bits & 0xffu);
+    }
+    return 0.0f;
+}
+
+__device__ __forceinline__ void cvt_raw_narrow(const Operand& o, uint4 r, float (&v)[V]) {
+    if (o.inner_bcast) {
+        const float x = narrow_value(r.x, o.dtype);
+#pragma unroll
+        for (int j = 0; j < V; j++) v[j] = x;
+    } else if (o.dtype == TADMA_F16 || o.dtype == TADMA_BF16) {
+        unpack8(r, o.dtype, v);
+    } else {
+#pragma unroll
+        for (int j = 0; j < V; j++) {
+            const uint32_t byte = ((j < 4 ? r.x : r.y) >> (8 * (j & 3))) & 0xffu;
+            v[j] = o.dtype == TADMA_I8 ? (float)(int8_t)byte : o.dtype == TADMA_BOOL ? (byte != 0u ? 1.0f : 0.0f) : (float)byte;
+        }
     }
 }
 
@@ -345,17 +430,23 @@ __device__ __forceinline__ void offsets(const ChainParams& p, uint64_t e, int64_
     for (int k = 0; k < NIN; k++) io[k] += (int64_t)e * p.in[k].stride[0];
 }
 
+// Both kernels give each CTA one contiguous chunk of work and are launched
+// with enough CTAs to cover the launch in one pass (the loop over chunks only
+// runs past one iteration when the work needs more than 2^31 - 1 CTAs): the
+// hardware block scheduler then balances SMs, where a persistent grid-stride
+// loop measured 10-15 % slower on B200.
 template <typename C, int NIN, int PROG>
 __global__ void __launch_bounds__(THREADS) chain_vec_kernel(const __grid_constant__ ChainParams p) {
     pdl_begin();
     constexpr int NI = NIN > 0 ? NIN : 1;
-    const int64_t gstride = (int64_t)gridDim.x * THREADS;
-    for (int64_t base = (int64_t)blockIdx.x * THREADS + threadIdx.x; base < p.n; base += gstride * U) {
+    constexpr int U = vec_steps<NIN>();
+    for (int64_t chunk = blockIdx.x; chunk * (THREADS * U) < p.n; chunk += gridDim.x) {
+        const int64_t base = chunk * (THREADS * U) + threadIdx.x;
         C val[U][NI][V];
         int64_t oo[U];
 #pragma unroll
         for (int u = 0; u < U; u++) {
-            const int64_t vi = base + u * gstride;
+            const int64_t vi = base + u * THREADS;
             if (vi < p.n) {
                 int64_t io[NI];
                 offsets<NIN>(p, (uint64_t)vi * V, oo[u], io);
@@ -365,7 +456,7 @@ __global__ void __launch_bounds__(THREADS) chain_vec_kernel(const __grid_constan
         }
 #pragma unroll
         for (int u = 0; u < U; u++) {
-            const int64_t vi = base + u * gstride;
+            const int64_t vi = base + u * THREADS;
             if (vi < p.n) {
                 C acc[V];
 #pragma unroll
@@ -377,20 +468,67 @@ __global__ void __launch_bounds__(THREADS) chain_vec_kernel(const __grid_constan
     }
 }
 
+// The narrow-operand variant of chain_vec_kernel (fp32 compute): raw words
+// of U vectors per thread are loaded before any compute.
+template <int NIN>
+constexpr int narrow_steps() { return NIN >= 3 ? 2 : 4; }
+
+template <int NIN, int PROG>
+__global__ void __launch_bounds__(THREADS) chain_narrow_kernel(const __grid_constant__ ChainParams p) {
+    pdl_begin();
+    constexpr int NI = NIN > 0 ? NIN : 1;
+    constexpr int U = narrow_steps<NIN>();
+    for (int64_t chunk = blockIdx.x; chunk * (THREADS * U) < p.n; chunk += gridDim.x) {
+        const int64_t base = chunk * (THREADS * U) + threadIdx.x;
+        uint4 raw[U][NI];
+        int64_t oo[U];
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int64_t vi = base + u * THREADS;
+            if (vi < p.n) {
+                int64_t io[NI];
+                offsets<NIN>(p, (uint64_t)vi * V, oo[u], io);
+#pragma unroll
+                for (int k = 0; k < NIN; k++) raw[u][k] = load_raw_narrow(p.in[k], io[k]);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int64_t vi = base + u * THREADS;
+            if (vi < p.n) {
+                float val[NI][V];
+#pragma unroll
+                for (int k = 0; k < NIN; k++) cvt_raw_narrow(p.in[k], raw[u][k], val[k]);
+                float acc[V];
+#pragma unroll
+                for (int j = 0; j < V; j++) acc[j] = NIN > 0 ? val[0][j] : 0.0f;
+                program<float, NIN, V, PROG>(p, acc, val);
+                store_vec<float>(p.out, p.out_dtype, oo[u], acc);
+            }
+        }
+    }
+}
+
+constexpr int SU = 4;  // elements per thread of the scalar kernel
+
 template <typename C, int NIN, int PROG>
 __global__ void __launch_bounds__(THREADS) chain_scalar_kernel(const __grid_constant__ ChainParams p) {
     pdl_begin();
     constexpr int NI = NIN > 0 ? NIN : 1;
-    const int64_t gstride = (int64_t)gridDim.x * THREADS;
-    for (int64_t e = p.start + (int64_t)blockIdx.x * THREADS + threadIdx.x; e < p.n; e += gstride) {
-        int64_t oo, io[NI];
-        offsets<NIN>(p, (uint64_t)e, oo, io);
-        C val[NI][1];
+    for (int64_t chunk = blockIdx.x; p.start + chunk * (THREADS * SU) < p.n; chunk += gridDim.x) {
 #pragma unroll
-        for (int k = 0; k < NIN; k++) val[k][0] = load_as<C>(p.in[k].base, p.in[k].dtype, io[k]);
-        C acc[1] = {NIN > 0 ? val[0][0] : C(0)};
-        program<C, NIN, 1, PROG>(p, acc, val);
-        store_from(p.out, p.out_dtype, oo, acc[0]);
+        for (int k = 0; k < SU; k++) {
+            const int64_t e = p.start + chunk * (THREADS * SU) + k * THREADS + threadIdx.x;
+            if (e >= p.n) break;
+            int64_t oo, io[NI];
+            offsets<NIN>(p, (uint64_t)e, oo, io);
+            C val[NI][1];
+#pragma unroll
+            for (int q = 0; q < NIN; q++) val[q][0] = load_as<C>(p.in[q].base, p.in[q].dtype, io[q]);
+            C acc[1] = {NIN > 0 ? val[0][0] : C(0)};
+            program<C, NIN, 1, PROG>(p, acc, val);
+            store_from(p.out, p.out_dtype, oo, acc[0]);
+        }
     }
 }
 
@@ -398,10 +536,10 @@ __global__ void __launch_bounds__(THREADS) chain_scalar_kernel(const __grid_cons
 //
 // y[r, c] = act(x[r, c] * s + b[c]) over a [rows, cols] layout (cols % 8 == 0)
 // with a row-broadcast b: the bias-plus-activation pattern of config 2 and of
-// every dense layer.  Each thread owns one 8-column vector for all of its rows,
-// so b is loaded and converted once and stays in registers, the row loop needs
-// no index division, and the next 4 rows' loads are in flight while 4 rows
-// compute.  x * s + b and the fast GELU polynomial run as packed fp32x2
+// every dense layer.  Each thread owns one 8-column vector of a tile of RB
+// rows, so b is loaded and converted once per RB rows, no index division is
+// needed, and all RB rows' loads are in flight before the first computes.
+// x * s + b and the fast GELU polynomial run as packed fp32x2
 // instructions (sm_100), every lane rounded as the scalar op would be, so the
 // bits equal the generic path's (__fmul_rn, __fadd_rn, activation<ACT, FAST>).
 
@@ -481,14 +619,31 @@ __device__ __forceinline__ void affine_row_compute(const Raw8x<XT>& raw, const f
     raw8_store<OT>(dst, v);
 }
 
+// One CTA per tile of RB consecutive rows x 256 column vectors, no loop: all
+// RB rows' loads are issued before the first row computes, and the hardware
+// block scheduler hands tiles to SMs as they free up (a persistent grid-stride
+// loop measured 10-15 % slower on B200 for streaming copies: its fixed share of
+// work per CTA leaves the slowest SMs finishing last).
+template <typename XT>
+constexpr int affine_rb() { return sizeof(XT) == 2 ? 8 : 4; }
+
 template <typename XT, typename OT, int ACT>
-__global__ void __launch_bounds__(THREADS, sizeof(XT) == 2 ? 3 : 2) affine_rows_kernel(const __grid_constant__ AffineRowsParams p) {
+__global__ void __launch_bounds__(THREADS) affine_rows_kernel(const __grid_constant__ AffineRowsParams p) {
     pdl_begin();
-    // Double-buffered over rows: the next UR rows' loads are in flight while
-    // the current UR rows compute and store.
-    constexpr int UR = 4;
-    const int64_t cv = (int64_t)blockIdx.x * THREADS + threadIdx.x;
+    constexpr int RB = affine_rb<XT>();
+    // blockIdx.x = row tile * column blocks + column block: the column blocks
+    // of one row tile are neighbours in launch order (one contiguous region).
+    const int64_t ncb = (p.ncv + THREADS - 1) / THREADS;
+    const int64_t tile = (int64_t)blockIdx.x / ncb;
+    const int64_t cv = ((int64_t)blockIdx.x - tile * ncb) * THREADS + threadIdx.x;
     if (cv >= p.ncv) return;
+    const int64_t r0 = tile * RB;
+    const XT* xcol = reinterpret_cast<const XT*>(p.x) + cv * 8;
+    OT* ocol = reinterpret_cast<OT*>(p.out) + cv * 8;
+    Raw8x<XT> cur[RB];
+#pragma unroll
+    for (int u = 0; u < RB; u++)
+        if (r0 + u < p.rows) raw8_load<XT>(xcol + (r0 + u) * p.x_rs, cur[u], true);
     float b[8];
     unsigned long long b2[4];
     {
@@ -498,27 +653,9 @@ __global__ void __launch_bounds__(THREADS, sizeof(XT) == 2 ? 3 : 2) affine_rows_
 #pragma unroll
         for (int j = 0; j < 4; j++) b2[j] = f2_pack(b[2 * j], b[2 * j + 1]);
     }
-    const XT* xcol = reinterpret_cast<const XT*>(p.x) + cv * 8;
-    OT* ocol = reinterpret_cast<OT*>(p.out) + cv * 8;
-    const int64_t ystep = gridDim.y;
-    Raw8x<XT> cur[UR], nxt[UR];
-    int64_t r0 = blockIdx.y;
 #pragma unroll
-    for (int u = 0; u < UR; u++)
-        if (r0 + u * ystep < p.rows) raw8_load<XT>(xcol + (r0 + u * ystep) * p.x_rs, cur[u], true);
-    for (; r0 < p.rows; r0 += ystep * UR) {
-        const int64_t rn = r0 + ystep * UR;
-#pragma unroll
-        for (int u = 0; u < UR; u++)
-            if (rn + u * ystep < p.rows) raw8_load<XT>(xcol + (rn + u * ystep) * p.x_rs, nxt[u], true);
-#pragma unroll
-        for (int u = 0; u < UR; u++) {
-            const int64_t r = r0 + u * ystep;
-            if (r < p.rows) affine_row_compute<XT, OT, ACT>(cur[u], b, b2, p.scale, ocol + r * p.out_rs);
-        }
-#pragma unroll
-        for (int u = 0; u < UR; u++) cur[u] = nxt[u];
-    }
+    for (int u = 0; u < RB; u++)
+        if (r0 + u < p.rows) affine_row_compute<XT, OT, ACT>(cur[u], b, b2, p.scale, ocol + (r0 + u) * p.out_rs);
 }
 
 // ---------------------------------------------------------- tiled transpose --
@@ -746,63 +883,72 @@ int blocks_per_sm(const void* fn) {
     return nb;
 }
 
+// `narrow`: fp32 compute and every operand narrow (see load_raw_narrow).
 template <typename C, int NIN, int PROG>
-int launch(const ChainParams& p, bool vec, int64_t work, cudaStream_t s) {
-    const void* fn = vec ? (const void*)chain_vec_kernel<C, NIN, PROG> : (const void*)chain_scalar_kernel<C, NIN, PROG>;
-    int64_t per_block = (int64_t)THREADS * (vec ? U : 1);
-    int64_t want = (work + per_block - 1) / per_block;
-    int64_t cap = (int64_t)sm_count() * blocks_per_sm(fn);
-    int grid = (int)(want < cap ? (want > 0 ? want : 1) : cap);
-    if (vec) (void)launch_pdl(chain_vec_kernel<C, NIN, PROG>, dim3(grid), dim3(THREADS), 0, s, p);
-    else (void)launch_pdl(chain_scalar_kernel<C, NIN, PROG>, dim3(grid), dim3(THREADS), 0, s, p);
+int launch(const ChainParams& p, bool vec, int64_t work, cudaStream_t s, bool narrow = false) {
+    narrow = narrow && vec && std::is_same<C, float>::value;
+    const int64_t per_block = (int64_t)THREADS * (!vec ? SU : narrow ? narrow_steps<NIN>() : vec_steps<NIN>());
+    const int64_t want = (work + per_block - 1) / per_block;
+    const int grid = (int)(want < 1 ? 1 : want > 0x7fffffff ? 0x7fffffff : want);
+    if (narrow) {
+        if constexpr (std::is_same<C, float>::value)
+            (void)launch_pdl(chain_narrow_kernel<NIN, PROG>, dim3(grid), dim3(THREADS), 0, s, p);
+    } else if (vec) {
+        (void)launch_pdl(chain_vec_kernel<C, NIN, PROG>, dim3(grid), dim3(THREADS), 0, s, p);
+    } else {
+        (void)launch_pdl(chain_scalar_kernel<C, NIN, PROG>, dim3(grid), dim3(THREADS), 0, s, p);
+    }
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? TADMA_OK : cuda_fail(e, "tadma_b200_eltwise launch");
 }
 
-// Interpreter launch; `fast` only exists for fp32 compute.
+// Interpreter launch; `fast` and `narrow` only exist for fp32 compute.
 template <typename C>
-int launch_interp(int nin, bool fast, const ChainParams& p, bool vec, int64_t work, cudaStream_t s) {
+int launch_interp(int nin, bool fast, const ChainParams& p, bool vec, int64_t work, cudaStream_t s, bool narrow) {
     if constexpr (std::is_same<C, float>::value) {
         if (fast) {
             switch (nin) {
-            case 0: return launch<C, 0, PROG_INTERP_FAST>(p, vec, work, s);
-            case 1: return launch<C, 1, PROG_INTERP_FAST>(p, vec, work, s);
-            case 2: return launch<C, 2, PROG_INTERP_FAST>(p, vec, work, s);
-            case 3: return launch<C, 3, PROG_INTERP_FAST>(p, vec, work, s);
-            default: return launch<C, 4, PROG_INTERP_FAST>(p, vec, work, s);
+            case 0: return launch<C, 0, PROG_INTERP_FAST>(p, vec, work, s, narrow);
+            case 1: return launch<C, 1, PROG_INTERP_FAST>(p, vec, work, s, narrow);
+            case 2: return launch<C, 2, PROG_INTERP_FAST>(p, vec, work, s, narrow);
+            case 3: return launch<C, 3, PROG_INTERP_FAST>(p, vec, work, s, narrow);
+            default: return launch<C, 4, PROG_INTERP_FAST>(p, vec, work, s, narrow);
             }
         }
     }
     switch (nin) {
-    case 0: return launch<C, 0, PROG_INTERP>(p, vec, work, s);
-    case 1: return launch<C, 1, PROG_INTERP>(p, vec, work, s);
-    case 2: return launch<C, 2, PROG_INTERP>(p, vec, work, s);
-    case 3: return launch<C, 3, PROG_INTERP>(p, vec, work, s);
-    default: return launch<C, 4, PROG_INTERP>(p, vec, work, s);
+    case 0: return launch<C, 0, PROG_INTERP>(p, vec, work, s, narrow);
+    case 1: return launch<C, 1, PROG_INTERP>(p, vec, work, s, narrow);
+    case 2: return launch<C, 2, PROG_INTERP>(p, vec, work, s, narrow);
+    case 3: return launch<C, 3, PROG_INTERP>(p, vec, work, s, narrow);
+    default: return launch<C, 4, PROG_INTERP>(p, vec, work, s, narrow);
     }
 }
 
 // Affine + activation vector kernels (fp32 compute).
 template <int ACT, bool FAST, bool MUL>
-int launch_affine_add(bool add, const ChainParams& p, int64_t work, cudaStream_t s) {
-    if (add) return launch<float, 2, affine_prog(ACT, FAST, MUL, true)>(p, true, work, s);
-    return launch<float, 1, affine_prog(ACT, FAST, MUL, false)>(p, true, work, s);
+int launch_affine_add(bool add, const ChainParams& p, int64_t work, cudaStream_t s, bool narrow) {
+    if (add) return launch<float, 2, affine_prog(ACT, FAST, MUL, true)>(p, true, work, s, narrow);
+    return launch<float, 1, affine_prog(ACT, FAST, MUL, false)>(p, true, work, s, narrow);
 }
 template <int ACT, bool FAST>
-int launch_affine_mul(bool mul, bool add, const ChainParams& p, int64_t work, cudaStream_t s) {
-    return mul ? launch_affine_add<ACT, FAST, true>(add, p, work, s) : launch_affine_add<ACT, FAST, false>(add, p, work, s);
+int launch_affine_mul(bool mul, bool add, const ChainParams& p, int64_t work, cudaStream_t s, bool narrow) {
+    return mul ? launch_affine_add<ACT, FAST, true>(add, p, work, s, narrow)
+               : launch_affine_add<ACT, FAST, false>(add, p, work, s, narrow);
 }
 template <int ACT>
-int launch_affine_fast(bool fast, bool mul, bool add, const ChainParams& p, int64_t work, cudaStream_t s) {
-    return fast ? launch_affine_mul<ACT, true>(mul, add, p, work, s) : launch_affine_mul<ACT, false>(mul, add, p, work, s);
+int launch_affine_fast(bool fast, bool mul, bool add, const ChainParams& p, int64_t work, cudaStream_t s, bool narrow) {
+    return fast ? launch_affine_mul<ACT, true>(mul, add, p, work, s, narrow)
+                : launch_affine_mul<ACT, false>(mul, add, p, work, s, narrow);
 }
-int launch_affine(int act, bool fast, bool mul, bool add, const ChainParams& p, int64_t work, cudaStream_t s) {
+int launch_affine(int act, bool fast, bool mul, bool add, const ChainParams& p, int64_t work, cudaStream_t s,
+                  bool narrow) {
     switch (act) {
-    case ACT_GELU: return launch_affine_fast<ACT_GELU>(fast, mul, add, p, work, s);
-    case ACT_RELU: return launch_affine_fast<ACT_RELU>(fast, mul, add, p, work, s);
-    case ACT_SIGMOID: return launch_affine_fast<ACT_SIGMOID>(fast, mul, add, p, work, s);
-    case ACT_TANH: return launch_affine_fast<ACT_TANH>(fast, mul, add, p, work, s);
-    default: return launch_affine_fast<ACT_NONE>(fast, mul, add, p, work, s);
+    case ACT_GELU: return launch_affine_fast<ACT_GELU>(fast, mul, add, p, work, s, narrow);
+    case ACT_RELU: return launch_affine_fast<ACT_RELU>(fast, mul, add, p, work, s, narrow);
+    case ACT_SIGMOID: return launch_affine_fast<ACT_SIGMOID>(fast, mul, add, p, work, s, narrow);
+    case ACT_TANH: return launch_affine_fast<ACT_TANH>(fast, mul, add, p, work, s, narrow);
+    default: return launch_affine_fast<ACT_NONE>(fast, mul, add, p, work, s, narrow);
     }
 }
 
@@ -842,15 +988,10 @@ AffineMatch match_affine(const tadma_instr* prog, int n_instr, int n_ins) {
 
 template <typename XT, typename OT, int ACT>
 int launch_rows_t(const AffineRowsParams& p, cudaStream_t s) {
-    const void* fn = (const void*)affine_rows_kernel<XT, OT, ACT>;
-    const int64_t gx = (p.ncv + THREADS - 1) / THREADS;
-    int64_t target = (int64_t)sm_count() * blocks_per_sm(fn);
-    int64_t gy = (target + gx - 1) / gx;
-    if (gy > p.rows) gy = p.rows;
-    if (gy > 65535) gy = 65535;
-    if (gy < 1) gy = 1;
-    if (gx > 0x7fffffff) return fail(TADMA_ERR_UNSUPPORTED, "eltwise: too many column vectors");
-    cudaError_t e = launch_pdl(affine_rows_kernel<XT, OT, ACT>, dim3((unsigned)gx, (unsigned)gy), dim3(THREADS), 0, s, p);
+    const int64_t ncb = (p.ncv + THREADS - 1) / THREADS;
+    const int64_t tiles = (p.rows + affine_rb<XT>() - 1) / affine_rb<XT>();
+    if (ncb * tiles > 0x7fffffff) return fail(TADMA_ERR_UNSUPPORTED, "eltwise: more than 2^31 row tiles");
+    cudaError_t e = launch_pdl(affine_rows_kernel<XT, OT, ACT>, dim3((unsigned)(ncb * tiles)), dim3(THREADS), 0, s, p);
     if (e == cudaSuccess) e = cudaGetLastError();
     return e == cudaSuccess ? TADMA_OK : cuda_fail(e, "tadma_b200_eltwise launch");
 }
@@ -1053,11 +1194,17 @@ extern "C" int tadma_b200_eltwise(const tadma_tensor* out, const tadma_tensor* i
         if (!(rd < 0 || rd == TADMA_F32 || rd == TADMA_F16 || rd == TADMA_BF16)) fast = false;
     }
     cudaStream_t s = (cudaStream_t)stream;
+    // Narrow operands (fp32 compute): the raw-word kernel keeps more loads in flight.
+    bool narrow = vec && cm == TADMA_COMPUTE_F32;
+    for (int k = 0; k < n_ins && narrow; k++) {
+        const int es = dtype_size(ins[k].dtype);
+        narrow = p.in[k].inner_bcast ? (es <= 4 && ins[k].dtype != TADMA_F64 && ins[k].dtype != TADMA_I64) : es <= 2;
+    }
     auto go = [&](const ChainParams& pp, bool v, int64_t work) {
         switch (cm) {
-        case TADMA_COMPUTE_F32: return launch_interp<float>(n_ins, fast, pp, v, work, s);
-        case TADMA_COMPUTE_F64: return launch_interp<double>(n_ins, false, pp, v, work, s);
-        default: return launch_interp<int64_t>(n_ins, false, pp, v, work, s);
+        case TADMA_COMPUTE_F32: return launch_interp<float>(n_ins, fast, pp, v, work, s, narrow);
+        case TADMA_COMPUTE_F64: return launch_interp<double>(n_ins, false, pp, v, work, s, false);
+        default: return launch_interp<int64_t>(n_ins, false, pp, v, work, s, false);
         }
     };
     if (!vec) {
@@ -1121,7 +1268,7 @@ extern "C" int tadma_b200_eltwise(const tadma_tensor* out, const tadma_tensor* i
         rc = launch_rows(ins[0].dtype, out->dtype, am.act, ap, s);
     } else if (am.ok) {
         pv.scale = am.scale;
-        rc = launch_affine(am.act, fast, am.mul, am.add, pv, nvec, s);
+        rc = launch_affine(am.act, fast, am.mul, am.add, pv, nvec, s, narrow);
     } else {
         rc = go(pv, true, nvec);
     }

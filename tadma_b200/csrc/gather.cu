@@ -236,10 +236,10 @@ int blocks_per_sm(const void* fn) {
 
 template <typename TT, typename AT, typename OT, bool ADD>
 int launch_rows(const GatherParams& p, cudaStream_t s) {
-    const void* fn = (const void*)gather_rows_kernel<TT, AT, OT, ADD>;
-    int64_t want = (p.nrows + (THREADS / 32) - 1) / (THREADS / 32);
-    int64_t cap = (int64_t)sm_count() * blocks_per_sm(fn);
-    int grid = (int)(want < cap ? (want > 0 ? want : 1) : cap);
+    // One row per warp and as many CTAs as that takes: the block scheduler
+    // balances the SMs (a persistent grid-stride grid measured slower on B200).
+    const int64_t want = (p.nrows + (THREADS / 32) - 1) / (THREADS / 32);
+    const int grid = (int)(want < 1 ? 1 : want > 0x7fffffff ? 0x7fffffff : want);
     (void)launch_pdl(gather_rows_kernel<TT, AT, OT, ADD>, dim3(grid), dim3(THREADS), 0, s, p);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? TADMA_OK : cuda_fail(e, "tadma_b200_gather launch");

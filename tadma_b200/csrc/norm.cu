@@ -462,6 +462,11 @@ int blocks_per_sm(const void* fn) {
 
 template <typename T, int CH, int MODE>
 int launch_warp(const NormParams& p, cudaStream_t s) {
+    // Persistent: resident CTAs only, each warp walking rows.  Launching one
+    // CTA per 8 rows (the block scheduler balancing SMs, which wins for the
+    // streaming kernels) measured slower here: config 4 at 5354 GB/s with one
+    // row per warp, 6043 with 4 and 6138 with 16, against 6185 persistent; a
+    // warp's row ends in a reduction whose latency the next row hides.
     const void* fn = (const void*)rownorm_warp_kernel<T, CH, MODE>;
     int64_t want = (p.nrows + (THREADS / 32) - 1) / (THREADS / 32);
     int64_t cap = (int64_t)sm_count() * blocks_per_sm(fn);

@@ -248,3 +248,47 @@ def test_transpose_with_chain():
     ref = np.zeros((6, 66, 130), np.uint16)
     assert O.eltwise(ref, [np.transpose(x, (0, 2, 1))], prog, Compute.F32, out_dtype=DType.BF16, in_dtypes=[DType.F32]) == 0
     assert ulp_diff(from_dev(out), ref, DType.BF16).max() <= 1
+
+
+# ---- narrow operands (raw-word vector kernel) -------------------------------
+# Every input 1 or 2 bytes wide, or an innermost broadcast of at most 4 bytes:
+# the kernel holds raw 16-byte words and converts at compute time.  Results
+# must equal the oracle bit for bit (only exact ops in these chains).
+
+@pytest.mark.parametrize("shape", [(64, 1024), (37, 1000), (3, 24), (5, 8)])
+def test_narrow_operand_kinds(shape):
+    R, C = shape
+    x16 = gen(shape, DType.F16, Dist.NORMAL, 0, 1, 40)
+    xb = gen(shape, DType.BF16, Dist.NORMAL, 0, 1, 41)
+    u8 = gen(shape, DType.U8, Dist.INDEX, 0, 256, 42)
+    i8 = (gen(shape, DType.I32, Dist.INDEX, 0, 256, 43) - 128).astype(np.int8)
+    m = gen(shape, DType.F32, Dist.UNIFORM, -1, 1, 44) > 0
+    # (m ? u8 : i8) + bf16: four narrow operands
+    got, ref = run_both(shape, DType.F32, [(m, DType.BOOL), (u8, DType.U8), (i8, DType.I8), (xb, DType.BF16)],
+                        [instr(Op.WHERE, b=1, c=2), instr(Op.ADD, b=3, round_dtype=DType.F32)])
+    assert np.array_equal(got, ref)
+    # f16 * u8 + i8 with a bool mask -> bool, u8, f16 outputs
+    for odt in (DType.BOOL, DType.U8, DType.F16, DType.BF16, DType.I8):
+        got, ref = run_both(shape, odt, [(x16, DType.F16), (u8, DType.U8), (i8, DType.I8)],
+                            [instr(Op.MUL, b=1, round_dtype=DType.F32), instr(Op.ADD, b=2, round_dtype=DType.F32)])
+        assert np.array_equal(got.view(np.uint8), ref.view(np.uint8)), odt
+    # innermost-broadcast scalars of 4-byte types (f32, i32) next to narrow operands
+    col_f = np.broadcast_to(gen((R, 1), DType.F32, Dist.NORMAL, 0, 1, 45), shape)
+    col_i = np.broadcast_to(gen((R, 1), DType.I32, Dist.INDEX, 0, 100, 46), shape)
+    got, ref = run_both(shape, DType.F32, [(x16, DType.F16), (col_f, DType.F32), (col_i, DType.I32)],
+                        [instr(Op.MUL, b=1), instr(Op.SUB, b=2)])
+    assert np.array_equal(got, ref)
+
+
+def test_narrow_add_full_size_bits():
+    # the same-shape 16-bit add at [8192, 8192]: every element checked
+    import torch
+    a = empty_dev((8192, 8192), DType.F16)
+    b = empty_dev((8192, 8192), DType.F16)
+    tb.fill(a, Dist.NORMAL, 0.0, 1.0, seed=0, stream_id=47)
+    tb.fill(b, Dist.NORMAL, 0.0, 1.0, seed=0, stream_id=48)
+    y = empty_dev((8192, 8192), DType.F16)
+    tb.eltwise(y, [a, b], [instr(Op.ADD, b=1)])
+    torch.cuda.synchronize()
+    ref = (a.float() + b.float()).half()  # one fp32 add rounded once to fp16
+    assert torch.equal(y.view(torch.int16), ref.view(torch.int16))
