@@ -658,6 +658,180 @@ __global__ void __launch_bounds__(THREADS) affine_rows_kernel(const __grid_const
         if (r0 + u < p.rows) affine_row_compute<XT, OT, ACT>(cur[u], b, b2, p.scale, ocol + (r0 + u) * p.out_rs);
 }
 
+// ------------------------------------------------------- contiguous typed --
+//
+// Every operand contiguous over the whole launch (folded rank 1) and of one
+// float dtype TI, the output of float dtype TO, fp32 compute (residual adds,
+// scalings, casts, contiguous copies): loads, conversions and stores are
+// compile-time and only the chain is interpreted.  The generic kernels decode
+// dtypes and strides per vector, which cost ~170 instructions per 8 elements
+// on a 16-bit add (ncu) and held it to 4.7 TB/s.
+
+// Two vectors per thread: with the interpreter inlined once per vector, more
+// would grow the kernel past what the instruction cache holds.
+template <typename TI>
+constexpr int typed_steps() { return 2; }
+
+template <typename TI, typename TO, int NIN, bool FAST>
+__global__ void __launch_bounds__(THREADS) typed_kernel(const __grid_constant__ ChainParams p) {
+    pdl_begin();
+    constexpr int U = typed_steps<TI>();
+    for (int64_t chunk = blockIdx.x; chunk * (THREADS * U) < p.n; chunk += gridDim.x) {
+        const int64_t base = chunk * (THREADS * U) + threadIdx.x;
+        Raw8x<TI> raw[U][NIN];
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int64_t vi = base + u * THREADS;
+            if (vi < p.n) {
+#pragma unroll
+                for (int k = 0; k < NIN; k++)
+                    raw8_load<TI>(reinterpret_cast<const TI*>(p.in[k].base) + vi * V, raw[u][k], p.in[k].streaming);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int64_t vi = base + u * THREADS;
+            if (vi < p.n) {
+                float val[NIN][V];
+#pragma unroll
+                for (int k = 0; k < NIN; k++) raw8_cvt<TI>(raw[u][k], val[k]);
+                float acc[V];
+#pragma unroll
+                for (int j = 0; j < V; j++) acc[j] = val[0][j];
+                run_chain<float, NIN, V, FAST>(p, acc, val);
+                raw8_store<TO>(reinterpret_cast<TO*>(p.out) + vi * V, acc);
+            }
+        }
+    }
+}
+
+// Single-instruction chains (every operator call of the eager API: a + b,
+// x * s, a cast): the op is a compile-time constant as well, so no
+// interpreter is inlined at all.  OP is ADD, SUB, MUL, DIV, RSUB, RDIV, MAX,
+// MIN or COPY; IMM: the second operand is the immediate, else ins[1].
+template <typename TI, typename TO, int OP, bool IMM>
+__global__ void __launch_bounds__(THREADS) typed1_kernel(const __grid_constant__ ChainParams p) {
+    pdl_begin();
+    constexpr int U = 2;
+    constexpr int NIN = (OP == TADMA_OP_COPY || IMM) ? 1 : 2;
+    const float imm = __double2float_rn(p.prog[0].imm);
+    for (int64_t chunk = blockIdx.x; chunk * (THREADS * U) < p.n; chunk += gridDim.x) {
+        const int64_t base = chunk * (THREADS * U) + threadIdx.x;
+        Raw8x<TI> raw[U][NIN];
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int64_t vi = base + u * THREADS;
+            if (vi < p.n) {
+#pragma unroll
+                for (int k = 0; k < NIN; k++)
+                    raw8_load<TI>(reinterpret_cast<const TI*>(p.in[k].base) + vi * V, raw[u][k], p.in[k].streaming);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int64_t vi = base + u * THREADS;
+            if (vi < p.n) {
+                float a[V], b[V];
+                raw8_cvt<TI>(raw[u][0], a);
+                if constexpr (NIN == 2) raw8_cvt<TI>(raw[u][NIN - 1], b);
+#pragma unroll
+                for (int j = 0; j < V; j++) {
+                    if constexpr (OP != TADMA_OP_COPY) a[j] = binary(OP, a[j], IMM ? imm : b[j], 0.0f);
+                }
+                raw8_store<TO>(reinterpret_cast<TO*>(p.out) + vi * V, a);
+            }
+        }
+    }
+}
+
+template <typename TI, typename TO, int OP, bool IMM>
+int launch_typed1_k(const ChainParams& p, int64_t nvec, cudaStream_t s) {
+    const int64_t per_block = (int64_t)THREADS * 2;
+    const int64_t want = (nvec + per_block - 1) / per_block;
+    const int grid = (int)(want < 1 ? 1 : want > 0x7fffffff ? 0x7fffffff : want);
+    (void)launch_pdl(typed1_kernel<TI, TO, OP, IMM>, dim3(grid), dim3(THREADS), 0, s, p);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? TADMA_OK : cuda_fail(e, "tadma_b200_eltwise launch");
+}
+
+template <typename TI, typename TO, bool IMM>
+int launch_typed1_op(int op, const ChainParams& p, int64_t nvec, cudaStream_t s) {
+    switch (op) {
+    case TADMA_OP_ADD: return launch_typed1_k<TI, TO, TADMA_OP_ADD, IMM>(p, nvec, s);
+    case TADMA_OP_SUB: return launch_typed1_k<TI, TO, TADMA_OP_SUB, IMM>(p, nvec, s);
+    case TADMA_OP_MUL: return launch_typed1_k<TI, TO, TADMA_OP_MUL, IMM>(p, nvec, s);
+    case TADMA_OP_DIV: return launch_typed1_k<TI, TO, TADMA_OP_DIV, IMM>(p, nvec, s);
+    case TADMA_OP_RSUB: return launch_typed1_k<TI, TO, TADMA_OP_RSUB, IMM>(p, nvec, s);
+    case TADMA_OP_RDIV: return launch_typed1_k<TI, TO, TADMA_OP_RDIV, IMM>(p, nvec, s);
+    case TADMA_OP_MAX: return launch_typed1_k<TI, TO, TADMA_OP_MAX, IMM>(p, nvec, s);
+    default: return launch_typed1_k<TI, TO, TADMA_OP_MIN, IMM>(p, nvec, s);
+    }
+}
+
+// Binary ops with an immediate or a second operand; casts / copies for every
+// (TI, TO) pair.  Same-dtype binary ops only (TI == TO), the eager API's case.
+template <typename TI, typename TO>
+int launch_typed1_io(int op, bool imm, const ChainParams& p, int64_t nvec, cudaStream_t s) {
+    if (op == TADMA_OP_COPY) return launch_typed1_k<TI, TO, TADMA_OP_COPY, false>(p, nvec, s);
+    if constexpr (std::is_same<TI, TO>::value) {
+        return imm ? launch_typed1_op<TI, TO, true>(op, p, nvec, s) : launch_typed1_op<TI, TO, false>(op, p, nvec, s);
+    }
+    return TADMA_ERR_UNSUPPORTED;
+}
+
+template <typename TI>
+int launch_typed1_i(int odt, int op, bool imm, const ChainParams& p, int64_t nvec, cudaStream_t s) {
+    switch (odt) {
+    case TADMA_F32: return launch_typed1_io<TI, float>(op, imm, p, nvec, s);
+    case TADMA_F16: return launch_typed1_io<TI, __half>(op, imm, p, nvec, s);
+    default: return launch_typed1_io<TI, __nv_bfloat16>(op, imm, p, nvec, s);
+    }
+}
+
+int launch_typed1(int idt, int odt, int op, bool imm, const ChainParams& p, int64_t nvec, cudaStream_t s) {
+    switch (idt) {
+    case TADMA_F32: return launch_typed1_i<float>(odt, op, imm, p, nvec, s);
+    case TADMA_F16: return launch_typed1_i<__half>(odt, op, imm, p, nvec, s);
+    default: return launch_typed1_i<__nv_bfloat16>(odt, op, imm, p, nvec, s);
+    }
+}
+
+template <typename TI, typename TO, int NIN, bool FAST>
+int launch_typed_k(const ChainParams& p, int64_t nvec, cudaStream_t s) {
+    const int64_t per_block = (int64_t)THREADS * typed_steps<TI>();
+    const int64_t want = (nvec + per_block - 1) / per_block;
+    const int grid = (int)(want < 1 ? 1 : want > 0x7fffffff ? 0x7fffffff : want);
+    (void)launch_pdl(typed_kernel<TI, TO, NIN, FAST>, dim3(grid), dim3(THREADS), 0, s, p);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? TADMA_OK : cuda_fail(e, "tadma_b200_eltwise launch");
+}
+
+template <typename TI, typename TO>
+int launch_typed_io(int nin, bool fast, const ChainParams& p, int64_t nvec, cudaStream_t s) {
+    if constexpr (sizeof(TO) == 2) {
+        if (fast) return nin == 1 ? launch_typed_k<TI, TO, 1, true>(p, nvec, s) : launch_typed_k<TI, TO, 2, true>(p, nvec, s);
+    }
+    return nin == 1 ? launch_typed_k<TI, TO, 1, false>(p, nvec, s) : launch_typed_k<TI, TO, 2, false>(p, nvec, s);
+}
+
+template <typename TI>
+int launch_typed_i(int odt, int nin, bool fast, const ChainParams& p, int64_t nvec, cudaStream_t s) {
+    switch (odt) {
+    case TADMA_F32: return launch_typed_io<TI, float>(nin, fast, p, nvec, s);
+    case TADMA_F16: return launch_typed_io<TI, __half>(nin, fast, p, nvec, s);
+    default: return launch_typed_io<TI, __nv_bfloat16>(nin, fast, p, nvec, s);
+    }
+}
+
+// idt, odt in {F32, F16, BF16}; nin in {1, 2}.
+int launch_typed(int idt, int odt, int nin, bool fast, const ChainParams& p, int64_t nvec, cudaStream_t s) {
+    switch (idt) {
+    case TADMA_F32: return launch_typed_i<float>(odt, nin, fast, p, nvec, s);
+    case TADMA_F16: return launch_typed_i<__half>(odt, nin, fast, p, nvec, s);
+    default: return launch_typed_i<__nv_bfloat16>(odt, nin, fast, p, nvec, s);
+    }
+}
+
 // ---------------------------------------------------------- tiled transpose --
 //
 // One input whose unit-stride dim is not the output's: a copy through a
@@ -1253,7 +1427,37 @@ extern "C" int tadma_b200_eltwise(const tadma_tensor* out, const tadma_tensor* i
                          (ins[0].dtype == TADMA_F32 || ins[0].dtype == TADMA_F16 || ins[0].dtype == TADMA_BF16) &&
                          (out->dtype == ins[0].dtype || out->dtype == TADMA_F32) && f.strides[2][0] == 0 &&
                          f.strides[2][1] == 1 && f.strides[1][1] == 1 && f.strides[0][1] == 1 && !p.in[1].inner_bcast;
-    if (rows_ok) {
+    auto fdt3 = [](int dt) { return dt == TADMA_F32 || dt == TADMA_F16 || dt == TADMA_BF16; };
+    bool typed_ok = f.rank == 1 && cm == TADMA_COMPUTE_F32 && (n_ins == 1 || n_ins == 2) && fdt3(out->dtype);
+    for (int k = 0; k < n_ins && typed_ok; k++)
+        typed_ok = ins[k].dtype == ins[0].dtype && fdt3(ins[k].dtype) && !p.in[k].inner_bcast;
+    // One instruction (or none: a cast) whose rounding is a no-op before the store.
+    int op1 = -1;
+    bool imm1 = false;
+    if (typed_ok && n_instr <= 1) {
+        const tadma_instr* I = n_instr == 1 ? &prog[0] : nullptr;
+        const int rd = I ? I->round_dtype : -1;
+        const bool round_ok = rd < 0 || rd == TADMA_F32 || rd == out->dtype;
+        if (!I) {
+            if (n_ins == 1) op1 = TADMA_OP_COPY;
+        } else if (round_ok && I->op == TADMA_OP_COPY && I->b != TADMA_SRC_IMM && n_ins == 1) {
+            op1 = TADMA_OP_COPY;
+        } else if (round_ok && ins[0].dtype == out->dtype && I->c == TADMA_SRC_NONE &&
+                   (I->op == TADMA_OP_ADD || I->op == TADMA_OP_SUB || I->op == TADMA_OP_MUL || I->op == TADMA_OP_DIV ||
+                    I->op == TADMA_OP_RSUB || I->op == TADMA_OP_RDIV || I->op == TADMA_OP_MAX || I->op == TADMA_OP_MIN)) {
+            if (I->b == TADMA_SRC_IMM && n_ins == 1) {
+                op1 = I->op;
+                imm1 = true;
+            } else if (I->b == 1 && n_ins == 2) {
+                op1 = I->op;
+            }
+        }
+    }
+    if (op1 >= 0) {
+        rc = launch_typed1(ins[0].dtype, out->dtype, op1, imm1, pv, nvec, s);
+    } else if (typed_ok) {
+        rc = launch_typed(ins[0].dtype, out->dtype, n_ins, fast, pv, nvec, s);
+    } else if (rows_ok) {
         // vec eligibility (checked above) already guarantees 16-byte alignment of
         // every row start and inner % 8 == 0.
         AffineRowsParams ap{};

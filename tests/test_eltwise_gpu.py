@@ -292,3 +292,34 @@ def test_narrow_add_full_size_bits():
     torch.cuda.synchronize()
     ref = (a.float() + b.float()).half()  # one fp32 add rounded once to fp16
     assert torch.equal(y.view(torch.int16), ref.view(torch.int16))
+
+
+# ---- contiguous typed kernels (compile-time dtypes; single-op chains) -------
+
+TYPED_OPS = [Op.ADD, Op.SUB, Op.MUL, Op.DIV, Op.RSUB, Op.RDIV, Op.MAX, Op.MIN]
+
+
+@pytest.mark.parametrize("dt", [DType.F32, DType.F16, DType.BF16])
+@pytest.mark.parametrize("op", TYPED_OPS)
+def test_typed_single_op_bit_exact(dt, op):
+    shape = (1000003,)  # odd: vector body + scalar tail
+    a = gen(shape, dt, Dist.NORMAL, 0, 1, 50)
+    b = gen(shape, dt, Dist.NORMAL, 1, 0.5, 51)
+    got, ref = run_both(shape, dt, [(a, dt), (b, dt)], [instr(op, b=1, round_dtype=dt)])
+    assert np.array_equal(got, ref), "tensor operand"
+    got, ref = run_both((64, 1024), dt, [(a[:65536].reshape(64, 1024), dt)], [instr(op, b=SRC_IMM, imm=0.37)])
+    assert np.array_equal(got, ref), "immediate"
+
+
+@pytest.mark.parametrize("idt", [DType.F32, DType.F16, DType.BF16])
+@pytest.mark.parametrize("odt", [DType.F32, DType.F16, DType.BF16])
+def test_typed_casts_and_chains(idt, odt):
+    shape = (4099, 24)
+    a = gen(shape, idt, Dist.NORMAL, 0, 3, 52)
+    b = gen(shape, idt, Dist.NORMAL, 0, 1, 53)
+    got, ref = run_both(shape, odt, [(a, idt)], [])  # cast
+    assert np.array_equal(got, ref)
+    prog = [instr(Op.MUL, b=1, round_dtype=DType.F32), instr(Op.ADD, b=SRC_IMM, imm=0.5, round_dtype=DType.F32),
+            instr(Op.RELU, round_dtype=DType.F32)]
+    got, ref = run_both(shape, odt, [(a, idt), (b, idt)], prog)  # interpreted typed chain
+    assert np.array_equal(got, ref)
