@@ -660,32 +660,49 @@ __global__ void __launch_bounds__(THREADS) affine_rows_kernel(const __grid_const
 
 // ------------------------------------------------------- contiguous typed --
 //
-// Every operand contiguous over the whole launch (folded rank 1) and of one
-// float dtype TI, the output of float dtype TO, fp32 compute (residual adds,
-// scalings, casts, contiguous copies): loads, conversions and stores are
-// compile-time and only the chain is interpreted.  The generic kernels decode
-// dtypes and strides per vector, which cost ~170 instructions per 8 elements
-// on a 16-bit add (ncu) and held it to 4.7 TB/s.
+// Every input of one float dtype TI with a contiguous innermost dim (no
+// innermost broadcast), the output of float dtype TO, fp32 compute (residual
+// adds, scalings, casts, copies into and out of strided views): loads,
+// conversions and stores are compile-time and only the chain is interpreted.
+// The generic kernels decode dtypes per vector, which cost ~170 instructions
+// per 8 elements on a 16-bit add (ncu) and held it to 4.7 TB/s.
 
 // Two vectors per thread: with the interpreter inlined once per vector, more
 // would grow the kernel past what the instruction cache holds.
 template <typename TI>
 constexpr int typed_steps() { return 2; }
 
-template <typename TI, typename TO, int NIN, bool FAST>
+// Element offsets of vector vi: R1 (folded rank 1, every operand contiguous)
+// needs no index decomposition; otherwise the folded dims are walked
+// (outer-dim broadcasts and strided views; the innermost dim is contiguous).
+template <int NIN, bool R1>
+__device__ __forceinline__ void typed_offsets(const ChainParams& p, int64_t vi, int64_t& oo, int64_t (&io)[NIN]) {
+    if constexpr (R1) {
+        oo = vi * V;
+#pragma unroll
+        for (int k = 0; k < NIN; k++) io[k] = vi * V;
+    } else {
+        offsets<NIN>(p, (uint64_t)vi * V, oo, io);
+    }
+}
+
+template <typename TI, typename TO, int NIN, bool FAST, bool R1>
 __global__ void __launch_bounds__(THREADS) typed_kernel(const __grid_constant__ ChainParams p) {
     pdl_begin();
     constexpr int U = typed_steps<TI>();
     for (int64_t chunk = blockIdx.x; chunk * (THREADS * U) < p.n; chunk += gridDim.x) {
         const int64_t base = chunk * (THREADS * U) + threadIdx.x;
         Raw8x<TI> raw[U][NIN];
+        int64_t oo[U];
 #pragma unroll
         for (int u = 0; u < U; u++) {
             const int64_t vi = base + u * THREADS;
             if (vi < p.n) {
+                int64_t io[NIN];
+                typed_offsets<NIN, R1>(p, vi, oo[u], io);
 #pragma unroll
                 for (int k = 0; k < NIN; k++)
-                    raw8_load<TI>(reinterpret_cast<const TI*>(p.in[k].base) + vi * V, raw[u][k], p.in[k].streaming);
+                    raw8_load<TI>(reinterpret_cast<const TI*>(p.in[k].base) + io[k], raw[u][k], p.in[k].streaming);
             }
         }
 #pragma unroll
@@ -699,7 +716,7 @@ __global__ void __launch_bounds__(THREADS) typed_kernel(const __grid_constant__ 
 #pragma unroll
                 for (int j = 0; j < V; j++) acc[j] = val[0][j];
                 run_chain<float, NIN, V, FAST>(p, acc, val);
-                raw8_store<TO>(reinterpret_cast<TO*>(p.out) + vi * V, acc);
+                raw8_store<TO>(reinterpret_cast<TO*>(p.out) + oo[u], acc);
             }
         }
     }
@@ -709,7 +726,7 @@ __global__ void __launch_bounds__(THREADS) typed_kernel(const __grid_constant__ 
 // x * s, a cast): the op is a compile-time constant as well, so no
 // interpreter is inlined at all.  OP is ADD, SUB, MUL, DIV, RSUB, RDIV, MAX,
 // MIN or COPY; IMM: the second operand is the immediate, else ins[1].
-template <typename TI, typename TO, int OP, bool IMM>
+template <typename TI, typename TO, int OP, bool IMM, bool R1>
 __global__ void __launch_bounds__(THREADS) typed1_kernel(const __grid_constant__ ChainParams p) {
     pdl_begin();
     constexpr int U = 2;
@@ -718,13 +735,16 @@ __global__ void __launch_bounds__(THREADS) typed1_kernel(const __grid_constant__
     for (int64_t chunk = blockIdx.x; chunk * (THREADS * U) < p.n; chunk += gridDim.x) {
         const int64_t base = chunk * (THREADS * U) + threadIdx.x;
         Raw8x<TI> raw[U][NIN];
+        int64_t oo[U];
 #pragma unroll
         for (int u = 0; u < U; u++) {
             const int64_t vi = base + u * THREADS;
             if (vi < p.n) {
+                int64_t io[NIN];
+                typed_offsets<NIN, R1>(p, vi, oo[u], io);
 #pragma unroll
                 for (int k = 0; k < NIN; k++)
-                    raw8_load<TI>(reinterpret_cast<const TI*>(p.in[k].base) + vi * V, raw[u][k], p.in[k].streaming);
+                    raw8_load<TI>(reinterpret_cast<const TI*>(p.in[k].base) + io[k], raw[u][k], p.in[k].streaming);
             }
         }
 #pragma unroll
@@ -738,7 +758,7 @@ __global__ void __launch_bounds__(THREADS) typed1_kernel(const __grid_constant__
                 for (int j = 0; j < V; j++) {
                     if constexpr (OP != TADMA_OP_COPY) a[j] = binary(OP, a[j], IMM ? imm : b[j], 0.0f);
                 }
-                raw8_store<TO>(reinterpret_cast<TO*>(p.out) + vi * V, a);
+                raw8_store<TO>(reinterpret_cast<TO*>(p.out) + oo[u], a);
             }
         }
     }
@@ -749,7 +769,8 @@ int launch_typed1_k(const ChainParams& p, int64_t nvec, cudaStream_t s) {
     const int64_t per_block = (int64_t)THREADS * 2;
     const int64_t want = (nvec + per_block - 1) / per_block;
     const int grid = (int)(want < 1 ? 1 : want > 0x7fffffff ? 0x7fffffff : want);
-    (void)launch_pdl(typed1_kernel<TI, TO, OP, IMM>, dim3(grid), dim3(THREADS), 0, s, p);
+    if (p.rank == 1) (void)launch_pdl(typed1_kernel<TI, TO, OP, IMM, true>, dim3(grid), dim3(THREADS), 0, s, p);
+    else (void)launch_pdl(typed1_kernel<TI, TO, OP, IMM, false>, dim3(grid), dim3(THREADS), 0, s, p);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? TADMA_OK : cuda_fail(e, "tadma_b200_eltwise launch");
 }
@@ -801,7 +822,8 @@ int launch_typed_k(const ChainParams& p, int64_t nvec, cudaStream_t s) {
     const int64_t per_block = (int64_t)THREADS * typed_steps<TI>();
     const int64_t want = (nvec + per_block - 1) / per_block;
     const int grid = (int)(want < 1 ? 1 : want > 0x7fffffff ? 0x7fffffff : want);
-    (void)launch_pdl(typed_kernel<TI, TO, NIN, FAST>, dim3(grid), dim3(THREADS), 0, s, p);
+    if (p.rank == 1) (void)launch_pdl(typed_kernel<TI, TO, NIN, FAST, true>, dim3(grid), dim3(THREADS), 0, s, p);
+    else (void)launch_pdl(typed_kernel<TI, TO, NIN, FAST, false>, dim3(grid), dim3(THREADS), 0, s, p);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? TADMA_OK : cuda_fail(e, "tadma_b200_eltwise launch");
 }
@@ -1428,7 +1450,7 @@ extern "C" int tadma_b200_eltwise(const tadma_tensor* out, const tadma_tensor* i
                          (out->dtype == ins[0].dtype || out->dtype == TADMA_F32) && f.strides[2][0] == 0 &&
                          f.strides[2][1] == 1 && f.strides[1][1] == 1 && f.strides[0][1] == 1 && !p.in[1].inner_bcast;
     auto fdt3 = [](int dt) { return dt == TADMA_F32 || dt == TADMA_F16 || dt == TADMA_BF16; };
-    bool typed_ok = f.rank == 1 && cm == TADMA_COMPUTE_F32 && (n_ins == 1 || n_ins == 2) && fdt3(out->dtype);
+    bool typed_ok = cm == TADMA_COMPUTE_F32 && (n_ins == 1 || n_ins == 2) && fdt3(out->dtype);
     for (int k = 0; k < n_ins && typed_ok; k++)
         typed_ok = ins[k].dtype == ins[0].dtype && fdt3(ins[k].dtype) && !p.in[k].inner_bcast;
     // One instruction (or none: a cast) whose rounding is a no-op before the store.

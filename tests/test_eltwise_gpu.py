@@ -323,3 +323,27 @@ def test_typed_casts_and_chains(idt, odt):
             instr(Op.RELU, round_dtype=DType.F32)]
     got, ref = run_both(shape, odt, [(a, idt), (b, idt)], prog)  # interpreted typed chain
     assert np.array_equal(got, ref)
+
+
+def test_typed_strided_views():
+    # typed kernels over folded rank > 1: a copy into a column slice (concat),
+    # a batched permute that keeps the inner dim, an outer-dim broadcast add
+    import torch
+    src = gen((4, 40, 64), DType.F16, Dist.NORMAL, 0, 1, 54)
+    big = torch.zeros((4, 100, 64), dtype=torch.float16, device="cuda")
+    tb.eltwise(big[:, 60:], [to_dev(src)], [instr(Op.COPY)])
+    torch.cuda.synchronize()
+    got = from_dev(big)
+    assert np.array_equal(got[:, 60:], src) and not got[:, :60].any()
+    x = gen((3, 24, 5, 16), DType.BF16, Dist.NORMAL, 0, 1, 55)
+    xd = to_dev(x, DType.BF16)
+    y = empty_dev((3, 5, 24, 16), DType.BF16)
+    tb.eltwise(y, [xd.permute(0, 2, 1, 3)], [instr(Op.COPY)])
+    torch.cuda.synchronize()
+    assert np.array_equal(from_dev(y), np.ascontiguousarray(x.transpose(0, 2, 1, 3)))
+    a = gen((33, 40), DType.F32, Dist.NORMAL, 0, 1, 56)
+    row = gen((1, 40), DType.F32, Dist.NORMAL, 0, 1, 57)
+    for op in (Op.ADD, Op.MUL, Op.RSUB):
+        got, ref = run_both((33, 40), DType.F32, [(a, DType.F32), (np.broadcast_to(row, (33, 40)), DType.F32)],
+                            [instr(op, b=1)])
+        assert np.array_equal(got, ref), op
