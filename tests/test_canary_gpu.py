@@ -114,7 +114,7 @@ def test_chain(shape, dt, pitch):
     same_bits(g.t, plain)
 
 
-@pytest.mark.parametrize("shape", [(33, 65), (2, 31, 97), (64, 64)])
+@pytest.mark.parametrize("shape", [(33, 65), (2, 31, 97), (64, 64), (72, 136), (3, 200, 264)])
 def test_transpose(shape):
     import torch
     x = rand(shape, torch.float32, 5)

@@ -219,7 +219,9 @@ def test_invalid_arguments_raise():
 # ---- copies through a transpose (tiled shared-memory path) -------------------
 
 @pytest.mark.parametrize("shape,perm", [((70, 45), (1, 0)), ((3, 33, 100), (0, 2, 1)), ((2, 5, 37, 64), (0, 2, 3, 1)),
-                                        ((4, 8, 96, 64), (0, 1, 3, 2))])
+                                        ((4, 8, 96, 64), (0, 1, 3, 2)),
+                                        # 16-byte aligned rows: the 64 x 64 vector tiles, with partial edge tiles
+                                        ((3, 72, 136), (0, 2, 1)), ((200, 264), (1, 0)), ((2, 24, 16, 8), (0, 2, 3, 1))])
 @pytest.mark.parametrize("dt,out_dt", [(DType.F32, DType.F32), (DType.BF16, DType.BF16), (DType.F16, DType.F32)])
 def test_transpose_copy_and_cast(shape, perm, dt, out_dt):
     import torch
@@ -234,6 +236,21 @@ def test_transpose_copy_and_cast(shape, perm, dt, out_dt):
     ref = np.zeros(out_shape, dtype=from_dev(out).dtype)
     assert O.eltwise(ref, [np.transpose(x, perm)], [instr(Op.COPY)], out_dtype=out_dt, in_dtypes=[dt]) == 0
     assert np.array_equal(from_dev(out).view(np.uint8), ref.view(np.uint8))
+
+
+def test_transpose64_with_chain():
+    # aligned rows: the vector-tile kernel runs the chain on the way out
+    import torch
+    x = gen((6, 136, 72), DType.F32, Dist.NORMAL, 0.0, 1.0, 32)
+    xd = to_dev(x)
+    view = make_tensor(xd.data_ptr(), DType.F32, [6, 72, 136], [136 * 72, 1, 72])
+    out = empty_dev((6, 72, 136), DType.BF16)
+    prog = [instr(Op.MUL, b=SRC_IMM, imm=1.5), instr(Op.GELU)]
+    tb.eltwise(out, [view], prog, Compute.F32)
+    torch.cuda.synchronize()
+    ref = np.zeros((6, 72, 136), np.uint16)
+    assert O.eltwise(ref, [np.transpose(x, (0, 2, 1))], prog, Compute.F32, out_dtype=DType.BF16, in_dtypes=[DType.F32]) == 0
+    assert ulp_diff(from_dev(out), ref, DType.BF16).max() <= 1
 
 
 def test_transpose_with_chain():
