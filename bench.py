@@ -2,6 +2,7 @@
 """Benchmark of the tadma_b200 hot path (achieved HBM GB/s), one JSON line.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2|3|4|5] [--impl ours|reference]
+    python bench.py --views      # view copies / element-wise calls vs torch, one line per case
 
 Metric: achieved HBM GB/s = algorithmic bytes (every input
 read once, every output written once; gathered rows counted per use) / time.
@@ -50,6 +51,9 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--no-ref-gpu", action="store_true",
                     help="skip timing the reference's GPU algorithm (baseline/refalgo) beside ours")
+    ap.add_argument("--views", action="store_true",
+                    help="instead of a config: one JSON line per view-copy / element-wise case of the generated-graph "
+                         "calls (permutes, transposes, casts, concat, where), ours and torch, 1 GPU")
     ap.add_argument("--batch", type=int, default=0,
                     help="leading-axis size per GPU (0 = the BASELINE size); smaller values give the small cases "
                          "used for ncu captures")
@@ -700,11 +704,105 @@ def run_reference(args, rank, world):
 
 # -------------------------------------------------------------------- main --
 
+def run_views(args):
+    """View copies and single element-wise calls of generated graph code
+    (contiguous() after transpose<perm>, concat, casts, residual adds, where,
+    comparisons, strided slices) through the public API, each with the torch
+    call that does the same.  Every call is prepared once and replayed 20x
+    from a CUDA graph (no Python in the timed region); GB/s = bytes of the
+    inputs read once + output written once, over the device time.  Inputs are
+    64-256 MB, some below L2 size: read these as per-launch kernel
+    throughput, not as cold-cache figures."""
+    import torch
+    import tadma_b200 as tb
+    from tadma_b200.abi import Dist, Op, instr
+
+    rep, side = 20, torch.cuda.Stream()
+
+    def graph_time(fns, iters=10):
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for f in fns:
+                f()
+        side.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=side):
+            for _ in range(rep):
+                for f in fns:
+                    f()
+        for _ in range(max(3, args.warmup)):
+            g.replay()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(iters):
+            g.replay()
+        e.record()
+        torch.cuda.synchronize()
+        del g
+        return s.elapsed_time(e) / iters / rep * 1e-3
+
+    def rnd(shape, dt):
+        t = torch.empty(shape, dtype=dt, device="cuda")
+        tb.fill(t, Dist.NORMAL, 0, 1, 0, 1)
+        return t
+
+    def P(out, ins, prog):
+        return tb.prepare_eltwise(out, ins, prog, stream=side)
+
+    f16, f32 = torch.float16, torch.float32
+    x = rnd((32, 512, 16, 64), f16)
+    y = torch.empty((32, 16, 512, 64), dtype=f16, device="cuda")
+    k = rnd((32, 16, 512, 64), f16)
+    kt = torch.empty((32, 16, 64, 512), dtype=f16, device="cuda")
+    qt = torch.empty((32, 16, 64, 512), dtype=f16, device="cuda")
+    a, a16 = rnd((8192, 8192), f32), rnd((8192, 8192), f16)
+    at, at16, h = torch.empty_like(a), torch.empty_like(a16), torch.empty_like(a16)
+    b16, s16 = rnd((8192, 8192), f16), torch.empty_like(a16)
+    c0, c1 = rnd((32, 512, 1024), f16), rnd((32, 512, 1024), f16)
+    cc = torch.empty((32, 1024, 1024), dtype=f16, device="cuda")
+    cond = torch.rand((8192, 8192), device="cuda") > 0.5
+    b2, w, gt = rnd((8192, 8192), f32), torch.empty_like(a), torch.empty_like(cond)
+    sl = torch.empty((4096, 8192), dtype=f32, device="cuda")
+    xp, kp, qp = x.permute(0, 2, 1, 3), k.permute(0, 1, 3, 2), x.permute(0, 2, 3, 1)
+    n = a.numel()
+    cases = [
+        ("head split: permute(0,2,1,3).contiguous() f16 [32,512,16,64]", 4 * x.numel(),
+         [P(y, [xp], [instr(Op.COPY)])], [lambda: y.copy_(xp)]),
+        ("K^T: permute(0,1,3,2).contiguous() f16 [32,16,512,64]", 4 * k.numel(),
+         [P(kt, [kp], [instr(Op.COPY)])], [lambda: kt.copy_(kp)]),
+        ("permute(0,2,3,1).contiguous() f16 [32,512,16,64]", 4 * x.numel(),
+         [P(qt, [qp], [instr(Op.COPY)])], [lambda: qt.copy_(qp)]),
+        ("transpose f32 [8192,8192]", 8 * n, [P(at, [a.t()], [instr(Op.COPY)])], [lambda: at.copy_(a.t())]),
+        ("transpose f16 [8192,8192]", 4 * n, [P(at16, [a16.t()], [instr(Op.COPY)])], [lambda: at16.copy_(a16.t())]),
+        ("cast f32 -> f16 [8192,8192]", 6 * n, [P(h, [a], [instr(Op.COPY)])], [lambda: h.copy_(a)]),
+        ("add f16 [8192,8192]", 6 * n, [P(s16, [a16, b16], [instr(Op.ADD, b=1)])],
+         [lambda: torch.add(a16, b16, out=s16)]),
+        ("copy f32 [8192,8192]", 8 * n, [P(at, [a], [instr(Op.COPY)])], [lambda: at.copy_(a)]),
+        ("concat axis 1 f16 2 x [32,512,1024]", 4 * cc.numel(),
+         [P(cc[:, :512], [c0], [instr(Op.COPY)]), P(cc[:, 512:], [c1], [instr(Op.COPY)])],
+         [lambda: torch.cat([c0, c1], 1, out=cc)]),
+        ("where(bool, f32, f32) [8192,8192]", 13 * n, [P(w, [cond, a, b2], [instr(Op.WHERE, b=1, c=2)])],
+         [lambda: torch.where(cond, a, b2, out=w)]),
+        ("greater f32 -> bool [8192,8192]", 9 * n, [P(gt, [a, b2], [instr(Op.GT, b=1)])],
+         [lambda: torch.gt(a, b2, out=gt)]),
+        ("slice [::2] f32 [8192,8192] -> [4096,8192]", 8 * sl.numel(), [P(sl, [a[::2]], [instr(Op.COPY)])],
+         [lambda: sl.copy_(a[::2])]),
+    ]
+    for name, nbytes, ours, theirs in cases:
+        t_ours, t_torch = graph_time(ours), graph_time(theirs)
+        print(json.dumps({"case": name, "us": round(t_ours * 1e6, 2), "GBs": round(nbytes / t_ours / GB, 1),
+                          "torch_GBs": round(nbytes / t_torch / GB, 1), "unit": "GB/s"}), flush=True)
+
+
 def main():
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.views:
+        run_views(args)
+        return
     if args.impl == "reference":
         run_reference(args, rank, world)
         return

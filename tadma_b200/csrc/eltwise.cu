@@ -817,6 +817,145 @@ int launch_typed1(int idt, int odt, int op, bool imm, const ChainParams& p, int6
     }
 }
 
+// Comparisons of one float dtype (a tensor or an immediate on the right) into
+// a bool tensor, and where(bool or u8 condition, T, T) -> T: the mask
+// producers and consumers of generated graphs, typed like typed1_kernel.
+__device__ __forceinline__ void store_bytes8(uint8_t* p, const float (&v)[V]) {
+    uint2 w = make_uint2(0u, 0u);
+#pragma unroll
+    for (int j = 0; j < V; j++) {
+        const uint32_t b = (v[j] != 0.0f ? 1u : 0u) << (8 * (j & 3));
+        if (j < 4) w.x |= b;
+        else w.y |= b;
+    }
+    __stcs(reinterpret_cast<uint2*>(p), w);
+}
+
+template <typename TI, int OP, bool IMM, bool R1>
+__global__ void __launch_bounds__(THREADS) typed_cmp_kernel(const __grid_constant__ ChainParams p) {
+    pdl_begin();
+    constexpr int U = 2;
+    constexpr int NIN = IMM ? 1 : 2;
+    const float imm = __double2float_rn(p.prog[0].imm);
+    for (int64_t chunk = blockIdx.x; chunk * (THREADS * U) < p.n; chunk += gridDim.x) {
+        const int64_t base = chunk * (THREADS * U) + threadIdx.x;
+        Raw8x<TI> raw[U][NIN];
+        int64_t oo[U];
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int64_t vi = base + u * THREADS;
+            if (vi < p.n) {
+                int64_t io[NIN];
+                typed_offsets<NIN, R1>(p, vi, oo[u], io);
+#pragma unroll
+                for (int k = 0; k < NIN; k++)
+                    raw8_load<TI>(reinterpret_cast<const TI*>(p.in[k].base) + io[k], raw[u][k], p.in[k].streaming);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int64_t vi = base + u * THREADS;
+            if (vi < p.n) {
+                float a[V], b[V];
+                raw8_cvt<TI>(raw[u][0], a);
+                if constexpr (!IMM) raw8_cvt<TI>(raw[u][1], b);
+#pragma unroll
+                for (int j = 0; j < V; j++) a[j] = binary(OP, a[j], IMM ? imm : b[j], 0.0f);
+                store_bytes8(reinterpret_cast<uint8_t*>(p.out) + oo[u], a);
+            }
+        }
+    }
+}
+
+template <typename T, bool R1>
+__global__ void __launch_bounds__(THREADS) typed_where_kernel(const __grid_constant__ ChainParams p) {
+    pdl_begin();
+    constexpr int U = 2;
+    const bool cond_bool = p.in[0].dtype == TADMA_BOOL;
+    for (int64_t chunk = blockIdx.x; chunk * (THREADS * U) < p.n; chunk += gridDim.x) {
+        const int64_t base = chunk * (THREADS * U) + threadIdx.x;
+        uint2 c[U];
+        Raw8x<T> x[U], y[U];
+        int64_t oo[U];
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int64_t vi = base + u * THREADS;
+            if (vi < p.n) {
+                int64_t io[3];
+                typed_offsets<3, R1>(p, vi, oo[u], io);
+                const uint8_t* cp = reinterpret_cast<const uint8_t*>(p.in[0].base) + io[0];
+                c[u] = p.in[0].streaming ? __ldcs(reinterpret_cast<const uint2*>(cp)) : *reinterpret_cast<const uint2*>(cp);
+                raw8_load<T>(reinterpret_cast<const T*>(p.in[1].base) + io[1], x[u], p.in[1].streaming);
+                raw8_load<T>(reinterpret_cast<const T*>(p.in[2].base) + io[2], y[u], p.in[2].streaming);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int64_t vi = base + u * THREADS;
+            if (vi < p.n) {
+                float fx[V], fy[V];
+                raw8_cvt<T>(x[u], fx);
+                raw8_cvt<T>(y[u], fy);
+#pragma unroll
+                for (int j = 0; j < V; j++) {
+                    const uint32_t byte = ((j < 4 ? c[u].x : c[u].y) >> (8 * (j & 3))) & 0xffu;
+                    const float cv = cond_bool ? (byte != 0u ? 1.0f : 0.0f) : (float)byte;
+                    fx[j] = binary(TADMA_OP_WHERE, cv, fx[j], fy[j]);
+                }
+                raw8_store<T>(reinterpret_cast<T*>(p.out) + oo[u], fx);
+            }
+        }
+    }
+}
+
+template <typename K>
+int launch_grid2(K kernel, const ChainParams& p, int64_t nvec, cudaStream_t s) {
+    const int64_t per_block = (int64_t)THREADS * 2;
+    const int64_t want = (nvec + per_block - 1) / per_block;
+    const int grid = (int)(want < 1 ? 1 : want > 0x7fffffff ? 0x7fffffff : want);
+    (void)launch_pdl(kernel, dim3(grid), dim3(THREADS), 0, s, p);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? TADMA_OK : cuda_fail(e, "tadma_b200_eltwise launch");
+}
+
+template <typename TI, int OP, bool IMM>
+int launch_cmp_k(const ChainParams& p, int64_t nvec, cudaStream_t s) {
+    return p.rank == 1 ? launch_grid2(typed_cmp_kernel<TI, OP, IMM, true>, p, nvec, s)
+                       : launch_grid2(typed_cmp_kernel<TI, OP, IMM, false>, p, nvec, s);
+}
+template <typename TI, bool IMM>
+int launch_cmp_op(int op, const ChainParams& p, int64_t nvec, cudaStream_t s) {
+    switch (op) {
+    case TADMA_OP_EQ: return launch_cmp_k<TI, TADMA_OP_EQ, IMM>(p, nvec, s);
+    case TADMA_OP_NE: return launch_cmp_k<TI, TADMA_OP_NE, IMM>(p, nvec, s);
+    case TADMA_OP_LT: return launch_cmp_k<TI, TADMA_OP_LT, IMM>(p, nvec, s);
+    case TADMA_OP_GT: return launch_cmp_k<TI, TADMA_OP_GT, IMM>(p, nvec, s);
+    case TADMA_OP_LE: return launch_cmp_k<TI, TADMA_OP_LE, IMM>(p, nvec, s);
+    default: return launch_cmp_k<TI, TADMA_OP_GE, IMM>(p, nvec, s);
+    }
+}
+// idt in {F32, F16, BF16}; the output is a bool tensor.
+int launch_cmp(int idt, int op, bool imm, const ChainParams& p, int64_t nvec, cudaStream_t s) {
+    switch (idt) {
+    case TADMA_F32: return imm ? launch_cmp_op<float, true>(op, p, nvec, s) : launch_cmp_op<float, false>(op, p, nvec, s);
+    case TADMA_F16: return imm ? launch_cmp_op<__half, true>(op, p, nvec, s) : launch_cmp_op<__half, false>(op, p, nvec, s);
+    default:
+        return imm ? launch_cmp_op<__nv_bfloat16, true>(op, p, nvec, s) : launch_cmp_op<__nv_bfloat16, false>(op, p, nvec, s);
+    }
+}
+// dt in {F32, F16, BF16}: the branches' and the output's dtype.
+int launch_where(int dt, const ChainParams& p, int64_t nvec, cudaStream_t s) {
+    const bool r1 = p.rank == 1;
+    switch (dt) {
+    case TADMA_F32: return r1 ? launch_grid2(typed_where_kernel<float, true>, p, nvec, s)
+                              : launch_grid2(typed_where_kernel<float, false>, p, nvec, s);
+    case TADMA_F16: return r1 ? launch_grid2(typed_where_kernel<__half, true>, p, nvec, s)
+                              : launch_grid2(typed_where_kernel<__half, false>, p, nvec, s);
+    default: return r1 ? launch_grid2(typed_where_kernel<__nv_bfloat16, true>, p, nvec, s)
+                       : launch_grid2(typed_where_kernel<__nv_bfloat16, false>, p, nvec, s);
+    }
+}
+
 template <typename TI, typename TO, int NIN, bool FAST>
 int launch_typed_k(const ChainParams& p, int64_t nvec, cudaStream_t s) {
     const int64_t per_block = (int64_t)THREADS * typed_steps<TI>();
@@ -1590,7 +1729,33 @@ extern "C" int tadma_b200_eltwise(const tadma_tensor* out, const tadma_tensor* i
             }
         }
     }
-    if (op1 >= 0) {
+    // Comparisons into bool and where(bool / u8, T, T) -> T, one instruction.
+    int cmp_op = -1;
+    bool cmp_imm = false, where_ok = false;
+    if (n_instr == 1 && cm == TADMA_COMPUTE_F32) {
+        const tadma_instr& I = prog[0];
+        const int rd = I.round_dtype;
+        bool no_bcast = true;
+        for (int k = 0; k < n_ins; k++) no_bcast = no_bcast && !p.in[k].inner_bcast;
+        if (no_bcast && out->dtype == TADMA_BOOL && (rd < 0 || rd == TADMA_BOOL || rd == TADMA_F32) &&
+            I.op >= TADMA_OP_EQ && I.op <= TADMA_OP_GE && I.c == TADMA_SRC_NONE && fdt3(ins[0].dtype)) {
+            if (I.b == TADMA_SRC_IMM && n_ins == 1) {
+                cmp_op = I.op;
+                cmp_imm = true;
+            } else if (I.b == 1 && n_ins == 2 && ins[1].dtype == ins[0].dtype) {
+                cmp_op = I.op;
+            }
+        }
+        where_ok = no_bcast && I.op == TADMA_OP_WHERE && I.b == 1 && I.c == 2 && n_ins == 3 &&
+                   (ins[0].dtype == TADMA_BOOL || ins[0].dtype == TADMA_U8) && fdt3(out->dtype) &&
+                   ins[1].dtype == out->dtype && ins[2].dtype == out->dtype &&
+                   (rd < 0 || rd == TADMA_F32 || rd == out->dtype);
+    }
+    if (cmp_op >= 0) {
+        rc = launch_cmp(ins[0].dtype, cmp_op, cmp_imm, pv, nvec, s);
+    } else if (where_ok) {
+        rc = launch_where(out->dtype, pv, nvec, s);
+    } else if (op1 >= 0) {
         rc = launch_typed1(ins[0].dtype, out->dtype, op1, imm1, pv, nvec, s);
     } else if (typed_ok) {
         rc = launch_typed(ins[0].dtype, out->dtype, n_ins, fast, pv, nvec, s);

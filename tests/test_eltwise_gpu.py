@@ -364,3 +364,22 @@ def test_typed_strided_views():
         got, ref = run_both((33, 40), DType.F32, [(a, DType.F32), (np.broadcast_to(row, (33, 40)), DType.F32)],
                             [instr(op, b=1)])
         assert np.array_equal(got, ref), op
+
+
+@pytest.mark.parametrize("dt", [DType.F32, DType.F16, DType.BF16])
+def test_typed_compare_and_where(dt):
+    shape = (257, 40)
+    a = gen(shape, dt, Dist.NORMAL, 0, 1, 58)
+    b = gen(shape, dt, Dist.NORMAL, 0, 1, 59)
+    b.reshape(-1)[::7] = a.reshape(-1)[::7]  # ties for EQ / LE / GE
+    for op in (Op.EQ, Op.NE, Op.LT, Op.GT, Op.LE, Op.GE):
+        got, ref = run_both(shape, DType.BOOL, [(a, dt), (b, dt)], [instr(op, b=1, round_dtype=DType.BOOL)])
+        assert np.array_equal(got, ref), op
+        got, ref = run_both(shape, DType.BOOL, [(a, dt)], [instr(op, b=SRC_IMM, imm=0.25)])
+        assert np.array_equal(got, ref), op
+    c = gen(shape, DType.F32, Dist.UNIFORM, -1, 1, 60) > 0
+    got, ref = run_both(shape, dt, [(c, DType.BOOL), (a, dt), (b, dt)], [instr(Op.WHERE, b=1, c=2)])
+    assert np.array_equal(got, ref)
+    cu8 = gen(shape, DType.U8, Dist.INDEX, 0, 3, 61)  # 0 -> y, 1 or 2 -> x
+    got, ref = run_both(shape, dt, [(cu8, DType.U8), (a, dt), (b, dt)], [instr(Op.WHERE, b=1, c=2)])
+    assert np.array_equal(got, ref)
