@@ -1751,15 +1751,9 @@ extern "C" int tadma_b200_eltwise(const tadma_tensor* out, const tadma_tensor* i
                    ins[1].dtype == out->dtype && ins[2].dtype == out->dtype &&
                    (rd < 0 || rd == TADMA_F32 || rd == out->dtype);
     }
-    if (cmp_op >= 0) {
-        rc = launch_cmp(ins[0].dtype, cmp_op, cmp_imm, pv, nvec, s);
-    } else if (where_ok) {
-        rc = launch_where(out->dtype, pv, nvec, s);
-    } else if (op1 >= 0) {
-        rc = launch_typed1(ins[0].dtype, out->dtype, op1, imm1, pv, nvec, s);
-    } else if (typed_ok) {
-        rc = launch_typed(ins[0].dtype, out->dtype, n_ins, fast, pv, nvec, s);
-    } else if (rows_ok) {
+    // First match wins: the row-broadcast affine kernel, the typed single-op
+    // kernels, compile-time affine programs, then the interpreted kernels.
+    if (rows_ok) {
         // vec eligibility (checked above) already guarantees 16-byte alignment of
         // every row start and inner % 8 == 0.
         AffineRowsParams ap{};
@@ -1772,9 +1766,17 @@ extern "C" int tadma_b200_eltwise(const tadma_tensor* out, const tadma_tensor* i
         ap.out_rs = f.strides[0][0];
         ap.scale = am.mul ? am.scale : 1.0f;
         rc = launch_rows(ins[0].dtype, out->dtype, am.act, ap, s);
+    } else if (cmp_op >= 0) {
+        rc = launch_cmp(ins[0].dtype, cmp_op, cmp_imm, pv, nvec, s);
+    } else if (where_ok) {
+        rc = launch_where(out->dtype, pv, nvec, s);
+    } else if (op1 >= 0) {
+        rc = launch_typed1(ins[0].dtype, out->dtype, op1, imm1, pv, nvec, s);
     } else if (am.ok) {
         pv.scale = am.scale;
         rc = launch_affine(am.act, fast, am.mul, am.add, pv, nvec, s, narrow);
+    } else if (typed_ok) {
+        rc = launch_typed(ins[0].dtype, out->dtype, n_ins, fast, pv, nvec, s);
     } else {
         rc = go(pv, true, nvec);
     }
