@@ -54,6 +54,8 @@ def parse():
     ap.add_argument("--views", action="store_true",
                     help="instead of a config: one JSON line per view-copy / element-wise case of the generated-graph "
                          "calls (permutes, transposes, casts, concat, where), ours and torch, 1 GPU")
+    ap.add_argument("--view-filter", default="",
+                    help="with --views: run only the cases whose name contains this text")
     ap.add_argument("--batch", type=int, default=0,
                     help="leading-axis size per GPU (0 = the BASELINE size); smaller values give the small cases "
                          "used for ncu captures")
@@ -790,6 +792,8 @@ def run_views(args):
          [lambda: sl.copy_(a[::2])]),
     ]
     for name, nbytes, ours, theirs in cases:
+        if args.view_filter not in name:
+            continue
         t_ours, t_torch = graph_time(ours), graph_time(theirs)
         print(json.dumps({"case": name, "us": round(t_ours * 1e6, 2), "GBs": round(nbytes / t_ours / GB, 1),
                           "torch_GBs": round(nbytes / t_torch / GB, 1), "unit": "GB/s"}), flush=True)

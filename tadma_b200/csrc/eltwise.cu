@@ -726,11 +726,16 @@ __global__ void __launch_bounds__(THREADS) typed_kernel(const __grid_constant__ 
 // x * s, a cast): the op is a compile-time constant as well, so no
 // interpreter is inlined at all.  OP is ADD, SUB, MUL, DIV, RSUB, RDIV, MAX,
 // MIN or COPY; IMM: the second operand is the immediate, else ins[1].
+// Vectors per thread: 64 bytes of loads in flight for one 16-bit operand
+// (4 x 16 B), as for an fp32 operand (2 x 32 B) or two 16-bit ones.
+template <typename TI, int NIN>
+constexpr int typed1_u() { return sizeof(TI) == 2 && NIN == 1 ? 4 : 2; }
+
 template <typename TI, typename TO, int OP, bool IMM, bool R1>
 __global__ void __launch_bounds__(THREADS) typed1_kernel(const __grid_constant__ ChainParams p) {
     pdl_begin();
-    constexpr int U = 2;
     constexpr int NIN = (OP == TADMA_OP_COPY || IMM) ? 1 : 2;
+    constexpr int U = typed1_u<TI, NIN>();
     const float imm = __double2float_rn(p.prog[0].imm);
     for (int64_t chunk = blockIdx.x; chunk * (THREADS * U) < p.n; chunk += gridDim.x) {
         const int64_t base = chunk * (THREADS * U) + threadIdx.x;
@@ -766,7 +771,7 @@ __global__ void __launch_bounds__(THREADS) typed1_kernel(const __grid_constant__
 
 template <typename TI, typename TO, int OP, bool IMM>
 int launch_typed1_k(const ChainParams& p, int64_t nvec, cudaStream_t s) {
-    const int64_t per_block = (int64_t)THREADS * 2;
+    const int64_t per_block = (int64_t)THREADS * typed1_u<TI, (OP == TADMA_OP_COPY || IMM) ? 1 : 2>();
     const int64_t want = (nvec + per_block - 1) / per_block;
     const int grid = (int)(want < 1 ? 1 : want > 0x7fffffff ? 0x7fffffff : want);
     if (p.rank == 1) (void)launch_pdl(typed1_kernel<TI, TO, OP, IMM, true>, dim3(grid), dim3(THREADS), 0, s, p);
@@ -1132,6 +1137,97 @@ __global__ void __launch_bounds__(THREADS) transpose64_kernel(const __grid_const
     }
 }
 
+// 16-bit in and out: 64 (i) x TJ (j) tiles kept as 16-bit element pairs.
+// Each thread loads the same 16-byte chunk (8 values of i) from two adjacent
+// input rows j, j + 1 and packs value k of both into one 32-bit word: the
+// output row i + k's elements j, j + 1.  Words go to shared memory as
+// W[i][j / 2]; the output side reads 16-byte chunks of 4 words (8 values of
+// j) and stores them along the output's contiguous dim.  The 4-word chunks of
+// row i are swizzled by XOR with (i / 8) % 8, so the scalar word stores (8
+// rows i = 8c + k, c = 0..7, per warp) and the 16-byte reads (8 consecutive
+// chunks per quarter warp) each cover all 32 banks once.  Half the shared
+// memory traffic of an fp32 tile, and TJ = 256 keeps 32 KB of loads in flight
+// per CTA (4x the 64 x 64 tile).  RAW: the chain is an identity on the same
+// dtype, so words are stored untouched (bit-exact, NaN payloads included).
+template <typename TI, typename TO, int PROG, int TJ, bool RAW>
+__global__ void __launch_bounds__(THREADS, 4) transpose16_kernel(const __grid_constant__ TransposeParams tp) {
+    pdl_begin();
+    static_assert(sizeof(TI) == 2 && sizeof(TO) == 2 && (TJ == 128 || TJ == 256));
+    constexpr int TI_ = 64;
+    constexpr int WPR = TJ / 2;                  // words per W row
+    constexpr int NP = TJ / 64;                  // row pairs per thread (32 pairs per pass)
+    constexpr int CPR = TJ / 8;                  // 16-byte output chunks per W row
+    constexpr int RPP = THREADS / CPR;           // W rows per output pass
+    constexpr int NS = TI_ / RPP;                // output chunks per thread
+    __shared__ __align__(16) uint32_t W[TI_ * WPR];
+    const int t = threadIdx.x;
+    const int c = t & 7, p0 = t >> 3;            // input chunk (i = 8c..8c+7), first row pair
+    const int q = t % CPR, r0 = t / CPR;         // output chunk (j = 8q..8q+7), first W row
+    const int64_t i0 = (int64_t)blockIdx.y * TI_, j0 = (int64_t)blockIdx.x * TJ;
+    for (int64_t bz = blockIdx.z; bz < tp.nbatch; bz += gridDim.z) {
+        uint64_t e = (uint64_t)bz;
+        int64_t ib = 0, ob = 0;
+        for (int d = tp.nb - 1; d >= 1; d--) {
+            uint64_t qq, rr;
+            tp.bdm[d].divmod(e, qq, rr);
+            ib += (int64_t)rr * tp.b_in[d];
+            ob += (int64_t)rr * tp.b_out[d];
+            e = qq;
+        }
+        if (tp.nb > 0) {
+            ib += (int64_t)e * tp.b_in[0];
+            ob += (int64_t)e * tp.b_out[0];
+        }
+        const TI* in = reinterpret_cast<const TI*>(tp.in) + ib;
+        const int64_t i = i0 + 8 * c;
+        uint4 a[NP], b[NP];
+#pragma unroll
+        for (int u = 0; u < NP; u++) {
+            const int64_t j = j0 + 2 * (p0 + 32 * u);
+            // n_j is a multiple of 8, so j < n_j implies j + 1 < n_j.
+            if (i < tp.n_i && j < tp.n_j) {
+                a[u] = ld_stream_v4(in + i + j * tp.in_sj);
+                b[u] = ld_stream_v4(in + i + (j + 1) * tp.in_sj);
+            } else {
+                a[u] = b[u] = make_uint4(0, 0, 0, 0);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < NP; u++) {
+            const int p = p0 + 32 * u;
+            const int pw = (((p >> 2) ^ c) << 2) | (p & 3);  // swizzled word of row 8c + k
+            const uint32_t av[4] = {a[u].x, a[u].y, a[u].z, a[u].w};
+            const uint32_t bv[4] = {b[u].x, b[u].y, b[u].z, b[u].w};
+#pragma unroll
+            for (int h = 0; h < 4; h++) {
+                W[(8 * c + 2 * h) * WPR + pw] = __byte_perm(av[h], bv[h], 0x5410);
+                W[(8 * c + 2 * h + 1) * WPR + pw] = __byte_perm(av[h], bv[h], 0x7632);
+            }
+        }
+        __syncthreads();
+        TO* out = reinterpret_cast<TO*>(tp.out) + ob;
+#pragma unroll
+        for (int u = 0; u < NS; u++) {
+            const int row = r0 + RPP * u;
+            const int64_t oi = i0 + row, oj = j0 + 8 * q;
+            if (oi < tp.n_i && oj < tp.n_j) {
+                const uint4 w = *reinterpret_cast<const uint4*>(&W[row * WPR + ((q ^ ((row >> 3) & 7)) << 2)]);
+                if constexpr (RAW) {
+                    st_stream_v4(out + oi * tp.out_si + oj, w);
+                } else {
+                    float val[1][8], acc[8];
+                    unpack8(w, std::is_same<TI, __half>::value ? TADMA_F16 : TADMA_BF16, val[0]);
+#pragma unroll
+                    for (int k = 0; k < 8; k++) acc[k] = val[0][k];
+                    program<float, 1, 8, PROG>(tp.chain, acc, val);
+                    raw8_store<TO>(out + oi * tp.out_si + oj, acc);
+                }
+            }
+        }
+        __syncthreads();
+    }
+}
+
 template <typename TI, typename TO>
 void launch_t64_io(bool fast, dim3 grid, const TransposeParams& tp, cudaStream_t s) {
     if (fast && sizeof(TO) == 2) (void)launch_pdl(transpose64_kernel<TI, TO, PROG_INTERP_FAST>, grid, dim3(THREADS), 0, s, tp);
@@ -1456,8 +1552,47 @@ int launch_rows(int xdt, int odt, int act, const AffineRowsParams& p, cudaStream
                              : launch_rows_act<__nv_bfloat16, float>(act, p, s);
 }
 
+// Whether the chain leaves a value of the input dtype unchanged: only copies
+// of the running value, rounded (if at all) to the input dtype or wider.
+bool identity_chain(const TransposeParams& tp) {
+    if (tp.in_dtype != tp.out_dtype) return false;
+    for (int k = 0; k < tp.chain.n_instr; k++) {
+        const tadma_instr& I = tp.chain.prog[k];
+        if (I.op != TADMA_OP_COPY || I.b == TADMA_SRC_IMM) return false;
+        const int rd = I.round_dtype;
+        if (rd >= 0 && rd != tp.in_dtype && rd != TADMA_F32 && rd != TADMA_F64) return false;
+    }
+    return true;
+}
+
+template <typename TI, typename TO, int TJ>
+void launch_t16_tj(bool fast, dim3 grid, const TransposeParams& tp, cudaStream_t s) {
+    if (identity_chain(tp)) (void)launch_pdl(transpose16_kernel<TI, TO, PROG_INTERP, TJ, true>, grid, dim3(THREADS), 0, s, tp);
+    else if (fast) (void)launch_pdl(transpose16_kernel<TI, TO, PROG_INTERP_FAST, TJ, false>, grid, dim3(THREADS), 0, s, tp);
+    else (void)launch_pdl(transpose16_kernel<TI, TO, PROG_INTERP, TJ, false>, grid, dim3(THREADS), 0, s, tp);
+}
+template <typename TI, typename TO>
+void launch_t16_io(bool fast, int64_t gz, const TransposeParams& tp, cudaStream_t s) {
+    const unsigned gy = (unsigned)((tp.n_i + 63) / 64);
+    if (tp.n_j >= 256) launch_t16_tj<TI, TO, 256>(fast, dim3((unsigned)((tp.n_j + 255) / 256), gy, (unsigned)gz), tp, s);
+    else launch_t16_tj<TI, TO, 128>(fast, dim3((unsigned)((tp.n_j + 127) / 128), gy, (unsigned)gz), tp, s);
+}
+template <typename TI>
+void launch_t16_i(bool fast, int64_t gz, const TransposeParams& tp, cudaStream_t s) {
+    if (tp.out_dtype == TADMA_F16) launch_t16_io<TI, __half>(fast, gz, tp, s);
+    else launch_t16_io<TI, __nv_bfloat16>(fast, gz, tp, s);
+}
+
 int launch_transpose(bool fast, const TransposeParams& tp, cudaStream_t s) {
     const int64_t gz = tp.nbatch < 65535 ? tp.nbatch : 65535;
+    const bool in16 = tp.in_dtype == TADMA_F16 || tp.in_dtype == TADMA_BF16;
+    const bool out16 = tp.out_dtype == TADMA_F16 || tp.out_dtype == TADMA_BF16;
+    if (in16 && out16 && transpose64_ok(tp)) {
+        if (tp.in_dtype == TADMA_F16) launch_t16_i<__half>(fast, gz > 0 ? gz : 1, tp, s);
+        else launch_t16_i<__nv_bfloat16>(fast, gz > 0 ? gz : 1, tp, s);
+        cudaError_t e = cudaGetLastError();
+        return e == cudaSuccess ? TADMA_OK : cuda_fail(e, "tadma_b200_eltwise launch");
+    }
     if (transpose64_ok(tp)) {
         dim3 grid((unsigned)((tp.n_j + 63) / 64), (unsigned)((tp.n_i + 63) / 64), (unsigned)(gz > 0 ? gz : 1));
         switch (tp.in_dtype) {

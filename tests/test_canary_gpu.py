@@ -129,6 +129,27 @@ def test_transpose(shape):
     same_bits(g.t, plain)
 
 
+@pytest.mark.parametrize("shape", [(72, 136), (3, 200, 264), (2, 520, 72)])
+@pytest.mark.parametrize("raw", [True, False])
+def test_transpose16(shape, raw):
+    # 16-bit in and out: pair-packed tiles, a plain copy (raw words) or a chain
+    import torch
+    x = rand(shape, torch.float16, 6)
+    before = snapshot(x)
+    xt = x.transpose(-1, -2)
+    odt = torch.float16 if raw else torch.bfloat16
+    prog = [instr(Op.COPY)] if raw else [instr(Op.TANH)]
+    g = Guarded(tuple(xt.shape), odt)
+    tb.eltwise(g.t, [xt], prog, Compute.F32)
+    plain = torch.empty(tuple(xt.shape), dtype=odt, device="cuda")
+    tb.eltwise(plain, [xt], prog, Compute.F32)
+    g.check()
+    unchanged([x], before)
+    same_bits(g.t, plain)
+    if raw:
+        assert torch.equal(plain.view(torch.int16), xt.contiguous().view(torch.int16))
+
+
 # ---- reductions -----------------------------------------------------------------
 
 @pytest.mark.parametrize("shape,axis", [((37, 1001), -1), ((37, 1001), 0), ((3, 777, 65), 1),

@@ -44,7 +44,8 @@ def test_config2_reaches_the_row_affine_kernel():
 
 @pytest.mark.parametrize("case,kernel", [("add", "typed1_kernel"), ("cast", "typed1_kernel"),
                                          ("gt", "typed_cmp_kernel"), ("where", "typed_where_kernel"),
-                                         ("chain", "typed_kernel"), ("transpose", "transpose64_kernel"),
+                                         ("chain", "typed_kernel"), ("transpose", "transpose16_kernel"),
+                                         ("transpose32", "transpose64_kernel"),
                                          ("gelu_add", "chain_narrow_kernel")])
 def test_eager_calls_reach_their_typed_kernels(case, kernel):
     import torch
@@ -66,6 +67,10 @@ def test_eager_calls_reach_their_typed_kernels(case, kernel):
     elif case == "transpose":
         at = torch.empty((1024, 512), dtype=torch.float16, device="cuda")
         fn = lambda: tb.eltwise(at, [a.t()], [instr(Op.COPY)])  # noqa: E731
+    elif case == "transpose32":
+        a32 = torch.empty((512, 1024), dtype=torch.float32, device="cuda")
+        at32 = torch.empty((1024, 512), dtype=torch.float32, device="cuda")
+        fn = lambda: tb.eltwise(at32, [a32.t()], [instr(Op.COPY)])  # noqa: E731
     else:  # act(x * s + y): compile-time affine program
         fn = lambda: tb.eltwise(out, [a, b], [instr(Op.MUL, b=SRC_IMM, imm=0.5), instr(Op.ADD, b=1),  # noqa: E731
                                               instr(Op.GELU)])

@@ -221,8 +221,11 @@ def test_invalid_arguments_raise():
 @pytest.mark.parametrize("shape,perm", [((70, 45), (1, 0)), ((3, 33, 100), (0, 2, 1)), ((2, 5, 37, 64), (0, 2, 3, 1)),
                                         ((4, 8, 96, 64), (0, 1, 3, 2)),
                                         # 16-byte aligned rows: the 64 x 64 vector tiles, with partial edge tiles
-                                        ((3, 72, 136), (0, 2, 1)), ((200, 264), (1, 0)), ((2, 24, 16, 8), (0, 2, 3, 1))])
-@pytest.mark.parametrize("dt,out_dt", [(DType.F32, DType.F32), (DType.BF16, DType.BF16), (DType.F16, DType.F32)])
+                                        ((3, 72, 136), (0, 2, 1)), ((200, 264), (1, 0)), ((2, 24, 16, 8), (0, 2, 3, 1)),
+                                        # 16-bit: 64 x 256 pair-packed tiles (n_j >= 256), partial in both dims
+                                        ((2, 520, 72), (0, 2, 1)), ((600, 136), (1, 0)), ((3, 264, 4, 16), (0, 2, 3, 1))])
+@pytest.mark.parametrize("dt,out_dt", [(DType.F32, DType.F32), (DType.BF16, DType.BF16), (DType.F16, DType.F32),
+                                       (DType.F16, DType.F16), (DType.F16, DType.BF16), (DType.BF16, DType.F16)])
 def test_transpose_copy_and_cast(shape, perm, dt, out_dt):
     import torch
     x = gen(shape, dt, Dist.NORMAL, 0.0, 1.0, 30)
@@ -251,6 +254,22 @@ def test_transpose64_with_chain():
     ref = np.zeros((6, 72, 136), np.uint16)
     assert O.eltwise(ref, [np.transpose(x, (0, 2, 1))], prog, Compute.F32, out_dtype=DType.BF16, in_dtypes=[DType.F32]) == 0
     assert ulp_diff(from_dev(out), ref, DType.BF16).max() <= 1
+
+
+@pytest.mark.parametrize("n_j", [136, 520])
+def test_transpose16_with_chain(n_j):
+    # 16-bit in and out: the pair-packed tile kernel runs the chain on the way out
+    import torch
+    x = gen((3, n_j, 72), DType.BF16, Dist.NORMAL, 0.0, 1.0, 33)
+    xd = to_dev(x, DType.BF16)
+    view = make_tensor(xd.data_ptr(), DType.BF16, [3, 72, n_j], [n_j * 72, 1, 72])
+    out = empty_dev((3, 72, n_j), DType.F16)
+    prog = [instr(Op.MUL, b=SRC_IMM, imm=1.5), instr(Op.GELU)]
+    tb.eltwise(out, [view], prog, Compute.F32)
+    torch.cuda.synchronize()
+    ref = np.zeros((3, 72, n_j), np.uint16)
+    assert O.eltwise(ref, [np.transpose(x, (0, 2, 1))], prog, Compute.F32, out_dtype=DType.F16, in_dtypes=[DType.BF16]) == 0
+    assert ulp_diff(from_dev(out), ref, DType.F16).max() <= 1
 
 
 def test_transpose_with_chain():
