@@ -189,9 +189,10 @@ __device__ __forceinline__ int64_t round_to(int64_t v, int dt) {
 // Exact floor(n / d) for every 64-bit n, d >= 1 (GM94 Fig. 4.1 with N = 64).
 struct DivMod {
     uint64_t d = 1;
-    uint64_t m = 0;   // magic multiplier
-    uint32_t s1 = 0;  // min(l, 1)
-    uint32_t s2 = 0;  // max(l - 1, 0)
+    uint64_t m = 0;    // magic multiplier, 64-bit dividends
+    uint32_t m32 = 0;  // magic multiplier, dividends below 2^32 (0 when d >= 2^32)
+    uint16_t s1 = 0;   // min(l, 1)
+    uint16_t s2 = 0;   // max(l - 1, 0)
 
     DivMod() = default;
     __host__ explicit DivMod(uint64_t d_) : d(d_ ? d_ : 1) {
@@ -200,8 +201,20 @@ struct DivMod {
         unsigned __int128 two64 = (unsigned __int128)1 << 64;
         unsigned __int128 num = two64 * (((unsigned __int128)1 << l) - d);
         m = (uint64_t)(num / d + 1);
-        s1 = l < 1 ? l : 1;
-        s2 = l > 0 ? l - 1 : 0;
+        // The same construction at N = 32 (2^l - d < d, so the quotient fits).
+        if (d <= 0xffffffffull) m32 = (uint32_t)((((uint64_t)1 << 32) * (((uint64_t)1 << l) - d)) / d + 1);
+        s1 = (uint16_t)(l < 1 ? l : 1);
+        s2 = (uint16_t)(l > 0 ? l - 1 : 0);
+    }
+    // n / d for n < 2^32 and d < 2^32: one 32-bit high multiply instead of
+    // the 64-bit one (several IMADs and carries on the GPU).
+    __host__ __device__ __forceinline__ uint32_t div32(uint32_t n) const {
+#ifdef __CUDA_ARCH__
+        uint32_t t1 = __umulhi(m32, n);
+#else
+        uint32_t t1 = (uint32_t)(((uint64_t)m32 * n) >> 32);
+#endif
+        return (t1 + ((n - t1) >> s1)) >> s2;
     }
     __host__ __device__ __forceinline__ uint64_t div(uint64_t n) const {
 #ifdef __CUDA_ARCH__

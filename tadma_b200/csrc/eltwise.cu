@@ -53,7 +53,8 @@ struct ChainParams {
     int32_t rank;
     int32_t n_instr;
     int32_t out_dtype;
-    int32_t pad;
+    int32_t idx32;  // 1: every element index is below 2^32 (32-bit quotients);
+                    // 2: also every operand offset below 2^31 (32-bit offset sums)
     int64_t start;  // first element (scalar tail launch)
     int64_t n;      // element count (scalar path) / vector count (vector path)
     int64_t dims[TADMA_MAX_RANK];
@@ -417,13 +418,45 @@ __device__ __forceinline__ void offsets(const ChainParams& p, uint64_t e, int64_
     oo = 0;
 #pragma unroll
     for (int k = 0; k < NIN; k++) io[k] = 0;
-    for (int d = p.rank - 1; d >= 1; d--) {
-        uint64_t q, r;
-        p.dm[d].divmod(e, q, r);
-        oo += (int64_t)r * p.out_stride[d];
+    if (p.idx32 == 2) {
+        // 32-bit quotients and offset sums: the host checked that every
+        // operand's largest offset (all strides >= 0) is below 2^31.
+        uint32_t e32 = (uint32_t)e, o32 = 0, i32[NIN > 0 ? NIN : 1];
 #pragma unroll
-        for (int k = 0; k < NIN; k++) io[k] += (int64_t)r * p.in[k].stride[d];
-        e = q;
+        for (int k = 0; k < NIN; k++) i32[k] = 0;
+        for (int d = p.rank - 1; d >= 1; d--) {
+            const uint32_t q = p.dm[d].div32(e32), r = e32 - q * (uint32_t)p.dm[d].d;
+            o32 += r * (uint32_t)p.out_stride[d];
+#pragma unroll
+            for (int k = 0; k < NIN; k++) i32[k] += r * (uint32_t)p.in[k].stride[d];
+            e32 = q;
+        }
+        oo = (int64_t)(o32 + e32 * (uint32_t)p.out_stride[0]);
+#pragma unroll
+        for (int k = 0; k < NIN; k++) io[k] = (int64_t)(i32[k] + e32 * (uint32_t)p.in[k].stride[0]);
+        return;
+    }
+    if (p.idx32) {
+        // Same walk with 32-bit quotients (the host sets idx32 only when the
+        // element count is below 2^32); offsets stay 64-bit.
+        uint32_t e32 = (uint32_t)e;
+        for (int d = p.rank - 1; d >= 1; d--) {
+            const uint32_t q = p.dm[d].div32(e32), r = e32 - q * (uint32_t)p.dm[d].d;
+            oo += (int64_t)r * p.out_stride[d];
+#pragma unroll
+            for (int k = 0; k < NIN; k++) io[k] += (int64_t)r * p.in[k].stride[d];
+            e32 = q;
+        }
+        e = e32;
+    } else {
+        for (int d = p.rank - 1; d >= 1; d--) {
+            uint64_t q, r;
+            p.dm[d].divmod(e, q, r);
+            oo += (int64_t)r * p.out_stride[d];
+#pragma unroll
+            for (int k = 0; k < NIN; k++) io[k] += (int64_t)r * p.in[k].stride[d];
+            e = q;
+        }
     }
     oo += (int64_t)e * p.out_stride[0];
 #pragma unroll
@@ -755,6 +788,15 @@ __global__ void __launch_bounds__(THREADS) typed1_kernel(const __grid_constant__
 #pragma unroll
         for (int u = 0; u < U; u++) {
             const int64_t vi = base + u * THREADS;
+            if constexpr (OP == TADMA_OP_COPY && std::is_same<TI, TO>::value) {
+                // A copy within one dtype moves the raw words (bit-exact).
+                if (vi < p.n) {
+                    TO* dst = reinterpret_cast<TO*>(p.out) + oo[u];
+                    st_stream_v4(dst, raw[u][0].w[0]);
+                    if constexpr (sizeof(TO) == 4) st_stream_v4(dst + 4, raw[u][0].w[1]);
+                }
+                continue;
+            }
             if (vi < p.n) {
                 float a[V], b[V];
                 raw8_cvt<TI>(raw[u][0], a);
@@ -1769,6 +1811,22 @@ extern "C" int tadma_b200_eltwise(const tadma_tensor* out, const tadma_tensor* i
     // Both paths decompose ELEMENT indices; a vector (V elements, inner % V
     // == 0 when rank > 1) never straddles a row.
     for (int d = 1; d < f.rank; d++) p.dm[d] = DivMod((uint64_t)f.dims[d]);
+    p.idx32 = (uint64_t)n < 0xffffffffull ? 1 : 0;
+    if (p.idx32) {
+        // Largest offset of the output and of each input, with non-negative
+        // strides only: below 2^31 everywhere allows 32-bit offset sums.
+        bool small = true;
+        for (int k = 0; k <= n_ins && small; k++) {
+            int64_t top = 0;
+            for (int d = 0; d < f.rank && small; d++) {
+                const int64_t st = f.strides[k][d];
+                if (st < 0 || st > 0x7fffffff) small = false;
+                else top += (f.dims[d] - 1) * st;
+                if (top > 0x7fffffff) small = false;
+            }
+        }
+        if (small) p.idx32 = 2;
+    }
 
     // Fast math (SFU exp / reciprocal) when an fp32 chain ends in a 16-bit
     // store and every intermediate rounding is to fp32 or coarser: the

@@ -103,3 +103,36 @@ def test_layer_norm_large_mean_and_constant_rows(dt):
     got = from_dev(y)
     assert ulp_diff(got, ref, dt).max() <= 1
     assert not got[4:6].astype(np.float32).any() if dt == DType.F16 else not (got[4:6] & 0x7FFF).any()
+
+
+# ---- index widths: 32-bit index walks where they fit, 64-bit beyond ---------------
+
+def test_strided_view_with_offsets_past_2_31():
+    # Elements < 2^32 but an input offset >= 2^31: 32-bit quotients, 64-bit offsets.
+    import torch
+    base = torch.empty((2 ** 31 + 1024,), dtype=torch.float16, device="cuda")
+    rows = torch.randn((2, 1024), device="cuda").to(torch.float16)
+    view = base.as_strided((2, 1024), (2 ** 31, 1))
+    view.copy_(rows)
+    out = torch.empty((2, 1024), dtype=torch.float16, device="cuda")
+    tb.eltwise(out, [view], [instr(Op.COPY)])
+    out2 = torch.empty((2, 1024), dtype=torch.float32, device="cuda")
+    tb.eltwise(out2, [view], [instr(Op.MUL, b=SRC_IMM, imm=2.0)], Compute.F32)
+    torch.cuda.synchronize()
+    assert torch.equal(out.view(torch.int16), rows.view(torch.int16))
+    assert torch.equal(out2, rows.float() * 2)
+    del base
+
+
+def test_broadcast_past_2_32_elements():
+    # More than 2^32 output elements: the 64-bit index walk.
+    import torch
+    rows = 2 ** 32 // 1024 + 3
+    row = torch.arange(1024, device="cuda", dtype=torch.int32).to(torch.uint8)
+    out = torch.empty((rows, 1024), dtype=torch.uint8, device="cuda")
+    tb.eltwise(out, [row.expand(rows, 1024)], [instr(Op.COPY)])
+    torch.cuda.synchronize()
+    for r in (0, 1, 2 ** 22 - 1, 2 ** 22, rows - 1):
+        assert torch.equal(out[r], row), r
+    assert bool((out[-4:] == row).all())
+    del out
