@@ -1104,7 +1104,8 @@ __global__ void __launch_bounds__(THREADS) transpose_chain_kernel(const __grid_c
 }
 
 // 64 x 64 tiles with 16-byte accesses on both sides, for f32 / f16 / bf16 in
-// and out with 16-byte aligned rows: each thread loads 2 (16-bit) or 4 (f32)
+// and out with 16-byte aligned rows and fp32 on at least one side (16-bit in
+// and out goes to transpose16_kernel): each thread loads 2 (16-bit) or 4 (f32)
 // 16-byte vectors along the input's contiguous dim, the tile is transposed
 // through shared memory as fp32, and each thread stores 2 vectors of 8
 // elements along the output's contiguous dim.  One tile per CTA.  The 32 x 32
