@@ -290,7 +290,7 @@ int tadma_b200_gather(const tadma_tensor* table, int32_t axis, const tadma_tenso
 /* ------------------------------------------------------- seeded generator -- */
 enum tadma_dist {
     TADMA_DIST_UNIFORM = 0, /* U(p0, p1) from a 24-bit grid: p0 + (p1 - p0) * k * 2^-24 */
-    TADMA_DIST_NORMAL = 1,  /* mean p0, std p1; Irwin-Hall(4) rescaled to unit variance */
+    TADMA_DIST_NORMAL = 1,  /* N(p0, p1^2): Box-Muller in double from two 53-bit uniforms, |z| < 8.6 */
     TADMA_DIST_INDEX = 2    /* integers in [0, p1) (p0 ignored), int64/int32 out */
 };
 

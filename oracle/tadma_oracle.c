@@ -111,13 +111,58 @@ static int64_t ldi(const void* p, int32_t dt, int64_t off) {
     }
 }
 
-/* Store a double: float types round via fp32 (fp16/bf16 are rounded from the
- * fp32 value, the path every kernel takes), integers truncate/saturate. */
+/* Double -> fp16 / bf16 with ONE round-to-nearest-even step (no detour
+ * through fp32, which could round twice).  The value is scaled by a power of
+ * two (exact) so that the target's unit in the last place becomes 1, rounded
+ * with nearbyint (the default rounding mode is nearest-even) and the bits are
+ * rebuilt; the significand carry into the next binade and the subnormal range
+ * fall out of the same formula.  NaN keeps the bits of the fp32 path. */
+static uint16_t f64_to_16(double v, int man_bits, int emin, int bias, double inf_at, uint16_t inf_bits,
+                          uint16_t (*nan_path)(float)) {
+    uint64_t x;
+    memcpy(&x, &v, 8);
+    uint16_t sign = (uint16_t)((x >> 48) & 0x8000u);
+    double a = fabs(v);
+    if (v != v) return nan_path((float)v);
+    if (a >= inf_at) return (uint16_t)(sign | inf_bits);
+    if (a == 0.0) return sign;
+    int e;
+    (void)frexp(a, &e); /* a in [2^(e-1), 2^e) */
+    int E = e - 1 < emin ? emin : e - 1;
+    double m = nearbyint(ldexp(a, man_bits - E));
+    return (uint16_t)(sign | (uint32_t)(((int64_t)(E + bias) << man_bits) + (int64_t)m - ((int64_t)1 << man_bits)));
+}
+
+uint16_t or_f64_to_f16(double v) {
+    /* >= 65520 rounds to inf; normal exponents from -14, 10 stored bits */
+    return f64_to_16(v, 10, -14, 15, 65520.0, 0x7c00u, or_f32_to_f16);
+}
+
+uint16_t or_f64_to_bf16(double v) {
+    /* >= (2 - 2^-8) * 2^127 rounds to inf; normal exponents from -126, 7 stored bits */
+    return f64_to_16(v, 7, -126, 127, ldexp(2.0 - ldexp(1.0, -8), 127), 0x7f80u, or_f32_to_bf16);
+}
+
+/* int64 -> bf16 in one rounding: below 2^53 the double is exact; above, the
+ * 8 significant bits are rounded on the integer (ties to even). */
+static uint16_t i64_to_bf16(int64_t v) {
+    if (v > -(1LL << 53) && v < (1LL << 53)) return or_f64_to_bf16((double)v);
+    uint64_t a = v < 0 ? 0 - (uint64_t)v : (uint64_t)v;
+    int p = 63 - __builtin_clzll(a), sh = p - 7;
+    uint64_t q = a >> sh, rem = a & ((1ULL << sh) - 1), half = 1ULL << (sh - 1);
+    if (rem > half || (rem == half && (q & 1u))) q++;
+    double r = ldexp((double)q, sh); /* exact: q <= 256 */
+    return or_f64_to_bf16(v < 0 ? -r : r);
+}
+
+/* Store a double: one rounding to the element type (fp32, fp16 and bf16 are
+ * each rounded from the double; a double that holds an fp32 value gives the
+ * same bits as rounding that fp32 value), integers truncate/saturate. */
 static void st(void* p, int32_t dt, int64_t off, double v) {
     switch (dt) {
     case TADMA_F32: ((float*)p)[off] = (float)v; break;
-    case TADMA_F16: ((uint16_t*)p)[off] = or_f32_to_f16((float)v); break;
-    case TADMA_BF16: ((uint16_t*)p)[off] = or_f32_to_bf16((float)v); break;
+    case TADMA_F16: ((uint16_t*)p)[off] = or_f64_to_f16(v); break;
+    case TADMA_BF16: ((uint16_t*)p)[off] = or_f64_to_bf16(v); break;
     case TADMA_F64: ((double*)p)[off] = v; break;
     case TADMA_I64: ((int64_t*)p)[off] = f2i(v); break;
     case TADMA_I32: ((int32_t*)p)[off] = (int32_t)f2i(v); break;
@@ -134,16 +179,33 @@ static void sti(void* p, int32_t dt, int64_t off, int64_t v) {
     case TADMA_U8: ((uint8_t*)p)[off] = (uint8_t)v; break;
     case TADMA_BOOL: ((uint8_t*)p)[off] = v != 0; break;
     case TADMA_I8: ((int8_t*)p)[off] = (int8_t)v; break;
-    default: st(p, dt, off, (double)v); break;
+    case TADMA_F32: ((float*)p)[off] = (float)v; break; /* one rounding (cvtsi2ss) */
+    case TADMA_BF16: ((uint16_t*)p)[off] = i64_to_bf16(v); break;
+    default: st(p, dt, off, (double)v); break; /* f16: |v| >= 2^53 is inf either way */
     }
+}
+
+/* Round an int64 to what a tensor of dtype `dt` would hold, read back as int64. */
+static int64_t round_to_i(int64_t v, int32_t dt) {
+    switch (dt) {
+    case TADMA_F32: return f2i((double)(float)v);
+    case TADMA_F16: return f2i(or_f16_to_f32(or_f64_to_f16((double)v)));
+    case TADMA_BF16: return f2i(or_bf16_to_f32(i64_to_bf16(v)));
+    case TADMA_F64: return f2i((double)v);
+    case TADMA_I32: return (int32_t)v;
+    case TADMA_U8: return (uint8_t)v;
+    case TADMA_BOOL: return v != 0;
+    case TADMA_I8: return (int8_t)v;
+    }
+    return v;
 }
 
 /* Round a double to what a tensor of dtype `dt` would hold. */
 static double round_to(double v, int32_t dt) {
     switch (dt) {
     case TADMA_F32: return (float)v;
-    case TADMA_F16: return or_f16_to_f32(or_f32_to_f16((float)v));
-    case TADMA_BF16: return or_bf16_to_f32(or_f32_to_bf16((float)v));
+    case TADMA_F16: return or_f16_to_f32(or_f64_to_f16(v));
+    case TADMA_BF16: return or_bf16_to_f32(or_f64_to_bf16(v));
     case TADMA_F64: return v;
     case TADMA_I64: return (double)f2i(v);
     case TADMA_I32: return (double)(int32_t)f2i(v);
@@ -170,12 +232,95 @@ static uint64_t gen_draw(uint64_t key, uint64_t idx, uint64_t j) {
     return or_mix64(key + (4 * idx + j + 1) * 0x9E3779B97F4A7C15ULL);
 }
 
+/* N(0, 1) by Box-Muller (G. E. P. Box and M. E. Muller, Ann. Math. Statist.
+ * 29(2), 1958): z = sqrt(-2 ln u1) cos(2 pi t), one value per element from
+ * its own two 53-bit uniforms.  ln and cos are evaluated here from their
+ * series with IEEE-rounded +, -, *, / and sqrt only (no libm call), in the
+ * same operation order as tadma_b200_fill, so host and device agree bit for
+ * bit:
+ *   ln u = e ln2 + 2 atanh(s) = e ln2 + s * sum_j 2/(2j+1) s^(2j),
+ *          u = m 2^e, m in [sqrt(1/2), sqrt 2], s = (m - 1) / (m + 1);
+ *   cos 2 pi t for t in turns, folded to [0, 1/8] by cos(2pi t) = cos(2pi(1-t)),
+ *          = -cos(2pi(1/2-t)), = sin(2pi(1/4-t)) (each fold exact), then the
+ *          Taylor series of cos or sin at x = 2 pi t <= pi/4.
+ * The coefficients are built once by exact-integer divisions (gen_coefs). */
+#define GEN_LN_TERMS 12
+#define GEN_TRIG_TERMS 9
+typedef struct {
+    double ln[GEN_LN_TERMS];  /* 2 / (2j + 1) */
+    double cs[GEN_TRIG_TERMS]; /* (-1)^k / (2k)! */
+    double sn[GEN_TRIG_TERMS]; /* (-1)^k / (2k + 1)! */
+} gen_coefs;
+
+static void gen_coefs_init(gen_coefs* c) {
+    for (int j = 0; j < GEN_LN_TERMS; j++) c->ln[j] = 2.0 / (double)(2 * j + 1);
+    c->cs[0] = 1.0;
+    c->sn[0] = 1.0;
+    for (int k = 1; k < GEN_TRIG_TERMS; k++) {
+        c->cs[k] = -c->cs[k - 1] / (double)((2 * k - 1) * (2 * k));
+        c->sn[k] = -c->sn[k - 1] / (double)((2 * k) * (2 * k + 1));
+    }
+}
+
+static double gen_ln(const gen_coefs* c, double u) { /* u in (0, 1] */
+    uint64_t bits;
+    memcpy(&bits, &u, 8);
+    int e = (int)((bits >> 52) & 0x7ffu) - 1023;
+    uint64_t mb = (bits & 0xfffffffffffffULL) | 0x3ff0000000000000ULL;
+    double m;
+    memcpy(&m, &mb, 8);
+    if (m > 0x1.6a09e667f3bcdp+0) { /* sqrt 2 */
+        m = m * 0.5;
+        e = e + 1;
+    }
+    double s = (m - 1.0) / (m + 1.0);
+    double w = s * s;
+    double p = c->ln[GEN_LN_TERMS - 1];
+    for (int j = GEN_LN_TERMS - 2; j >= 0; j--) p = c->ln[j] + w * p;
+    return (double)e * 0x1.62e42fefa39efp-1 + s * p; /* ln 2 */
+}
+
+static double gen_cos_turns(const gen_coefs* c, double t) { /* t in [0, 1) */
+    int neg = 0, use_sin = 0;
+    if (t > 0.5) t = 1.0 - t;
+    if (t > 0.25) {
+        t = 0.5 - t;
+        neg = 1;
+    }
+    if (t > 0.125) {
+        t = 0.25 - t;
+        use_sin = 1;
+    }
+    double x = t * 0x1.921fb54442d18p+2; /* 2 pi */
+    double y = x * x;
+    const double* k = use_sin ? c->sn : c->cs;
+    double p = k[GEN_TRIG_TERMS - 1];
+    for (int j = GEN_TRIG_TERMS - 2; j >= 0; j--) p = k[j] + y * p;
+    if (use_sin) p = x * p;
+    return neg ? -p : p;
+}
+
+static double gen_normal(const gen_coefs* c, uint64_t key, uint64_t g) {
+    double u1 = (double)((gen_draw(key, g, 0) >> 11) + 1) * 0x1p-53; /* (0, 1] */
+    double t = (double)(gen_draw(key, g, 1) >> 11) * 0x1p-53;        /* [0, 1) */
+    double r = sqrt(-2.0 * gen_ln(c, u1));
+    return r * gen_cos_turns(c, t);
+}
+
+double or_gen_normal(uint64_t seed, uint64_t stream_id, uint64_t g) {
+    gen_coefs c;
+    gen_coefs_init(&c);
+    return gen_normal(&c, gen_key(seed, stream_id), g);
+}
+
 int or_fill(const tadma_tensor* out, int32_t dist, double p0, double p1, uint64_t seed,
             uint64_t stream_id, int64_t offset) {
     int64_t n = 1;
     for (int d = 0; d < out->rank; d++) n *= out->dims[d];
     uint64_t key = gen_key(seed, stream_id);
     double span = p1 - p0;
+    gen_coefs coefs;
+    gen_coefs_init(&coefs);
 #pragma omp parallel for schedule(static)
     for (int64_t i = 0; i < n; i++) {
         int64_t idx[TADMA_MAX_RANK], off = 0;
@@ -190,10 +335,7 @@ int or_fill(const tadma_tensor* out, int32_t dist, double p0, double p1, uint64_
             double u = (double)(gen_draw(key, g, 0) >> 40) * 0x1p-24;
             st(out->data, out->dtype, off, p0 + span * u);
         } else {
-            double s = 0.0;
-            for (int j = 0; j < 4; j++) s += (double)(gen_draw(key, g, (uint64_t)j) >> 40) * 0x1p-23 - 1.0;
-            double z = s * 0.8660254037844386;
-            st(out->data, out->dtype, off, p0 + p1 * z);
+            st(out->data, out->dtype, off, p0 + p1 * gen_normal(&coefs, key, g));
         }
     }
     return TADMA_OK;
@@ -381,15 +523,18 @@ int or_eltwise(const tadma_tensor* out, const tadma_tensor* ins, int32_t n_ins,
                 int64_t c = I->c >= 0 ? iin[I->c] : (int64_t)I->imm;
                 if (op_is_unary(I->op)) acc = (I->op == TADMA_OP_COPY && I->b == TADMA_SRC_IMM) ? b : bin_i(I->op, acc, 0, 0);
                 else acc = bin_i(I->op, acc, b, c);
-                if (I->round_dtype >= 0) acc = f2i(round_to((double)acc, I->round_dtype));
+                if (I->round_dtype >= 0) acc = round_to_i(acc, I->round_dtype);
             }
             sti(out->data, out->dtype, offset_of(out, idx), acc);
         } else if (cm == TADMA_COMPUTE_F32) {
-            float acc = n_ins > 0 ? (float)vin[0] : 0.0f;
+            float fin[TADMA_MAX_INPUTS];
+            for (int k = 0; k < n_ins; k++) /* an int64 input rounds to fp32 once, as load_as<float> does */
+                fin[k] = ins[k].dtype == TADMA_I64 ? (float)((const int64_t*)ins[k].data)[offset_of(&ins[k], idx)] : (float)vin[k];
+            float acc = n_ins > 0 ? fin[0] : 0.0f;
             for (int i = 0; i < n_instr; i++) {
                 const tadma_instr* I = &prog[i];
-                float b = I->b >= 0 ? (float)vin[I->b] : (float)I->imm;
-                float c = I->c >= 0 ? (float)vin[I->c] : (float)I->imm;
+                float b = I->b >= 0 ? fin[I->b] : (float)I->imm;
+                float c = I->c >= 0 ? fin[I->c] : (float)I->imm;
                 if (I->op == TADMA_OP_COPY && I->b == TADMA_SRC_IMM) acc = b;
                 else if (I->op == TADMA_OP_POW) acc = (b == 2.0f) ? acc * acc : (float)pow((double)acc, (double)b);
                 else if (op_is_unary(I->op)) {

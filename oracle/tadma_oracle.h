@@ -30,11 +30,15 @@ uint16_t or_f32_to_f16(float f);
 float or_f16_to_f32(uint16_t h);
 uint16_t or_f32_to_bf16(float f);
 float or_bf16_to_f32(uint16_t h);
+uint16_t or_f64_to_f16(double v);  /* one rounding, no detour through fp32 */
+uint16_t or_f64_to_bf16(double v);
 
 /* seeded generator (same definition as tadma_b200_fill) */
 uint64_t or_mix64(uint64_t z);
 int or_fill(const tadma_tensor* out, int32_t dist, double p0, double p1, uint64_t seed,
             uint64_t stream_id, int64_t offset);
+/* The standard normal value of global element g (before mean / std / rounding). */
+double or_gen_normal(uint64_t seed, uint64_t stream_id, uint64_t g);
 
 /* MapToShape (include/tadma/Utils.hpp:9-17): linear -> row-major multi-index */
 void or_map_to_shape(const int64_t* dims, int32_t rank, int64_t index, int64_t* out_idx);

@@ -1,0 +1,195 @@
+// chain_reduce.cu - tadma_b200_reduce_chain's kernel: a reduction whose
+// elements are a fused chain, evaluated on the fly.
+#include "eltwise_impl.cuh"
+
+namespace tadma_b200 {
+namespace {
+
+// ------------------------------------------------------ chain reduction --
+//
+// tadma_b200_reduce_chain: a reduction whose elements are a fused chain of
+// up to 4 broadcast operands, evaluated on the fly.  One warp per output
+// element (the kept dims, folded); its lanes walk the reduced axis.  With the
+// axis contiguous (stride 1) or broadcast (stride 0) in every operand and
+// fp32 compute, lanes take 8 elements per step with 16-byte loads (the
+// eltwise vector loader) and run the chain on the 8 at once; otherwise one
+// element per lane step.  Lanes fold their elements in increasing index
+// order and combine in a fixed butterfly, as the reduction kernels do.
+
+// Raw 16-byte words of one 8-element vector (fp32: 2 words, fp16 / bf16: 1),
+// converted to the compute type at use.
+struct RawV {
+    uint4 a, b;
+};
+__device__ __forceinline__ void load_raw_vec(const Operand& o, int64_t off, RawV& r) {
+    const char* p = o.base + off * dtype_size(o.dtype);
+    r.a = ld_stream_v4(p);
+    if (o.dtype == TADMA_F32) r.b = ld_stream_v4(p + 16);
+}
+template <typename C>
+__device__ __forceinline__ void cvt_raw_vec(int dt, const RawV& r, C (&v)[V]) {
+    if (dt == TADMA_F32) {
+        const uint32_t w[8] = {r.a.x, r.a.y, r.a.z, r.a.w, r.b.x, r.b.y, r.b.z, r.b.w};
+#pragma unroll
+        for (int j = 0; j < V; j++) v[j] = from_f<C>(__uint_as_float(w[j]));
+    } else {
+        float f[8];
+        unpack8(r.a, dt, f);
+#pragma unroll
+        for (int j = 0; j < V; j++) v[j] = from_f<C>(f[j]);
+    }
+}
+
+
+
+template <typename C, int K, bool VEC, int NIN>
+__global__ void __launch_bounds__(THREADS, !VEC ? 2 : NIN == 1 ? 3 : 2) chain_reduce_kernel(const __grid_constant__ ChainReduceParams p) {
+    pdl_begin();
+    const int lane = threadIdx.x & 31;
+    const int64_t gw = ((int64_t)blockIdx.x * THREADS + threadIdx.x) >> 5;
+    const int64_t nw = ((int64_t)gridDim.x * THREADS) >> 5;
+    for (int64_t row = gw; row < p.nrows; row += nw) {
+        int64_t base[TADMA_MAX_INPUTS] = {0, 0, 0, 0};
+        int64_t ooff = 0;
+        {
+            uint64_t e = (uint64_t)row;
+            for (int d = p.krank - 1; d >= 0; d--) {
+                uint64_t q, r;
+                if (d > 0) {
+                    p.kdm[d].divmod(e, q, r);
+                } else {
+                    r = e;
+                    q = 0;
+                }
+                ooff += (int64_t)r * p.kout[d];
+#pragma unroll
+                for (int k = 0; k < TADMA_MAX_INPUTS; k++) base[k] += (int64_t)r * p.kin[k][d];
+                e = q;
+            }
+        }
+        State<C> s = init_state<K, C>();
+        int64_t done = 0;
+        if constexpr (VEC) {
+            // An operand broadcast along the axis is one value per output,
+            // loaded once.  The others are double-buffered as raw 16-byte
+            // words: the next vector step's loads are in flight while this
+            // step converts, runs the chain and folds.
+            const int64_t nv = p.R / V;
+            C bc[NIN];
+#pragma unroll
+            for (int k = 0; k < NIN; k++)
+                bc[k] = p.ax[k] == 0 ? load_as<C>(p.chain.in[k].base, p.chain.in[k].dtype, base[k]) : C(0);
+            RawV cur[NIN], nxt[NIN];
+            int64_t v = lane;
+            if (v < nv) {
+#pragma unroll
+                for (int k = 0; k < NIN; k++)
+                    if (p.ax[k] != 0) load_raw_vec(p.chain.in[k], base[k] + v * V, cur[k]);
+            }
+            for (; v < nv; v += 32) {
+                if (v + 32 < nv) {
+#pragma unroll
+                    for (int k = 0; k < NIN; k++)
+                        if (p.ax[k] != 0) load_raw_vec(p.chain.in[k], base[k] + (v + 32) * V, nxt[k]);
+                }
+                C val[NIN][V];
+#pragma unroll
+                for (int k = 0; k < NIN; k++) {
+                    if (p.ax[k] == 0) {
+#pragma unroll
+                        for (int j = 0; j < V; j++) val[k][j] = bc[k];
+                    } else {
+                        cvt_raw_vec<C>(p.chain.in[k].dtype, cur[k], val[k]);
+                    }
+                }
+                C acc[V];
+#pragma unroll
+                for (int j = 0; j < V; j++) acc[j] = val[0][j];
+                run_chain<C, NIN, V, false>(p.chain, acc, val);
+#pragma unroll
+                for (int j = 0; j < V; j++) update<K, C>(s, p.square ? acc[j] * acc[j] : acc[j], v * V + j);
+#pragma unroll
+                for (int k = 0; k < NIN; k++) cur[k] = nxt[k];
+            }
+            done = nv * V;
+        }
+        for (int64_t r = done + lane; r < p.R; r += 32) {
+            C val[TADMA_MAX_INPUTS][1];
+#pragma unroll
+            for (int k = 0; k < TADMA_MAX_INPUTS; k++)
+                if (k < p.n_ins) val[k][0] = load_as<C>(p.chain.in[k].base, p.chain.in[k].dtype, base[k] + r * p.ax[k]);
+            C acc[1] = {p.n_ins > 0 ? val[0][0] : C(0)};
+            run_chain<C, TADMA_MAX_INPUTS, 1, false>(p.chain, acc, val);
+            update<K, C>(s, p.square ? acc[0] * acc[0] : acc[0], r);
+        }
+        s = warp_combine<K, C>(s);
+        if (lane == 0) {
+            if constexpr (K == K_ARGMAX || K == K_ARGMIN) {
+                store_from(p.out, p.out_dtype, ooff, (int64_t)(s.i < 0 ? 0 : s.i));
+            } else {
+                C v = s.v;
+                if constexpr (std::is_floating_point<C>::value) {
+                    if (p.post == POST_MEAN) v = v / (C)p.R;
+                    else if (p.post == POST_RMS) v = sqrt(v / (C)p.R);
+                } else {
+                    if (p.post == POST_MEAN) v = v / p.R;
+                }
+                store_from(p.out, p.out_dtype, ooff, v);
+            }
+        }
+    }
+}
+
+template <typename C, int K, bool VEC, int NIN>
+int launch_chain_reduce_k(const ChainReduceParams& p, cudaStream_t s) {
+    const void* fn = (const void*)chain_reduce_kernel<C, K, VEC, NIN>;
+    const int64_t want = (p.nrows + (THREADS / 32) - 1) / (THREADS / 32);
+    const int64_t cap = (int64_t)sm_count() * blocks_per_sm(fn);
+    const int grid = (int)(want < cap ? (want > 0 ? want : 1) : cap);
+    cudaError_t e = launch_pdl(chain_reduce_kernel<C, K, VEC, NIN>, dim3(grid), dim3(THREADS), 0, s, p);
+    if (e == cudaSuccess) e = cudaGetLastError();
+    return e == cudaSuccess ? TADMA_OK : cuda_fail(e, "tadma_b200_reduce_chain launch");
+}
+
+// The scalar path takes the operand count at run time (NIN = 4 arrays); the
+// vector path is instantiated per operand count to keep its registers.
+template <typename C, bool VEC, int NIN>
+int launch_chain_reduce_n(int kind, const ChainReduceParams& p, cudaStream_t s) {
+    switch (kind) {
+    case K_SUM: return launch_chain_reduce_k<C, K_SUM, VEC, NIN>(p, s);
+    case K_MAX: return launch_chain_reduce_k<C, K_MAX, VEC, NIN>(p, s);
+    case K_MIN: return launch_chain_reduce_k<C, K_MIN, VEC, NIN>(p, s);
+    case K_ARGMAX: return launch_chain_reduce_k<C, K_ARGMAX, VEC, NIN>(p, s);
+    default: return launch_chain_reduce_k<C, K_ARGMIN, VEC, NIN>(p, s);
+    }
+}
+
+template <typename C, bool VEC>
+int launch_chain_reduce(int kind, const ChainReduceParams& p, cudaStream_t s) {
+    if constexpr (!VEC) {
+        return launch_chain_reduce_n<C, false, TADMA_MAX_INPUTS>(kind, p, s);
+    } else {
+        switch (p.n_ins) {
+        case 1: return launch_chain_reduce_n<C, true, 1>(kind, p, s);
+        case 2: return launch_chain_reduce_n<C, true, 2>(kind, p, s);
+        case 3: return launch_chain_reduce_n<C, true, 3>(kind, p, s);
+        default: return launch_chain_reduce_n<C, true, 4>(kind, p, s);
+        }
+    }
+}
+
+}  // namespace
+
+int launch_chain_reduce_f32(int kind, bool vec, const ChainReduceParams& p, cudaStream_t s) {
+    return vec ? launch_chain_reduce<float, true>(kind, p, s) : launch_chain_reduce<float, false>(kind, p, s);
+}
+
+int launch_chain_reduce_f64(int kind, const ChainReduceParams& p, cudaStream_t s) {
+    return launch_chain_reduce<double, false>(kind, p, s);
+}
+
+int launch_chain_reduce_i64(int kind, const ChainReduceParams& p, cudaStream_t s) {
+    return launch_chain_reduce<int64_t, false>(kind, p, s);
+}
+
+}  // namespace tadma_b200

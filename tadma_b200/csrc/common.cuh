@@ -96,8 +96,14 @@ __device__ __forceinline__ int64_t load_as<int64_t>(const char* p, int dt, int64
     return 0;
 }
 
-// Store compute value into element `off` of run-time dtype `dt`.  fp16/bf16
-// round from the fp32 value (a double is first rounded to fp32).
+// One rounding from double / int64 to a 16-bit float (no detour through
+// fp32, which could round twice).  A NaN keeps the bits of the fp32 path.
+__device__ __forceinline__ __half d2h(double v) { return v != v ? __float2half_rn(__double2float_rn(v)) : __double2half(v); }
+__device__ __forceinline__ __nv_bfloat16 d2bf(double v) {
+    return v != v ? __float2bfloat16_rn(__double2float_rn(v)) : __double2bfloat16(v);
+}
+
+// Store compute value into element `off` of run-time dtype `dt`, rounded once.
 __device__ __forceinline__ void store_from(char* p, int dt, int64_t off, float v) {
     switch (dt) {
     case TADMA_F32: reinterpret_cast<float*>(p)[off] = v; break;
@@ -115,8 +121,8 @@ __device__ __forceinline__ void store_from(char* p, int dt, int64_t off, float v
 __device__ __forceinline__ void store_from(char* p, int dt, int64_t off, double v) {
     switch (dt) {
     case TADMA_F32: reinterpret_cast<float*>(p)[off] = __double2float_rn(v); break;
-    case TADMA_F16: reinterpret_cast<__half*>(p)[off] = __float2half_rn(__double2float_rn(v)); break;
-    case TADMA_BF16: reinterpret_cast<__nv_bfloat16*>(p)[off] = __float2bfloat16_rn(__double2float_rn(v)); break;
+    case TADMA_F16: reinterpret_cast<__half*>(p)[off] = d2h(v); break;
+    case TADMA_BF16: reinterpret_cast<__nv_bfloat16*>(p)[off] = d2bf(v); break;
     case TADMA_F64: reinterpret_cast<double*>(p)[off] = v; break;
     case TADMA_I64: reinterpret_cast<long long*>(p)[off] = f2i(v); break;
     case TADMA_I32: reinterpret_cast<int32_t*>(p)[off] = (int32_t)f2i(v); break;
@@ -129,8 +135,8 @@ __device__ __forceinline__ void store_from(char* p, int dt, int64_t off, double 
 __device__ __forceinline__ void store_from(char* p, int dt, int64_t off, int64_t v) {
     switch (dt) {
     case TADMA_F32: reinterpret_cast<float*>(p)[off] = __ll2float_rn(v); break;
-    case TADMA_F16: reinterpret_cast<__half*>(p)[off] = __float2half_rn(__ll2float_rn(v)); break;
-    case TADMA_BF16: reinterpret_cast<__nv_bfloat16*>(p)[off] = __float2bfloat16_rn(__ll2float_rn(v)); break;
+    case TADMA_F16: reinterpret_cast<__half*>(p)[off] = __ll2half_rn(v); break;
+    case TADMA_BF16: reinterpret_cast<__nv_bfloat16*>(p)[off] = __ll2bfloat16_rn(v); break;
     case TADMA_F64: reinterpret_cast<double*>(p)[off] = __ll2double_rn(v); break;
     case TADMA_I64: reinterpret_cast<long long*>(p)[off] = v; break;
     case TADMA_I32: reinterpret_cast<int32_t*>(p)[off] = (int32_t)v; break;
@@ -158,8 +164,8 @@ __device__ __forceinline__ float round_to(float v, int dt) {
 __device__ __forceinline__ double round_to(double v, int dt) {
     switch (dt) {
     case TADMA_F32: return (double)__double2float_rn(v);
-    case TADMA_F16: return (double)__half2float(__float2half_rn(__double2float_rn(v)));
-    case TADMA_BF16: return (double)__bfloat162float(__float2bfloat16_rn(__double2float_rn(v)));
+    case TADMA_F16: return (double)__half2float(d2h(v));
+    case TADMA_BF16: return (double)__bfloat162float(d2bf(v));
     case TADMA_F64: return v;
     case TADMA_I64: return __ll2double_rn(f2i(v));
     case TADMA_I32: return (double)(int32_t)f2i(v);
@@ -177,8 +183,8 @@ __device__ __forceinline__ int64_t round_to(int64_t v, int dt) {
     case TADMA_BOOL: return v != 0;
     case TADMA_I8: return (int8_t)v;
     case TADMA_F32: return f2i(__ll2float_rn(v));
-    case TADMA_F16: return f2i(__half2float(__float2half_rn(__ll2float_rn(v))));
-    case TADMA_BF16: return f2i(__bfloat162float(__float2bfloat16_rn(__ll2float_rn(v))));
+    case TADMA_F16: return f2i(__half2float(__ll2half_rn(v)));
+    case TADMA_BF16: return f2i(__bfloat162float(__ll2bfloat16_rn(v)));
     case TADMA_F64: return f2i(__ll2double_rn(v));
     }
     return v;

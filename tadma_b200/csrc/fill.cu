@@ -4,11 +4,20 @@
 // (seed, stream_id, g): the splitmix64 finaliser of a Weyl sequence keyed by
 // (seed, stream_id).  Any shard therefore generates bit-identically on any
 // GPU count, and the host oracle regenerates any element.  Floating values
-// are built in double with explicitly rounded operations (no contraction),
-// then rounded to fp32 and, for 16-bit types, from fp32 to the target.
+// are built in double with explicitly rounded operations (no contraction)
+// and rounded once to the element type.
 //   UNIFORM: p0 + (p1 - p0) * (k * 2^-24),        k = top 24 bits of draw 0
-//   NORMAL : p0 + p1 * (sqrt(3)/2 * sum_{j<4} (k_j * 2^-23 - 1))
-//            (Irwin-Hall(4) of U(-1,1), rescaled to unit variance)
+//   NORMAL : p0 + p1 * z, z = sqrt(-2 ln u1) cos(2 pi t)  (Box-Muller, Box &
+//            Muller 1958), u1 = (a + 1) 2^-53, t = b 2^-53 with a, b the top
+//            53 bits of draws 0 and 1.  ln and cos are evaluated here from
+//            their series with IEEE-rounded + - * / and sqrt only:
+//              ln u = e ln2 + s * sum_j 2/(2j+1) s^2j, u = m 2^e,
+//                     m in [sqrt(1/2), sqrt 2], s = (m - 1)/(m + 1);
+//              cos 2 pi t folded to t in [0, 1/8] (cos(2pi(1-t)),
+//                     -cos(2pi(1/2-t)), sin(2pi(1/4-t)); exact folds), then
+//                     the Taylor series of cos or sin at x = 2 pi t.
+//            No device math-library call is involved, so the host oracle
+//            reproduces every value bit for bit; |z| reaches 8.6 (u1 = 2^-53).
 //   INDEX  : floor(draw0 * n / 2^64)  (multiply-shift, bias < n / 2^64)
 // The reference's randn (Operations.hpp:290-297) is host-only and seeded
 // from std::random_device, so it cannot reproduce runs.
@@ -19,6 +28,8 @@ namespace tadma_b200 {
 namespace {
 
 constexpr int THREADS = 256;
+constexpr int LN_TERMS = 12;
+constexpr int TRIG_TERMS = 9;
 
 __host__ __device__ __forceinline__ uint64_t mix64(uint64_t z) {
     z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ULL;
@@ -28,6 +39,63 @@ __host__ __device__ __forceinline__ uint64_t mix64(uint64_t z) {
 
 __device__ __forceinline__ uint64_t draw(uint64_t key, uint64_t g, uint64_t j) {
     return mix64(key + (4 * g + j + 1) * 0x9E3779B97F4A7C15ULL);
+}
+
+struct GenCoefs {
+    double ln[LN_TERMS];   // 2 / (2j + 1)
+    double cs[TRIG_TERMS]; // (-1)^k / (2k)!
+    double sn[TRIG_TERMS]; // (-1)^k / (2k + 1)!
+};
+
+// Built on the host by exact-integer divisions (IEEE-rounded, the same on
+// every machine).
+GenCoefs make_coefs() {
+    GenCoefs c{};
+    for (int j = 0; j < LN_TERMS; j++) c.ln[j] = 2.0 / (double)(2 * j + 1);
+    c.cs[0] = 1.0;
+    c.sn[0] = 1.0;
+    for (int k = 1; k < TRIG_TERMS; k++) {
+        c.cs[k] = -c.cs[k - 1] / (double)((2 * k - 1) * (2 * k));
+        c.sn[k] = -c.sn[k - 1] / (double)((2 * k) * (2 * k + 1));
+    }
+    return c;
+}
+
+__device__ __forceinline__ double gen_ln(const GenCoefs& c, double u) {  // u in (0, 1]
+    const uint64_t bits = (uint64_t)__double_as_longlong(u);
+    int e = (int)((bits >> 52) & 0x7ffu) - 1023;
+    double m = __longlong_as_double((long long)((bits & 0xfffffffffffffULL) | 0x3ff0000000000000ULL));
+    if (m > 0x1.6a09e667f3bcdp+0) {  // sqrt 2
+        m = __dmul_rn(m, 0.5);
+        e = e + 1;
+    }
+    const double s = __ddiv_rn(__dsub_rn(m, 1.0), __dadd_rn(m, 1.0));
+    const double w = __dmul_rn(s, s);
+    double p = c.ln[LN_TERMS - 1];
+#pragma unroll
+    for (int j = LN_TERMS - 2; j >= 0; j--) p = __dadd_rn(c.ln[j], __dmul_rn(w, p));
+    return __dadd_rn(__dmul_rn((double)e, 0x1.62e42fefa39efp-1), __dmul_rn(s, p));  // ln 2
+}
+
+__device__ __forceinline__ double gen_cos_turns(const GenCoefs& c, double t) {  // t in [0, 1)
+    bool neg = false, use_sin = false;
+    if (t > 0.5) t = __dsub_rn(1.0, t);
+    if (t > 0.25) {
+        t = __dsub_rn(0.5, t);
+        neg = true;
+    }
+    if (t > 0.125) {
+        t = __dsub_rn(0.25, t);
+        use_sin = true;
+    }
+    const double x = __dmul_rn(t, 0x1.921fb54442d18p+2);  // 2 pi
+    const double y = __dmul_rn(x, x);
+    const double* k = use_sin ? c.sn : c.cs;
+    double p = k[TRIG_TERMS - 1];
+#pragma unroll
+    for (int j = TRIG_TERMS - 2; j >= 0; j--) p = __dadd_rn(k[j], __dmul_rn(y, p));
+    if (use_sin) p = __dmul_rn(x, p);
+    return neg ? -p : p;
 }
 
 struct FillParams {
@@ -40,6 +108,7 @@ struct FillParams {
     int32_t rank, contiguous;
     DivMod dm[TADMA_MAX_RANK];
     int64_t strides[TADMA_MAX_RANK];
+    GenCoefs coefs;
 };
 
 __global__ void __launch_bounds__(THREADS) fill_kernel(const __grid_constant__ FillParams p) {
@@ -66,11 +135,10 @@ __global__ void __launch_bounds__(THREADS) fill_kernel(const __grid_constant__ F
             const double u = __dmul_rn(__ull2double_rn(draw(p.key, g, 0) >> 40), 0x1p-24);
             store_from(p.out, p.dtype, off, __dadd_rn(p.p0, __dmul_rn(p.span, u)));
         } else {
-            double s = 0.0;
-#pragma unroll
-            for (int j = 0; j < 4; j++)
-                s = __dadd_rn(s, __dsub_rn(__dmul_rn(__ull2double_rn(draw(p.key, g, (uint64_t)j) >> 40), 0x1p-23), 1.0));
-            const double z = __dmul_rn(s, 0.8660254037844386);
+            const double u1 = __dmul_rn(__ull2double_rn((draw(p.key, g, 0) >> 11) + 1), 0x1p-53);  // (0, 1]
+            const double t = __dmul_rn(__ull2double_rn(draw(p.key, g, 1) >> 11), 0x1p-53);        // [0, 1)
+            const double r = __dsqrt_rn(__dmul_rn(-2.0, gen_ln(p.coefs, u1)));
+            const double z = __dmul_rn(r, gen_cos_turns(p.coefs, t));
             store_from(p.out, p.dtype, off, __dadd_rn(p.p0, __dmul_rn(p.p1, z)));
         }
     }
@@ -104,6 +172,7 @@ extern "C" int tadma_b200_fill(const tadma_tensor* out, int32_t dist, double p0,
     p.n_ids = dist == TADMA_DIST_INDEX ? (uint64_t)p1 : 0;
     p.offset = offset;
     p.n = n;
+    p.coefs = make_coefs();
     p.rank = out->rank > 0 ? out->rank : 1;
     // contiguous row-major?
     int64_t expect = 1;

@@ -39,14 +39,66 @@ def f32(x):
     return struct.unpack("<f", struct.pack("<f", x))[0]
 
 
+LN_COEF = [2.0 / (2 * j + 1) for j in range(12)]
+
+
+def _alt_coefs(div):
+    c = [1.0]
+    for k in range(1, 9):
+        c.append(-c[-1] / float(div(k)))
+    return c
+
+
+COS_COEF = _alt_coefs(lambda k: (2 * k - 1) * (2 * k))
+SIN_COEF = _alt_coefs(lambda k: (2 * k) * (2 * k + 1))
+SQRT2 = float.fromhex("0x1.6a09e667f3bcdp+0")
+LN2 = float.fromhex("0x1.62e42fefa39efp-1")
+TWO_PI = float.fromhex("0x1.921fb54442d18p+2")
+
+
+def ln_series(u):
+    """ln u for u in (0, 1]: u = m 2^e, ln u = e ln2 + 2 atanh((m-1)/(m+1))."""
+    m, e = math.frexp(u)  # u = m 2^e, m in [0.5, 1)
+    m, e = m * 2.0, e - 1
+    if m > SQRT2:
+        m, e = m * 0.5, e + 1
+    s = (m - 1.0) / (m + 1.0)
+    w = s * s
+    p = LN_COEF[-1]
+    for c in reversed(LN_COEF[:-1]):
+        p = c + w * p
+    return float(e) * LN2 + s * p
+
+
+def cos_turns(t):
+    """cos(2 pi t), t in [0, 1), folded to [0, 1/8] then a Taylor series."""
+    neg = use_sin = False
+    if t > 0.5:
+        t = 1.0 - t
+    if t > 0.25:
+        t, neg = 0.5 - t, True
+    if t > 0.125:
+        t, use_sin = 0.25 - t, True
+    x = t * TWO_PI
+    y = x * x
+    k = SIN_COEF if use_sin else COS_COEF
+    p = k[-1]
+    for c in reversed(k[:-1]):
+        p = c + y * p
+    if use_sin:
+        p = x * p
+    return -p if neg else p
+
+
 def gen_normal_f32(seed, sid, n, p0=0.0, p1=1.0):
+    """Box-Muller from two 53-bit uniforms per element, ln and cos from their
+    series (the generator's definition, each operation an IEEE double op)."""
     k = key(seed, sid)
     out = []
     for g in range(n):
-        s = 0.0
-        for j in range(4):
-            s += float(draw(k, g, j) >> 40) * 2.0 ** -23 - 1.0
-        z = s * 0.8660254037844386
+        u1 = float((draw(k, g, 0) >> 11) + 1) * 2.0 ** -53
+        t = float(draw(k, g, 1) >> 11) * 2.0 ** -53
+        z = math.sqrt(-2.0 * ln_series(u1)) * cos_turns(t)
         out.append(f32(p0 + p1 * z))
     return out
 

@@ -160,3 +160,17 @@ def test_config4_full_size_sampled():
     assert ulp_diff(ys, ref, DType.F16).max() <= 1
     row_sums = sy.view(-1, 2048).float().sum(dim=1)
     assert float((row_sums - 1).abs().max()) < 2e-2
+    # The reference's softmax (exp, then divide by the sum; Operations.hpp:190-193)
+    # overflows fp16 exp for x > 11.09.  N(0, 3) over 2^31 elements puts about
+    # 2.3e5 values there (z > 3.70); every output stays finite here, and those
+    # rows match the oracle like the others.
+    hot = (s.view(-1, 2048) > 11.09).any(dim=1)
+    n_hot = int(hot.sum())
+    assert n_hot > 100_000, n_hot
+    assert float(s.float().max()) > 15.0
+    assert bool(torch.isfinite(sy).all())
+    rows = torch.nonzero(hot).flatten()[:: max(1, n_hot // 128)][:128]
+    xs, ys = from_dev(s.view(-1, 2048)[rows]), from_dev(sy.view(-1, 2048)[rows])
+    ref = np.zeros_like(xs)
+    O.softmax(xs, -1, ref)
+    assert ulp_diff(ys, ref, DType.F16).max() <= 1

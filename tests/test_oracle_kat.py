@@ -2,8 +2,11 @@
 (pure-Python values, tests/golden/make_kats.py) and against numpy where numpy
 implements the same IEEE operation.  Parity with the reference itself is
 unpinned: it cannot be built here and ships no expected outputs."""
+import ctypes
 import json
+import math
 import os
+import sys
 
 import numpy as np
 import pytest
@@ -12,6 +15,9 @@ from oracle import oracle as O
 from tadma_b200.abi import SRC_IMM, Compute, Dist, DType, LNMode, Op, Reduce, bf16_bits_to_f32, f32_to_bf16_bits, instr
 
 KATS = json.load(open(os.path.join(os.path.dirname(__file__), "golden", "kats.json")))
+sys.path.insert(0, os.path.join(os.path.dirname(__file__), "golden"))
+from make_kats import draw as KATS_DRAW  # noqa: E402  (pure-Python generator definition)
+from make_kats import key as KATS_KEY  # noqa: E402
 
 
 def unary_f64(op, xs):
@@ -49,15 +55,100 @@ def test_generator_golden_values():
     assert list(a) == KATS["gen_index_seed0_sid2_v50257"]
 
 
-def test_generator_statistics_and_sharding():
-    a = O.fill((512, 1024), DType.F32, Dist.NORMAL, 0.0, 1.0, 0, 1)
-    assert abs(a.mean()) < 5e-3 and abs(a.std() - 1) < 5e-3 and np.abs(a).max() <= 2 * np.sqrt(3) + 1e-6
+def _normal_cdf(x):
+    return 0.5 * (1.0 + np.vectorize(math.erf)(x / math.sqrt(2.0)))
+
+
+def test_generator_is_normal_and_shards():
+    """NORMAL is a true N(p0, p1): moments, tail mass beyond 3 and 4 sigma, and
+    the Kolmogorov-Smirnov distance against the normal CDF; an offset shard
+    equals the rows it covers; fp16 / bf16 are the double value rounded once."""
+    n = 1 << 20
+    z = O.fill((n,), DType.F64, Dist.NORMAL, 0.0, 1.0, 0, 1)
+    assert abs(z.mean()) < 5e-3 and abs(z.std() - 1) < 5e-3
+    for k, p in ((3.0, 2.6998e-3), (4.0, 6.334e-5)):
+        count, want = int((np.abs(z) > k).sum()), p * n
+        assert abs(count - want) < 6 * math.sqrt(want), (k, count, want)
+    zs = np.sort(z[:1 << 18])
+    ecdf = np.arange(1, zs.size + 1) / zs.size
+    assert np.abs(ecdf - _normal_cdf(zs)).max() < 1.63 / math.sqrt(zs.size) * 1.5
+    assert np.abs(z).max() < 8.6  # u1 >= 2^-53 bounds |z| by sqrt(106 ln 2)
+    a = O.fill((512, 1024), DType.F64, Dist.NORMAL, 0.0, 1.0, 0, 1)
+    b = O.fill((256, 1024), DType.F64, Dist.NORMAL, 0.0, 1.0, 0, 1, offset=256 * 1024)
+    assert np.array_equal(b, a[256:])
+    with np.errstate(over="ignore"):
+        h = O.fill((512, 1024), DType.F16, Dist.NORMAL, 0.0, 3.0, 0, 1)
+        d = O.fill((512, 1024), DType.F64, Dist.NORMAL, 0.0, 3.0, 0, 1)
+        assert np.array_equal(h, d.astype(np.float16))  # numpy rounds float64 -> float16 once
+        f = O.fill((512, 1024), DType.F32, Dist.NORMAL, 0.0, 3.0, 0, 1)
+        assert np.array_equal(f, d.astype(np.float32))
+    bf = O.fill((4096,), DType.BF16, Dist.NORMAL, 0.0, 3.0, 0, 1)
+    d = O.fill((4096,), DType.F64, Dist.NORMAL, 0.0, 3.0, 0, 1)
+    assert [int(v) for v in bf] == [_bf16_exact(float(v)) for v in d]
     u = O.fill((512, 1024), DType.F32, Dist.UNIFORM, -1.0, 1.0, 0, 2)
     assert u.min() >= -1 and u.max() < 1 and abs(u.var() - 1 / 3) < 5e-3
-    b = O.fill((256, 1024), DType.F32, Dist.NORMAL, 0.0, 1.0, 0, 1, offset=256 * 1024)
-    assert np.array_equal(b, a[256:])
-    h = O.fill((512, 1024), DType.F16, Dist.NORMAL, 0.0, 1.0, 0, 1)
-    assert np.array_equal(h, a.astype(np.float16))  # fp16 = RNE of the fp32 value
+
+
+def test_generator_matches_libm_box_muller():
+    """The series ln / cos of the generator agree with libm's to ~1e-13."""
+    k = KATS_KEY(0, 1)
+    got = O.fill((4096,), DType.F64, Dist.NORMAL, 0.0, 1.0, 0, 1)
+    for g in range(4096):
+        u1 = float((KATS_DRAW(k, g, 0) >> 11) + 1) * 2.0 ** -53
+        t = float(KATS_DRAW(k, g, 1) >> 11) * 2.0 ** -53
+        want = math.sqrt(-2.0 * math.log(u1)) * math.cos(2.0 * math.pi * t)
+        assert abs(got[g] - want) <= 1e-12 * max(1.0, abs(want))
+
+
+def _bf16_exact(v):
+    """Round a double to bf16 bits with exact rational arithmetic (ties to even)."""
+    from fractions import Fraction
+    if v != v:
+        return None
+    sign = 0x8000 if math.copysign(1.0, v) < 0 else 0
+    a = Fraction(abs(v))
+    if a == 0:
+        return sign
+    top = Fraction(2) ** 127 * (2 - Fraction(1, 256))
+    if a >= top:
+        return sign | 0x7F80
+    E = max(math.floor(math.log2(abs(v))), -126)
+    while Fraction(2) ** E > a and E > -126:
+        E -= 1
+    while Fraction(2) ** (E + 1) <= a:
+        E += 1
+    scaled = a / Fraction(2) ** (E - 7)
+    m = math.floor(scaled)
+    rem = scaled - m
+    if rem > Fraction(1, 2) or (rem == Fraction(1, 2) and m % 2 == 1):
+        m += 1
+    return sign | (((E + 127) << 7) + m - 128)
+
+
+def test_double_to_16bit_rounds_once():
+    """or_f64_to_f16 equals numpy's float64 -> float16 cast; or_f64_to_bf16 the
+    exact rounding, on values whose fp32 detour would round twice."""
+    rng = np.random.default_rng(3)
+    L = O.lib()
+    L.or_f64_to_f16.argtypes = [ctypes.c_double]
+    L.or_f64_to_f16.restype = ctypes.c_uint16
+    L.or_f64_to_bf16.argtypes = [ctypes.c_double]
+    L.or_f64_to_bf16.restype = ctypes.c_uint16
+    # halfway points of fp16 / bf16 nudged by one double ulp (the fp32 detour rounds them to the tie)
+    h = rng.standard_normal(4000).astype(np.float16).astype(np.float64)
+    ulp16 = np.spacing(h.astype(np.float16)).astype(np.float64)
+    ties = h + ulp16 / 2
+    x = np.concatenate([rng.standard_normal(4000) * 3e4, np.nextafter(ties, np.inf), np.nextafter(ties, -np.inf),
+                        [65504.0, 65519.99999, 65520.0, 6e-8, 2.9802322387695312e-08, 2.98e-8, -0.0, 1e-300, np.inf,
+                         -np.inf]])
+    with np.errstate(over="ignore"):
+        want = x.astype(np.float16).view(np.uint16)
+    got = np.array([L.or_f64_to_f16(float(v)) for v in x], np.uint16)
+    assert np.array_equal(got, want)
+    bx = np.concatenate([rng.standard_normal(3000) * 1e3, [3.0e38, 3.4e38, 1e-39, 9.2e-41, -0.0, 1.0 + 2.0 ** -8 + 2.0 ** -40,
+                                                         1.0 + 2.0 ** -8 - 2.0 ** -40, 1.0 + 2.0 ** -8]])
+    got = [int(L.or_f64_to_bf16(float(v))) for v in bx]
+    assert got == [_bf16_exact(float(v)) for v in bx]
 
 
 def test_conversions_match_numpy():

@@ -13,7 +13,7 @@ CSRC = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
 
 def _sources():
     for f in sorted(os.listdir(CSRC)):
-        if f.endswith(".cu"):
+        if f.endswith((".cu", ".cuh")):
             with open(os.path.join(CSRC, f)) as fh:
                 yield f, fh.read()
 
