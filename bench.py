@@ -1,22 +1,30 @@
 #!/usr/bin/env python3
 """Benchmark of the tadma_b200 hot path (achieved HBM GB/s), one JSON line.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2|3|4|5] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 1-5] [--impl ours|reference]
     python bench.py --views      # view copies / element-wise calls vs torch, one line per case
 
 Metric: achieved HBM GB/s = algorithmic bytes (every input
 read once, every output written once; gathered rows counted per use) / time.
-Default workload: config 2, y = gelu(x * 0.5 +
-bias), x[8192, 8192] bf16, bias[8192] bf16 -> y bf16, one fused kernel.
-Configs 3-5 are selectable for their own lines.
+Headline (`value`): config 2, y = gelu(x * 0.5 +
+bias), x[8192, 8192] bf16, bias[8192] bf16 -> y bf16, one fused kernel.  The
+other configs (1, 3, 4, 5) are timed after it in the same process and
+reported under "configs", each with its own roofline parts, restated
+reference kernels and CPU baseline.
 
-Multi-GPU (torchrun, one process per GPU): every rank processes its own
-batch of the config's shape (a shard of an N-times larger global batch,
-generated at its global offset), no collective on the data path -> weak
-scaling.  Timing: W warm-up steps, then K steps back to back between two CUDA
-events on the launching stream, barrier + synchronize on both sides, the max
-over ranks reported.  No L2 flush: every step's inputs are larger than L2 and
-were not touched by the previous step (config 2 rotates 4 input/output sets).
+Multi-GPU (torchrun, one process per GPU): every config's GLOBAL workload is
+split on its leading axis (config 2: 8192 / N rows per rank; config 3: 32 / N
+batches; config 4: 64 / N LayerNorm and 32 / N softmax batches; config 5:
+2048 / N id rows), each shard generated at its global element offset, so the
+N ranks together do exactly the 1-GPU job (strong scaling); config 1 runs as
+N replicas.  No collective on the data path; the one exchange of the path, a
+sum over the sharded axis, is measured separately ("cross_shard_reduce":
+config 3's X summed over axis 0, a local reduction per rank plus one NCCL
+all-reduce, checked at sampled positions).  Timing: W warm-up steps, then K
+steps back to back between two CUDA events on the launching stream, barrier +
+synchronize on both sides, the max over ranks reported.  No L2 flush: every
+step's inputs are larger than L2 or rotate through sets whose total is
+(config 2 keeps at least 252 MB, twice the L2, of x/y sets in rotation).
 
 --impl reference times the reference's algorithm on the host cores: the
 reference itself cannot be built here (it needs clang >= 19 / C++23), so this
@@ -37,7 +45,10 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 GB = 1e9
-NBUF = 4  # rotating input/output sets of the config-2 workload
+L2_BYTES = 126 << 20
+# Steps timed per extra config (the headline takes --steps): enough for a
+# timed region of tens of milliseconds each at 1 GPU.
+EXTRA_STEPS = {1: 200, 2: 200, 3: 20, 4: 20, 5: 6}
 
 
 def parse():
@@ -49,11 +60,15 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="budget of the CPU-baseline sample")
     ap.add_argument("--e2e-steps", type=int, default=20)
+    ap.add_argument("--no-extras", action="store_true",
+                    help="time the headline config only (no other configs, no cross-shard reduce)")
     ap.add_argument("--no-ref-gpu", action="store_true",
                     help="skip timing the reference's GPU algorithm (baseline/refalgo) beside ours")
     ap.add_argument("--views", action="store_true",
                     help="instead of a config: one JSON line per view-copy / element-wise case of the generated-graph "
                          "calls (permutes, transposes, casts, concat, where), ours and torch, 1 GPU")
+    ap.add_argument("--chain-reduce", action="store_true",
+                    help="fused chain -> reduction calls (tadma_b200_reduce_chain) on X[32768, 4096], one line per case")
     ap.add_argument("--view-filter", default="",
                     help="with --views: run only the cases whose name contains this text")
     ap.add_argument("--batch", type=int, default=0,
@@ -133,6 +148,7 @@ class ClockSampler:
 
     def __enter__(self):
         if self.ok:
+            self._stop.clear()
             self.t = threading.Thread(target=self._run, daemon=True)
             self.t.start()
         return self
@@ -160,7 +176,9 @@ class Config1:
     composition (eltwise, then reduce with an exp pre-op) are timed beside it."""
     dtype = "f32"
 
-    def __init__(self, rank, batch=0):
+    scaling = "replicas"  # too small to split: every GPU runs the whole workload
+
+    def __init__(self, rank, world, batch=0):
         import torch
         import tadma_b200 as tb
         from tadma_b200.abi import Compute, Dist, DType, Op, Reduce, instr, make_tensor
@@ -168,7 +186,8 @@ class Config1:
         self.name = f"cfg1: y = sum_last(exp(A + b)), A[{R},128] fp32, b[128] fp32 -> [{R}] (one fused kernel, CUDA graph)"
         self.A = torch.empty((R, 128), dtype=torch.float32, device="cuda")
         self.b = torch.empty((128,), dtype=torch.float32, device="cuda")
-        tb.fill(self.A, Dist.NORMAL, 0.0, 1.0, 0, 1, offset=rank * R * 128)
+        tb.fill(self.A, Dist.NORMAL, 0.0, 1.0, 0, 1)
+        self.shard = "the whole workload (replica)"
         tb.fill(self.b, Dist.NORMAL, 0.0, 1.0, 0, 2)
         self.t = torch.empty_like(self.A)
         self.y = torch.empty((R,), dtype=torch.float32, device="cuda")
@@ -224,29 +243,40 @@ class Config1:
 
 
 class Config2:
-    """y = gelu(x * 0.5 + bias), x[8192, 8192] bf16, bias[8192] bf16, y bf16."""
-    ROWS, COLS = 8192, 8192
+    """y = gelu(x * 0.5 + bias), x[8192, 8192] bf16, bias[8192] bf16, y bf16;
+    a rank owns a contiguous block of x's rows."""
+    COLS = 8192
     dtype = "bf16"
+    scaling = "strong"
 
-    def __init__(self, rank, batch=0):
-        self.ROWS = batch or Config2.ROWS
-        self.name = f"cfg2: y = gelu(x*0.5 + bias), x[{self.ROWS},8192] bf16, bias[8192] bf16 -> bf16"
+    def __init__(self, rank, world, batch=0):
         import torch
         import tadma_b200 as tb
-        from tadma_b200.abi import Dist, DType, make_tensor
+        from tadma_b200.abi import Compute, Dist, DType, make_tensor
+        from tadma_b200.shard import shard_range
         self.tb = tb
-        R, C = self.ROWS, self.COLS
-        from tadma_b200.abi import Compute
+        self.GLOBAL_ROWS = batch or 8192
+        sh = shard_range(self.GLOBAL_ROWS, rank, world)
+        self.ROWS = R = sh.size
+        C = self.COLS
+        self.name = f"cfg2: y = gelu(x*0.5 + bias), x[{self.GLOBAL_ROWS},8192] bf16, bias[8192] bf16 -> bf16"
+        self.shard = f"rows {sh.start}:{sh.stop} of {self.GLOBAL_ROWS}"
         self.bias = torch.empty((C,), dtype=torch.bfloat16, device="cuda")
         tb.fill(self.bias, Dist.NORMAL, 0.0, 0.1, seed=0, stream_id=2)
         self.bview = make_tensor(self.bias.data_ptr(), DType.BF16, [R, C], [0, 1])
         self.prog = self.program()
-        # NBUF batches (consecutive shards of the global batch) rotate so that
-        # no step finds its input in L2: each x is 134 MB > the 126 MB L2.
+        # The rank's rows of x, plus copies at other addresses: the step rotates
+        # through them so that no step finds its input (or output) in L2; the
+        # sets in rotation hold at least twice the L2 size.
+        set_bytes = 2 * R * C * 2
+        self.nbuf = max(4, min(64, -(-2 * L2_BYTES // set_bytes)))
         self.xs, self.ys, self.calls = [], [], []
-        for k in range(NBUF):
+        for k in range(self.nbuf):
             x = torch.empty((R, C), dtype=torch.bfloat16, device="cuda")
-            tb.fill(x, Dist.NORMAL, 0.0, 1.0, seed=0, stream_id=1, offset=(rank * NBUF + k) * R * C)
+            if k == 0:
+                tb.fill(x, Dist.NORMAL, 0.0, 1.0, seed=0, stream_id=1, offset=sh.start * C)
+            else:
+                x.copy_(self.xs[0])
             y = torch.empty((R, C), dtype=torch.bfloat16, device="cuda")
             self.xs.append(x)
             self.ys.append(y)
@@ -255,6 +285,7 @@ class Config2:
         self.bytes = 2 * R * C * 2 + C * 2
         self.launches = 1
         self.units = R * C
+        self.l2_note = f"{self.nbuf} x/y sets of {set_bytes / 1e6:.0f} MB in rotation"
 
     @staticmethod
     def program():
@@ -263,7 +294,7 @@ class Config2:
                 instr(Op.GELU, round_dtype=DType.F32)]
 
     def step(self):
-        self.calls[self.i % NBUF]()
+        self.calls[self.i % self.nbuf]()
         self.i += 1
 
     def parts(self):
@@ -324,19 +355,6 @@ class Config2:
         bytes_ = done * (2 * rows * self.COLS * 2 + self.COLS * 2)
         return bytes_ / el / GB, L.or_num_threads(), f"{done} x {rows} rows of [8192, 8192] ({rows * self.COLS} elements per call)"
 
-    def reference_step(self, state):
-        from oracle import oracle as O
-        x, b, y, rows = state
-        O.lib().or_cfg2_gelu_affine_bf16(O.ptr(x), O.ptr(b), 0.5, O.ptr(y), rows, self.COLS)
-        return 2 * rows * self.COLS * 2 + self.COLS * 2
-
-    def reference_state(self):
-        import numpy as np
-        rows = 512
-        x = self.x[:rows].contiguous().view(torch_int16()).cpu().numpy().view(np.uint16)
-        b = self.bias.view(torch_int16()).cpu().numpy().view(np.uint16)
-        return (x, b, np.zeros_like(x), rows), f"512 rows of x[8192, 8192] per step"
-
 
 def torch_int16():
     import torch
@@ -347,15 +365,22 @@ class Config3:
     """sum / max / argmax over the last axis and mean over the middle axis of X[32, 4096, 4096] fp32."""
     dtype = "f32"
 
-    def __init__(self, rank, batch=0):
+    scaling = "strong"
+
+    def __init__(self, rank, world, batch=0):
         import torch
         import tadma_b200 as tb
         from tadma_b200.abi import Dist, Reduce
+        from tadma_b200.shard import shard_range
         self.tb = tb
-        B, R, C = batch or 32, 4096, 4096
-        self.name = f"cfg3: sum/max/argmax over axis -1 + mean over axis 1 of X[{B},4096,4096] fp32"
+        GB_, R, C = batch or 32, 4096, 4096
+        sh = shard_range(GB_, rank, world)
+        B = sh.size
+        self.name = f"cfg3: sum/max/argmax over axis -1 + mean over axis 1 of X[{GB_},4096,4096] fp32"
+        self.shard = f"batches {sh.start}:{sh.stop} of {GB_}"
+        self.global_batch, self.batch0 = GB_, sh.start
         self.x = torch.empty((B, R, C), dtype=torch.float32, device="cuda")
-        tb.fill(self.x, Dist.UNIFORM, -1.0, 1.0, seed=0, stream_id=1, offset=rank * B * R * C)
+        tb.fill(self.x, Dist.UNIFORM, -1.0, 1.0, seed=0, stream_id=1, offset=sh.start * R * C)
         self.s = torch.empty((B, R, 1), dtype=torch.float32, device="cuda")
         self.m = torch.empty((B, R, 1), dtype=torch.float32, device="cuda")
         self.a = torch.empty((B, R), dtype=torch.int64, device="cuda")
@@ -402,23 +427,29 @@ class Config4:
     """LayerNorm over the last axis of [64, 2048, 1024] fp16 + softmax over the last axis of [32, 16, 2048, 2048] fp16."""
     dtype = "f16"
 
-    def __init__(self, rank, batch=0):
+    scaling = "strong"
+
+    def __init__(self, rank, world, batch=0):
         import torch
         import tadma_b200 as tb
         from tadma_b200.abi import Dist, LNMode
+        from tadma_b200.shard import shard_range
         self.tb = tb
-        lb = batch or 64
-        sb = max(1, lb // 2)
-        self.name = f"cfg4: LayerNorm [{lb},2048,1024] fp16 + softmax [{sb},16,2048,2048] fp16 (last axis)"
+        glb = batch or 64
+        gsb = max(1, glb // 2)
+        ls, ss = shard_range(glb, rank, world), shard_range(gsb, rank, world)
+        lb, sb = ls.size, ss.size
+        self.name = f"cfg4: LayerNorm [{glb},2048,1024] fp16 + softmax [{gsb},16,2048,2048] fp16 (last axis)"
+        self.shard = f"LayerNorm batches {ls.start}:{ls.stop}, softmax batches {ss.start}:{ss.stop}"
         self.x = torch.empty((lb, 2048, 1024), dtype=torch.float16, device="cuda")
         self.g = torch.empty((1024,), dtype=torch.float16, device="cuda")
         self.b = torch.empty((1024,), dtype=torch.float16, device="cuda")
-        tb.fill(self.x, Dist.NORMAL, 0.0, 1.0, 0, 1, offset=rank * self.x.numel())
+        tb.fill(self.x, Dist.NORMAL, 0.0, 1.0, 0, 1, offset=ls.start * 2048 * 1024)
         tb.fill(self.g, Dist.NORMAL, 1.0, 0.02, 0, 2)
         tb.fill(self.b, Dist.NORMAL, 0.0, 0.02, 0, 3)
         self.y = torch.empty_like(self.x)
         self.s = torch.empty((sb, 16, 2048, 2048), dtype=torch.float16, device="cuda")
-        tb.fill(self.s, Dist.NORMAL, 0.0, 3.0, 0, 4, offset=rank * self.s.numel())
+        tb.fill(self.s, Dist.NORMAL, 0.0, 3.0, 0, 4, offset=ss.start * 16 * 2048 * 2048)
         self.sy = torch.empty_like(self.s)
         self.bytes = (2 * self.x.numel() * 2 + 2 * 1024 * 2) + 2 * self.s.numel() * 2
         self.launches = 2
@@ -458,19 +489,25 @@ class Config5:
     dtype = "f16/bf16"
     V, B, S, D = 50257, 2048, 4096, 4096
 
-    def __init__(self, rank, batch=0):
+    scaling = "strong"
+
+    def __init__(self, rank, world, batch=0):
         import torch
         import tadma_b200 as tb
         from tadma_b200.abi import Dist, DType, make_tensor
+        from tadma_b200.shard import shard_range
         self.tb = tb
-        self.B = batch or Config5.B
+        gb = batch or Config5.B
+        sh = shard_range(gb, rank, world)
+        self.B = sh.size
         V, B, S, D = self.V, self.B, self.S, self.D
-        self.name = f"cfg5: gather table[50257,4096] fp16 by ids[{B},4096] int64 + pos[4096,4096] bf16 -> bf16"
+        self.name = f"cfg5: gather table[50257,4096] fp16 by ids[{gb},4096] int64 + pos[4096,4096] bf16 -> bf16"
+        self.shard = f"id rows {sh.start}:{sh.stop} of {gb} (table and pos replicated)"
         self.table = torch.empty((V, D), dtype=torch.float16, device="cuda")
         self.ids = torch.empty((B, S), dtype=torch.int64, device="cuda")
         self.pos = torch.empty((S, D), dtype=torch.bfloat16, device="cuda")
         tb.fill(self.table, Dist.NORMAL, 0.0, 0.02, 0, 1)
-        tb.fill(self.ids, Dist.INDEX, 0, V, 0, 2, offset=rank * B * S)
+        tb.fill(self.ids, Dist.INDEX, 0, V, 0, 2, offset=sh.start * S)
         tb.fill(self.pos, Dist.NORMAL, 0.0, 0.02, 0, 3)
         self.out = torch.empty((B, S, D), dtype=torch.bfloat16, device="cuda")
         self.addv = make_tensor(self.pos.data_ptr(), DType.BF16, [B, S, D], [0, D, 1])
@@ -623,7 +660,7 @@ def reference_workload(cfg_id):
         return ("cfg1: y = sum_last(exp(A + b)), A[64,128] fp32, b[128] fp32 -> [64]", "the whole workload per step",
                 64 * 128 * 4 + 128 * 4 + 64 * 4, step)
     if cfg_id == 2:
-        rows, C = 512, Config2.COLS
+        rows, C = 1024, Config2.COLS
         x = O.fill((rows, C), DType.BF16, Dist.NORMAL, 0.0, 1.0, 0, 1)
         b = O.fill((C,), DType.BF16, Dist.NORMAL, 0.0, 0.1, 0, 2)
         y = np.zeros_like(x)
@@ -683,19 +720,29 @@ def run_reference(args, rank, world):
         print(json.dumps({"impl": "reference", "unavailable": f"no reference workload for config {args.config}"}))
         return
     name, sample, per, step = wl
-    for _ in range(args.warmup):
+    for _ in range(max(1, args.warmup)):
         step()
+    # Each timed step repeats the sample so that the K steps take >= 1.5 s
+    # (thread start-up and the first-touch of pages do not dominate), capped
+    # so the whole arm ends within a couple of minutes.
+    t0 = time.perf_counter()
+    step()
+    one = max(time.perf_counter() - t0, 1e-6)
+    reps = max(1, min(int(-(-1.5 // (one * args.steps))), int(120 // (one * args.steps)) or 1))
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        step()
+        for _ in range(reps):
+            step()
     el = time.perf_counter() - t0
-    v = per * args.steps / el / GB
+    v = per * reps * args.steps / el / GB
+    sample = f"{sample}, repeated {reps}x per step"
     cores = L.or_num_threads()
     print(json.dumps({
         "impl": "reference", "metric": "achieved HBM GB/s", "value": round(v, 3), "unit": "GB/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 4),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": CONFIGS[args.config].dtype,
-        "data": "synthetic", "config": {"workload": name, "sample": sample},
+        "higher_is_better": True, "scaling": CONFIGS[args.config].scaling, "vs_baseline": None,
+        "dtype": CONFIGS[args.config].dtype, "data": "synthetic", "config": {"workload": name, "sample": sample},
+        "region_s": round(el, 3),
         "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": cores, "kind": "port",
                          "sample": f"{sample}, {args.steps} steps"},
         "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -710,39 +757,41 @@ def run_views(args):
     """View copies and single element-wise calls of generated graph code
     (contiguous() after transpose<perm>, concat, casts, residual adds, where,
     comparisons, strided slices) through the public API, each with the torch
-    call that does the same.  Every call is prepared once and replayed 20x
-    from a CUDA graph (no Python in the timed region); GB/s = bytes of the
-    inputs read once + output written once, over the device time.  Inputs are
-    64-256 MB, some below L2 size: read these as per-launch kernel
-    throughput, not as cold-cache figures."""
+    call that does the same.  Every case builds as many independent
+    input/output sets as it takes to hold at least twice the L2 (252 MB), and
+    one pass over all sets is captured in a CUDA graph and replayed, so no
+    launch finds its operands in L2 from the launch before: GB/s = bytes of
+    the inputs read once + output written once, over the device time."""
     import torch
     import tadma_b200 as tb
     from tadma_b200.abi import Dist, Op, instr
 
-    rep, side = 20, torch.cuda.Stream()
+    side = torch.cuda.Stream()
 
-    def graph_time(fns, iters=10):
+    def graph_time(fns, launches):
         side.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(side):
             for f in fns:
                 f()
         side.synchronize()
+        passes = max(1, -(-20 // len(fns)))
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=side):
-            for _ in range(rep):
+            for _ in range(passes):
                 for f in fns:
                     f()
         for _ in range(max(3, args.warmup)):
             g.replay()
         torch.cuda.synchronize()
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        iters = 10
         s.record()
         for _ in range(iters):
             g.replay()
         e.record()
         torch.cuda.synchronize()
         del g
-        return s.elapsed_time(e) / iters / rep * 1e-3
+        return s.elapsed_time(e) / iters / (passes * launches) * 1e-3
 
     def rnd(shape, dt):
         t = torch.empty(shape, dtype=dt, device="cuda")
@@ -753,50 +802,137 @@ def run_views(args):
         return tb.prepare_eltwise(out, ins, prog, stream=side)
 
     f16, f32 = torch.float16, torch.float32
-    x = rnd((32, 512, 16, 64), f16)
-    y = torch.empty((32, 16, 512, 64), dtype=f16, device="cuda")
-    k = rnd((32, 16, 512, 64), f16)
-    kt = torch.empty((32, 16, 64, 512), dtype=f16, device="cuda")
-    qt = torch.empty((32, 16, 64, 512), dtype=f16, device="cuda")
-    a, a16 = rnd((8192, 8192), f32), rnd((8192, 8192), f16)
-    at, at16, h = torch.empty_like(a), torch.empty_like(a16), torch.empty_like(a16)
-    b16, s16 = rnd((8192, 8192), f16), torch.empty_like(a16)
-    c0, c1 = rnd((32, 512, 1024), f16), rnd((32, 512, 1024), f16)
-    cc = torch.empty((32, 1024, 1024), dtype=f16, device="cuda")
-    cond = torch.rand((8192, 8192), device="cuda") > 0.5
-    b2, w, gt = rnd((8192, 8192), f32), torch.empty_like(a), torch.empty_like(cond)
-    sl = torch.empty((4096, 8192), dtype=f32, device="cuda")
-    xp, kp, qp = x.permute(0, 2, 1, 3), k.permute(0, 1, 3, 2), x.permute(0, 2, 3, 1)
-    n = a.numel()
+
+    # Each case: (name, bytes per call, builder).  builder() allocates one
+    # independent set and returns (our calls, torch calls) on it.
+    def head_split():
+        x, y = rnd((32, 512, 16, 64), f16), torch.empty((32, 16, 512, 64), dtype=f16, device="cuda")
+        xp = x.permute(0, 2, 1, 3)
+        return [P(y, [xp], [instr(Op.COPY)])], [lambda: y.copy_(xp)]
+
+    def kt():
+        k, o = rnd((32, 16, 512, 64), f16), torch.empty((32, 16, 64, 512), dtype=f16, device="cuda")
+        kp = k.permute(0, 1, 3, 2)
+        return [P(o, [kp], [instr(Op.COPY)])], [lambda: o.copy_(kp)]
+
+    def perm0231():
+        x, o = rnd((32, 512, 16, 64), f16), torch.empty((32, 16, 64, 512), dtype=f16, device="cuda")
+        xp = x.permute(0, 2, 3, 1)
+        return [P(o, [xp], [instr(Op.COPY)])], [lambda: o.copy_(xp)]
+
+    def transpose(dt):
+        def build():
+            a, o = rnd((8192, 8192), dt), torch.empty((8192, 8192), dtype=dt, device="cuda")
+            return [P(o, [a.t()], [instr(Op.COPY)])], [lambda: o.copy_(a.t())]
+        return build
+
+    def cast():
+        a, h = rnd((8192, 8192), f32), torch.empty((8192, 8192), dtype=f16, device="cuda")
+        return [P(h, [a], [instr(Op.COPY)])], [lambda: h.copy_(a)]
+
+    def add16():
+        a, b, o = rnd((8192, 8192), f16), rnd((8192, 8192), f16), torch.empty((8192, 8192), dtype=f16, device="cuda")
+        return [P(o, [a, b], [instr(Op.ADD, b=1)])], [lambda: torch.add(a, b, out=o)]
+
+    def copy32():
+        a, o = rnd((8192, 8192), f32), torch.empty((8192, 8192), dtype=f32, device="cuda")
+        return [P(o, [a], [instr(Op.COPY)])], [lambda: o.copy_(a)]
+
+    def concat():
+        c0, c1 = rnd((32, 512, 1024), f16), rnd((32, 512, 1024), f16)
+        cc = torch.empty((32, 1024, 1024), dtype=f16, device="cuda")
+        return ([P(cc[:, :512], [c0], [instr(Op.COPY)]), P(cc[:, 512:], [c1], [instr(Op.COPY)])],
+                [lambda: torch.cat([c0, c1], 1, out=cc)])
+
+    def where():
+        cond = torch.rand((8192, 8192), device="cuda") > 0.5
+        a, b, w = rnd((8192, 8192), f32), rnd((8192, 8192), f32), torch.empty((8192, 8192), dtype=f32, device="cuda")
+        return [P(w, [cond, a, b], [instr(Op.WHERE, b=1, c=2)])], [lambda: torch.where(cond, a, b, out=w)]
+
+    def greater():
+        a, b = rnd((8192, 8192), f32), rnd((8192, 8192), f32)
+        gt = torch.empty((8192, 8192), dtype=torch.bool, device="cuda")
+        return [P(gt, [a, b], [instr(Op.GT, b=1)])], [lambda: torch.gt(a, b, out=gt)]
+
+    def slice2():
+        a, sl = rnd((8192, 8192), f32), torch.empty((4096, 8192), dtype=f32, device="cuda")
+        return [P(sl, [a[::2]], [instr(Op.COPY)])], [lambda: sl.copy_(a[::2])]
+
+    n = 8192 * 8192
+    hs = 32 * 512 * 16 * 64
     cases = [
-        ("head split: permute(0,2,1,3).contiguous() f16 [32,512,16,64]", 4 * x.numel(),
-         [P(y, [xp], [instr(Op.COPY)])], [lambda: y.copy_(xp)]),
-        ("K^T: permute(0,1,3,2).contiguous() f16 [32,16,512,64]", 4 * k.numel(),
-         [P(kt, [kp], [instr(Op.COPY)])], [lambda: kt.copy_(kp)]),
-        ("permute(0,2,3,1).contiguous() f16 [32,512,16,64]", 4 * x.numel(),
-         [P(qt, [qp], [instr(Op.COPY)])], [lambda: qt.copy_(qp)]),
-        ("transpose f32 [8192,8192]", 8 * n, [P(at, [a.t()], [instr(Op.COPY)])], [lambda: at.copy_(a.t())]),
-        ("transpose f16 [8192,8192]", 4 * n, [P(at16, [a16.t()], [instr(Op.COPY)])], [lambda: at16.copy_(a16.t())]),
-        ("cast f32 -> f16 [8192,8192]", 6 * n, [P(h, [a], [instr(Op.COPY)])], [lambda: h.copy_(a)]),
-        ("add f16 [8192,8192]", 6 * n, [P(s16, [a16, b16], [instr(Op.ADD, b=1)])],
-         [lambda: torch.add(a16, b16, out=s16)]),
-        ("copy f32 [8192,8192]", 8 * n, [P(at, [a], [instr(Op.COPY)])], [lambda: at.copy_(a)]),
-        ("concat axis 1 f16 2 x [32,512,1024]", 4 * cc.numel(),
-         [P(cc[:, :512], [c0], [instr(Op.COPY)]), P(cc[:, 512:], [c1], [instr(Op.COPY)])],
-         [lambda: torch.cat([c0, c1], 1, out=cc)]),
-        ("where(bool, f32, f32) [8192,8192]", 13 * n, [P(w, [cond, a, b2], [instr(Op.WHERE, b=1, c=2)])],
-         [lambda: torch.where(cond, a, b2, out=w)]),
-        ("greater f32 -> bool [8192,8192]", 9 * n, [P(gt, [a, b2], [instr(Op.GT, b=1)])],
-         [lambda: torch.gt(a, b2, out=gt)]),
-        ("slice [::2] f32 [8192,8192] -> [4096,8192]", 8 * sl.numel(), [P(sl, [a[::2]], [instr(Op.COPY)])],
-         [lambda: sl.copy_(a[::2])]),
+        ("head split: permute(0,2,1,3).contiguous() f16 [32,512,16,64]", 4 * hs, head_split),
+        ("K^T: permute(0,1,3,2).contiguous() f16 [32,16,512,64]", 4 * hs, kt),
+        ("permute(0,2,3,1).contiguous() f16 [32,512,16,64]", 4 * hs, perm0231),
+        ("transpose f32 [8192,8192]", 8 * n, transpose(f32)),
+        ("transpose f16 [8192,8192]", 4 * n, transpose(f16)),
+        ("cast f32 -> f16 [8192,8192]", 6 * n, cast),
+        ("add f16 [8192,8192]", 6 * n, add16),
+        ("copy f32 [8192,8192]", 8 * n, copy32),
+        ("concat axis 1 f16 2 x [32,512,1024]", 4 * 32 * 1024 * 1024, concat),
+        ("where(bool, f32, f32) [8192,8192]", 13 * n, where),
+        ("greater f32 -> bool [8192,8192]", 9 * n, greater),
+        ("slice [::2] f32 [8192,8192] -> [4096,8192]", 8 * n // 2, slice2),
     ]
-    for name, nbytes, ours, theirs in cases:
+    for name, nbytes, build in cases:
         if args.view_filter not in name:
             continue
-        t_ours, t_torch = graph_time(ours), graph_time(theirs)
+        nsets = max(1, -(-2 * L2_BYTES // nbytes))
+        sets = [build() for _ in range(nsets)]
+        ours = [f for o, _ in sets for f in o]
+        theirs = [f for _, t in sets for f in t]
+        per_call = len(sets[0][0])
+        t_ours = graph_time(ours, nsets) / 1.0
+        t_torch = graph_time(theirs, nsets)
         print(json.dumps({"case": name, "us": round(t_ours * 1e6, 2), "GBs": round(nbytes / t_ours / GB, 1),
-                          "torch_GBs": round(nbytes / t_torch / GB, 1), "unit": "GB/s"}), flush=True)
+                          "torch_GBs": round(nbytes / t_torch / GB, 1), "unit": "GB/s", "sets": nsets,
+                          "calls_per_set": per_call}), flush=True)
+        del sets, ours, theirs
+        torch.cuda.empty_cache()
+
+
+def run_chain_reduce(args):
+    """tadma_b200_reduce_chain on rows of X[32768, 4096] (512 MB fp32, larger
+    than L2): the row-operand forms that run on the reduction engine's row
+    kernel (row variance, softmax denominator) and chains that need the
+    general chain interpreter (a per-column operand, two binary steps).
+    GB/s = X read once + the per-row / per-column operand + the output, over
+    the average of 20 back-to-back launches."""
+    import torch
+    import tadma_b200 as tb
+    from tadma_b200.abi import SRC_IMM, Compute, Dist, DType, Op, Reduce, instr, make_tensor
+    R, C = 32768, 4096
+    peak, _ = measured_peak()
+    stream = torch.cuda.current_stream()
+    for dt, tdt in ((DType.F32, torch.float32), (DType.BF16, torch.bfloat16)):
+        x = torch.empty((R, C), dtype=tdt, device="cuda")
+        tb.fill(x, Dist.NORMAL, 0.0, 1.0, 0, 1)
+        m = torch.empty((R, 1), dtype=torch.float32, device="cuda")
+        tb.fill(m, Dist.NORMAL, 0.0, 0.1, 0, 2)
+        b = torch.empty((C,), dtype=torch.float32, device="cuda")
+        tb.fill(b, Dist.NORMAL, 0.0, 0.1, 0, 3)
+        mv = make_tensor(m.data_ptr(), DType.F32, [R, C], [1, 0])
+        bv = make_tensor(b.data_ptr(), DType.F32, [R, C], [0, 1])
+        out = torch.empty((R, 1), dtype=torch.float32, device="cuda")
+        xb = x.numel() * x.element_size()
+        cases = [
+            ("mean((x - m)^2), m per row", Reduce.MEAN, [x, mv], [instr(Op.SUB, b=1), instr(Op.POW, b=SRC_IMM, imm=2.0)],
+             xb + R * 4 + R * 4),
+            ("sum(exp(x - m)), m per row", Reduce.SUM, [x, mv], [instr(Op.SUB, b=1), instr(Op.EXP)], xb + R * 8),
+            ("sum(x * 0.5)", Reduce.SUM, [x], [instr(Op.MUL, b=SRC_IMM, imm=0.5)], xb + R * 4),
+            ("sum(exp(x + b)), b per column (general kernel)", Reduce.SUM, [x, bv], [instr(Op.ADD, b=1), instr(Op.EXP)],
+             xb + C * 4 + R * 4),
+            ("sum((x - m) * 1.5), m per row (general kernel)", Reduce.SUM, [x, mv],
+             [instr(Op.SUB, b=1), instr(Op.MUL, b=SRC_IMM, imm=1.5)], xb + R * 8),
+        ]
+        for name, op, ins, prog, nbytes in cases:
+            call = tb.prepare_reduce_chain(op, ins, prog, -1, out, Compute.F32)
+            sec = time_steps(call, 20, 3, stream)
+            print(json.dumps({"case": f"{name}, X[{R},{C}] {dt.name.lower()}", "us": round(sec * 1e6, 2),
+                              "GBs": round(nbytes / sec / GB, 1), "frac": round(nbytes / sec / GB / peak, 4),
+                              "unit": "GB/s"}), flush=True)
+        del x
+        torch.cuda.empty_cache()
 
 
 def main():
@@ -806,6 +942,9 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.views:
         run_views(args)
+        return
+    if args.chain_reduce:
+        run_chain_reduce(args)
         return
     if args.impl == "reference":
         run_reference(args, rank, world)
@@ -843,18 +982,18 @@ def time_parts(cfg, args, stream):
     return out
 
 
-def roofline(cfg, args, parts, peak, peak_kind, step_s):
+def roofline(cid, cfg, args, parts, peak, peak_kind, step_s):
     """Roofline of the dominant launch (the part with the largest time per
     step): achieved = its algorithmic bytes / its average launch duration."""
     rows = []
     for kernel, label, nbytes, sec in parts:
-        tr = NCU_TRAFFIC.get((args.config, label))
+        tr = NCU_TRAFFIC.get((cid, label))
         rows.append({"kernel": kernel, "part": label, "ms": round(sec * 1e3, 4),
                      "achieved": round(nbytes / sec / GB, 1), "frac": round(nbytes / sec / GB / peak, 4),
                      "algorithmic_bytes": nbytes, "traffic": tr["bytes"] if tr else None,
                      "share": round(sec / sum(p[3] for p in parts), 4)})
     top = max(rows, key=lambda r: r["ms"])
-    tr = NCU_TRAFFIC.get((args.config, top["part"]))
+    tr = NCU_TRAFFIC.get((cid, top["part"]))
     return {"bound": "hbm", "achieved": top["achieved"], "peak": peak, "unit": "GB/s", "frac": top["frac"],
             "traffic": top["traffic"], "kernel": top["kernel"], "part": top["part"],
             "algorithmic_bytes_per_launch": top["algorithmic_bytes"],
@@ -866,71 +1005,184 @@ def roofline(cfg, args, parts, peak, peak_kind, step_s):
             "parts": rows}
 
 
-def run(args, rank, world, local):
+def timed_region(cfg, steps, warmup, world, stream, sampler=None):
+    """W warm-up steps, then `steps` steps back to back between two CUDA events
+    on the launching stream, barrier + synchronize on both sides.  Returns
+    (max over ranks of the seconds per step, wall seconds of the region)."""
     import torch
     import torch.distributed as dist
-    cfg = CONFIGS[args.config](rank, args.batch)
-    stream = torch.cuda.current_stream()
-    for _ in range(max(args.warmup, 3)):
+    for _ in range(max(warmup, 3)):
         cfg.step()
     barrier(world)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    sampler = ClockSampler(local)
-    t_region = time.perf_counter()
-    with sampler:
+    t0 = time.perf_counter()
+    if sampler:
+        sampler.__enter__()
+    try:
         start.record(stream)
-        for _ in range(args.steps):
+        for _ in range(steps):
             cfg.step()
         end.record(stream)
         barrier(world)
-    region_s = time.perf_counter() - t_region
-    step_s = start.elapsed_time(end) / 1e3 / args.steps
-    t = torch.tensor([step_s], dtype=torch.float64, device="cuda")
+    finally:
+        if sampler:
+            sampler.__exit__(None, None, None)
+    region = time.perf_counter() - t0
+    t = torch.tensor([start.elapsed_time(end) / 1e3 / steps], dtype=torch.float64, device="cuda")
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    step_max = float(t.item())
-    value = cfg.bytes * world / step_max / GB
+    return float(t.item()), region
 
+
+def job_total(x, world):
+    """Sum over ranks of a per-rank quantity (bytes, elements)."""
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([float(x)], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def cross_shard_reduce(cfg3, world, rank, stream):
+    """The path's one exchange: X[32, 4096, 4096] of config 3, split by batch,
+    summed over axis 0 -- each rank reduces its slab (tadma_b200_reduce), then
+    one all-reduce of the [4096, 4096] fp32 partial (NCCL over NVLink at N > 1).
+    Timed with CUDA events (max over ranks) and checked on rank 0 at 64 sampled
+    positions against a float64 sum of the same elements, regenerated on the
+    device from the seeded generator at their global offsets."""
+    import torch
+    import tadma_b200 as tb
+    from tadma_b200.abi import Dist
+    from tadma_b200.shard import reduce_leading_axis_sharded
+    R = C = 4096
+    out = torch.empty((R, C), dtype=torch.float32, device="cuda")
+
+    def step():
+        reduce_leading_axis_sharded(cfg3.x, out.view(1, R, C))
+
+    class _Step:
+        pass
+    st = _Step()
+    st.step = step
+    n = 5
+    sec, _ = timed_region(st, n, 3, world, stream)
+    step()
+    torch.cuda.synchronize()
+    res = {"op": "sum over axis 0 of X[32,4096,4096] fp32, batch-sharded", "bytes_allreduced": R * C * 4,
+           "collective": "nccl all_reduce (sum)" if world > 1 else "none (one GPU holds every batch)",
+           "ms": round(sec * 1e3, 4), "steps": n}
+    if rank == 0:
+        g = torch.Generator().manual_seed(7)
+        pos = torch.randint(0, R * C, (64,), generator=g).tolist()
+        err = 0.0
+        col = torch.empty((1,), dtype=torch.float64, device="cuda")
+        for p in pos:
+            acc = 0.0
+            for b in range(cfg3.global_batch):
+                tb.fill(col, Dist.UNIFORM, -1.0, 1.0, seed=0, stream_id=1, offset=b * R * C + p)
+                acc += float(col.item())
+            err = max(err, abs(float(out.view(-1)[p].item()) - acc))
+        # fp32 partial sums of 32 values in (-1, 1): far below 1e-4.
+        res["check"] = {"positions": len(pos), "max_abs_err": err, "ok": err < 1e-4,
+                        "against": "float64 sum of the regenerated elements (seeded generator, global offsets)"}
+    return res
+
+
+def measure(cid, args, rank, world, stream, peak, peak_kind, steps, warmup, sampler=None, headline=False):
+    """One config: its timed region, per-launch parts (rank 0), the restated
+    reference kernels and the CPU baseline (N = 1, rank 0).  Returns (cfg,
+    result dict)."""
+    cfg = CONFIGS[cid](rank, world, args.batch)
+    step_s, region = timed_region(cfg, steps, warmup, world, stream, sampler)
+    total = job_total(cfg.bytes, world)
+    units = job_total(cfg.units, world)
+    value = total / step_s / GB
+    res = {"workload": cfg.name, "value": round(value, 3), "unit": "GB/s", "scaling": cfg.scaling,
+           "per_gpu": round(value / world, 3), "frac_per_gpu": round(value / world / peak, 4),
+           "ms_per_step": round(step_s * 1e3, 5), "steps": steps, "warmup": max(warmup, 3),
+           "elements_per_s": round(units / step_s, 1), "launches_per_step": cfg.launches,
+           "shard_rank0": cfg.shard if rank == 0 else None, "region_s": round(region, 4)}
+    if hasattr(cfg, "compulsory"):
+        res["compulsory_bytes_gbs"] = round(job_total(cfg.compulsory, world) / step_s / GB, 3)
+    if hasattr(cfg, "l2_note"):
+        res["l2"] = cfg.l2_note
+    refg = None
+    if world == 1 and not args.no_ref_gpu:
+        refg = ref_gpu(cfg, args, stream)
+    parts = time_parts(cfg, args, stream) if rank == 0 else None
+    barrier(world)
+    if rank == 0:
+        roof = roofline(cid, cfg, args, parts, peak, peak_kind, step_s)
+        res["roofline"] = roof
+        res["kernel"] = roof["kernel"]
+        res["reference_gpu_restated"] = refg
+        if world == 1 and args.cpu_seconds > 0:
+            budget = args.cpu_seconds if headline else min(args.cpu_seconds, 3.0)
+            v, cores, sample = cfg.cpu_sample(budget)
+            res["cpu_baseline"] = {"value": round(v, 3), "unit": "GB/s", "cores": cores, "kind": "port",
+                                   "sample": sample}
+    return cfg, res
+
+
+def run(args, rank, world, local):
+    import torch
+    stream = torch.cuda.current_stream()
+    peak, peak_kind = measured_peak()
+    sampler = ClockSampler(local)
+    cfg, head = measure(args.config, args, rank, world, stream, peak, peak_kind, args.steps, args.warmup,
+                        sampler=sampler, headline=True)
     e2e = None
     if hasattr(cfg, "e2e"):
         e2e_steps = max(1, min(args.e2e_steps, args.steps))
         e_s, h2d, d2h = cfg.e2e(e2e_steps, stream)
         te = torch.tensor([e_s], dtype=torch.float64, device="cuda")
         if world > 1:
+            import torch.distributed as dist
             dist.all_reduce(te, op=dist.ReduceOp.MAX)
-        e2e = {"value": round(cfg.bytes * world / float(te.item()) / GB, 3), "unit": "GB/s",
-               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(float(te.item()) * 1e3, 4),
-               "steps": e2e_steps}
-    refg = None
-    if world == 1 and not args.no_ref_gpu:
-        refg = ref_gpu(cfg, args, stream)
-    parts = time_parts(cfg, args, stream) if rank == 0 else None
-    barrier(world)
+        total = job_total(cfg.bytes, world)
+        e2e = {"value": round(total / float(te.item()) / GB, 3), "unit": "GB/s",
+               "h2d_bytes_per_step": int(job_total(h2d, world)), "d2h_bytes_per_step": int(job_total(d2h, world)),
+               "ms_per_step": round(float(te.item()) * 1e3, 4), "steps": e2e_steps,
+               "path": "public API from pinned host buffers (tadma_b200.pipeline.RowPipeline, 8 row chunks per rank)"}
+    launches = cfg.launches * args.steps
+    del cfg
+    torch.cuda.empty_cache()
+
+    extras, cross = {}, None
+    ids = [c for c in (1, 2, 3, 4, 5) if c != args.config] if not args.no_extras else []
+    clocks_all = ClockSampler(local)
+    for cid in ids:
+        c, r = measure(cid, args, rank, world, stream, peak, peak_kind, EXTRA_STEPS[cid], 3, sampler=clocks_all)
+        if cid == 3:
+            cross = cross_shard_reduce(c, world, rank, stream)
+        extras[f"cfg{cid}"] = r
+        del c
+        torch.cuda.empty_cache()
+        barrier(world)
     if rank != 0:
         return
-    peak, peak_kind = measured_peak()
-    roof = roofline(cfg, args, parts, peak, peak_kind, step_s)
-    cpu = None
-    if world == 1 and args.cpu_seconds > 0:
-        v, cores, sample = cfg.cpu_sample(args.cpu_seconds)
-        cpu = {"value": round(v, 3), "unit": "GB/s", "cores": cores, "kind": "port", "sample": sample}
     line = {
-        "metric": "achieved HBM GB/s", "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
-        "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": round(step_max * 1e3, 5),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": cfg.dtype,
-        "data": "synthetic (seeded counter-based generator, BASELINE.json distributions)",
-        "config": {"workload": cfg.name, "per_gpu_batch": "one full config batch per GPU (global batch = N x)",
-                   "l2": "inputs larger than L2: every step reads > 126 MB of input not touched by the previous "
-                         "step (config 2 rotates 4 x/y sets of 134 MB each); no flush; K steps timed back to back",
+        "metric": "achieved HBM GB/s", "value": head["value"], "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": head["ms_per_step"],
+        "higher_is_better": True, "scaling": head["scaling"], "vs_baseline": None, "dtype": CONFIGS[args.config].dtype,
+        "data": ("synthetic, BASELINE.json's distributions: N(mu, sigma) by Box-Muller and U(-1, 1) from a seeded "
+                 "counter-based generator (bit-identical on the host), ids U[0, 50257); seed 0"),
+        "config": {"workload": head["workload"], "global_batch": "the whole config (BASELINE.json sizes) split "
+                   "across the N GPUs on its leading axis" if world > 1 else "the whole config on one GPU",
+                   "shard_rank0": head["shard_rank0"],
+                   "l2": ("inputs larger than L2, no flush, K steps back to back: " + head.get("l2", "")).strip(),
                    "parallelism": f"dp{world} (leading-axis shards, no data-path collective)"},
-        "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "reference_gpu_restated": refg,
-        "gpu_launches": cfg.launches * args.steps,
+        "roofline": head["roofline"], "cpu_baseline": head.get("cpu_baseline"), "e2e": e2e,
+        "reference_gpu_restated": head.get("reference_gpu_restated"),
+        "gpu_launches": launches,
         "clocks": sampler.result(),
-        "elements_per_s": round(cfg.units * world / step_max, 1),
-        "region_s": round(region_s, 4),
+        "elements_per_s": head["elements_per_s"],
+        "region_s": head["region_s"],
+        "configs": extras,
+        "cross_shard_reduce": cross,
+        "clocks_all_configs": clocks_all.result() if extras else None,
     }
-    if hasattr(cfg, "compulsory"):
-        line["compulsory_bytes_gbs"] = round(cfg.compulsory * world / step_max / GB, 3)
     print(json.dumps(line))
 
 

@@ -169,6 +169,18 @@ struct Allocator<kCPU> {
     }
 };
 
+// A tensor with no memory: its value lives in a register of the thread that
+// computes it (ExecutionTape::Optimize; the reference's Allocator<kTrampoline>,
+// Allocator.hpp:39-44, and TrampolineStorage, Storage.hpp:131-148).
+template <>
+struct Allocator<kTrampoline> {
+    static constexpr Memory device = kTrampoline;
+    template <typename T, int64_t Count>
+    static HeapStorage<T> allocate() {
+        return HeapStorage<T>();
+    }
+};
+
 template <typename T>
 concept AnyAllocator = requires { T::device; };
 

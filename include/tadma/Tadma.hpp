@@ -5,7 +5,10 @@
 
 #include "Constexpr.hpp"
 #include "Core.hpp"
+#include "ExecutionTape.hpp"
 #include "Lazy.hpp"
+#include "Node.hpp"
+#include "NodeOps.hpp"
 #include "Operations.hpp"
 #include "Sequence.hpp"
 #include "Tensor.hpp"

@@ -136,6 +136,58 @@ consteval auto reversed_arr(const std::array<int64_t, Dims::Size>& src) {
     return out;
 }
 
+// ------------------------------------------------------ weight staging --
+
+namespace detail {
+
+// Pinned host slots through which weight files reach the device: slot k is
+// refilled only after its previous copy has completed (its event), so file
+// reads overlap the host-to-device copies of earlier slots.  One per thread,
+// created on the first CUDA weight load; released at thread exit.
+struct WeightStager {
+    static constexpr int kSlots = 4;
+    static constexpr int64_t kSlotBytes = 16 << 20;
+    char* slot[kSlots] = {};
+    cudaEvent_t done[kSlots] = {};
+    bool pending[kSlots] = {};
+    int next = 0;
+
+    void load(std::ifstream& file, char* dst, int64_t bytes, cudaStream_t s) {
+        if (!slot[0]) {
+            for (int k = 0; k < kSlots; k++) {
+                check_cuda(cudaMallocHost(reinterpret_cast<void**>(&slot[k]), kSlotBytes));
+                check_cuda(cudaEventCreateWithFlags(&done[k], cudaEventDisableTiming));
+            }
+        }
+        for (int64_t off = 0; off < bytes; off += kSlotBytes) {
+            const int64_t n = bytes - off < kSlotBytes ? bytes - off : kSlotBytes;
+            const int k = next;
+            next = (next + 1) % kSlots;
+            if (pending[k]) check_cuda(cudaEventSynchronize(done[k]));
+            pending[k] = false;
+            file.read(slot[k], n);
+            if (!file) throw std::runtime_error("tadma: weight file read failed");
+            check_cuda(cudaMemcpyAsync(dst + off, slot[k], (size_t)n, cudaMemcpyHostToDevice, s));
+            check_cuda(cudaEventRecord(done[k], s));
+            pending[k] = true;
+        }
+    }
+    ~WeightStager() {
+        for (int k = 0; k < kSlots; k++) {
+            if (pending[k]) cudaEventSynchronize(done[k]);
+            if (done[k]) cudaEventDestroy(done[k]);
+            if (slot[k]) cudaFreeHost(slot[k]);
+        }
+    }
+};
+
+inline WeightStager& weight_stager() {
+    static thread_local WeightStager stager;
+    return stager;
+}
+
+}  // namespace detail
+
 // -------------------------------------------------------------- Tensor --
 
 template <typename T, typename Allocator_, AnySequence Dims_, AnySequence StridesInit = Sequence<>>
@@ -191,23 +243,21 @@ struct Tensor {
     Tensor& operator=(const Tensor& o) = default;
 
     // Weight load: SizeBytes at `offset` of a flat little-endian file, the
-    // layout the ONNX-to-C++ generator writes (Tensor.hpp:86-99).
+    // layout the ONNX-to-C++ generator writes (raw tensors back to back,
+    // cppgen.py:111-116; the reference's loader, Tensor.hpp:86-99, allocates,
+    // copies and synchronises once per tensor).  A CUDA tensor streams through
+    // the calling thread's ring of pinned staging slots (detail::WeightStager):
+    // the file is read into one slot while earlier slots copy to the device,
+    // and nothing synchronises per tensor; ops on tadma::stream are ordered
+    // after the copies.
     Tensor(std::ifstream& file, uint64_t offset) : Tensor() {
         static_assert(NormalStrides, "weights load into a contiguous tensor");
         file.seekg((std::streamoff)offset);
         if constexpr (device == kCPU) {
             file.read(reinterpret_cast<char*>(data.view), SizeBytes);
+            if (!file) throw std::runtime_error("tadma: weight file read failed");
         } else {
-            void* staging = nullptr;
-            check_cuda(cudaMallocHost(&staging, SizeBytes > 0 ? SizeBytes : 1));
-            file.read(static_cast<char*>(staging), SizeBytes);
-            if (!file) {
-                cudaFreeHost(staging);
-                throw std::runtime_error("tadma: weight file read failed");
-            }
-            check_cuda(cudaMemcpyAsync(data.view, staging, SizeBytes, cudaMemcpyHostToDevice, stream));
-            check_cuda(cudaStreamSynchronize(stream));
-            cudaFreeHost(staging);
+            detail::weight_stager().load(file, reinterpret_cast<char*>(data.view), SizeBytes, stream);
         }
     }
 

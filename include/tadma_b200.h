@@ -223,12 +223,15 @@ int tadma_b200_reduce_chain(int32_t op, const tadma_tensor* ins, int32_t n_ins, 
  * pool has already claimed the device's HBM (so any further allocation
  * fails), a latency-critical path that must not enter the allocator, or a
  * host that only lends the library the buffers it passes in.
- * Same arguments, results and errors as tadma_b200_reduce.  Reductions that
- * split a long axis across CTAs keep their partial results in a 2 MiB static
- * device buffer inside the library (every GPU that loads the library holds it
- * until the process exits) instead of a per-call workspace; a reduction that
- * would need more than 2 MiB of partials returns TADMA_ERR_INVALID with a
- * message naming the size (tadma_b200_reduce handles it).
+ * Same arguments and errors as tadma_b200_reduce, results within the same
+ * tolerance.  Reductions that split a long axis across CTAs keep their
+ * partial results in a 2 MiB static device buffer inside the library (every
+ * GPU that loads the library holds it until the process exits) instead of a
+ * per-call workspace.  When the split that tadma_b200_reduce would choose
+ * needs more than 2 MiB of partials, this entry point splits the axis into
+ * fewer parts, so that they fit, or reduces it in one pass (no partials);
+ * every shape therefore runs, possibly slower than tadma_b200_reduce, and
+ * summed in a different order (a different rounding of the same sum).
  * - The first call on a device looks up the buffer's device address
  *   (cudaGetSymbolAddress) and caches it; make that first call outside any
  *   stream capture.

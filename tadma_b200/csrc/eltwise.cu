@@ -75,6 +75,51 @@ AffineMatch match_affine(const tadma_instr* prog, int n_instr, int n_ins) {
 
 bool is_transcendental(int op) { return op >= TADMA_OP_EXP && op <= TADMA_OP_GELU && op != TADMA_OP_RELU; }
 
+// A chain of the row-operand reduction's form: [op1 m]? [unary]? [pow 2]?
+// over ins[0], with m = ins[1] broadcast along the reduced axis (one value
+// per output row) or an immediate, and only no-op roundings (fp32 compute).
+struct RowOpMatch {
+    bool ok = false;
+    int op1 = TADMA_OP_COPY, pre = TADMA_OP_COPY, square = 0;
+    const tadma_tensor* rop = nullptr;
+    double imm1 = 0.0;
+};
+
+RowOpMatch match_rowop(const tadma_instr* prog, int n_instr, const tadma_tensor* ins, int n_ins, int ax) {
+    RowOpMatch m;
+    auto noop_round = [](int rd) { return rd < 0 || rd == TADMA_F32 || rd == TADMA_F64; };
+    auto binop = [](int op) {
+        return op == TADMA_OP_ADD || op == TADMA_OP_SUB || op == TADMA_OP_MUL || op == TADMA_OP_DIV ||
+               op == TADMA_OP_RSUB || op == TADMA_OP_RDIV || op == TADMA_OP_MAX || op == TADMA_OP_MIN;
+    };
+    int i = 0;
+    if (i < n_instr && binop(prog[i].op) && prog[i].c == TADMA_SRC_NONE && noop_round(prog[i].round_dtype)) {
+        if (prog[i].b == TADMA_SRC_IMM && n_ins == 1) {
+            m.op1 = prog[i].op;
+            m.imm1 = prog[i].imm;
+            i++;
+        } else if (prog[i].b == 1 && n_ins == 2 && (ins[1].dims[ax] == 1 || ins[1].strides[ax] == 0)) {
+            m.op1 = prog[i].op;
+            m.rop = &ins[1];
+            i++;
+        }
+    }
+    auto is_pow2 = [&](int k) {
+        return prog[k].op == TADMA_OP_POW && prog[k].b == TADMA_SRC_IMM && prog[k].imm == 2.0 && noop_round(prog[k].round_dtype);
+    };
+    if (i < n_instr && prog[i].op > TADMA_OP_COPY && prog[i].op < 32 && prog[i].op != TADMA_OP_NOT &&
+        noop_round(prog[i].round_dtype)) {
+        m.pre = prog[i].op;
+        i++;
+    }
+    if (i < n_instr && is_pow2(i)) {
+        m.square = 1;
+        i++;
+    }
+    m.ok = i == n_instr && (n_ins == 1 || m.rop != nullptr);
+    return m;
+}
+
 bool valid_op(int op) {
     return (op >= 0 && op <= TADMA_OP_NOT) || (op >= TADMA_OP_ADD && op <= TADMA_OP_LOR) || op == TADMA_OP_WHERE;
 }
@@ -426,6 +471,17 @@ extern "C" int tadma_b200_reduce_chain(int32_t op, const tadma_tensor* ins, int3
     if (R == 0 && op != TADMA_REDUCE_SUM && op != TADMA_REDUCE_SUMSQ)
         return fail(TADMA_ERR_INVALID, "empty reduction has no identity for this op");
     if (numel(out) == 0) return TADMA_OK;
+
+    if (cm == TADMA_COMPUTE_F32) {
+        // The row-operand form runs on the reduction engine's row kernel.
+        RowOpMatch rm = match_rowop(prog, n_instr, ins, n_ins, ax);
+        const bool op_sq = op == TADMA_REDUCE_SUMSQ || op == TADMA_REDUCE_RMS;
+        if (rm.ok && !(rm.square && op_sq)) {
+            int rc = reduce_rowop(op, S, rank, ax, &ins[0], rm.op1, rm.rop, rm.imm1, rm.pre, rm.square || op_sq, out,
+                                  (cudaStream_t)stream);
+            if (rc != TADMA_ERR_UNSUPPORTED) return rc;
+        }
+    }
 
     ChainReduceParams p{};
     p.chain.n_instr = n_instr;

@@ -142,6 +142,12 @@ int launch_transpose(bool fast, const TransposeParams& tp, cudaStream_t s);
 int launch_chain_reduce_f32(int kind, bool vec, const ChainReduceParams& p, cudaStream_t s);
 int launch_chain_reduce_f64(int kind, const ChainReduceParams& p, cudaStream_t s);
 int launch_chain_reduce_i64(int kind, const ChainReduceParams& p, cudaStream_t s);
+// reduce.cu: a chain reduction of the form sq(pre(op1(x, m))) with m one value
+// per output row, on the reduction engine's row kernel (TADMA_ERR_UNSUPPORTED
+// when the layout is not its own; nothing recorded then).
+int reduce_rowop(int32_t op, const int64_t* shape, int32_t rank, int32_t ax, const tadma_tensor* in, int32_t op1,
+                 const tadma_tensor* rop, double imm1, int32_t pre_op, int32_t square, const tadma_tensor* out,
+                 cudaStream_t s);
 
 namespace {
 

@@ -90,6 +90,30 @@ __device__ __forceinline__ uint4 cvt_out(const float* f) {
     }
 }
 
+// N elements of a strided operand of run-time dtype as fp32, the dtype
+// dispatched once for all N (per-element gamma / beta layouts).
+template <int N>
+__device__ __forceinline__ void load_strided(const char* p, int dt, int64_t off, int64_t stride, float (&f)[N]) {
+    switch (dt) {
+    case TADMA_F32:
+#pragma unroll
+        for (int j = 0; j < N; j++) f[j] = reinterpret_cast<const float*>(p)[off + j * stride];
+        break;
+    case TADMA_F16:
+#pragma unroll
+        for (int j = 0; j < N; j++) f[j] = __half2float(reinterpret_cast<const __half*>(p)[off + j * stride]);
+        break;
+    case TADMA_BF16:
+#pragma unroll
+        for (int j = 0; j < N; j++) f[j] = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[off + j * stride]);
+        break;
+    default:
+#pragma unroll
+        for (int j = 0; j < N; j++) f[j] = load_as<float>(p, dt, off + j * stride);
+        break;
+    }
+}
+
 template <typename T>
 __device__ __forceinline__ float fast_exp(float x) {
     // 16-bit outputs: the fast exponential's few-ulp fp32 error is far below
@@ -225,12 +249,19 @@ __device__ __forceinline__ void rownorm_finish_packed(float (&v)[CH][VecT<T>::N]
                         f2_unpack(t, v[c][2 * h], v[c][2 * h + 1]);
                     }
                 } else {
+                    // a pair of gamma / beta values at a time keeps 4 registers live
 #pragma unroll
-                    for (int j = 0; j < N; j++) {
-                        float t = (v[c][j] - mean) * rstd;
-                        if (p.gamma) t = t * load_as<float>(p.gamma, p.g_dtype, (col + j) * p.g_stride);
-                        if (p.beta) t = t + load_as<float>(p.beta, p.b_dtype, (col + j) * p.b_stride);
-                        v[c][j] = t;
+                    for (int h = 0; h < H; h++) {
+                        float g[2], b[2];
+                        if (p.gamma) load_strided<2>(p.gamma, p.g_dtype, (col + 2 * h) * p.g_stride, p.g_stride, g);
+                        if (p.beta) load_strided<2>(p.beta, p.b_dtype, (col + 2 * h) * p.b_stride, p.b_stride, b);
+#pragma unroll
+                        for (int k = 0; k < 2; k++) {
+                            float t = (v[c][2 * h + k] - mean) * rstd;
+                            if (p.gamma) t = t * g[k];
+                            if (p.beta) t = t + b[k];
+                            v[c][2 * h + k] = t;
+                        }
                     }
                 }
             }
@@ -317,11 +348,8 @@ __device__ __forceinline__ void rownorm_finish(float (&v)[CH][VecT<T>::N], const
                     if (p.gamma) cvt_in<T>(ld_nc_v4(reinterpret_cast<const T*>(p.gamma) + col), g);
                     if (p.beta) cvt_in<T>(ld_nc_v4(reinterpret_cast<const T*>(p.beta) + col), b);
                 } else {
-#pragma unroll
-                    for (int j = 0; j < N; j++) {
-                        if (p.gamma) g[j] = load_as<float>(p.gamma, p.g_dtype, (col + j) * p.g_stride);
-                        if (p.beta) b[j] = load_as<float>(p.beta, p.b_dtype, (col + j) * p.b_stride);
-                    }
+                    if (p.gamma) load_strided<N>(p.gamma, p.g_dtype, col * p.g_stride, p.g_stride, g);
+                    if (p.beta) load_strided<N>(p.beta, p.b_dtype, col * p.b_stride, p.b_stride, b);
                 }
 #pragma unroll
                 for (int j = 0; j < N; j++) {

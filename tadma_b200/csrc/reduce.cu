@@ -62,6 +62,13 @@ struct RedParams {
     int64_t splits;  // CTAs per row (ROW) / per column tile (COL)
     int64_t chunk;   // reduced-axis elements per split
     void* partials;  // State<float> workspace
+    // row operand (reduce_rowop_kernel): element x of row r becomes
+    // op1(x, m_r) before the pre-op, m_r = rop[r * rop_row_stride], or imm1
+    // when rop is null
+    const char* rop;
+    int32_t rop_dtype, op1;
+    int64_t rop_row_stride;
+    double imm1;
 };
 
 // Element pre-op (fused unary and/or square).  PRE = false: the call has
@@ -152,8 +159,9 @@ struct ArgVec {
         raw.z = take ? r.z : raw.z;
         raw.w = take ? r.w : raw.w;
     }
-    template <bool PRE>
-    __device__ __forceinline__ State<float> resolve(const RedParams& p) const {
+    // tf: the element transform the reduction applied (its pre-op).
+    template <typename TF>
+    __device__ __forceinline__ State<float> resolve(const TF& tf) const {
         State<float> s;
         s.v = v;
         s.i = -1;
@@ -163,7 +171,7 @@ struct ArgVec {
         int jj = 0;
 #pragma unroll
         for (int j = N - 1; j >= 0; j--) {
-            const float x = prep<PRE>(p, f[j]);
+            const float x = tf(f[j]);
             if (v != v ? x != x : x == v) jj = j;
         }
         s.i = vi * N + jj;
@@ -207,10 +215,111 @@ __global__ void __launch_bounds__(THREADS) reduce_row_kernel(const __grid_consta
                     }
                 }
             }
-            if constexpr (ARG) s = av.template resolve<PRE>(p);
+            if constexpr (ARG) s = av.resolve([&](float x) { return prep<PRE>(p, x); });
             done = nv * N;
         }
         for (int64_t i = done + lane; i < p.R; i += 32) update<K, float>(s, prep<PRE>(p, ld1(x + i * p.r_stride)), i);
+        s = warp_combine<K, float>(s);
+        if (lane == 0) finish<K, float>(p, s, row * p.out_row_stride);
+    }
+}
+
+// ------------------------------------------------- ROW path, row operand --
+//
+// A chain reduction whose chain is op1(x, m) [then a unary op] [then a
+// square], with m one value per output row (a per-row tensor or an
+// immediate): the row variance sum((x - mean)^2), the softmax denominator
+// sum(exp(x - max)), scaled sums.  tadma_b200_reduce_chain sends those here
+// instead of its interpreter: the same warp-per-row loop as
+// reduce_row_kernel, with each op dispatched once per 16-byte vector (the op
+// bodies of the element-wise engine, so the chain's values are bit-identical).
+
+template <int N>
+__device__ __forceinline__ void rowop_vec(const RedParams& p, float m, float (&f)[N]) {
+#define TADMA_ROWOP_B(OPC)                                                         \
+    case OPC:                                                                      \
+        _Pragma("unroll") for (int j = 0; j < N; j++) f[j] = binary(OPC, f[j], m, 0.0f); \
+        break;
+    switch (p.op1) {
+        TADMA_ROWOP_B(TADMA_OP_ADD)
+        TADMA_ROWOP_B(TADMA_OP_SUB)
+        TADMA_ROWOP_B(TADMA_OP_MUL)
+        TADMA_ROWOP_B(TADMA_OP_DIV)
+        TADMA_ROWOP_B(TADMA_OP_RSUB)
+        TADMA_ROWOP_B(TADMA_OP_RDIV)
+        TADMA_ROWOP_B(TADMA_OP_MAX)
+        TADMA_ROWOP_B(TADMA_OP_MIN)
+    default:
+        break;
+    }
+#undef TADMA_ROWOP_B
+#define TADMA_ROWOP_U(OPC)                                                         \
+    case OPC:                                                                      \
+        _Pragma("unroll") for (int j = 0; j < N; j++) f[j] = unary(OPC, f[j]);    \
+        break;
+    switch (p.pre_op) {
+    case TADMA_OP_COPY:
+        break;
+        TADMA_ROWOP_U(TADMA_OP_EXP)
+        TADMA_ROWOP_U(TADMA_OP_ABS)
+        TADMA_ROWOP_U(TADMA_OP_NEG)
+        TADMA_ROWOP_U(TADMA_OP_SQRT)
+    default:
+#pragma unroll
+        for (int j = 0; j < N; j++) f[j] = unary(p.pre_op, f[j]);
+        break;
+    }
+#undef TADMA_ROWOP_U
+    if (p.square) {
+#pragma unroll
+        for (int j = 0; j < N; j++) f[j] = f[j] * f[j];
+    }
+}
+
+__device__ __forceinline__ float rowop_one(const RedParams& p, float m, float x) {
+    float f[1] = {x};
+    rowop_vec<1>(p, m, f);
+    return f[0];
+}
+
+template <typename T, int K>
+__global__ void __launch_bounds__(THREADS) reduce_rowop_kernel(const __grid_constant__ RedParams p, int vec) {
+    pdl_begin();
+    constexpr int N = Vec<T>::N;
+    constexpr int UNR = 4;
+    const int lane = threadIdx.x & 31;
+    const int64_t gw = ((int64_t)blockIdx.x * THREADS + threadIdx.x) >> 5;
+    const int64_t nw = ((int64_t)gridDim.x * THREADS) >> 5;
+    for (int64_t row = gw; row < p.nrows; row += nw) {
+        const T* x = reinterpret_cast<const T*>(p.in) + row * p.in_row_stride;
+        const float m = p.rop ? load_as<float>(p.rop, p.rop_dtype, row * p.rop_row_stride) : __double2float_rn(p.imm1);
+        State<float> s = init_state<K, float>();
+        int64_t done = 0;
+        if (vec) {
+            constexpr bool ARG = K == K_ARGMAX || K == K_ARGMIN;
+            ArgVec<K, T, N> av;
+            if constexpr (ARG) av.init();
+            const int64_t nv = p.R / N;
+            for (int64_t i0 = lane; i0 < nv; i0 += 32 * UNR) {
+                uint4 r[UNR];
+#pragma unroll
+                for (int u = 0; u < UNR; u++)
+                    if (i0 + 32 * u < nv) r[u] = ld_stream_v4(x + (i0 + 32 * u) * N);
+#pragma unroll
+                for (int u = 0; u < UNR; u++) {
+                    if (i0 + 32 * u < nv) {
+                        float f[N];
+                        Vec<T>::cvt(r[u], f);
+                        rowop_vec<N>(p, m, f);
+                        if constexpr (ARG) av.add(r[u], f, i0 + 32 * u);
+                        else update_vec<K, N>(s, f, (i0 + 32 * u) * N);
+                    }
+                }
+            }
+            if constexpr (ARG) s = av.resolve([&](float v) { return rowop_one(p, m, v); });
+            done = nv * N;
+        }
+        for (int64_t i = done + lane; i < p.R; i += 32) update<K, float>(s, rowop_one(p, m, ld1(x + i)), i);
         s = warp_combine<K, float>(s);
         if (lane == 0) finish<K, float>(p, s, row * p.out_row_stride);
     }
@@ -324,7 +433,7 @@ __global__ void __launch_bounds__(THREADS) reduce_row_split_kernel(const __grid_
                 }
             }
         }
-        if constexpr (ARG) s = av.template resolve<PRE>(p);
+        if constexpr (ARG) s = av.resolve([&](float x) { return prep<PRE>(p, x); });
         done = v1 * N;
     }
     for (int64_t i = done + threadIdx.x; i < r1; i += THREADS) update<K, float>(s, prep<PRE>(p, ld1(x + i * p.r_stride)), i);
@@ -547,10 +656,19 @@ int run_fast(int dt, int kind, int path, RedParams& p, bool vec, cudaStream_t s,
     const int64_t ws = split_workspace_bytes(p, path);
     if (ws == 0) return dispatch_fast(dt, kind, path, p, vec, s);
     if (fixed.ptr) {
-        if (ws > fixed.bytes)
-            return fail(TADMA_ERR_INVALID, "tadma_b200_reduce_noalloc: this reduction needs " + std::to_string(ws) +
-                                               " bytes of scratch, more than the " + std::to_string(fixed.bytes) +
-                                               "-byte static scratch; use tadma_b200_reduce");
+        if (ws > fixed.bytes) {
+            // Fewer splits, so the partials fit the static scratch; with room
+            // for fewer than two, the reduction runs in one pass (no scratch).
+            const int64_t per_split = ws / p.splits;
+            const int64_t g = fixed.bytes / per_split;
+            if (g < 2) {
+                p.splits = 1;
+                return dispatch_fast(dt, kind, path, p, vec, s);
+            }
+            p.chunk = (p.R + g - 1) / g;
+            if (path == 0) p.chunk = (p.chunk + 7) / 8 * 8;  // a multiple of every vector width
+            p.splits = (p.R + p.chunk - 1) / p.chunk;
+        }
         p.partials = fixed.ptr;
         return dispatch_fast(dt, kind, path, p, vec, s);
     }
@@ -709,7 +827,8 @@ static int noalloc_scratch(void** ptr) {
     if (!cache[dev]) {
         void* p = nullptr;
         e = cudaGetSymbolAddress(&p, g_reduce_scratch);
-        if (e != cudaSuccess || !p) return cuda_fail(e, "tadma_b200_reduce_noalloc: cudaGetSymbolAddress");
+        if (e != cudaSuccess) return cuda_fail(e, "tadma_b200_reduce_noalloc: cudaGetSymbolAddress");
+        if (!p) return fail(TADMA_ERR_CUDA, "tadma_b200_reduce_noalloc: cudaGetSymbolAddress returned a null address");
         cache[dev] = p;
     }
     *ptr = cache[dev];
@@ -724,3 +843,94 @@ extern "C" int tadma_b200_reduce_noalloc(int32_t op, const tadma_tensor* in, int
     fixed.bytes = NOALLOC_SCRATCH_BYTES;
     return reduce_impl(op, in, axis, pre_op, out, stream, fixed);
 }
+
+namespace tadma_b200 {
+
+// The row-operand reduction (reduce_rowop_kernel) for tadma_b200_reduce_chain:
+// out = reduce over `axis` of sq(pre(op1(in, m))), m = rop broadcast along
+// the axis (or imm1 when rop is null), `shape` the broadcast execution shape
+// of in and rop.  Only the unsplit ROW layout is taken: the reduced axis
+// contiguous in `in`, the kept dims of in, rop and out folding to one.  Any
+// other layout returns TADMA_ERR_UNSUPPORTED without recording an error, and
+// the caller runs its general kernel instead.
+int reduce_rowop(int32_t op, const int64_t* shape, int32_t rank, int32_t ax, const tadma_tensor* in, int32_t op1,
+                 const tadma_tensor* rop, double imm1, int32_t pre_op, int32_t square, const tadma_tensor* out,
+                 cudaStream_t s) {
+    const int dt = in->dtype;
+    if (!(dt == TADMA_F32 || dt == TADMA_F16 || dt == TADMA_BF16)) return TADMA_ERR_UNSUPPORTED;
+    const int64_t R = shape[ax];
+    if (R < 2 || in->dims[ax] != R || in->strides[ax] != 1) return TADMA_ERR_UNSUPPORTED;
+    if (rop && rop->dims[ax] != 1 && rop->strides[ax] != 0) return TADMA_ERR_UNSUPPORTED;
+    const bool keep = out->rank == rank;
+    int64_t kd[TADMA_MAX_RANK], ks[3][TADMA_MAX_RANK];
+    int kr = 0;
+    for (int d = 0; d < rank; d++) {
+        if (d == ax) continue;
+        kd[kr] = shape[d];
+        ks[0][kr] = in->dims[d] == 1 ? 0 : in->strides[d];
+        ks[1][kr] = out->strides[keep ? d : (d < ax ? d : d - 1)];
+        ks[2][kr] = !rop || rop->dims[d] == 1 ? 0 : rop->strides[d];
+        kr++;
+    }
+    int64_t nrows = 1, in_rs = 0, out_rs = 0, rop_rs = 0;
+    if (kr > 0) {
+        Folded f = fold(kr, kd, ks, 3);
+        if (f.rank != 1) return TADMA_ERR_UNSUPPORTED;
+        nrows = f.dims[0];
+        in_rs = f.strides[0][0];
+        out_rs = f.strides[1][0];
+        rop_rs = f.strides[2][0];
+    }
+    RedParams p{};
+    p.in = (const char*)in->data;
+    p.out = (char*)out->data;
+    p.in_dtype = dt;
+    p.out_dtype = out->dtype;
+    p.pre_op = pre_op;
+    p.square = square;
+    p.post = op == TADMA_REDUCE_MEAN ? P_MEAN : (op == TADMA_REDUCE_RMS ? P_RMS : P_NONE);
+    int kind;
+    switch (op) {
+    case TADMA_REDUCE_MAX: kind = K_MAX; break;
+    case TADMA_REDUCE_MIN: kind = K_MIN; break;
+    case TADMA_REDUCE_ARGMAX: kind = K_ARGMAX; break;
+    case TADMA_REDUCE_ARGMIN: kind = K_ARGMIN; break;
+    default: kind = K_SUM; break;
+    }
+    p.kind = kind;
+    p.R = R;
+    p.r_stride = 1;
+    p.nrows = nrows;
+    p.in_row_stride = in_rs;
+    p.out_row_stride = out_rs;
+    p.rop = rop ? (const char*)rop->data : nullptr;
+    p.rop_dtype = rop ? rop->dtype : TADMA_F32;
+    p.rop_row_stride = rop_rs;
+    p.op1 = op1;
+    p.imm1 = imm1;
+    plan_row_split(p, R, sm_count());
+    if (p.splits > 1) return TADMA_ERR_UNSUPPORTED;  // few long rows: the general kernel's split-free path
+    const int es = dtype_size(dt);
+    const bool vec = ((uintptr_t)in->data % 16) == 0 && R >= 16 / es && (nrows == 1 || (in_rs * es) % 16 == 0);
+    auto go = [&](auto kern) {
+        const int grid = grid_for((const void*)kern, (p.nrows + WARPS - 1) / WARPS);
+        (void)launch_pdl(kern, dim3(grid), dim3(THREADS), 0, s, p, vec ? 1 : 0);
+        cudaError_t e = cudaGetLastError();
+        return e == cudaSuccess ? TADMA_OK : cuda_fail(e, "tadma_b200_reduce_chain launch");
+    };
+    auto by_kind = [&](auto tag) {
+        using T = decltype(tag);
+        switch (kind) {
+        case K_SUM: return go(reduce_rowop_kernel<T, K_SUM>);
+        case K_MAX: return go(reduce_rowop_kernel<T, K_MAX>);
+        case K_MIN: return go(reduce_rowop_kernel<T, K_MIN>);
+        case K_ARGMAX: return go(reduce_rowop_kernel<T, K_ARGMAX>);
+        default: return go(reduce_rowop_kernel<T, K_ARGMIN>);
+        }
+    };
+    if (dt == TADMA_F32) return by_kind(float{});
+    if (dt == TADMA_F16) return by_kind(__half{});
+    return by_kind(__nv_bfloat16{});
+}
+
+}  // namespace tadma_b200

@@ -10,11 +10,12 @@ import subprocess
 import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-REFERENCE = os.environ.get("TADMA_REFERENCE", "/root/reference")
+# The reference checkout: $TADMA_REFERENCE, else ../reference beside the repository.
+REFERENCE = os.environ.get("TADMA_REFERENCE", os.path.join(os.path.dirname(ROOT), "reference"))
 GENERATED = os.path.join(REFERENCE, "scripts", "generated.cu")
 
 
-@pytest.mark.skipif(not os.path.exists(GENERATED), reason="reference checkout not present")
+@pytest.mark.skipif(not os.path.exists(GENERATED), reason="reference checkout not present (set TADMA_REFERENCE)")
 def test_reference_generated_graph_compiles_unchanged(tmp_path):
     wrapper = tmp_path / "instantiate.cu"
     seq = "Tensor<int64_t, ALLOCATOR, Sequence<(int64_t)1, (int64_t)8>>"

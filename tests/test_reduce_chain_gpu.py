@@ -155,3 +155,44 @@ def test_vector_path_with_ragged_tail(op):
     ref = np.zeros((4, 1), np.int64 if arg else np.float32)
     assert O.reduce(op, tmp, -1, ref) == 0
     close(from_dev(out), ref, tmp, op, -1)
+
+
+# Chains of the row-operand form op1(x, m) -> [unary] -> [square], m one value
+# per output row or an immediate: tadma_b200_reduce_chain runs them on the
+# reduction engine's row kernel (reduce_rowop_kernel).
+ROWOP_PROGS = {
+    "variance": [instr(Op.SUB, b=1), instr(Op.POW, b=SRC_IMM, imm=2.0)],
+    "softmax_denominator": [instr(Op.SUB, b=1), instr(Op.EXP)],
+    "scaled": [instr(Op.MUL, b=SRC_IMM, imm=0.5)],
+    "plain": [],
+    "square": [instr(Op.POW, b=SRC_IMM, imm=2.0)],
+    "ratio_abs": [instr(Op.DIV, b=1), instr(Op.ABS)],
+}
+
+
+@pytest.mark.parametrize("name", list(ROWOP_PROGS))
+@pytest.mark.parametrize("op", list(Reduce))
+@pytest.mark.parametrize("dt,shape", [(DType.F32, (37, 1000)), (DType.BF16, (37, 1000)), (DType.F16, (5, 1003))])
+def test_row_operand_chains(name, op, dt, shape):
+    prog = ROWOP_PROGS[name]
+    x = gen(shape, dt, Dist.NORMAL, 0.0, 1.0, 11)
+    ins, dts = [x], [dt]
+    if any(i.b == 1 for i in prog):
+        ins.append(gen((shape[0], 1), DType.F32, Dist.NORMAL, 0.5, 0.3, 12))
+        dts.append(DType.F32)
+    got, ref, tmp = both(op, ins, dts, prog, -1)
+    # exp through CUDA's expf: max / min within its 2 ulp
+    close(got, ref, tmp, op, -1, max_ulp=2 if name == "softmax_denominator" else 0)
+
+
+def test_row_operand_chain_reaches_the_row_kernel():
+    import torch
+    from tests.test_dispatch_gpu import kernels_of
+    x = torch.empty((256, 4096), dtype=torch.float32, device="cuda")
+    tb.fill(x, Dist.NORMAL, 0.0, 1.0, 0, 13)
+    m = torch.empty((256, 1), dtype=torch.float32, device="cuda")
+    tb.fill(m, Dist.NORMAL, 0.0, 0.1, 0, 14)
+    mv = make_tensor(m.data_ptr(), DType.F32, [256, 4096], [1, 0])
+    out = torch.empty((256, 1), dtype=torch.float32, device="cuda")
+    names = kernels_of(lambda: tb.reduce_chain(Reduce.MEAN, [x, mv], ROWOP_PROGS["variance"], -1, out, Compute.F32))
+    assert "reduce_rowop_kernel" in names, names

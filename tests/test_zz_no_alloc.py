@@ -61,13 +61,37 @@ def test_noalloc_matches_reduce_twice(shape, axis, op, dt):
         assert _close(got, want, n, exact=op == Reduce.ARGMAX), (call, shape)
 
 
-def test_noalloc_rejects_more_scratch_than_it_has():
+@pytest.mark.parametrize("shape", [
+    (1, 4096, 36864),  # 144 column tiles x 5 splits x 36864 columns of 16-byte partials = 2.95 MB: 3 splits fit
+    (1, 4096, 70000),  # one split's partials (1.1 MB) leave no room for two: one pass, no scratch
+])
+def test_noalloc_fits_its_split_to_the_static_scratch(shape):
     import torch
-    # bf16 [1, 4096, 36864] over axis 1: 144 column tiles x 5 splits x 36864
-    # columns of 16-byte partials = 2.95 MB > the 2 MiB static buffer.
     L = tb.lib()
-    x = torch.zeros((1, 4096, 36864), dtype=torch.bfloat16, device="cuda")
-    out = torch.empty((1, 1, 36864), dtype=torch.float32, device="cuda")
-    rc = _reduce(L.tadma_b200_reduce_noalloc, Reduce.SUM, x, 1, out)
-    assert rc == 1 and b"2097152-byte static scratch" in L.tadma_b200_last_error()
-    assert _reduce(L.tadma_b200_reduce, Reduce.SUM, x, 1, out) == 0  # the allocating entry point handles it
+    x = torch.empty(shape, dtype=torch.bfloat16, device="cuda")
+    tb.fill(x, Dist.NORMAL, 0.0, 1.0, seed=3, stream_id=41)
+    oshape = (shape[0], 1, shape[2])
+    want = torch.empty(oshape, dtype=torch.float32, device="cuda")
+    got = torch.full(oshape, -7.0, dtype=torch.float32, device="cuda")
+    assert _reduce(L.tadma_b200_reduce, Reduce.SUM, x, 1, want) == 0
+    for _ in range(2):
+        assert _reduce(L.tadma_b200_reduce_noalloc, Reduce.SUM, x, 1, got) == 0, L.tadma_b200_last_error()
+        assert _close(got, want, shape[1])
+
+
+def test_noalloc_on_two_devices():
+    """The static buffer's address is looked up per device: a call on cuda:1
+    after one on cuda:0 must use cuda:1's copy of the buffer."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    L = tb.lib()
+    for dev in (0, 1, 0, 1):
+        with torch.cuda.device(dev):
+            x = torch.empty((3, 200003), dtype=torch.float32, device="cuda")
+            tb.fill(x, Dist.NORMAL, 0.0, 1.0, seed=dev, stream_id=42)
+            want = torch.empty((3, 1), dtype=torch.float32, device="cuda")
+            got = torch.full((3, 1), -7.0, dtype=torch.float32, device="cuda")
+            assert _reduce(L.tadma_b200_reduce, Reduce.SUM, x, -1, want) == 0
+            assert _reduce(L.tadma_b200_reduce_noalloc, Reduce.SUM, x, -1, got) == 0, L.tadma_b200_last_error()
+            assert _close(got, want, 200003)
