@@ -16,8 +16,10 @@
 #include <cstdint>
 #include <cstdlib>
 #include <functional>
+#include <memory>
 #include <stdexcept>
 #include <string>
+#include <vector>
 
 #include "../tadma_b200.h"
 
@@ -68,19 +70,33 @@ struct CUDAStreamGuard {
 };
 
 namespace detail {
+// Library calls made by the header API on this thread (every C-ABI call goes
+// through check()); tests read it to count launches.
+inline thread_local int64_t calls = 0;
+
 // Turns a C-ABI status into the reference's error convention (std::runtime_error).
 inline void check(int rc, const char* what) {
+    calls++;
     if (rc != TADMA_OK) throw std::runtime_error(std::string(what) + ": " + tadma_b200_last_error());
 }
+
+struct Deferred;
+
+// Control block of an owned buffer: its reference count and deleter, the
+// deferred work that will write it (not yet enqueued), and the deferred work
+// that reads it (Deferred.hpp).
+struct StorageCtl {
+    std::atomic<int> refs{1};
+    std::function<void()> deleter;
+    std::shared_ptr<Deferred> pending;
+    std::vector<std::weak_ptr<Deferred>> readers;
+};
 }  // namespace detail
 
 // Ref-counted pointer on the host side, a raw pointer when copied into a kernel.
 template <typename T>
 struct HeapStorage {
-    struct Ctl {
-        std::atomic<int> refs{1};
-        std::function<void()> deleter;
-    };
+    using Ctl = detail::StorageCtl;
     T* view = nullptr;
     Ctl* ctl = nullptr;
 
@@ -117,6 +133,9 @@ struct HeapStorage {
 
     void release() noexcept {
         if (ctl && --ctl->refs == 0) {
+            // Work deferred into a buffer nobody holds any more is dropped
+            // unrun; the buffer is freed behind everything already enqueued.
+            ctl->pending.reset();
             if (ctl->deleter) ctl->deleter();
             delete ctl;
         }

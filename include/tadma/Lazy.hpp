@@ -20,7 +20,7 @@
 // * any other call that takes a tensor (softmax, layer_norm, gather, an
 //   eager operator with a lazy operand): a lazy value satisfies AnyTensor, and
 //   its describe() materialises it once and keeps the result.
-// A chain holds at most 16 instructions and 3 tensors besides its source,
+// A chain holds at most 16 instructions and 5 tensors besides its source,
 // each broadcast to the source's dims.  An instruction that would exceed
 // either limit, or that the eager call would compute in another precision
 // than the chain's (a double result after float ones, an integer op after
@@ -45,27 +45,8 @@ struct is_lazy : std::false_type {};
 template <typename R, typename D>
 struct is_lazy<Lazy<R, D>> : std::true_type {};
 
-inline bool dtype_float(int d) { return d == TADMA_F32 || d == TADMA_F16 || d == TADMA_BF16 || d == TADMA_F64; }
-inline bool dtype_wide(int d) { return d == TADMA_F64 || d == TADMA_I64; }
-inline bool op_transcendental(int op) {
-    return (op >= TADMA_OP_EXP && op <= TADMA_OP_GELU && op != TADMA_OP_RELU) || op == TADMA_OP_POW;
-}
-
-// The precision tadma_b200_eltwise picks (TADMA_COMPUTE_AUTO) for the one-op
-// call y = op(a[, b | imm][, c]) that the eager API makes (-1: no operand).
-inline int eager_compute(int out_dt, int a_dt, int b_dt, int op, bool has_imm, double imm, int c_dt = -1) {
-    bool all_int = !dtype_float(out_dt) && !dtype_float(a_dt);
-    bool wide = dtype_wide(out_dt) || dtype_wide(a_dt);
-    for (int d : {b_dt, c_dt}) {
-        if (d < 0) continue;
-        all_int = all_int && !dtype_float(d);
-        wide = wide || dtype_wide(d);
-    }
-    if (op_transcendental(op)) all_int = false;
-    if (has_imm && imm != (double)(int64_t)imm) all_int = false;
-    if (all_int) return TADMA_COMPUTE_I64;
-    return wide ? TADMA_COMPUTE_F64 : TADMA_COMPUTE_F32;
-}
+// dtype_float, dtype_wide, op_transcendental, eager_compute and same_view
+// are shared with the deferred evaluation (Deferred.hpp).
 
 // The recorded chain: operands (ins[0] is the source), instructions, the
 // chain's precision (AUTO until the first instruction fixes it) and shared
@@ -77,11 +58,6 @@ struct LazyChain {
     int n_instr = 0, n_ins = 1, compute = TADMA_COMPUTE_AUTO;
 };
 
-inline bool same_view(const tadma_tensor& u, const tadma_tensor& t) {
-    bool same = u.data == t.data && u.dtype == t.dtype && u.rank == t.rank;
-    for (int d = 0; same && d < t.rank; d++) same = u.dims[d] == t.dims[d] && u.strides[d] == t.strides[d];
-    return same;
-}
 // Index of the operand of `c` that is the same view as `t`, or -1.
 inline int find_operand(const LazyChain& c, const tadma_tensor& t) {
     for (int k = 0; k < c.n_ins; k++)
@@ -302,7 +278,7 @@ auto lazy_combine(const A& a, const B& b) {
 
 template <int OP, bool Bool, LazyTensor L, Scalar S>
 auto lazy_scalar(const L& l, S v) {
-    using R = std::conditional_t<Bool, bool, arith_t<typename L::ValueType, S>>;
+    using R = std::conditional_t<Bool, bool, arith_t<typename L::ValueType, scalar_t<S>>>;
     return l.template then<R>(OP, TADMA_SRC_IMM, (double)v);
 }
 
@@ -406,7 +382,7 @@ template <bool Inplace = true, AnyTensor T, Scalar S>
     requires LazyTensor<T>
 auto pow(T&& t, S s) {
     using TT = std::decay_t<T>;
-    using R2 = std::conditional_t<Inplace, typename TT::ValueType, arith_t<math_t<typename TT::ValueType>, S>>;
+    using R2 = std::conditional_t<Inplace, typename TT::ValueType, arith_t<math_t<typename TT::ValueType>, scalar_t<S>>>;
     return t.template then<R2>(TADMA_OP_POW, TADMA_SRC_IMM, (double)s);
 }
 

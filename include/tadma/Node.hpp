@@ -351,6 +351,8 @@ struct Node {
             constexpr int64_t per = (int64_t)detail::NODE_THREADS * detail::NODE_PER_THREAD;
             constexpr int64_t want = (N + per - 1) / per;
             constexpr unsigned grid = (unsigned)(want < 0x7fffffff ? want : 0x7fffffff);
+            // The functor may read or write any of its tensors.
+            (detail::sync_write(std::get<I>(tensors).data.ctl), ...);
             node_kernel<ExecutionShape><<<grid, detail::NODE_THREADS, 0, stream>>>(f, make_view(std::get<I>(tensors))...);
             check_cuda(cudaGetLastError());
         }
@@ -362,6 +364,7 @@ struct Node {
     template <std::size_t... I>
     void run_on_host(std::index_sequence<I...>) {
         constexpr int64_t N = ExecutionShape::Product();
+        (detail::sync_write(std::get<I>(tensors).data.ctl), ...);
         if constexpr (device == kCUDA) {
             auto host = std::make_tuple(stage_in<I>()...);
             check_cuda(cudaStreamSynchronize(stream));

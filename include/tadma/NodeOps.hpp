@@ -144,18 +144,18 @@ TADMA_NODE_UNARY(Negate, -x)
 }  // namespace nodefn
 
 // tensor (op) scalar, scalar (op) tensor
-template <TapeTensor T, Scalar S> auto operator+(const T& t, S v) { return EltwiseNode(t, nodefn::AddS<S>{v}); }
-template <TapeTensor T, Scalar S> auto operator-(const T& t, S v) { return EltwiseNode(t, nodefn::SubS<S>{v}); }
-template <TapeTensor T, Scalar S> auto operator*(const T& t, S v) { return EltwiseNode(t, nodefn::MulS<S>{v}); }
-template <TapeTensor T, Scalar S> auto operator/(const T& t, S v) { return EltwiseNode(t, nodefn::DivS<S>{v}); }
-template <TapeTensor T, Scalar S> auto operator-(S v, const T& t) { return EltwiseNode(t, nodefn::RSubS<S>{v}); }
-template <TapeTensor T, Scalar S> auto operator/(S v, const T& t) { return EltwiseNode(t, nodefn::RDivS<S>{v}); }
-template <TapeTensor T, Scalar S> auto operator+(S v, const T& t) { return EltwiseNode(t, nodefn::AddS<S>{v}); }
-template <TapeTensor T, Scalar S> auto operator*(S v, const T& t) { return EltwiseNode(t, nodefn::MulS<S>{v}); }
-template <TapeTensor T, Scalar S> auto operator>(const T& t, S v) { return EltwiseNode(t, nodefn::GtS<S>{v}); }
-template <TapeTensor T, Scalar S> auto operator<(const T& t, S v) { return EltwiseNode(t, nodefn::LtS<S>{v}); }
-template <TapeTensor T, Scalar S> auto operator==(const T& t, S v) { return EltwiseNode(t, nodefn::EqS<S>{v}); }
-template <TapeTensor T, Scalar S> auto operator!=(const T& t, S v) { return EltwiseNode(t, nodefn::NeS<S>{v}); }
+template <TapeTensor T, Scalar S> auto operator+(const T& t, S v) { return EltwiseNode(t, nodefn::AddS<scalar_t<S>>{(scalar_t<S>)v}); }
+template <TapeTensor T, Scalar S> auto operator-(const T& t, S v) { return EltwiseNode(t, nodefn::SubS<scalar_t<S>>{(scalar_t<S>)v}); }
+template <TapeTensor T, Scalar S> auto operator*(const T& t, S v) { return EltwiseNode(t, nodefn::MulS<scalar_t<S>>{(scalar_t<S>)v}); }
+template <TapeTensor T, Scalar S> auto operator/(const T& t, S v) { return EltwiseNode(t, nodefn::DivS<scalar_t<S>>{(scalar_t<S>)v}); }
+template <TapeTensor T, Scalar S> auto operator-(S v, const T& t) { return EltwiseNode(t, nodefn::RSubS<scalar_t<S>>{(scalar_t<S>)v}); }
+template <TapeTensor T, Scalar S> auto operator/(S v, const T& t) { return EltwiseNode(t, nodefn::RDivS<scalar_t<S>>{(scalar_t<S>)v}); }
+template <TapeTensor T, Scalar S> auto operator+(S v, const T& t) { return EltwiseNode(t, nodefn::AddS<scalar_t<S>>{(scalar_t<S>)v}); }
+template <TapeTensor T, Scalar S> auto operator*(S v, const T& t) { return EltwiseNode(t, nodefn::MulS<scalar_t<S>>{(scalar_t<S>)v}); }
+template <TapeTensor T, Scalar S> auto operator>(const T& t, S v) { return EltwiseNode(t, nodefn::GtS<scalar_t<S>>{(scalar_t<S>)v}); }
+template <TapeTensor T, Scalar S> auto operator<(const T& t, S v) { return EltwiseNode(t, nodefn::LtS<scalar_t<S>>{(scalar_t<S>)v}); }
+template <TapeTensor T, Scalar S> auto operator==(const T& t, S v) { return EltwiseNode(t, nodefn::EqS<scalar_t<S>>{(scalar_t<S>)v}); }
+template <TapeTensor T, Scalar S> auto operator!=(const T& t, S v) { return EltwiseNode(t, nodefn::NeS<scalar_t<S>>{(scalar_t<S>)v}); }
 
 // tensor (op) tensor, when either side is a tape tensor
 #define TADMA_TAPE_BINARY(op, Fn)                                                   \
@@ -182,10 +182,10 @@ TADMA_TAPE_BINARY(||, LOr)
 template <TapeTensor T> auto operator-(const T& t) { return EltwiseNode(t, nodefn::Neg{}); }
 
 // compound assignment: x = f(x, y) in place (CombineNode / InplaceNode)
-template <TapeTensor T, Scalar S> auto operator+=(T& t, S v) { return InplaceNode(t, nodefn::AddS<S>{v}); }
-template <TapeTensor T, Scalar S> auto operator-=(T& t, S v) { return InplaceNode(t, nodefn::SubS<S>{v}); }
-template <TapeTensor T, Scalar S> auto operator*=(T& t, S v) { return InplaceNode(t, nodefn::MulS<S>{v}); }
-template <TapeTensor T, Scalar S> auto operator/=(T& t, S v) { return InplaceNode(t, nodefn::DivS<S>{v}); }
+template <TapeTensor T, Scalar S> auto operator+=(T& t, S v) { return InplaceNode(t, nodefn::AddS<scalar_t<S>>{(scalar_t<S>)v}); }
+template <TapeTensor T, Scalar S> auto operator-=(T& t, S v) { return InplaceNode(t, nodefn::SubS<scalar_t<S>>{(scalar_t<S>)v}); }
+template <TapeTensor T, Scalar S> auto operator*=(T& t, S v) { return InplaceNode(t, nodefn::MulS<scalar_t<S>>{(scalar_t<S>)v}); }
+template <TapeTensor T, Scalar S> auto operator/=(T& t, S v) { return InplaceNode(t, nodefn::DivS<scalar_t<S>>{(scalar_t<S>)v}); }
 #define TADMA_TAPE_COMPOUND(op, Fn)                                                 \
     template <AnyTensor A, AnyTensor B>                                             \
         requires(TapeTensor<A> || TapeTensor<B>)                                    \
@@ -230,7 +230,7 @@ TADMA_TAPE_MKOP(negate, Negate)
 
 template <bool Inplace = true, TapeTensor T, Scalar S>
 auto pow(T&& t, S s) {
-    return MakeEltwiseNode<Inplace>(t, nodefn::PowS<S>{s});
+    return MakeEltwiseNode<Inplace>(t, nodefn::PowS<scalar_t<S>>{(scalar_t<S>)s});
 }
 
 }  // namespace tadma

@@ -103,7 +103,7 @@ A& combine_inplace(A& x, const B& y) {
 
 template <int OP, bool Bool, AnyTensor T, Scalar S>
 auto with_scalar(const T& t, S s) {
-    using R = std::conditional_t<Bool, bool, arith_t<typename T::ValueType, S>>;
+    using R = std::conditional_t<Bool, bool, arith_t<typename T::ValueType, scalar_t<S>>>;
     return unary_new<R>(t, OP, (double)s, TADMA_SRC_IMM);
 }
 
@@ -194,7 +194,8 @@ auto pow(T&& t, S s) {
         detail::unary_inplace(t, TADMA_OP_POW, (double)s, TADMA_SRC_IMM);
         return TT(t);
     } else {
-        return detail::unary_new<arith_t<math_t<typename TT::ValueType>, S>>(t, TADMA_OP_POW, (double)s, TADMA_SRC_IMM);
+        return detail::unary_new<arith_t<math_t<typename TT::ValueType>, scalar_t<S>>>(t, TADMA_OP_POW, (double)s,
+                                                                                       TADMA_SRC_IMM);
     }
 }
 
@@ -210,6 +211,8 @@ auto reduce_to(const T& t) {
     static_assert(Ax >= 0 && Ax < T::Rank, "reduction axis out of range");
     using OutDims = std::conditional_t<KeepDims, typename T::Dims::template Set<Ax, 1>, typename T::Dims::template Remove<Ax>>;
     Tensor<R, Allocator<kCUDA>, OutDims> out;
+    // A reduction of a deferred element-wise result: one reduce_chain, deferred.
+    if (defer_reduce(OP, Ax, out, t)) return out;
     tadma_tensor i = t.describe(), o = out.describe();
     check(tadma_b200_reduce(OP, &i, Ax, TADMA_OP_COPY, &o, stream), "tadma reduce");
     return out;
@@ -241,6 +244,7 @@ auto Tensor<T, A, D, S>::argmin() const { return detail::reduce_to<TADMA_REDUCE_
 template <int Dim, bool Inplace = true, AnyTensor T>
 auto softmax(T t) {
     constexpr int Ax = detail::real_dim<Dim, T::Rank>;
+    if constexpr (Inplace) detail::sync_write_of(t);
     tadma_tensor i = t.describe();
     if constexpr (Inplace) {
         detail::check(tadma_b200_softmax(&i, Ax, &i, stream), "tadma softmax");
@@ -269,6 +273,7 @@ template <int D, bool Inplace, int Mode, AnyTensor T, AnyTensor G, AnyTensor B>
 auto layer_norm_impl(T& t, const G& gamma, const B& beta, double eps) {
     constexpr int Ax = real_dim<D, T::Rank>;
     static_assert(Ax == T::Rank - 1, "layer_norm normalises the last axis");
+    if constexpr (Inplace) sync_write_of(t);
     tadma_tensor i = t.describe(), g = vec_desc(gamma, T::Dims::Arr[Ax]), b = vec_desc(beta, T::Dims::Arr[Ax]);
     if constexpr (Inplace) {
         check(tadma_b200_layer_norm(&i, Ax, &g, &b, eps, Mode, &i, stream), "tadma layer_norm");
@@ -300,6 +305,7 @@ template <int D, bool Inplace = true, AnyTensor T>
 auto rms_norm(T&& t) {
     using TT = std::decay_t<T>;
     constexpr int Ax = detail::real_dim<D, TT::Rank>;
+    if constexpr (Inplace) detail::sync_write_of(t);
     tadma_tensor i = t.describe();
     if constexpr (Inplace) {
         detail::check(tadma_b200_rms_norm(&i, Ax, 0.0, &i, stream), "tadma rms_norm");
@@ -459,7 +465,7 @@ struct FuseBuilder {
     void push(const fuse::Un& s) { prog.at(n_instr++) = detail::ins(s.op); }
     template <AnyTensor T>
     void push(const fuse::Ten<T>& s) {
-        if (n_ins >= TADMA_MAX_INPUTS) throw std::runtime_error("tadma fused: at most 3 tensor operands");
+        if (n_ins >= TADMA_MAX_INPUTS) throw std::runtime_error("tadma fused: at most 5 tensor operands");
         ins[n_ins] = s.t->template broadcastTo<typename X::Dims>().describe();
         prog.at(n_instr++) = detail::ins(s.op, n_ins++);
     }

@@ -30,6 +30,7 @@
 #include <vector>
 
 #include "Core.hpp"
+#include "Deferred.hpp"
 #include "Sequence.hpp"
 
 namespace tadma {
@@ -53,8 +54,29 @@ concept Element = requires { DTypeOf<T>::value; };
 template <typename T>
 constexpr int dtype_v = DTypeOf<T>::value;
 
+// A scalar operand: an arithmetic value, or a compile-time value holder of the
+// generated code (ConstexprHolder<v>: `x + _LayerNorm_Constant_1_output_0`).
 template <typename T>
-concept Scalar = std::is_arithmetic_v<T>;
+concept HeldScalar = requires {
+    typename T::ValueType;
+    T::value;
+} && std::is_arithmetic_v<typename T::ValueType>;
+template <typename T>
+concept Scalar = std::is_arithmetic_v<T> || HeldScalar<T>;
+
+namespace detail {
+template <typename S>
+struct scalar_type {
+    using type = S;
+};
+template <HeldScalar S>
+struct scalar_type<S> {
+    using type = typename S::ValueType;
+};
+}  // namespace detail
+// The arithmetic type of a scalar operand.
+template <typename S>
+using scalar_t = typename detail::scalar_type<S>::type;
 
 // ------------------------------------------------------- layout algebra --
 
@@ -261,8 +283,20 @@ struct Tensor {
         }
     }
 
-    // The C-ABI descriptor of this view.
+    // The C-ABI descriptor of this view, for a call that reads it: work
+    // deferred into the buffer is enqueued first (Deferred.hpp).
     tadma_tensor describe() const {
+        detail::sync_read(data.ctl);
+        return describe_raw();
+    }
+    // Readable contents: enqueues the work deferred into the buffer.  Needed
+    // before reading `data.view` directly (every API call does this itself).
+    const Tensor& materialize() const {
+        detail::sync_read(data.ctl);
+        return *this;
+    }
+    // The descriptor without synchronising (deferral bookkeeping).
+    tadma_tensor describe_raw() const {
         tadma_tensor d{};
         d.data = static_cast<void*>(data.view);
         d.dtype = dtype_v<T>;
@@ -448,7 +482,7 @@ struct Tensor {
     // ------------------------------------------------------------- copies --
     auto clone() const;
     auto contiguous() const {
-        if constexpr (NormalStrides) return *this;
+        if constexpr (NormalStrides) return materialize();
         else return clone();
     }
     template <Memory NewDevice>
@@ -500,6 +534,7 @@ struct Tensor {
             return data.view[0];
         } else {
             T v;
+            detail::sync_read(data.ctl);
             check_cuda(cudaMemcpyAsync(&v, data.view, sizeof(T), cudaMemcpyDeviceToHost, stream));
             check_cuda(cudaStreamSynchronize(stream));
             return v;
@@ -551,10 +586,15 @@ inline tadma_instr ins(int op, int b = TADMA_SRC_NONE, double imm = 0.0, int rou
 }
 
 // out = chain(ins...) on tadma::stream; every input already has out's dims.
+// out = chain(ins...) on tadma::stream; every input already has out's dims.
+// Deferred (recorded in out's storage, Deferred.hpp) when it can be; else
+// launched now, after the buffers' pending work.
 template <AnyTensor Out, AnyTensor... In>
 void chain(const Out& out, std::initializer_list<tadma_instr> prog, const In&... inputs) {
     static_assert(Out::device == kCUDA && ((In::device == kCUDA) && ...), "tadma ops run on CUDA tensors");
-    tadma_tensor o = out.describe();
+    if (defer_eltwise(out, prog, inputs...)) return;
+    sync_write(out.data.ctl);
+    tadma_tensor o = out.describe_raw();
     std::array<tadma_tensor, sizeof...(In) + 1> arr{inputs.describe()..., tadma_tensor{}};
     check(tadma_b200_eltwise(&o, arr.data(), (int32_t)sizeof...(In), prog.begin(), (int32_t)prog.size(),
                              TADMA_COMPUTE_AUTO, stream),
@@ -580,6 +620,8 @@ void Tensor<T, A, D, S>::copyTo(U& other) const {
     } else if constexpr (U::NormalStrides && NormalStrides && std::is_same_v<UT, T>) {
         cudaMemcpyKind kind = device == kCPU ? (U::device == kCPU ? cudaMemcpyHostToHost : cudaMemcpyHostToDevice)
                                              : cudaMemcpyDeviceToHost;
+        detail::sync_read(data.ctl);
+        detail::sync_write(other.data.ctl);
         check_cuda(cudaMemcpyAsync(other.data.view, data.view, Size * sizeof(T), kind, stream));
     } else if constexpr (device == kCUDA) {
         auto tmp = this->template to<UT>().contiguous();

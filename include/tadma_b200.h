@@ -144,10 +144,16 @@ enum tadma_compute {
     TADMA_COMPUTE_AUTO = -1, /* F64 if any operand is f64/i64 and no float op needs F32, else F32 */
     TADMA_COMPUTE_F32 = 0,
     TADMA_COMPUTE_F64 = 1,
-    TADMA_COMPUTE_I64 = 2
+    TADMA_COMPUTE_I64 = 2,
+    /* fp32 without the fast-math bodies: an fp32 chain with a 16-bit output
+     * otherwise evaluates exp / sigmoid / gelu with the SFU exponential and
+     * reciprocal (error far below half a 16-bit ulp); this mode keeps the
+     * precise bodies, as a chain whose transcendental steps each round to fp32
+     * needs to equal those steps made as separate calls */
+    TADMA_COMPUTE_F32_PRECISE = 3
 };
 
-#define TADMA_MAX_INPUTS 4
+#define TADMA_MAX_INPUTS 6
 #define TADMA_MAX_INSTR 16
 
 /*
@@ -211,11 +217,28 @@ int tadma_b200_reduce(int32_t op, const tadma_tensor* in, int32_t axis, int32_t 
  * Replaces: an EltwiseNode / CombineToNode chain feeding a ReduceNode
  * (Kernels.hpp:20-45 -> kernels/Reduce.hpp:10-71), i.e. the ReduceKernel
  * pre-functor (Reduce.hpp:29-56) generalised from one unary op to a chain
- * over up to 4 broadcast operands; e.g. sum<-1>(exp(A + b)) in one launch.
+ * over up to 6 broadcast operands; e.g. sum<-1>(exp(A + b)) in one launch.
  */
 int tadma_b200_reduce_chain(int32_t op, const tadma_tensor* ins, int32_t n_ins, const tadma_instr* prog,
                             int32_t n_instr, int32_t compute, int32_t axis, const tadma_tensor* out,
                             void* stream);
+
+/*
+ * tadma_b200_reduce_chain followed by a chain on each reduced value:
+ * out = post(reduce(chain(ins...))).  `post` holds up to TADMA_MAX_INSTR
+ * instructions whose operands are immediates (b / c = TADMA_SRC_IMM or
+ * TADMA_SRC_NONE); it runs in the compute type on the value the reduction
+ * would store (after MEAN's division / RMS's square root), each instruction
+ * rounding to its round_dtype, then the result is stored to out->dtype.  Not
+ * for ARGMAX / ARGMIN.  One kernel: a variance and the + eps and sqrt that
+ * make it a layer_norm denominator never round-trip through HBM.
+ * Replaces: ReduceKernel's post functor (kernels/Reduce.hpp:29-56, the sqrt
+ * post of layer_norm's standard deviation, Operations.hpp:195-203),
+ * generalised to a chain, plus the eager nodes that follow a reduction.
+ */
+int tadma_b200_reduce_chain_post(int32_t op, const tadma_tensor* ins, int32_t n_ins, const tadma_instr* prog,
+                                 int32_t n_instr, const tadma_instr* post, int32_t n_post, int32_t compute,
+                                 int32_t axis, const tadma_tensor* out, void* stream);
 
 /*
  * tadma_b200_reduce without any device allocation.  No counterpart in the

@@ -419,6 +419,7 @@ static double unary_d(int32_t op, double x) {
 
 static int resolve_compute(const tadma_tensor* out, const tadma_tensor* ins, int32_t n_ins,
                            const tadma_instr* prog, int32_t n_instr, int32_t compute) {
+    if (compute == TADMA_COMPUTE_F32_PRECISE) return TADMA_COMPUTE_F32; /* the oracle has no fast-math bodies */
     if (compute != TADMA_COMPUTE_AUTO) return compute;
     int all_int = !is_float_dt(out->dtype), any_wide = out->dtype == TADMA_F64 || out->dtype == TADMA_I64;
     for (int k = 0; k < n_ins; k++) {

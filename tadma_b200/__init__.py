@@ -26,7 +26,7 @@ EXPORTS = (
     "tadma_b200_eltwise", "tadma_b200_reduce", "tadma_b200_softmax", "tadma_b200_layer_norm",
     "tadma_b200_rms_norm", "tadma_b200_gather", "tadma_b200_fill", "tadma_b200_last_error",
     "tadma_b200_version", "tadma_b200_error_flags", "tadma_b200_dtype_size", "tadma_b200_reduce_noalloc",
-    "tadma_b200_reduce_chain",
+    "tadma_b200_reduce_chain", "tadma_b200_reduce_chain_post",
 )
 
 
@@ -53,6 +53,8 @@ def lib() -> ctypes.CDLL:
     L.tadma_b200_reduce.argtypes = [c_int, P(T), c_int, c_int, P(T), c_void]
     L.tadma_b200_reduce_noalloc.argtypes = [c_int, P(T), c_int, c_int, P(T), c_void]
     L.tadma_b200_reduce_chain.argtypes = [c_int, P(T), c_int, P(I), c_int, c_int, c_int, P(T), c_void]
+    L.tadma_b200_reduce_chain_post.argtypes = [c_int, P(T), c_int, P(I), c_int, P(I), c_int, c_int, c_int, P(T),
+                                               c_void]
     L.tadma_b200_softmax.argtypes = [P(T), c_int, P(T), c_void]
     L.tadma_b200_layer_norm.argtypes = [P(T), c_int, P(T), P(T), c_double, c_int, P(T), c_void]
     L.tadma_b200_rms_norm.argtypes = [P(T), c_int, c_double, P(T), c_void]
@@ -152,11 +154,17 @@ def prepare_reduce(op, x, axis, out, pre_op=Op.COPY, stream=None) -> Prepared:
                                               _stream(stream)), (i, o))
 
 
-def prepare_reduce_chain(op, ins, prog, axis, out, compute=Compute.AUTO, stream=None) -> Prepared:
-    """out = reduce `op` over `axis` of chain(ins...) in one kernel (tadma_b200_reduce_chain)."""
+def prepare_reduce_chain(op, ins, prog, axis, out, compute=Compute.AUTO, stream=None, post=None) -> Prepared:
+    """out = reduce `op` over `axis` of chain(ins...) in one kernel (tadma_b200_reduce_chain); with `post`
+    (instructions with immediate operands), out = post(reduce(...)) (tadma_b200_reduce_chain_post)."""
     arr = (TadmaTensor * max(1, len(ins)))(*[_d(x) for x in ins])
     p, n = program(prog)
     o = _d(out)
+    if post:
+        q, m = program(post)
+        return Prepared(lib().tadma_b200_reduce_chain_post, (int(op), arr, len(ins), p, n, q, m, int(compute),
+                                                             int(axis), ctypes.byref(o), _stream(stream)),
+                        (arr, p, q, o))
     return Prepared(lib().tadma_b200_reduce_chain, (int(op), arr, len(ins), p, n, int(compute), int(axis),
                                                     ctypes.byref(o), _stream(stream)), (arr, p, o))
 
@@ -202,8 +210,8 @@ def reduce(op, x, axis, out, pre_op=Op.COPY, stream=None) -> None:
     prepare_reduce(op, x, axis, out, pre_op, stream)()
 
 
-def reduce_chain(op, ins, prog, axis, out, compute=Compute.AUTO, stream=None) -> None:
-    prepare_reduce_chain(op, ins, prog, axis, out, compute, stream)()
+def reduce_chain(op, ins, prog, axis, out, compute=Compute.AUTO, stream=None, post=None) -> None:
+    prepare_reduce_chain(op, ins, prog, axis, out, compute, stream, post)()
 
 
 def softmax(x, axis, out, stream=None) -> None:

@@ -12,7 +12,7 @@ import enum
 import numpy as np
 
 MAX_RANK = 8
-MAX_INPUTS = 4
+MAX_INPUTS = 6
 MAX_INSTR = 16
 SRC_IMM = -1
 SRC_NONE = -2
@@ -88,6 +88,7 @@ class Compute(enum.IntEnum):
     F32 = 0
     F64 = 1
     I64 = 2
+    F32_PRECISE = 3
 
 
 class Reduce(enum.IntEnum):

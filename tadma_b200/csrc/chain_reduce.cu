@@ -8,7 +8,7 @@ namespace {
 // ------------------------------------------------------ chain reduction --
 //
 // tadma_b200_reduce_chain: a reduction whose elements are a fused chain of
-// up to 4 broadcast operands, evaluated on the fly.  One warp per output
+// up to 6 broadcast operands, evaluated on the fly.  One warp per output
 // element (the kept dims, folded); its lanes walk the reduced axis.  With the
 // axis contiguous (stride 1) or broadcast (stride 0) in every operand and
 // fp32 compute, lanes take 8 elements per step with 16-byte loads (the
@@ -43,13 +43,13 @@ __device__ __forceinline__ void cvt_raw_vec(int dt, const RawV& r, C (&v)[V]) {
 
 
 template <typename C, int K, bool VEC, int NIN>
-__global__ void __launch_bounds__(THREADS, !VEC ? 2 : NIN == 1 ? 3 : 2) chain_reduce_kernel(const __grid_constant__ ChainReduceParams p) {
+__global__ void __launch_bounds__(THREADS, !VEC ? 2 : NIN == 1 ? 3 : NIN <= 4 ? 2 : 1) chain_reduce_kernel(const __grid_constant__ ChainReduceParams p) {
     pdl_begin();
     const int lane = threadIdx.x & 31;
     const int64_t gw = ((int64_t)blockIdx.x * THREADS + threadIdx.x) >> 5;
     const int64_t nw = ((int64_t)gridDim.x * THREADS) >> 5;
     for (int64_t row = gw; row < p.nrows; row += nw) {
-        int64_t base[TADMA_MAX_INPUTS] = {0, 0, 0, 0};
+        int64_t base[TADMA_MAX_INPUTS] = {};
         int64_t ooff = 0;
         {
             uint64_t e = (uint64_t)row;
@@ -134,9 +134,158 @@ __global__ void __launch_bounds__(THREADS, !VEC ? 2 : NIN == 1 ? 3 : 2) chain_re
                 } else {
                     if (p.post == POST_MEAN) v = v / p.R;
                 }
+                if (p.pc.n) v = apply_post<C>(p.pc, v);
                 store_from(p.out, p.out_dtype, ooff, v);
             }
         }
+    }
+}
+
+// Typed vector path (fp32 compute): every operand either streams along the
+// reduced axis (stride 1, one dtype T for all of them, 16-byte aligned rows)
+// or is broadcast along it (one value per output, loaded once).  Lanes take
+// 16-byte vectors of T (4 fp32 or 8 16-bit values) and keep UNR of them in
+// flight per streamed operand before the first one is folded, four times
+// the bytes in flight of the double-buffered path above; the chain runs on
+// the N values of a vector at once.
+template <int NIN>
+constexpr int typed_unr() { return NIN <= 2 ? 4 : NIN <= 4 ? 2 : 1; }
+
+template <typename T>
+__device__ __forceinline__ void cvt_typed(uint4 r, float (&f)[16 / sizeof(T)]) {
+    if constexpr (sizeof(T) == 4) {
+        f[0] = __uint_as_float(r.x);
+        f[1] = __uint_as_float(r.y);
+        f[2] = __uint_as_float(r.z);
+        f[3] = __uint_as_float(r.w);
+    } else {
+        unpack8(r, std::is_same<T, __half>::value ? TADMA_F16 : TADMA_BF16, f);
+    }
+}
+
+template <typename T, int K, int NIN>
+__global__ void __launch_bounds__(THREADS) chain_reduce_typed_kernel(const __grid_constant__ ChainReduceParams p) {
+    pdl_begin();
+    constexpr int N = 16 / (int)sizeof(T);
+    constexpr int UNR = typed_unr<NIN>();
+    const int lane = threadIdx.x & 31;
+    const int64_t gw = ((int64_t)blockIdx.x * THREADS + threadIdx.x) >> 5;
+    const int64_t nw = ((int64_t)gridDim.x * THREADS) >> 5;
+    for (int64_t row = gw; row < p.nrows; row += nw) {
+        int64_t base[NIN];
+        int64_t ooff = 0;
+#pragma unroll
+        for (int k = 0; k < NIN; k++) base[k] = 0;
+        {
+            uint64_t e = (uint64_t)row;
+            for (int d = p.krank - 1; d >= 0; d--) {
+                uint64_t q, r;
+                if (d > 0) {
+                    p.kdm[d].divmod(e, q, r);
+                } else {
+                    r = e;
+                    q = 0;
+                }
+                ooff += (int64_t)r * p.kout[d];
+#pragma unroll
+                for (int k = 0; k < NIN; k++) base[k] += (int64_t)r * p.kin[k][d];
+                e = q;
+            }
+        }
+        float bc[NIN];
+#pragma unroll
+        for (int k = 0; k < NIN; k++)
+            bc[k] = p.ax[k] == 0 ? load_as<float>(p.chain.in[k].base, p.chain.in[k].dtype, base[k]) : 0.0f;
+        State<float> s = init_state<K, float>();
+        const int64_t nv = p.R / N;
+        for (int64_t i0 = lane; i0 < nv; i0 += 32 * UNR) {
+            uint4 raw[UNR][NIN];
+#pragma unroll
+            for (int u = 0; u < UNR; u++) {
+                if (i0 + 32 * u < nv) {
+#pragma unroll
+                    for (int k = 0; k < NIN; k++)
+                        if (p.ax[k] != 0)
+                            raw[u][k] = ld_stream_v4(reinterpret_cast<const T*>(p.chain.in[k].base) + base[k] + (i0 + 32 * u) * N);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < UNR; u++) {
+                if (i0 + 32 * u < nv) {
+                    float val[NIN][N];
+#pragma unroll
+                    for (int k = 0; k < NIN; k++) {
+                        if (p.ax[k] == 0) {
+#pragma unroll
+                            for (int j = 0; j < N; j++) val[k][j] = bc[k];
+                        } else {
+                            cvt_typed<T>(raw[u][k], val[k]);
+                        }
+                    }
+                    float acc[N];
+#pragma unroll
+                    for (int j = 0; j < N; j++) acc[j] = val[0][j];
+                    run_chain<float, NIN, N, false>(p.chain, acc, val);
+                    const int64_t e0 = (i0 + 32 * u) * N;
+#pragma unroll
+                    for (int j = 0; j < N; j++) update<K, float>(s, p.square ? acc[j] * acc[j] : acc[j], e0 + j);
+                }
+            }
+        }
+        for (int64_t r = nv * N + lane; r < p.R; r += 32) {
+            float val[NIN][1];
+#pragma unroll
+            for (int k = 0; k < NIN; k++) val[k][0] = load_as<float>(p.chain.in[k].base, p.chain.in[k].dtype, base[k] + r * p.ax[k]);
+            float acc[1] = {val[0][0]};
+            run_chain<float, NIN, 1, false>(p.chain, acc, val);
+            update<K, float>(s, p.square ? acc[0] * acc[0] : acc[0], r);
+        }
+        s = warp_combine<K, float>(s);
+        if (lane == 0) {
+            if constexpr (K == K_ARGMAX || K == K_ARGMIN) {
+                store_from(p.out, p.out_dtype, ooff, (int64_t)(s.i < 0 ? 0 : s.i));
+            } else {
+                float v = s.v;
+                if (p.post == POST_MEAN) v = v / (float)p.R;
+                else if (p.post == POST_RMS) v = sqrtf(v / (float)p.R);
+                if (p.pc.n) v = apply_post<float>(p.pc, v);
+                store_from(p.out, p.out_dtype, ooff, v);
+            }
+        }
+    }
+}
+
+template <typename T, int K, int NIN>
+int launch_typed_k(const ChainReduceParams& p, cudaStream_t s) {
+    const void* fn = (const void*)chain_reduce_typed_kernel<T, K, NIN>;
+    const int64_t want = (p.nrows + (THREADS / 32) - 1) / (THREADS / 32);
+    const int64_t cap = (int64_t)sm_count() * blocks_per_sm(fn);
+    const int grid = (int)(want < cap ? (want > 0 ? want : 1) : cap);
+    cudaError_t e = launch_pdl(chain_reduce_typed_kernel<T, K, NIN>, dim3(grid), dim3(THREADS), 0, s, p);
+    if (e == cudaSuccess) e = cudaGetLastError();
+    return e == cudaSuccess ? TADMA_OK : cuda_fail(e, "tadma_b200_reduce_chain launch");
+}
+
+template <typename T, int NIN>
+int launch_typed_n(int kind, const ChainReduceParams& p, cudaStream_t s) {
+    switch (kind) {
+    case K_SUM: return launch_typed_k<T, K_SUM, NIN>(p, s);
+    case K_MAX: return launch_typed_k<T, K_MAX, NIN>(p, s);
+    case K_MIN: return launch_typed_k<T, K_MIN, NIN>(p, s);
+    case K_ARGMAX: return launch_typed_k<T, K_ARGMAX, NIN>(p, s);
+    default: return launch_typed_k<T, K_ARGMIN, NIN>(p, s);
+    }
+}
+
+template <typename T>
+int launch_typed_t(int kind, const ChainReduceParams& p, cudaStream_t s) {
+    switch (p.n_ins) {
+    case 1: return launch_typed_n<T, 1>(kind, p, s);
+    case 2: return launch_typed_n<T, 2>(kind, p, s);
+    case 3: return launch_typed_n<T, 3>(kind, p, s);
+    case 4: return launch_typed_n<T, 4>(kind, p, s);
+    case 5: return launch_typed_n<T, 5>(kind, p, s);
+    default: return launch_typed_n<T, 6>(kind, p, s);
     }
 }
 
@@ -173,7 +322,9 @@ int launch_chain_reduce(int kind, const ChainReduceParams& p, cudaStream_t s) {
         case 1: return launch_chain_reduce_n<C, true, 1>(kind, p, s);
         case 2: return launch_chain_reduce_n<C, true, 2>(kind, p, s);
         case 3: return launch_chain_reduce_n<C, true, 3>(kind, p, s);
-        default: return launch_chain_reduce_n<C, true, 4>(kind, p, s);
+        case 4: return launch_chain_reduce_n<C, true, 4>(kind, p, s);
+        case 5: return launch_chain_reduce_n<C, true, 5>(kind, p, s);
+        default: return launch_chain_reduce_n<C, true, 6>(kind, p, s);
         }
     }
 }
@@ -182,6 +333,14 @@ int launch_chain_reduce(int kind, const ChainReduceParams& p, cudaStream_t s) {
 
 int launch_chain_reduce_f32(int kind, bool vec, const ChainReduceParams& p, cudaStream_t s) {
     return vec ? launch_chain_reduce<float, true>(kind, p, s) : launch_chain_reduce<float, false>(kind, p, s);
+}
+
+int launch_chain_reduce_typed(int kind, int dt, const ChainReduceParams& p, cudaStream_t s) {
+    switch (dt) {
+    case TADMA_F32: return launch_typed_t<float>(kind, p, s);
+    case TADMA_F16: return launch_typed_t<__half>(kind, p, s);
+    default: return launch_typed_t<__nv_bfloat16>(kind, p, s);
+    }
 }
 
 int launch_chain_reduce_f64(int kind, const ChainReduceParams& p, cudaStream_t s) {

@@ -155,7 +155,7 @@ extern "C" int tadma_b200_eltwise(const tadma_tensor* out, const tadma_tensor* i
                                   const tadma_instr* prog, int32_t n_instr, int32_t compute, void* stream) {
     std::string err = check_tensor(out, "out");
     if (!err.empty()) return fail(TADMA_ERR_INVALID, err);
-    if (n_ins < 0 || n_ins > TADMA_MAX_INPUTS) return fail(TADMA_ERR_INVALID, "n_ins out of range [0, 4]");
+    if (n_ins < 0 || n_ins > TADMA_MAX_INPUTS) return fail(TADMA_ERR_INVALID, "n_ins out of range [0, 6]");
     if (n_instr < 0 || n_instr > TADMA_MAX_INSTR) return fail(TADMA_ERR_INVALID, "n_instr out of range [0, 16]");
     if (n_ins > 0 && !ins) return fail(TADMA_ERR_INVALID, "ins is NULL");
     if (n_instr > 0 && !prog) return fail(TADMA_ERR_INVALID, "prog is NULL");
@@ -177,7 +177,8 @@ extern "C" int tadma_b200_eltwise(const tadma_tensor* out, const tadma_tensor* i
             return fail(TADMA_ERR_INVALID, "operand selector c out of range");
         if (I.round_dtype >= 0 && dtype_size(I.round_dtype) == 0) return fail(TADMA_ERR_INVALID, "bad round_dtype");
     }
-    int cm = resolve_compute(out, ins, n_ins, prog, n_instr, compute);
+    const bool precise = compute == TADMA_COMPUTE_F32_PRECISE;
+    int cm = precise ? TADMA_COMPUTE_F32 : resolve_compute(out, ins, n_ins, prog, n_instr, compute);
     if (cm < TADMA_COMPUTE_F32 || cm > TADMA_COMPUTE_I64) return fail(TADMA_ERR_INVALID, "bad compute mode");
     if (cm == TADMA_COMPUTE_I64)
         for (int i = 0; i < n_instr; i++)
@@ -259,7 +260,7 @@ extern "C" int tadma_b200_eltwise(const tadma_tensor* out, const tadma_tensor* i
     // Fast math (SFU exp / reciprocal) when an fp32 chain ends in a 16-bit
     // store and every intermediate rounding is to fp32 or coarser: the
     // approximation error is far below the output's half-ulp.
-    bool fast = cm == TADMA_COMPUTE_F32 && (out->dtype == TADMA_F16 || out->dtype == TADMA_BF16);
+    bool fast = !precise && cm == TADMA_COMPUTE_F32 && (out->dtype == TADMA_F16 || out->dtype == TADMA_BF16);
     for (int i = 0; i < n_instr && fast; i++) {
         int rd = prog[i].round_dtype;
         if (!(rd < 0 || rd == TADMA_F32 || rd == TADMA_F16 || rd == TADMA_BF16)) fast = false;
@@ -323,7 +324,8 @@ extern "C" int tadma_b200_eltwise(const tadma_tensor* out, const tadma_tensor* i
     const bool rows_ok = am.ok && am.add && f.rank == 2 && fdt && ins[0].dtype == ins[1].dtype &&
                          (ins[0].dtype == TADMA_F32 || ins[0].dtype == TADMA_F16 || ins[0].dtype == TADMA_BF16) &&
                          (out->dtype == ins[0].dtype || out->dtype == TADMA_F32) && f.strides[2][0] == 0 &&
-                         f.strides[2][1] == 1 && f.strides[1][1] == 1 && f.strides[0][1] == 1 && !p.in[1].inner_bcast;
+                         f.strides[2][1] == 1 && f.strides[1][1] == 1 && f.strides[0][1] == 1 && !p.in[1].inner_bcast &&
+                         !(precise && am.act != ACT_NONE);  // the row kernel's 16-bit activations are the fast bodies
     auto fdt3 = [](int dt) { return dt == TADMA_F32 || dt == TADMA_F16 || dt == TADMA_BF16; };
     bool typed_ok = cm == TADMA_COMPUTE_F32 && (n_ins == 1 || n_ins == 2) && fdt3(out->dtype);
     for (int k = 0; k < n_ins && typed_ok; k++)
@@ -410,12 +412,12 @@ extern "C" int tadma_b200_eltwise(const tadma_tensor* out, const tadma_tensor* i
     return TADMA_OK;
 }
 
-extern "C" int tadma_b200_reduce_chain(int32_t op, const tadma_tensor* ins, int32_t n_ins, const tadma_instr* prog,
-                                       int32_t n_instr, int32_t compute, int32_t axis, const tadma_tensor* out,
-                                       void* stream) {
+static int reduce_chain_impl(int32_t op, const tadma_tensor* ins, int32_t n_ins, const tadma_instr* prog,
+                             int32_t n_instr, const tadma_instr* post, int32_t n_post, int32_t compute, int32_t axis,
+                             const tadma_tensor* out, void* stream) {
     std::string err = check_tensor(out, "out");
     if (!err.empty()) return fail(TADMA_ERR_INVALID, err);
-    if (n_ins < 1 || n_ins > TADMA_MAX_INPUTS) return fail(TADMA_ERR_INVALID, "n_ins out of range [1, 4]");
+    if (n_ins < 1 || n_ins > TADMA_MAX_INPUTS) return fail(TADMA_ERR_INVALID, "n_ins out of range [1, 6]");
     if (n_instr < 0 || n_instr > TADMA_MAX_INSTR) return fail(TADMA_ERR_INVALID, "n_instr out of range [0, 16]");
     if (!ins) return fail(TADMA_ERR_INVALID, "ins is NULL");
     if (n_instr > 0 && !prog) return fail(TADMA_ERR_INVALID, "prog is NULL");
@@ -444,6 +446,16 @@ extern "C" int tadma_b200_reduce_chain(int32_t op, const tadma_tensor* ins, int3
             return fail(TADMA_ERR_INVALID, "operand selector c out of range");
         if (I.round_dtype >= 0 && dtype_size(I.round_dtype) == 0) return fail(TADMA_ERR_INVALID, "bad round_dtype");
     }
+    if (n_post < 0 || n_post > TADMA_MAX_INSTR) return fail(TADMA_ERR_INVALID, "n_post out of range [0, 16]");
+    if (n_post > 0 && !post) return fail(TADMA_ERR_INVALID, "post is NULL");
+    for (int i = 0; i < n_post; i++) {
+        const tadma_instr& I = post[i];
+        if (!valid_op(I.op)) return fail(TADMA_ERR_INVALID, "unknown op code in post");
+        if (I.op == TADMA_OP_WHERE) return fail(TADMA_ERR_INVALID, "post: WHERE needs tensor operands");
+        const bool needs_b = I.op >= 32 || (I.op == TADMA_OP_COPY && I.b == TADMA_SRC_IMM);
+        if (needs_b && I.b != TADMA_SRC_IMM) return fail(TADMA_ERR_INVALID, "post: operands must be immediates");
+        if (I.round_dtype >= 0 && dtype_size(I.round_dtype) == 0) return fail(TADMA_ERR_INVALID, "bad round_dtype in post");
+    }
     const int ax = axis < 0 ? axis + rank : axis;
     if (ax < 0 || ax >= rank) return fail(TADMA_ERR_INVALID, "axis out of range");
     const bool keep = out->rank == rank;
@@ -458,9 +470,11 @@ extern "C" int tadma_b200_reduce_chain(int32_t op, const tadma_tensor* ins, int3
     const bool arg = op == TADMA_REDUCE_ARGMAX || op == TADMA_REDUCE_ARGMIN;
     if (arg && out->dtype != TADMA_I64 && out->dtype != TADMA_I32)
         return fail(TADMA_ERR_INVALID, "argmax/argmin output must be int64 or int32");
+    if (arg && n_post > 0) return fail(TADMA_ERR_INVALID, "argmax/argmin take no post chain");
     // The chain's natural result type decides the compute type, as for a
     // materialised chain (ins[0]'s dtype standing in for the temporary's).
     tadma_tensor chain_out = ins[0];
+    if (compute == TADMA_COMPUTE_F32_PRECISE) compute = TADMA_COMPUTE_F32;  // the reduction has no fast-math bodies
     int cm = resolve_compute(&chain_out, ins, n_ins, prog, n_instr, compute);
     if (cm < TADMA_COMPUTE_F32 || cm > TADMA_COMPUTE_I64) return fail(TADMA_ERR_INVALID, "bad compute mode");
     if (cm == TADMA_COMPUTE_I64)
@@ -477,13 +491,15 @@ extern "C" int tadma_b200_reduce_chain(int32_t op, const tadma_tensor* ins, int3
         RowOpMatch rm = match_rowop(prog, n_instr, ins, n_ins, ax);
         const bool op_sq = op == TADMA_REDUCE_SUMSQ || op == TADMA_REDUCE_RMS;
         if (rm.ok && !(rm.square && op_sq)) {
-            int rc = reduce_rowop(op, S, rank, ax, &ins[0], rm.op1, rm.rop, rm.imm1, rm.pre, rm.square || op_sq, out,
-                                  (cudaStream_t)stream);
+            int rc = reduce_rowop(op, S, rank, ax, &ins[0], rm.op1, rm.rop, rm.imm1, rm.pre, rm.square || op_sq, post,
+                                  n_post, out, (cudaStream_t)stream);
             if (rc != TADMA_ERR_UNSUPPORTED) return rc;
         }
     }
 
     ChainReduceParams p{};
+    p.pc.n = n_post;
+    for (int i = 0; i < n_post; i++) p.pc.prog[i] = post[i];
     p.chain.n_instr = n_instr;
     for (int i = 0; i < n_instr; i++) p.chain.prog[i] = prog[i];
     p.n_ins = n_ins;
@@ -533,10 +549,34 @@ extern "C" int tadma_b200_reduce_chain(int32_t op, const tadma_tensor* ins, int3
         vec = vec && ok;
     }
     cudaStream_t s = (cudaStream_t)stream;
+    if (vec) {
+        // Typed vector path when every streamed operand has one dtype.
+        int sdt = -1;
+        bool one_dt = true;
+        for (int k = 0; k < n_ins; k++) {
+            if (p.ax[k] == 0) continue;
+            if (sdt < 0) sdt = ins[k].dtype;
+            else if (ins[k].dtype != sdt) one_dt = false;
+        }
+        if (one_dt && sdt >= 0 && R >= 16 / dtype_size(sdt)) return launch_chain_reduce_typed(kind, sdt, p, s);
+    }
     switch (cm) {
     case TADMA_COMPUTE_F32:
         return launch_chain_reduce_f32(kind, vec, p, s);
     case TADMA_COMPUTE_F64: return launch_chain_reduce_f64(kind, p, s);
     default: return launch_chain_reduce_i64(kind, p, s);
     }
+}
+
+extern "C" int tadma_b200_reduce_chain(int32_t op, const tadma_tensor* ins, int32_t n_ins, const tadma_instr* prog,
+                                       int32_t n_instr, int32_t compute, int32_t axis, const tadma_tensor* out,
+                                       void* stream) {
+    return reduce_chain_impl(op, ins, n_ins, prog, n_instr, nullptr, 0, compute, axis, out, stream);
+}
+
+extern "C" int tadma_b200_reduce_chain_post(int32_t op, const tadma_tensor* ins, int32_t n_ins,
+                                            const tadma_instr* prog, int32_t n_instr, const tadma_instr* post,
+                                            int32_t n_post, int32_t compute, int32_t axis, const tadma_tensor* out,
+                                            void* stream) {
+    return reduce_chain_impl(op, ins, n_ins, prog, n_instr, post, n_post, compute, axis, out, stream);
 }

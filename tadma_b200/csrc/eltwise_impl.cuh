@@ -38,7 +38,7 @@
 namespace tadma_b200 {
 
 constexpr int V = 8;        // elements per vector step
-// Vector steps in flight per thread: 2, or 1 with 3-4 operands (their
+// Vector steps in flight per thread: 2, or 1 with 3-6 operands (their
 // registers would otherwise halve the resident warps).
 template <int NIN>
 constexpr int vec_steps() { return NIN >= 3 ? 1 : 2; }
@@ -121,6 +121,7 @@ struct ChainReduceParams {
     int64_t kin[TADMA_MAX_INPUTS][TADMA_MAX_RANK];
     int64_t kout[TADMA_MAX_RANK];
     char* out;
+    PostChain pc;  // applied to each reduced value before its store (n = 0: none)
 };
 
 constexpr int POST_NONE = 0, POST_MEAN = 1, POST_RMS = 2;
@@ -140,14 +141,17 @@ int launch_typed(int idt, int odt, int nin, bool fast, const ChainParams& p, int
 int launch_rows(int xdt, int odt, int act, const AffineRowsParams& p, cudaStream_t s);
 int launch_transpose(bool fast, const TransposeParams& tp, cudaStream_t s);
 int launch_chain_reduce_f32(int kind, bool vec, const ChainReduceParams& p, cudaStream_t s);
+// fp32 compute, every operand streamed along the axis with dtype dt (F32 / F16
+// / BF16) or broadcast along it.
+int launch_chain_reduce_typed(int kind, int dt, const ChainReduceParams& p, cudaStream_t s);
 int launch_chain_reduce_f64(int kind, const ChainReduceParams& p, cudaStream_t s);
 int launch_chain_reduce_i64(int kind, const ChainReduceParams& p, cudaStream_t s);
 // reduce.cu: a chain reduction of the form sq(pre(op1(x, m))) with m one value
 // per output row, on the reduction engine's row kernel (TADMA_ERR_UNSUPPORTED
 // when the layout is not its own; nothing recorded then).
 int reduce_rowop(int32_t op, const int64_t* shape, int32_t rank, int32_t ax, const tadma_tensor* in, int32_t op1,
-                 const tadma_tensor* rop, double imm1, int32_t pre_op, int32_t square, const tadma_tensor* out,
-                 cudaStream_t s);
+                 const tadma_tensor* rop, double imm1, int32_t pre_op, int32_t square, const tadma_instr* post,
+                 int32_t n_post, const tadma_tensor* out, cudaStream_t s);
 
 namespace {
 

@@ -1,5 +1,5 @@
 // eltwise_interp_wide.cu - the interpreted chain kernels in fp64 and int64
-// compute, instantiated for 0..4 operands.
+// compute, instantiated for 0..6 operands.
 #include "eltwise_impl.cuh"
 
 namespace tadma_b200 {
@@ -12,7 +12,9 @@ int launch_wide(int nin, const ChainParams& p, bool vec, int64_t work, cudaStrea
     case 1: return launch<C, 1, PROG_INTERP>(p, vec, work, s);
     case 2: return launch<C, 2, PROG_INTERP>(p, vec, work, s);
     case 3: return launch<C, 3, PROG_INTERP>(p, vec, work, s);
-    default: return launch<C, 4, PROG_INTERP>(p, vec, work, s);
+    case 4: return launch<C, 4, PROG_INTERP>(p, vec, work, s);
+    case 5: return launch<C, 5, PROG_INTERP>(p, vec, work, s);
+    default: return launch<C, 6, PROG_INTERP>(p, vec, work, s);
     }
 }
 

@@ -4,6 +4,8 @@
 // op rounds once, as each reference node writes a rounded tensor.
 #pragma once
 
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace tadma_b200 {
@@ -210,6 +212,35 @@ __device__ __forceinline__ int64_t binary(int op, int64_t a, int64_t b, int64_t 
     case TADMA_OP_WHERE: return a != 0 ? b : c;
     }
     return a;
+}
+
+// A reduction's post chain: instructions with immediate operands only,
+// applied to each reduced value before its store -- ReduceKernel's post
+// functor (kernels/Reduce.hpp:29-56; e.g. the + eps and sqrt that turn a
+// variance into layer_norm's denominator, Operations.hpp:195-203) as a chain.
+struct PostChain {
+    int32_t n;
+    int32_t pad;
+    tadma_instr prog[TADMA_MAX_INSTR];
+};
+
+template <typename C>
+__device__ __forceinline__ C post_imm(double v) {
+    if constexpr (std::is_same<C, float>::value) return __double2float_rn(v);
+    else if constexpr (std::is_same<C, double>::value) return v;
+    else return __double2ll_rz(v);
+}
+
+template <typename C>
+__device__ __forceinline__ C apply_post(const PostChain& pc, C v) {
+    for (int i = 0; i < pc.n; i++) {
+        const tadma_instr& I = pc.prog[i];
+        const C imm = post_imm<C>(I.imm);
+        if (I.op < 32) v = I.op == TADMA_OP_COPY ? (I.b == TADMA_SRC_IMM ? imm : v) : unary<false>(I.op, v);
+        else v = binary(I.op, v, imm, imm);
+        if (I.round_dtype >= 0) v = round_to(v, I.round_dtype);
+    }
+    return v;
 }
 
 }  // namespace

@@ -69,6 +69,7 @@ struct RedParams {
     int32_t rop_dtype, op1;
     int64_t rop_row_stride;
     double imm1;
+    PostChain pc;  // applied to each reduced value before its store (n = 0: none)
 };
 
 // Element pre-op (fused unary and/or square).  PRE = false: the call has
@@ -95,6 +96,7 @@ __device__ __forceinline__ void finish(const RedParams& p, const State<A>& s, in
     } else {
         if (p.post == P_MEAN) v = p.R ? v / p.R : 0;  // integer mean (x / Dim(D), Tensor.hpp:448)
     }
+    if (p.pc.n) v = apply_post<A>(p.pc, v);
     store_from(p.out, p.out_dtype, off, v);
 }
 
@@ -854,8 +856,8 @@ namespace tadma_b200 {
 // other layout returns TADMA_ERR_UNSUPPORTED without recording an error, and
 // the caller runs its general kernel instead.
 int reduce_rowop(int32_t op, const int64_t* shape, int32_t rank, int32_t ax, const tadma_tensor* in, int32_t op1,
-                 const tadma_tensor* rop, double imm1, int32_t pre_op, int32_t square, const tadma_tensor* out,
-                 cudaStream_t s) {
+                 const tadma_tensor* rop, double imm1, int32_t pre_op, int32_t square, const tadma_instr* post,
+                 int32_t n_post, const tadma_tensor* out, cudaStream_t s) {
     const int dt = in->dtype;
     if (!(dt == TADMA_F32 || dt == TADMA_F16 || dt == TADMA_BF16)) return TADMA_ERR_UNSUPPORTED;
     const int64_t R = shape[ax];
@@ -908,6 +910,8 @@ int reduce_rowop(int32_t op, const int64_t* shape, int32_t rank, int32_t ax, con
     p.rop_row_stride = rop_rs;
     p.op1 = op1;
     p.imm1 = imm1;
+    p.pc.n = n_post;
+    for (int i = 0; i < n_post; i++) p.pc.prog[i] = post[i];
     plan_row_split(p, R, sm_count());
     if (p.splits > 1) return TADMA_ERR_UNSUPPORTED;  // few long rows: the general kernel's split-free path
     const int es = dtype_size(dt);

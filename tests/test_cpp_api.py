@@ -8,6 +8,12 @@ def test_conformance_program_builds(tmp_path):
     assert exe.endswith("conformance")
 
 
+def test_generated_blocks_program_builds(tmp_path):
+    # generated-code statements with ConstexprHolder operands, deferred evaluation
+    from tests.cpp_build import build_program
+    assert build_program("fusion", str(tmp_path)).endswith("fusion")
+
+
 def test_allocator_fault_injection_throws(tmp_path):
     # TADMA_B200_FAIL_ALLOC=1: the header API's device allocator throws
     # std::runtime_error before calling CUDA (runs without a GPU).

@@ -402,3 +402,31 @@ def test_typed_compare_and_where(dt):
     cu8 = gen(shape, DType.U8, Dist.INDEX, 0, 3, 61)  # 0 -> y, 1 or 2 -> x
     got, ref = run_both(shape, dt, [(cu8, DType.U8), (a, dt), (b, dt)], [instr(Op.WHERE, b=1, c=2)])
     assert np.array_equal(got, ref)
+
+
+@pytest.mark.parametrize("n_ins", [5, 6])
+def test_five_and_six_operand_chains(n_ins):
+    """Chains over up to TADMA_MAX_INPUTS = 6 operands (a LayerNorm with its
+    affine parameters: x, mean, std, gamma, beta), broadcasts included;
+    +, -, *, / round once, so the result is bit-exact against the oracle."""
+    R, C = 96, 1024
+    x = gen((R, C), DType.F32, Dist.NORMAL, 0.0, 1.0, 31)
+    m = gen((R, 1), DType.F32, Dist.NORMAL, 0.0, 0.1, 32)
+    s = gen((R, 1), DType.F32, Dist.UNIFORM, 0.5, 2.0, 33)
+    g = gen((C,), DType.F32, Dist.NORMAL, 1.0, 0.02, 34)
+    b = gen((C,), DType.F32, Dist.NORMAL, 0.0, 0.02, 35)
+    c = gen((R, C), DType.F32, Dist.NORMAL, 0.0, 1.0, 36)
+    ops = [x, m, s, g, b, c][:n_ins]
+    prog = [instr(Op.SUB, b=1), instr(Op.DIV, b=2), instr(Op.MUL, b=3), instr(Op.ADD, b=4)]
+    if n_ins == 6:
+        prog.append(instr(Op.MUL, b=5))
+    views, keep = [], []
+    for a in ops:
+        k, d = dev_view(np.broadcast_to(a, (R, C)), DType.F32)
+        keep.append(k)
+        views.append(d)
+    out = empty_dev((R, C), DType.F32)
+    tb.eltwise(out, views, prog, Compute.F32)
+    ref = np.zeros((R, C), np.float32)
+    assert O.eltwise(ref, [np.broadcast_to(a, (R, C)) for a in ops], prog, Compute.F32) == 0
+    assert np.array_equal(from_dev(out), ref)

@@ -196,3 +196,50 @@ def test_row_operand_chain_reaches_the_row_kernel():
     out = torch.empty((256, 1), dtype=torch.float32, device="cuda")
     names = kernels_of(lambda: tb.reduce_chain(Reduce.MEAN, [x, mv], ROWOP_PROGS["variance"], -1, out, Compute.F32))
     assert "reduce_rowop_kernel" in names, names
+
+
+POST = [instr(Op.ADD, b=SRC_IMM, imm=1e-5, round_dtype=DType.F32), instr(Op.SQRT, round_dtype=DType.F32)]
+
+
+@pytest.mark.parametrize("name,axis", [("variance", -1), ("plain", -1), ("ratio_abs", -1), ("plain", 0)])
+@pytest.mark.parametrize("op", [Reduce.SUM, Reduce.MEAN, Reduce.MAX, Reduce.RMS])
+def test_post_chain(name, axis, op):
+    """out = post(reduce(chain)): sqrt(reduced + 1e-5) applied before the
+    store, in the row-operand kernel (last axis) and the general kernel
+    (axis 0); the oracle applies the same post chain to its reduction."""
+    prog = ROWOP_PROGS[name]
+    x = gen((37, 1000), DType.F32, Dist.UNIFORM, 0.0, 2.0, 15)
+    ins, dts = [x], [DType.F32]
+    if any(i.b == 1 for i in prog):
+        ins.append(gen((37, 1), DType.F32, Dist.NORMAL, 0.5, 0.3, 16))
+        dts.append(DType.F32)
+    shape = x.shape
+    ax = axis % 2
+    oshape = tuple(1 if d == ax else s for d, s in enumerate(shape))
+    keep_alive, devs = [], []
+    for a, dt in zip(ins, dts):
+        k, d = dev_view(np.broadcast_to(a, shape), dt)
+        keep_alive.append(k)
+        devs.append(d)
+    out = empty_dev(oshape, DType.F32)
+    tb.reduce_chain(op, devs, prog, axis, out, Compute.F32, post=POST)
+    tmp = np.zeros(shape, np.float32)
+    assert O.eltwise(tmp, [np.broadcast_to(a, shape) for a in ins], prog, Compute.F32, out_dtype=DType.F32,
+                     in_dtypes=dts) == 0
+    red = np.zeros(oshape, np.float32)
+    assert O.reduce(op, tmp, axis, red) == 0
+    ref = np.zeros_like(red)
+    assert O.eltwise(ref, [red], POST, Compute.F32) == 0
+    got = from_dev(out)
+    if op == Reduce.MAX:
+        assert np.array_equal(got, ref)
+    else:
+        # the reduction's tolerance, halved by the square root
+        assert np.all(np.abs(got.astype(np.float64) / ref - 1) <= 1e-5 * np.sqrt(shape[ax])), (op, name)
+
+
+def test_post_chain_rejected_for_arg_ops():
+    x = empty_dev((4, 64), DType.F32)
+    out = empty_dev((4,), DType.I64)
+    with pytest.raises(Exception):
+        tb.reduce_chain(Reduce.ARGMAX, [x], [], -1, out, Compute.F32, post=POST)
