@@ -1,7 +1,8 @@
 // refalgo.cu - "reference algorithm, restated": TADMA's own GPU kernels as
 // they would run on this B200, for timing next to tadma_b200.  NOT the product
-// and NOT the oracle; only bench.py (its reference_gpu_restated object)
-// launches it.
+// and NOT the oracle; bench.py (its reference_gpu_restated object) launches
+// it, and tests/test_reference_order_gpu.py checks the oracle's
+// reference-order reduction against its ReduceKernel.
 //
 // The reference (OgnianM/TADMA) cannot be compiled here (C++23 / clang >= 19),
 // so its three kernels are restated with their exact launch geometry and
@@ -225,6 +226,25 @@ int ref_cfg5_b64(const void* table, const void* ids, const void* pos, void* g, v
     exec2<B * S, D>([=] __device__(int64_t r, int64_t d) {
         op[r * D + d] = __half2float(gp[r * D + d]) + __bfloat162float(pp[(r % S) * D + d]);
     }, s);
+    return (int)cudaGetLastError();
+}
+
+// A row reduction through ReduceKernel alone, for the parity test of the
+// oracle's reference-order mode: x [rows, R] contiguous, fp32 (dtype 0) or
+// fp16 (dtype 1, accumulated in fp16); op 0 sum, 1 max, 2 mean.
+int ref_reduce_rows(const void* x, int dtype, void* out, int64_t rows, int64_t R, int op, void* stream) {
+    cudaStream_t s = (cudaStream_t)stream;
+#define TADMA_REF_ROWS(T, OPC) reduce<T, T, OPC>((const T*)x, (T*)out, rows, R, 1, rows, R, 0, 1, 0, nullptr, 0, s)
+    if (dtype == 0) {
+        if (op == 0) TADMA_REF_ROWS(float, 0);
+        else if (op == 1) TADMA_REF_ROWS(float, 1);
+        else TADMA_REF_ROWS(float, 2);
+    } else {
+        if (op == 0) TADMA_REF_ROWS(__half, 0);
+        else if (op == 1) TADMA_REF_ROWS(__half, 1);
+        else TADMA_REF_ROWS(__half, 2);
+    }
+#undef TADMA_REF_ROWS
     return (int)cudaGetLastError();
 }
 

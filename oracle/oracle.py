@@ -62,6 +62,8 @@ def lib() -> ctypes.CDLL:
     L.or_cfg4_layer_norm_f16.argtypes = [vp, vp, vp, c_double, vp, c_i64, c_i64]
     L.or_cfg4_softmax_f16.argtypes = [vp, vp, c_i64, c_i64]
     L.or_cfg5_gather_add.argtypes = [vp, c_i64, vp, vp, vp, c_i64, c_i64, c_i64]
+    L.or_reduce_rows_reference_order.argtypes = [c_int, vp, c_int, c_i64, c_i64, vp]
+    L.or_reduce_rows_reference_order.restype = c_int
     L.or_num_threads.restype = c_int
     L.or_set_num_threads.argtypes = [c_int]
     for name in ("or_eltwise", "or_reduce", "or_softmax", "or_layer_norm", "or_rms_norm", "or_gather", "or_fill"):
@@ -94,6 +96,19 @@ def eltwise(out: np.ndarray, ins, prog, compute=Compute.AUTO, out_dtype=None, in
 def reduce(op, x, axis, out, pre_op=Op.COPY, x_dtype=None, out_dtype=None) -> int:
     return lib().or_reduce(int(op), ctypes.byref(_t(x, x_dtype)), int(axis), int(pre_op),
                            ctypes.byref(_t(out, out_dtype)))
+
+
+def reduce_rows_reference_order(op: int, x: np.ndarray, dtype: int) -> np.ndarray:
+    """Row reductions of a 2-D array in the reference's ReduceKernel fold
+    order and accumulator type (op 0 sum, 1 max, 2 mean; dtype F32 or F16,
+    fp16 given as np.float16)."""
+    x = np.ascontiguousarray(x)
+    rows, R = x.shape
+    out = np.zeros(rows, dtype=x.dtype)
+    rc = lib().or_reduce_rows_reference_order(int(op), x.ctypes.data, int(dtype), rows, R, out.ctypes.data)
+    if rc != 0:
+        raise ValueError("unsupported dtype or op")
+    return out
 
 
 def softmax(x, axis, out, dtype=None) -> int:

@@ -856,6 +856,49 @@ void or_cfg3_mean_midaxis_f32(const float* x, float* y, int64_t outer, int64_t R
     }
 }
 
+/* The reference's own fold order and accumulator type for a reduction over
+ * rows (include/tadma/kernels/Reduce.hpp:10-55, ReduceNode :58-69): Threads =
+ * min(1024, floor_pow2(R)); thread t folds elements t, t + Threads, ... in
+ * increasing order; then a shared-memory tree halves the partials (partial t
+ * += partial t + i for i = Threads / 2 .. 1).  The accumulator is decltype(a
+ * + b) of the element type: fp32 for fp32, fp16 for fp16 (every fp16 add
+ * rounds once to fp16, as __hadd does; the exact sum of two fp16 values fits
+ * a double).  op: 0 sum, 1 max (std::max: a < b ? b : a, so a NaN survives
+ * only where it lands in the accumulator), 2 mean (the sum divided by R in
+ * the accumulator type, Tensor.hpp:448).  dtype TADMA_F32 or TADMA_F16;
+ * R >= 1.  Returns 0, or -1 for an unsupported dtype / op. */
+static double ref_acc_add(double a, double b, int32_t dt) {
+    return dt == TADMA_F16 ? (double)or_f16_to_f32(or_f64_to_f16(a + b)) : (double)(float)((float)a + (float)b);
+}
+static double ref_acc_max(double a, double b) { return a < b ? b : a; }
+int or_reduce_rows_reference_order(int32_t op, const void* x, int32_t dtype, int64_t rows, int64_t R, void* out) {
+    if ((dtype != TADMA_F32 && dtype != TADMA_F16) || op < 0 || op > 2 || R < 1) return -1;
+    int64_t th = 1;
+    while (th * 2 <= R && th < 1024) th *= 2;
+#pragma omp parallel for schedule(static)
+    for (int64_t r = 0; r < rows; r++) {
+        double part[1024];
+        for (int64_t t = 0; t < th; t++) {
+            double v = ld(x, dtype, r * R + t);
+            for (int64_t i = t + th; i < R; i += th) {
+                double e = ld(x, dtype, r * R + i);
+                v = op == 1 ? ref_acc_max(v, e) : ref_acc_add(v, e, dtype);
+            }
+            part[t] = v;
+        }
+        for (int64_t i = th / 2; i > 0; i /= 2)
+            for (int64_t t = 0; t < i; t++)
+                part[t] = op == 1 ? ref_acc_max(part[t], part[t + i]) : ref_acc_add(part[t], part[t + i], dtype);
+        double v = part[0];
+        if (op == 2) {
+            v = dtype == TADMA_F16 ? (double)or_f16_to_f32(or_f64_to_f16(v / (double)or_f16_to_f32(or_f64_to_f16((double)R))))
+                                   : (double)((float)v / (float)R);
+        }
+        st(out, dtype, r, v);
+    }
+    return 0;
+}
+
 void or_cfg4_layer_norm_f16(const uint16_t* x, const uint16_t* g, const uint16_t* b, double eps,
                             uint16_t* y, int64_t rows, int64_t cols) {
 #pragma omp parallel for schedule(static)

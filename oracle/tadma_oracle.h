@@ -58,6 +58,9 @@ int or_gather(const tadma_tensor* table, int32_t axis, const tadma_tensor* ids,
 /* straightforward per-config host loops (the timed CPU baseline), OpenMP over rows */
 void or_cfg2_gelu_affine_bf16(const uint16_t* x, const uint16_t* bias, float s, uint16_t* y,
                               int64_t rows, int64_t cols);
+/* Row reductions in the reference's own ReduceKernel fold order and
+ * accumulator type (fp32, or fp16 in fp16): op 0 sum, 1 max, 2 mean. */
+int or_reduce_rows_reference_order(int32_t op, const void* x, int32_t dtype, int64_t rows, int64_t R, void* out);
 void or_cfg3_sum_lastaxis_f32(const float* x, float* y, int64_t rows, int64_t cols);
 void or_cfg3_max_lastaxis_f32(const float* x, float* y, int64_t rows, int64_t cols);
 void or_cfg3_argmax_lastaxis_f32(const float* x, int64_t* y, int64_t rows, int64_t cols);

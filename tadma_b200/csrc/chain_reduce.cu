@@ -144,15 +144,22 @@ __global__ void __launch_bounds__(THREADS, !VEC ? 2 : NIN == 1 ? 3 : NIN <= 4 ? 
 // Typed vector path (fp32 compute): every operand either streams along the
 // reduced axis (stride 1, one dtype T for all of them, 16-byte aligned rows)
 // or is broadcast along it (one value per output, loaded once).  Lanes take
-// 16-byte vectors of T (4 fp32 or 8 16-bit values) and keep UNR of them in
-// flight per streamed operand before the first one is folded, four times
-// the bytes in flight of the double-buffered path above; the chain runs on
-// the N values of a vector at once.
-template <int NIN>
-constexpr int typed_unr() { return NIN <= 2 ? 4 : NIN <= 4 ? 2 : 1; }
+// 16-byte vectors of T (4 fp32 or 8 16-bit values): UNR of them per streamed
+// operand are loaded before any is used (64 bytes per operand in flight per
+// lane with one or two operands), then a rolled loop runs the pre-decoded
+// program on G vectors at a time (W = G x N = 8 values per step with up to
+// four operands) and shifts the next G down.  Values fold in increasing
+// index order.
+template <typename T, int NIN>
+struct TypedShape {
+    static constexpr int N = 16 / (int)sizeof(T);
+    static constexpr int UNR = NIN <= 2 ? 4 : NIN <= 4 ? 2 : (sizeof(T) == 4 ? 2 : 1);
+    static constexpr int G = sizeof(T) == 4 && NIN <= 4 ? 2 : 1;
+    static constexpr int W = G * N;
+};
 
 template <typename T>
-__device__ __forceinline__ void cvt_typed(uint4 r, float (&f)[16 / sizeof(T)]) {
+__device__ __forceinline__ void cvt_typed(uint4 r, float* f) {
     if constexpr (sizeof(T) == 4) {
         f[0] = __uint_as_float(r.x);
         f[1] = __uint_as_float(r.y);
@@ -164,10 +171,10 @@ __device__ __forceinline__ void cvt_typed(uint4 r, float (&f)[16 / sizeof(T)]) {
 }
 
 template <typename T, int K, int NIN>
-__global__ void __launch_bounds__(THREADS) chain_reduce_typed_kernel(const __grid_constant__ ChainReduceParams p) {
+__global__ void __launch_bounds__(THREADS, NIN == 1 ? 3 : 2) chain_reduce_typed_kernel(const __grid_constant__ ChainReduceParams p) {
     pdl_begin();
-    constexpr int N = 16 / (int)sizeof(T);
-    constexpr int UNR = typed_unr<NIN>();
+    using S = TypedShape<T, NIN>;
+    constexpr int N = S::N, UNR = S::UNR, G = S::G, W = S::W;
     const int lane = threadIdx.x & 31;
     const int64_t gw = ((int64_t)blockIdx.x * THREADS + threadIdx.x) >> 5;
     const int64_t nw = ((int64_t)gridDim.x * THREADS) >> 5;
@@ -199,37 +206,54 @@ __global__ void __launch_bounds__(THREADS) chain_reduce_typed_kernel(const __gri
         State<float> s = init_state<K, float>();
         const int64_t nv = p.R / N;
         for (int64_t i0 = lane; i0 < nv; i0 += 32 * UNR) {
+            // Vectors i0, i0 + 32, ..., i0 + 32 (UNR - 1) of every streamed
+            // operand (zeros past the row's last vector).
             uint4 raw[UNR][NIN];
 #pragma unroll
             for (int u = 0; u < UNR; u++) {
-                if (i0 + 32 * u < nv) {
 #pragma unroll
-                    for (int k = 0; k < NIN; k++)
-                        if (p.ax[k] != 0)
-                            raw[u][k] = ld_stream_v4(reinterpret_cast<const T*>(p.chain.in[k].base) + base[k] + (i0 + 32 * u) * N);
+                for (int k = 0; k < NIN; k++) {
+                    if (p.ax[k] != 0 && i0 + 32 * u < nv)
+                        raw[u][k] = ld_stream_v4(reinterpret_cast<const T*>(p.chain.in[k].base) + base[k] + (i0 + 32 * u) * N);
+                    else
+                        raw[u][k] = make_uint4(0u, 0u, 0u, 0u);
                 }
             }
+#pragma unroll 1
+            for (int h = 0; h < UNR / G; h++) {
+                float val[NIN][W];
 #pragma unroll
-            for (int u = 0; u < UNR; u++) {
-                if (i0 + 32 * u < nv) {
-                    float val[NIN][N];
+                for (int k = 0; k < NIN; k++) {
 #pragma unroll
-                    for (int k = 0; k < NIN; k++) {
+                    for (int g = 0; g < G; g++) {
                         if (p.ax[k] == 0) {
 #pragma unroll
-                            for (int j = 0; j < N; j++) val[k][j] = bc[k];
+                            for (int j = 0; j < N; j++) val[k][g * N + j] = bc[k];
                         } else {
-                            cvt_typed<T>(raw[u][k], val[k]);
+                            cvt_typed<T>(raw[g][k], &val[k][g * N]);
                         }
                     }
-                    float acc[N];
-#pragma unroll
-                    for (int j = 0; j < N; j++) acc[j] = val[0][j];
-                    run_chain<float, NIN, N, false>(p.chain, acc, val);
-                    const int64_t e0 = (i0 + 32 * u) * N;
-#pragma unroll
-                    for (int j = 0; j < N; j++) update<K, float>(s, p.square ? acc[j] * acc[j] : acc[j], e0 + j);
                 }
+                float acc[W];
+#pragma unroll
+                for (int j = 0; j < W; j++) acc[j] = val[0][j];
+                run_fprog<NIN, W, false>(p.chain.fp, acc, val);
+#pragma unroll
+                for (int g = 0; g < G; g++) {
+                    const int64_t vg = i0 + 32 * (h * G + g);
+                    if (vg < nv) {
+#pragma unroll
+                        for (int j = 0; j < N; j++) {
+                            const float a = acc[g * N + j];
+                            update<K, float>(s, p.square ? a * a : a, vg * N + j);
+                        }
+                    }
+                }
+                // the next G vectors move to the front
+#pragma unroll
+                for (int u = 0; u + G < UNR; u++)
+#pragma unroll
+                    for (int k = 0; k < NIN; k++) raw[u][k] = raw[u + G][k];
             }
         }
         for (int64_t r = nv * N + lane; r < p.R; r += 32) {
@@ -237,7 +261,7 @@ __global__ void __launch_bounds__(THREADS) chain_reduce_typed_kernel(const __gri
 #pragma unroll
             for (int k = 0; k < NIN; k++) val[k][0] = load_as<float>(p.chain.in[k].base, p.chain.in[k].dtype, base[k] + r * p.ax[k]);
             float acc[1] = {val[0][0]};
-            run_chain<float, NIN, 1, false>(p.chain, acc, val);
+            run_fprog<NIN, 1, false>(p.chain.fp, acc, val);
             update<K, float>(s, p.square ? acc[0] * acc[0] : acc[0], r);
         }
         s = warp_combine<K, float>(s);

@@ -327,9 +327,14 @@ extern "C" int tadma_b200_eltwise(const tadma_tensor* out, const tadma_tensor* i
                          f.strides[2][1] == 1 && f.strides[1][1] == 1 && f.strides[0][1] == 1 && !p.in[1].inner_bcast &&
                          !(precise && am.act != ACT_NONE);  // the row kernel's 16-bit activations are the fast bodies
     auto fdt3 = [](int dt) { return dt == TADMA_F32 || dt == TADMA_F16 || dt == TADMA_BF16; };
-    bool typed_ok = cm == TADMA_COMPUTE_F32 && (n_ins == 1 || n_ins == 2) && fdt3(out->dtype);
-    for (int k = 0; k < n_ins && typed_ok; k++)
-        typed_ok = ins[k].dtype == ins[0].dtype && fdt3(ins[k].dtype) && !p.in[k].inner_bcast;
+    // One float dtype over every operand: the typed kernels.  Single
+    // instructions (typed1) take one or two streaming operands; chains take
+    // 1-6 operands, innermost broadcasts included, on the pre-decoded program.
+    bool one_dt = cm == TADMA_COMPUTE_F32 && n_ins >= 1 && fdt3(out->dtype);
+    for (int k = 0; k < n_ins && one_dt; k++) one_dt = ins[k].dtype == ins[0].dtype && fdt3(ins[k].dtype);
+    bool typed_ok = one_dt && (n_ins == 1 || n_ins == 2);
+    for (int k = 0; k < n_ins && typed_ok; k++) typed_ok = !p.in[k].inner_bcast;
+    const bool chain_ok = one_dt && decode_fprog(prog, n_instr, n_ins, pv.fp);
     // One instruction (or none: a cast) whose rounding is a no-op before the store.
     int op1 = -1;
     bool imm1 = false;
@@ -398,7 +403,7 @@ extern "C" int tadma_b200_eltwise(const tadma_tensor* out, const tadma_tensor* i
     } else if (am.ok) {
         pv.scale = am.scale;
         rc = launch_affine(am.act, fast, am.mul, am.add, pv, nvec, s, narrow);
-    } else if (typed_ok) {
+    } else if (chain_ok) {
         rc = launch_typed(ins[0].dtype, out->dtype, n_ins, fast, pv, nvec, s);
     } else {
         rc = go(pv, true, nvec);
@@ -558,7 +563,8 @@ static int reduce_chain_impl(int32_t op, const tadma_tensor* ins, int32_t n_ins,
             if (sdt < 0) sdt = ins[k].dtype;
             else if (ins[k].dtype != sdt) one_dt = false;
         }
-        if (one_dt && sdt >= 0 && R >= 16 / dtype_size(sdt)) return launch_chain_reduce_typed(kind, sdt, p, s);
+        if (one_dt && sdt >= 0 && R >= 16 / dtype_size(sdt) && decode_fprog(prog, n_instr, n_ins, p.chain.fp))
+            return launch_chain_reduce_typed(kind, sdt, p, s);
     }
     switch (cm) {
     case TADMA_COMPUTE_F32:

@@ -31,6 +31,7 @@
 #include <unordered_map>
 
 #include "common.cuh"
+#include "fprog.cuh"
 #include "layout.hpp"
 #include "ops.cuh"
 #include "reduce_state.cuh"
@@ -68,6 +69,8 @@ struct ChainParams {
     Operand in[TADMA_MAX_INPUTS];
     tadma_instr prog[TADMA_MAX_INSTR];
     float scale;  // affine program: the MUL immediate, rounded to fp32
+    int32_t pad2;
+    FProg fp;     // the program pre-decoded for the typed fp32 kernels
 };
 
 // Program selector of a kernel instance: the run-time interpreter (precise or
@@ -137,12 +140,15 @@ int launch_affine(int act, bool fast, bool mul, bool add, const ChainParams& p, 
 int launch_typed1(int idt, int odt, int op, bool imm, const ChainParams& p, int64_t nvec, cudaStream_t s);
 int launch_cmp(int idt, int op, bool imm, const ChainParams& p, int64_t nvec, cudaStream_t s);
 int launch_where(int dt, const ChainParams& p, int64_t nvec, cudaStream_t s);
+// One-dtype chains (fp32 compute, every operand of dtype idt, F32 / F16 /
+// BF16, possibly broadcast along the innermost dim; 1-6 operands) on the
+// pre-decoded program p.fp.
 int launch_typed(int idt, int odt, int nin, bool fast, const ChainParams& p, int64_t nvec, cudaStream_t s);
 int launch_rows(int xdt, int odt, int act, const AffineRowsParams& p, cudaStream_t s);
 int launch_transpose(bool fast, const TransposeParams& tp, cudaStream_t s);
 int launch_chain_reduce_f32(int kind, bool vec, const ChainReduceParams& p, cudaStream_t s);
 // fp32 compute, every operand streamed along the axis with dtype dt (F32 / F16
-// / BF16) or broadcast along it.
+// / BF16) or broadcast along it; runs the pre-decoded program p.chain.fp.
 int launch_chain_reduce_typed(int kind, int dt, const ChainReduceParams& p, cudaStream_t s);
 int launch_chain_reduce_f64(int kind, const ChainReduceParams& p, cudaStream_t s);
 int launch_chain_reduce_i64(int kind, const ChainReduceParams& p, cudaStream_t s);

@@ -88,14 +88,23 @@ __global__ void __launch_bounds__(THREADS) affine_rows_kernel(const __grid_const
 // The generic kernels decode dtypes per vector, which cost ~170 instructions
 // per 8 elements on a 16-bit add (ncu) and held it to 4.7 TB/s.
 
-// Two vectors per thread: with the interpreter inlined once per vector, more
-// would grow the kernel past what the instruction cache holds.
-template <typename TI>
-constexpr int typed_steps() { return 2; }
+// One-dtype chains: every operand is a TI tensor (F32 / F16 / BF16) that is
+// either contiguous along the folded innermost dim or broadcast along it (a
+// per-row mean or scale: one value per vector, loaded once), so no operand
+// needs a run-time dtype switch.  A thread loads U vectors of every operand
+// before any compute, then runs the pre-decoded program: once on all 16
+// values with one operand, else one vector (8 values) at a time in a rolled
+// loop that shifts the next vector's words down, so the program is inlined
+// once and the registers of the second vector are only its raw words.
+template <int NIN>
+constexpr int typed_steps() { return NIN <= 2 ? 2 : 1; }
+template <int NIN>
+constexpr int typed_width() { return NIN == 1 ? 2 * V : V; }
 
 // Element offsets of vector vi: R1 (folded rank 1, every operand contiguous)
 // needs no index decomposition; otherwise the folded dims are walked
-// (outer-dim broadcasts and strided views; the innermost dim is contiguous).
+// (outer-dim broadcasts and strided views; the innermost dim is contiguous
+// or broadcast).
 template <int NIN, bool R1>
 __device__ __forceinline__ void typed_offsets(const ChainParams& p, int64_t vi, int64_t& oo, int64_t (&io)[NIN]) {
     if constexpr (R1) {
@@ -107,10 +116,27 @@ __device__ __forceinline__ void typed_offsets(const ChainParams& p, int64_t vi, 
     }
 }
 
+// An innermost-broadcast operand's one value, repeated in the raw words of
+// a vector, so every operand converts the same way.
+template <typename TI>
+__device__ __forceinline__ void raw8_splat(const TI* src, Raw8x<TI>& r) {
+    if constexpr (sizeof(TI) == 4) {
+        const uint32_t b = *reinterpret_cast<const uint32_t*>(src);
+        r.w[0] = make_uint4(b, b, b, b);
+        r.w[1] = r.w[0];
+    } else {
+        const uint32_t h = *reinterpret_cast<const uint16_t*>(src);
+        const uint32_t b = h | (h << 16);
+        r.w[0] = make_uint4(b, b, b, b);
+    }
+}
+
 template <typename TI, typename TO, int NIN, bool FAST, bool R1>
-__global__ void __launch_bounds__(THREADS) typed_kernel(const __grid_constant__ ChainParams p) {
+__global__ void __launch_bounds__(THREADS, 3) typed_kernel(const __grid_constant__ ChainParams p) {
     pdl_begin();
-    constexpr int U = typed_steps<TI>();
+    constexpr int U = typed_steps<NIN>();
+    constexpr int W = typed_width<NIN>();
+    constexpr int G = W / V;  // vectors per program run
     for (int64_t chunk = blockIdx.x; chunk * (THREADS * U) < p.n; chunk += gridDim.x) {
         const int64_t base = chunk * (THREADS * U) + threadIdx.x;
         Raw8x<TI> raw[U][NIN];
@@ -122,22 +148,41 @@ __global__ void __launch_bounds__(THREADS) typed_kernel(const __grid_constant__ 
                 int64_t io[NIN];
                 typed_offsets<NIN, R1>(p, vi, oo[u], io);
 #pragma unroll
+                for (int k = 0; k < NIN; k++) {
+                    const TI* src = reinterpret_cast<const TI*>(p.in[k].base) + io[k];
+                    if (!R1 && p.in[k].inner_bcast) raw8_splat<TI>(src, raw[u][k]);
+                    else raw8_load<TI>(src, raw[u][k], p.in[k].streaming);
+                }
+            } else {
+                oo[u] = 0;
+#pragma unroll
                 for (int k = 0; k < NIN; k++)
-                    raw8_load<TI>(reinterpret_cast<const TI*>(p.in[k].base) + io[k], raw[u][k], p.in[k].streaming);
+#pragma unroll
+                    for (int w = 0; w < (int)(sizeof(raw[u][k].w) / sizeof(uint4)); w++) raw[u][k].w[w] = make_uint4(0u, 0u, 0u, 0u);
             }
         }
+#pragma unroll 1
+        for (int h = 0; h < U / G; h++) {
+            float val[NIN][W];
 #pragma unroll
-        for (int u = 0; u < U; u++) {
-            const int64_t vi = base + u * THREADS;
-            if (vi < p.n) {
-                float val[NIN][V];
+            for (int g = 0; g < G; g++)
 #pragma unroll
-                for (int k = 0; k < NIN; k++) raw8_cvt<TI>(raw[u][k], val[k]);
-                float acc[V];
+                for (int k = 0; k < NIN; k++) raw8_cvt<TI>(raw[g][k], &val[k][g * V]);
+            float acc[W];
 #pragma unroll
-                for (int j = 0; j < V; j++) acc[j] = val[0][j];
-                run_chain<float, NIN, V, FAST>(p, acc, val);
-                raw8_store<TO>(reinterpret_cast<TO*>(p.out) + oo[u], acc);
+            for (int j = 0; j < W; j++) acc[j] = val[0][j];
+            run_fprog<NIN, W, FAST>(p.fp, acc, val);
+#pragma unroll
+            for (int g = 0; g < G; g++) {
+                const int64_t vi = base + (h * G + g) * THREADS;
+                if (vi < p.n) raw8_store<TO>(reinterpret_cast<TO*>(p.out) + oo[g], &acc[g * V]);
+            }
+            // the next vector moves to the front
+#pragma unroll
+            for (int u = 0; u + G < U; u++) {
+                oo[u] = oo[u + G];
+#pragma unroll
+                for (int k = 0; k < NIN; k++) raw[u][k] = raw[u + G][k];
             }
         }
     }
@@ -363,21 +408,43 @@ int launch_cmp_op(int op, const ChainParams& p, int64_t nvec, cudaStream_t s) {
 }
 template <typename TI, typename TO, int NIN, bool FAST>
 int launch_typed_k(const ChainParams& p, int64_t nvec, cudaStream_t s) {
-    const int64_t per_block = (int64_t)THREADS * typed_steps<TI>();
+    const int64_t per_block = (int64_t)THREADS * typed_steps<NIN>();
     const int64_t want = (nvec + per_block - 1) / per_block;
     const int grid = (int)(want < 1 ? 1 : want > 0x7fffffff ? 0x7fffffff : want);
-    if (p.rank == 1) (void)launch_pdl(typed_kernel<TI, TO, NIN, FAST, true>, dim3(grid), dim3(THREADS), 0, s, p);
-    else (void)launch_pdl(typed_kernel<TI, TO, NIN, FAST, false>, dim3(grid), dim3(THREADS), 0, s, p);
+    bool r1 = p.rank == 1;
+    for (int k = 0; k < NIN; k++) r1 = r1 && !p.in[k].inner_bcast;
+    // Broadcasts fold to rank >= 2 except a whole-tensor scalar operand:
+    // the rank-1 instance exists for one or two operands only.
+    if constexpr (NIN <= 2) {
+        if (r1) {
+            (void)launch_pdl(typed_kernel<TI, TO, NIN, FAST, true>, dim3(grid), dim3(THREADS), 0, s, p);
+            cudaError_t e = cudaGetLastError();
+            return e == cudaSuccess ? TADMA_OK : cuda_fail(e, "tadma_b200_eltwise launch");
+        }
+    }
+    (void)launch_pdl(typed_kernel<TI, TO, NIN, FAST, false>, dim3(grid), dim3(THREADS), 0, s, p);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? TADMA_OK : cuda_fail(e, "tadma_b200_eltwise launch");
+}
+
+template <typename TI, typename TO, bool FAST>
+int launch_typed_nin(int nin, const ChainParams& p, int64_t nvec, cudaStream_t s) {
+    switch (nin) {
+    case 1: return launch_typed_k<TI, TO, 1, FAST>(p, nvec, s);
+    case 2: return launch_typed_k<TI, TO, 2, FAST>(p, nvec, s);
+    case 3: return launch_typed_k<TI, TO, 3, FAST>(p, nvec, s);
+    case 4: return launch_typed_k<TI, TO, 4, FAST>(p, nvec, s);
+    case 5: return launch_typed_k<TI, TO, 5, FAST>(p, nvec, s);
+    default: return launch_typed_k<TI, TO, 6, FAST>(p, nvec, s);
+    }
 }
 
 template <typename TI, typename TO>
 int launch_typed_io(int nin, bool fast, const ChainParams& p, int64_t nvec, cudaStream_t s) {
     if constexpr (sizeof(TO) == 2) {
-        if (fast) return nin == 1 ? launch_typed_k<TI, TO, 1, true>(p, nvec, s) : launch_typed_k<TI, TO, 2, true>(p, nvec, s);
+        if (fast) return launch_typed_nin<TI, TO, true>(nin, p, nvec, s);
     }
-    return nin == 1 ? launch_typed_k<TI, TO, 1, false>(p, nvec, s) : launch_typed_k<TI, TO, 2, false>(p, nvec, s);
+    return launch_typed_nin<TI, TO, false>(nin, p, nvec, s);
 }
 
 template <typename TI>
