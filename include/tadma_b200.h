@@ -241,6 +241,70 @@ int tadma_b200_reduce_chain_post(int32_t op, const tadma_tensor* ins, int32_t n_
                                  int32_t axis, const tadma_tensor* out, void* stream);
 
 /*
+ * One pass over the rows of a [rows, cols] grid: per-row reductions of
+ * element chains (stages), then an element-wise chain that may read them.
+ * A LayerNorm, RMSNorm or softmax written as separate ops (mean, -, pow,
+ * mean, + eps, sqrt, /, *, + as generated code spells it) runs as one
+ * kernel that reads each row once, with the bits of the separate calls.
+ *
+ * Operands (prog / stage chains select them by number):
+ *   0 .. n_ins - 1        ins[k], each a rank-2 view of the grid: dims
+ *                         {rows or 1, cols or 1}, strides {rs, cs}:
+ *                         a row operand (cs = 1, rs != 0), a column operand
+ *                         (rows dim 1 or rs = 0, cs = 1) or a row scalar
+ *                         (cols dim 1 or cs = 0);
+ *   n_ins + s             the value stage s stored for the row (after its
+ *                         post chain and the rounding to its out dtype),
+ *                         readable by later stages and by prog.
+ * Each stage is tadma_b200_reduce_chain_post over the last axis with op
+ * SUM, MEAN, MAX or MIN, fp32 compute; its out holds rows values (a rank-1
+ * view {rows} with its stride).  prog runs in fp32 (TADMA_COMPUTE_F32, or
+ * TADMA_COMPUTE_F32_PRECISE: as tadma_b200_eltwise) and writes out, a
+ * {rows, cols} view with unit column stride.
+ *
+ * Limits: cols a multiple of 16 / dtype size, at most 32 x 8 x that (1024
+ * fp32, 2048 fp16 / bf16 values); at most 2 row operands and 2 column
+ * operands, all of one float dtype, 16-byte aligned rows; at most 2 row
+ * scalars (any float dtype); at most TADMA_ROWPROG_MAX_STAGES stages; out
+ * F32, F16 or BF16.  Other grids return TADMA_ERR_UNSUPPORTED with nothing
+ * launched: the caller runs the ops one by one.
+ *
+ * The result equals the separate calls bit for bit: each stage folds in the
+ * order of the row reductions (lane l of a warp takes 16-byte vectors l,
+ * l + 32, ... in order, then the fixed lane butterfly), the chains use the
+ * element-wise engine's op bodies and roundings.
+ * Replaces: the ReduceNode / EltwiseNode sequence of a decomposed
+ * normalisation (Kernels.hpp:20-45, kernels/Reduce.hpp:10-71), as
+ * layer_norm / softmax compose it (Operations.hpp:190-220).
+ */
+#define TADMA_ROWPROG_MAX_STAGES 3
+typedef struct tadma_row_stage {
+    int32_t op; /* TADMA_REDUCE_SUM, MEAN, MAX or MIN */
+    int32_t n_instr;
+    int32_t n_post;
+    int32_t acc;                       /* the operand the element chain starts from */
+    tadma_instr prog[TADMA_MAX_INSTR]; /* element chain */
+    tadma_instr post[TADMA_MAX_INSTR]; /* on the reduced value, immediates only */
+    tadma_tensor out;                  /* rank 1, rows values */
+} tadma_row_stage;
+
+typedef struct tadma_row_program {
+    int64_t rows, cols;
+    int32_t n_ins;
+    int32_t n_stages;
+    int32_t n_instr;
+    int32_t compute; /* TADMA_COMPUTE_F32 or TADMA_COMPUTE_F32_PRECISE */
+    int32_t acc;     /* the operand the final chain starts from */
+    int32_t pad;
+    tadma_tensor ins[TADMA_MAX_INPUTS];
+    tadma_row_stage stages[TADMA_ROWPROG_MAX_STAGES];
+    tadma_instr prog[TADMA_MAX_INSTR]; /* the final chain */
+    tadma_tensor out;                  /* rank 2 {rows, cols} */
+} tadma_row_program;
+
+int tadma_b200_row_program(const tadma_row_program* rp, void* stream);
+
+/*
  * tadma_b200_reduce without any device allocation.  No counterpart in the
  * reference.  For callers that cannot call cudaMalloc: a process whose memory
  * pool has already claimed the device's HBM (so any further allocation

@@ -107,7 +107,7 @@ __global__ void __launch_bounds__(THREADS, !VEC ? 2 : NIN == 1 ? 3 : NIN <= 4 ? 
                 for (int j = 0; j < V; j++) acc[j] = val[0][j];
                 run_chain<C, NIN, V, false>(p.chain, acc, val);
 #pragma unroll
-                for (int j = 0; j < V; j++) update<K, C>(s, p.square ? acc[j] * acc[j] : acc[j], v * V + j);
+                for (int j = 0; j < V; j++) update<K, C>(s, p.square ? sq(acc[j]) : acc[j], v * V + j);
 #pragma unroll
                 for (int k = 0; k < NIN; k++) cur[k] = nxt[k];
             }
@@ -120,7 +120,7 @@ __global__ void __launch_bounds__(THREADS, !VEC ? 2 : NIN == 1 ? 3 : NIN <= 4 ? 
                 if (k < p.n_ins) val[k][0] = load_as<C>(p.chain.in[k].base, p.chain.in[k].dtype, base[k] + r * p.ax[k]);
             C acc[1] = {p.n_ins > 0 ? val[0][0] : C(0)};
             run_chain<C, TADMA_MAX_INPUTS, 1, false>(p.chain, acc, val);
-            update<K, C>(s, p.square ? acc[0] * acc[0] : acc[0], r);
+            update<K, C>(s, p.square ? sq(acc[0]) : acc[0], r);
         }
         s = warp_combine<K, C>(s);
         if (lane == 0) {
@@ -245,7 +245,7 @@ __global__ void __launch_bounds__(THREADS, NIN == 1 ? 3 : 2) chain_reduce_typed_
 #pragma unroll
                         for (int j = 0; j < N; j++) {
                             const float a = acc[g * N + j];
-                            update<K, float>(s, p.square ? a * a : a, vg * N + j);
+                            update<K, float>(s, p.square ? sq(a) : a, vg * N + j);
                         }
                     }
                 }
@@ -262,7 +262,7 @@ __global__ void __launch_bounds__(THREADS, NIN == 1 ? 3 : 2) chain_reduce_typed_
             for (int k = 0; k < NIN; k++) val[k][0] = load_as<float>(p.chain.in[k].base, p.chain.in[k].dtype, base[k] + r * p.ax[k]);
             float acc[1] = {val[0][0]};
             run_fprog<NIN, 1, false>(p.chain.fp, acc, val);
-            update<K, float>(s, p.square ? acc[0] * acc[0] : acc[0], r);
+            update<K, float>(s, p.square ? sq(acc[0]) : acc[0], r);
         }
         s = warp_combine<K, float>(s);
         if (lane == 0) {

@@ -334,7 +334,24 @@ extern "C" int tadma_b200_eltwise(const tadma_tensor* out, const tadma_tensor* i
     for (int k = 0; k < n_ins && one_dt; k++) one_dt = ins[k].dtype == ins[0].dtype && fdt3(ins[k].dtype);
     bool typed_ok = one_dt && (n_ins == 1 || n_ins == 2);
     for (int k = 0; k < n_ins && typed_ok; k++) typed_ok = !p.in[k].inner_bcast;
-    const bool chain_ok = one_dt && decode_fprog(prog, n_instr, n_ins, pv.fp);
+    // Typed chains: vector operands first, then the (at most two) operands
+    // broadcast along the innermost dim, which the kernel keeps as scalars.
+    ChainParams pt;
+    int n_vec = 0, n_scal = 0;
+    bool chain_ok = one_dt;
+    if (chain_ok) {
+        int slot_of[TADMA_MAX_INPUTS];
+        for (int k = 0; k < n_ins; k++)
+            if (!p.in[k].inner_bcast) slot_of[k] = n_vec++;
+        for (int k = 0; k < n_ins; k++)
+            if (p.in[k].inner_bcast) slot_of[k] = n_vec + n_scal++;
+        chain_ok = n_vec >= 1 && n_scal <= 2;
+        if (chain_ok) {
+            pt = pv;
+            for (int k = 0; k < n_ins; k++) pt.in[slot_of[k]] = pv.in[k];
+            chain_ok = decode_fprog(prog, n_instr, n_ins, pt.fp, slot_of);
+        }
+    }
     // One instruction (or none: a cast) whose rounding is a no-op before the store.
     int op1 = -1;
     bool imm1 = false;
@@ -404,7 +421,7 @@ extern "C" int tadma_b200_eltwise(const tadma_tensor* out, const tadma_tensor* i
         pv.scale = am.scale;
         rc = launch_affine(am.act, fast, am.mul, am.add, pv, nvec, s, narrow);
     } else if (chain_ok) {
-        rc = launch_typed(ins[0].dtype, out->dtype, n_ins, fast, pv, nvec, s);
+        rc = launch_typed(ins[0].dtype, out->dtype, n_vec, n_scal, fast, pt, nvec, s);
     } else {
         rc = go(pv, true, nvec);
     }

@@ -141,9 +141,10 @@ int launch_typed1(int idt, int odt, int op, bool imm, const ChainParams& p, int6
 int launch_cmp(int idt, int op, bool imm, const ChainParams& p, int64_t nvec, cudaStream_t s);
 int launch_where(int dt, const ChainParams& p, int64_t nvec, cudaStream_t s);
 // One-dtype chains (fp32 compute, every operand of dtype idt, F32 / F16 /
-// BF16, possibly broadcast along the innermost dim; 1-6 operands) on the
-// pre-decoded program p.fp.
-int launch_typed(int idt, int odt, int nin, bool fast, const ChainParams& p, int64_t nvec, cudaStream_t s);
+// BF16) on the pre-decoded program p.fp: p.in[0 .. nv) contiguous along the
+// innermost folded dim, p.in[nv .. nv + ns) broadcast along it; 1 <= nv,
+// ns <= 2, nv + ns <= 6 (else TADMA_ERR_UNSUPPORTED, nothing launched).
+int launch_typed(int idt, int odt, int nv, int ns, bool fast, const ChainParams& p, int64_t nvec, cudaStream_t s);
 int launch_rows(int xdt, int odt, int act, const AffineRowsParams& p, cudaStream_t s);
 int launch_transpose(bool fast, const TransposeParams& tp, cudaStream_t s);
 int launch_chain_reduce_f32(int kind, bool vec, const ChainReduceParams& p, cudaStream_t s);

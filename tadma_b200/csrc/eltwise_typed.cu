@@ -89,17 +89,19 @@ __global__ void __launch_bounds__(THREADS) affine_rows_kernel(const __grid_const
 // per 8 elements on a 16-bit add (ncu) and held it to 4.7 TB/s.
 
 // One-dtype chains: every operand is a TI tensor (F32 / F16 / BF16) that is
-// either contiguous along the folded innermost dim or broadcast along it (a
-// per-row mean or scale: one value per vector, loaded once), so no operand
-// needs a run-time dtype switch.  A thread loads U vectors of every operand
-// before any compute, then runs the pre-decoded program: once on all 16
-// values with one operand, else one vector (8 values) at a time in a rolled
-// loop that shifts the next vector's words down, so the program is inlined
-// once and the registers of the second vector are only its raw words.
-template <int NIN>
-constexpr int typed_steps() { return NIN <= 2 ? 2 : 1; }
-template <int NIN>
-constexpr int typed_width() { return NIN == 1 ? 2 * V : V; }
+// either contiguous along the folded innermost dim (a vector operand) or
+// broadcast along it (a scalar operand: a per-row mean or scale, one value
+// per vector).  The host orders the operands vectors first, so the kernel
+// knows at compile time which are scalars: those cost one register, not
+// eight.  No operand needs a run-time dtype switch.  A thread loads U
+// vectors of every operand before any compute, then runs the pre-decoded
+// program: once on all 16 values with one operand, else one vector (8
+// values) at a time in a rolled loop that shifts the next vector's words
+// down, so the program is inlined once.
+template <int NV, int NS>
+constexpr int typed_steps() { return NV <= 2 ? 2 : 1; }
+template <int NV, int NS>
+constexpr int typed_width() { return NV + NS == 1 ? 2 * V : V; }
 
 // Element offsets of vector vi: R1 (folded rank 1, every operand contiguous)
 // needs no index decomposition; otherwise the folded dims are walked
@@ -116,30 +118,24 @@ __device__ __forceinline__ void typed_offsets(const ChainParams& p, int64_t vi, 
     }
 }
 
-// An innermost-broadcast operand's one value, repeated in the raw words of
-// a vector, so every operand converts the same way.
-template <typename TI>
-__device__ __forceinline__ void raw8_splat(const TI* src, Raw8x<TI>& r) {
-    if constexpr (sizeof(TI) == 4) {
-        const uint32_t b = *reinterpret_cast<const uint32_t*>(src);
-        r.w[0] = make_uint4(b, b, b, b);
-        r.w[1] = r.w[0];
-    } else {
-        const uint32_t h = *reinterpret_cast<const uint16_t*>(src);
-        const uint32_t b = h | (h << 16);
-        r.w[0] = make_uint4(b, b, b, b);
-    }
+template <typename T>
+__device__ __forceinline__ float typed_scalar(const T* p) {
+    if constexpr (sizeof(T) == 4) return *p;
+    else if constexpr (std::is_same<T, __half>::value) return __half2float(*p);
+    else return __bfloat162float(*p);
 }
 
-template <typename TI, typename TO, int NIN, bool FAST, bool R1>
+template <typename TI, typename TO, int NV, int NS, bool FAST, bool R1>
 __global__ void __launch_bounds__(THREADS, 3) typed_kernel(const __grid_constant__ ChainParams p) {
     pdl_begin();
-    constexpr int U = typed_steps<NIN>();
-    constexpr int W = typed_width<NIN>();
+    constexpr int NIN = NV + NS;
+    constexpr int U = typed_steps<NV, NS>();
+    constexpr int W = typed_width<NV, NS>();
     constexpr int G = W / V;  // vectors per program run
     for (int64_t chunk = blockIdx.x; chunk * (THREADS * U) < p.n; chunk += gridDim.x) {
         const int64_t base = chunk * (THREADS * U) + threadIdx.x;
-        Raw8x<TI> raw[U][NIN];
+        Raw8x<TI> raw[U][NV];
+        float sc[U][NS > 0 ? NS : 1];
         int64_t oo[U];
 #pragma unroll
         for (int u = 0; u < U; u++) {
@@ -148,30 +144,30 @@ __global__ void __launch_bounds__(THREADS, 3) typed_kernel(const __grid_constant
                 int64_t io[NIN];
                 typed_offsets<NIN, R1>(p, vi, oo[u], io);
 #pragma unroll
-                for (int k = 0; k < NIN; k++) {
-                    const TI* src = reinterpret_cast<const TI*>(p.in[k].base) + io[k];
-                    if (!R1 && p.in[k].inner_bcast) raw8_splat<TI>(src, raw[u][k]);
-                    else raw8_load<TI>(src, raw[u][k], p.in[k].streaming);
-                }
+                for (int k = 0; k < NV; k++)
+                    raw8_load<TI>(reinterpret_cast<const TI*>(p.in[k].base) + io[k], raw[u][k], p.in[k].streaming);
+#pragma unroll
+                for (int k = 0; k < NS; k++) sc[u][k] = typed_scalar<TI>(reinterpret_cast<const TI*>(p.in[NV + k].base) + io[NV + k]);
             } else {
                 oo[u] = 0;
 #pragma unroll
-                for (int k = 0; k < NIN; k++)
+                for (int k = 0; k < NS; k++) sc[u][k] = 0.0f;
+#pragma unroll
+                for (int k = 0; k < NV; k++)
 #pragma unroll
                     for (int w = 0; w < (int)(sizeof(raw[u][k].w) / sizeof(uint4)); w++) raw[u][k].w[w] = make_uint4(0u, 0u, 0u, 0u);
             }
         }
 #pragma unroll 1
         for (int h = 0; h < U / G; h++) {
-            float val[NIN][W];
+            float val[NV][W];
 #pragma unroll
             for (int g = 0; g < G; g++)
 #pragma unroll
-                for (int k = 0; k < NIN; k++) raw8_cvt<TI>(raw[g][k], &val[k][g * V]);
+                for (int k = 0; k < NV; k++) raw8_cvt<TI>(raw[g][k], &val[k][g * V]);
             float acc[W];
-#pragma unroll
-            for (int j = 0; j < W; j++) acc[j] = val[0][j];
-            run_fprog<NIN, W, FAST>(p.fp, acc, val);
+            // G > 1 only with one vector operand and no scalar
+            run_fprog<NV, NS, W, FAST>(p.fp, acc, val, sc[0]);
 #pragma unroll
             for (int g = 0; g < G; g++) {
                 const int64_t vi = base + (h * G + g) * THREADS;
@@ -182,7 +178,9 @@ __global__ void __launch_bounds__(THREADS, 3) typed_kernel(const __grid_constant
             for (int u = 0; u + G < U; u++) {
                 oo[u] = oo[u + G];
 #pragma unroll
-                for (int k = 0; k < NIN; k++) raw[u][k] = raw[u + G][k];
+                for (int k = 0; k < NV; k++) raw[u][k] = raw[u + G][k];
+#pragma unroll
+                for (int k = 0; k < NS; k++) sc[u][k] = sc[u + G][k];
             }
         }
     }
@@ -406,53 +404,62 @@ int launch_cmp_op(int op, const ChainParams& p, int64_t nvec, cudaStream_t s) {
     default: return launch_cmp_k<TI, TADMA_OP_GE, IMM>(p, nvec, s);
     }
 }
-template <typename TI, typename TO, int NIN, bool FAST>
+template <typename TI, typename TO, int NV, int NS, bool FAST>
 int launch_typed_k(const ChainParams& p, int64_t nvec, cudaStream_t s) {
-    const int64_t per_block = (int64_t)THREADS * typed_steps<NIN>();
+    const int64_t per_block = (int64_t)THREADS * typed_steps<NV, NS>();
     const int64_t want = (nvec + per_block - 1) / per_block;
     const int grid = (int)(want < 1 ? 1 : want > 0x7fffffff ? 0x7fffffff : want);
-    bool r1 = p.rank == 1;
-    for (int k = 0; k < NIN; k++) r1 = r1 && !p.in[k].inner_bcast;
-    // Broadcasts fold to rank >= 2 except a whole-tensor scalar operand:
-    // the rank-1 instance exists for one or two operands only.
-    if constexpr (NIN <= 2) {
-        if (r1) {
-            (void)launch_pdl(typed_kernel<TI, TO, NIN, FAST, true>, dim3(grid), dim3(THREADS), 0, s, p);
+    // The rank-1 instance (no index walk) exists for one or two vector
+    // operands without scalars: broadcasts fold to rank >= 2.
+    if constexpr (NS == 0 && NV <= 2) {
+        if (p.rank == 1) {
+            (void)launch_pdl(typed_kernel<TI, TO, NV, NS, FAST, true>, dim3(grid), dim3(THREADS), 0, s, p);
             cudaError_t e = cudaGetLastError();
             return e == cudaSuccess ? TADMA_OK : cuda_fail(e, "tadma_b200_eltwise launch");
         }
     }
-    (void)launch_pdl(typed_kernel<TI, TO, NIN, FAST, false>, dim3(grid), dim3(THREADS), 0, s, p);
+    (void)launch_pdl(typed_kernel<TI, TO, NV, NS, FAST, false>, dim3(grid), dim3(THREADS), 0, s, p);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? TADMA_OK : cuda_fail(e, "tadma_b200_eltwise launch");
 }
 
+template <typename TI, typename TO, bool FAST, int NS>
+int launch_typed_nv(int nv, const ChainParams& p, int64_t nvec, cudaStream_t s) {
+    switch (nv) {
+    case 1: return launch_typed_k<TI, TO, 1, NS, FAST>(p, nvec, s);
+    case 2: return launch_typed_k<TI, TO, 2, NS, FAST>(p, nvec, s);
+    case 3: return launch_typed_k<TI, TO, 3, NS, FAST>(p, nvec, s);
+    case 4: return launch_typed_k<TI, TO, 4, NS, FAST>(p, nvec, s);
+    case 5: if constexpr (NS <= 1) return launch_typed_k<TI, TO, 5, NS, FAST>(p, nvec, s);
+            return TADMA_ERR_UNSUPPORTED;
+    default: if constexpr (NS == 0) return launch_typed_k<TI, TO, 6, NS, FAST>(p, nvec, s);
+             return TADMA_ERR_UNSUPPORTED;
+    }
+}
+
 template <typename TI, typename TO, bool FAST>
-int launch_typed_nin(int nin, const ChainParams& p, int64_t nvec, cudaStream_t s) {
-    switch (nin) {
-    case 1: return launch_typed_k<TI, TO, 1, FAST>(p, nvec, s);
-    case 2: return launch_typed_k<TI, TO, 2, FAST>(p, nvec, s);
-    case 3: return launch_typed_k<TI, TO, 3, FAST>(p, nvec, s);
-    case 4: return launch_typed_k<TI, TO, 4, FAST>(p, nvec, s);
-    case 5: return launch_typed_k<TI, TO, 5, FAST>(p, nvec, s);
-    default: return launch_typed_k<TI, TO, 6, FAST>(p, nvec, s);
+int launch_typed_nin(int nv, int ns, const ChainParams& p, int64_t nvec, cudaStream_t s) {
+    switch (ns) {
+    case 0: return launch_typed_nv<TI, TO, FAST, 0>(nv, p, nvec, s);
+    case 1: return launch_typed_nv<TI, TO, FAST, 1>(nv, p, nvec, s);
+    default: return launch_typed_nv<TI, TO, FAST, 2>(nv, p, nvec, s);
     }
 }
 
 template <typename TI, typename TO>
-int launch_typed_io(int nin, bool fast, const ChainParams& p, int64_t nvec, cudaStream_t s) {
+int launch_typed_io(int nv, int ns, bool fast, const ChainParams& p, int64_t nvec, cudaStream_t s) {
     if constexpr (sizeof(TO) == 2) {
-        if (fast) return launch_typed_nin<TI, TO, true>(nin, p, nvec, s);
+        if (fast) return launch_typed_nin<TI, TO, true>(nv, ns, p, nvec, s);
     }
-    return launch_typed_nin<TI, TO, false>(nin, p, nvec, s);
+    return launch_typed_nin<TI, TO, false>(nv, ns, p, nvec, s);
 }
 
 template <typename TI>
-int launch_typed_i(int odt, int nin, bool fast, const ChainParams& p, int64_t nvec, cudaStream_t s) {
+int launch_typed_i(int odt, int nv, int ns, bool fast, const ChainParams& p, int64_t nvec, cudaStream_t s) {
     switch (odt) {
-    case TADMA_F32: return launch_typed_io<TI, float>(nin, fast, p, nvec, s);
-    case TADMA_F16: return launch_typed_io<TI, __half>(nin, fast, p, nvec, s);
-    default: return launch_typed_io<TI, __nv_bfloat16>(nin, fast, p, nvec, s);
+    case TADMA_F32: return launch_typed_io<TI, float>(nv, ns, fast, p, nvec, s);
+    case TADMA_F16: return launch_typed_io<TI, __half>(nv, ns, fast, p, nvec, s);
+    default: return launch_typed_io<TI, __nv_bfloat16>(nv, ns, fast, p, nvec, s);
     }
 }
 
@@ -511,11 +518,11 @@ int launch_where(int dt, const ChainParams& p, int64_t nvec, cudaStream_t s) {
 }
 
 // idt, odt in {F32, F16, BF16}; nin in {1, 2}.
-int launch_typed(int idt, int odt, int nin, bool fast, const ChainParams& p, int64_t nvec, cudaStream_t s) {
+int launch_typed(int idt, int odt, int nv, int ns, bool fast, const ChainParams& p, int64_t nvec, cudaStream_t s) {
     switch (idt) {
-    case TADMA_F32: return launch_typed_i<float>(odt, nin, fast, p, nvec, s);
-    case TADMA_F16: return launch_typed_i<__half>(odt, nin, fast, p, nvec, s);
-    default: return launch_typed_i<__nv_bfloat16>(odt, nin, fast, p, nvec, s);
+    case TADMA_F32: return launch_typed_i<float>(odt, nv, ns, fast, p, nvec, s);
+    case TADMA_F16: return launch_typed_i<__half>(odt, nv, ns, fast, p, nvec, s);
+    default: return launch_typed_i<__nv_bfloat16>(odt, nv, ns, fast, p, nvec, s);
     }
 }
 

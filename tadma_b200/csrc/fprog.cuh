@@ -36,15 +36,18 @@ struct FInstr {
 
 struct FProg {
     int32_t n;
-    int32_t pad;
+    int32_t acc;  // the operand the accumulator starts from (ins[0] before any reordering)
     FInstr ins[2 * TADMA_MAX_INSTR];
 };
 
-// Host: decodes an fp32-compute program over `nin` operands.  False when a
-// step has no code (the caller keeps the run-time interpreter).
-inline bool decode_fprog(const tadma_instr* prog, int n_instr, int nin, FProg& fp) {
+// Host: decodes an fp32-compute program over `nin` operands.  `slot_of`
+// (optional) renumbers the operands: ins[k] of the program is operand
+// slot_of[k] of the kernel.  False when a step has no code (the caller keeps
+// the run-time interpreter).
+inline bool decode_fprog(const tadma_instr* prog, int n_instr, int nin, FProg& fp, const int* slot_of = nullptr) {
     static const int kRound[] = {TADMA_F16, TADMA_BF16, TADMA_I64, TADMA_I32, TADMA_U8, TADMA_BOOL, TADMA_I8};
     fp = FProg{};
+    fp.acc = slot_of ? slot_of[0] : 0;
     auto emit = [&](int code, int b, int c, double imm) {
         FInstr& f = fp.ins[fp.n++];
         f.code = (uint8_t)code;
@@ -52,7 +55,7 @@ inline bool decode_fprog(const tadma_instr* prog, int n_instr, int nin, FProg& f
         f.c = (int8_t)c;
         f.imm = (float)imm;
     };
-    auto slot = [&](int sel) { return sel >= 0 && sel < nin ? sel : -1; };
+    auto slot = [&](int sel) { return sel >= 0 && sel < nin ? (slot_of ? slot_of[sel] : sel) : -1; };
     for (int i = 0; i < n_instr; i++) {
         const tadma_instr& I = prog[i];
         if (I.op >= 0 && I.op < 32) {
@@ -95,31 +98,43 @@ __device__ __forceinline__ float funary(float a) {
     else return unary<FAST>(OP, a);
 }
 
-// acc's second argument: operand `sel` (0 <= sel < NIN, checked on the host).
-template <int NIN, int W>
-__device__ __forceinline__ void pick(int sel, const float (&val)[NIN][W], float (&dst)[W]) {
-    if constexpr (NIN == 1) {
+// An operand of a step: vector operands 0 .. NV-1 hold W values, scalar
+// operands NV .. NV+NS-1 one value for all W (an innermost broadcast);
+// sel < 0 is the step's immediate.
+template <int NV, int NS, int W>
+__device__ __forceinline__ void pick_or_imm(int sel, float imm, const float (&vv)[NV][W], const float (&sv)[NS > 0 ? NS : 1],
+                                            float (&dst)[W]) {
+    float s = imm;
 #pragma unroll
-        for (int j = 0; j < W; j++) dst[j] = val[0][j];
-    } else {
+    for (int k = 0; k < NS; k++)
+        if (sel == NV + k) s = sv[k];
+    bool vec = false;
 #pragma unroll
-        for (int k = 0; k < NIN; k++) {
-            if (sel == k) {
+    for (int k = 0; k < NV; k++) {
+        if (sel == k) {
+            vec = true;
 #pragma unroll
-                for (int j = 0; j < W; j++) dst[j] = val[k][j];
-            }
+            for (int j = 0; j < W; j++) dst[j] = vv[k][j];
         }
+    }
+    if (!vec) {
+#pragma unroll
+        for (int j = 0; j < W; j++) dst[j] = s;
     }
 }
 
-template <int NIN, int W>
-__device__ __forceinline__ void pick_or_imm(int sel, float imm, const float (&val)[NIN][W], float (&dst)[W]) {
-    if (sel < 0) {
+// Value j of operand sel (WHERE's third argument, chosen per element).
+template <int NV, int NS, int W>
+__device__ __forceinline__ float operand_at(int sel, float imm, const float (&vv)[NV][W], const float (&sv)[NS > 0 ? NS : 1],
+                                            int j) {
+    float v = imm;
 #pragma unroll
-        for (int j = 0; j < W; j++) dst[j] = imm;
-    } else {
-        pick<NIN, W>(sel, val, dst);
-    }
+    for (int k = 0; k < NV; k++)
+        if (sel == k) v = vv[k][j];
+#pragma unroll
+    for (int k = 0; k < NS; k++)
+        if (sel == NV + k) v = sv[k];
+    return v;
 }
 
 #define TADMA_FU(OP)                                                        \
@@ -139,15 +154,18 @@ __device__ __forceinline__ void pick_or_imm(int sel, float imm, const float (&va
         _Pragma("unroll") for (int j = 0; j < W; j++) acc[j] = round_to(acc[j], DT); \
     } break;
 
-// Runs the decoded program on W values per operand.
-template <int NIN, int W, bool FAST>
-__device__ __forceinline__ void run_fprog(const FProg& fp, float (&acc)[W], const float (&val)[NIN][W]) {
+// Runs the decoded program on W values: the accumulator starts from operand
+// fp.acc; NV vector operands, NS scalar ones.
+template <int NV, int NS, int W, bool FAST>
+__device__ __forceinline__ void run_fprog(const FProg& fp, float (&acc)[W], const float (&vv)[NV][W],
+                                          const float (&sv)[NS > 0 ? NS : 1]) {
+    pick_or_imm<NV, NS, W>(fp.acc, 0.0f, vv, sv, acc);
     for (int i = 0; i < fp.n; i++) {
         const FInstr I = fp.ins[i];
         // The second argument of a binary or WHERE step, picked once here
         // rather than in each case: one W-wide temporary for the whole switch.
         float bsel[W];
-        if (I.code >= FC_BV && I.code <= FC_WHERE) pick_or_imm<NIN, W>(I.b, I.imm, val, bsel);
+        if (I.code >= FC_BV && I.code <= FC_WHERE) pick_or_imm<NV, NS, W>(I.b, I.imm, vv, sv, bsel);
         switch (I.code) {
         case FC_FILL: {
 #pragma unroll
@@ -196,13 +214,7 @@ __device__ __forceinline__ void run_fprog(const FProg& fp, float (&acc)[W], cons
         case FC_WHERE: {
             // c is chosen per element, so no second W-wide temporary is live
 #pragma unroll
-            for (int j = 0; j < W; j++) {
-                float cv = I.imm;
-#pragma unroll
-                for (int k = 0; k < NIN; k++)
-                    if (I.c == k) cv = val[k][j];
-                acc[j] = acc[j] != 0.0f ? bsel[j] : cv;
-            }
+            for (int j = 0; j < W; j++) acc[j] = acc[j] != 0.0f ? bsel[j] : operand_at<NV, NS, W>(I.c, I.imm, vv, sv, j);
         } break;
             TADMA_FR(0, TADMA_F16)
             TADMA_FR(1, TADMA_BF16)
@@ -220,6 +232,13 @@ __device__ __forceinline__ void run_fprog(const FProg& fp, float (&acc)[W], cons
 #undef TADMA_FU
 #undef TADMA_FB
 #undef TADMA_FR
+
+// The same on NIN vector operands.
+template <int NIN, int W, bool FAST>
+__device__ __forceinline__ void run_fprog(const FProg& fp, float (&acc)[W], const float (&val)[NIN][W]) {
+    const float none[1] = {0.0f};
+    run_fprog<NIN, 0, W, FAST>(fp, acc, val, none);
+}
 
 }  // namespace
 }  // namespace tadma_b200

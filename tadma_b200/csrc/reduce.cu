@@ -78,7 +78,7 @@ template <bool PRE = true, typename A>
 __device__ __forceinline__ A prep(const RedParams& p, A v) {
     if constexpr (PRE) {
         if (p.pre_op != TADMA_OP_COPY) v = unary(p.pre_op, v);
-        if (p.square) v = v * v;
+        if (p.square) v = sq(v);
     }
     return v;
 }
@@ -274,7 +274,7 @@ __device__ __forceinline__ void rowop_vec(const RedParams& p, float m, float (&f
 #undef TADMA_ROWOP_U
     if (p.square) {
 #pragma unroll
-        for (int j = 0; j < N; j++) f[j] = f[j] * f[j];
+        for (int j = 0; j < N; j++) f[j] = sq(f[j]);
     }
 }
 

@@ -18,6 +18,12 @@ namespace {
 
 enum Kind { K_SUM = 0, K_MAX = 1, K_MIN = 2, K_ARGMAX = 3, K_ARGMIN = 4 };
 
+// A squared element (sum of squares, variance): one rounded multiply, never
+// contracted into the fold's add, as a materialised square would be.
+__device__ __forceinline__ float sq(float v) { return __fmul_rn(v, v); }
+__device__ __forceinline__ double sq(double v) { return __dmul_rn(v, v); }
+__device__ __forceinline__ int64_t sq(int64_t v) { return v * v; }
+
 // ------------------------------------------------------------ state ops --
 
 template <typename A>

@@ -1,0 +1,382 @@
+// rowprog.cu - tadma_b200_row_program: per-row reductions of element chains
+// and the element-wise chain that reads them, in one pass over each row.
+//
+// A decomposed normalisation (generated code's LayerNorm: mean, -, pow,
+// mean, + eps, sqrt, /, *, +) is three kernels otherwise: two row
+// reductions and a 5-operand element-wise chain, reading the row three
+// times.  Here one warp owns a row at a time:
+// * the row's 16-byte chunks are copied into the warp's shared-memory
+//   buffer with cp.async (LDGSTS, L2-only), lane l taking chunks l, l + 32,
+//   ...; the next row's copies are issued before the current row is
+//   computed (two buffers per warp), so a row's load latency hides behind
+//   the previous row's arithmetic without holding the row in registers;
+// * each lane reads back only the chunks it copied, in the same order, so
+//   cp.async.wait_group alone orders the copy before the use;
+// * column operands (gamma, beta) are staged once per CTA;
+// * each stage folds its chain exactly as the row reductions fold (lane l
+//   visits vectors l, l + 32, ... in order, elements in order, then the
+//   fixed lane butterfly; MEAN divides by cols; the post chain; rounding to
+//   the stage's out dtype), so its value is the bits the separate reduction
+//   call stores; the final chain is the typed kernels' pre-decoded program.
+// There is no spin-wait: cp.async.wait_group is the hardware's own wait.
+#include "eltwise_impl.cuh"
+
+namespace tadma_b200 {
+
+constexpr int RP_MAX_RV = 2, RP_MAX_CV = 2, RP_MAX_SC = 2;
+constexpr int RP_NS = RP_MAX_SC + TADMA_ROWPROG_MAX_STAGES;  // scalar slots
+
+struct RowStageParams {
+    int32_t kind;  // K_SUM, K_MAX, K_MIN
+    int32_t mean;  // divide by cols
+    char* out;
+    int32_t out_dtype, pad;
+    int64_t out_stride;
+    FProg fp;
+    PostChain pc;
+};
+
+struct RowProgParams {
+    int64_t rows;
+    int32_t cols, nvec;  // nvec: 16-byte chunks per row
+    int32_t n_stages, pad;
+    const char* rv[RP_MAX_RV];
+    int64_t rv_rs[RP_MAX_RV];  // row strides in bytes
+    const char* cv[RP_MAX_CV];
+    const char* sc[RP_MAX_SC];
+    int32_t sc_dtype[RP_MAX_SC];
+    int64_t sc_rs[RP_MAX_SC];  // row strides in elements
+    RowStageParams st[TADMA_ROWPROG_MAX_STAGES];
+    FProg fp;
+    char* out;
+    int64_t out_rs;  // row stride in elements
+};
+
+namespace {
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
+
+template <typename TI>
+__device__ __forceinline__ void cvt16(uint4 r, float (&f)[16 / sizeof(TI)]) {
+    if constexpr (sizeof(TI) == 4) {
+        f[0] = __uint_as_float(r.x);
+        f[1] = __uint_as_float(r.y);
+        f[2] = __uint_as_float(r.z);
+        f[3] = __uint_as_float(r.w);
+    } else {
+        unpack8(r, std::is_same<TI, __half>::value ? TADMA_F16 : TADMA_BF16, f);
+    }
+}
+
+// The row reductions' fold (reduce_state.cuh update / combine) with the kind
+// known at run time.
+__device__ __forceinline__ float fold(int kind, float s, float v) {
+    return kind == K_SUM ? s + v : kind == K_MAX ? fmax_nan(s, v) : fmin_nan(s, v);
+}
+__device__ __forceinline__ float combine_k(int kind, float a, float b) {
+    return kind == K_SUM ? a + b : kind == K_MAX ? ((b > a || b != b) ? b : a) : ((b < a || b != b) ? b : a);
+}
+
+template <typename TI, typename TO, int NRV, int NCV, bool FAST>
+__global__ void __launch_bounds__(THREADS) rowprog_kernel(const __grid_constant__ RowProgParams p) {
+    pdl_begin();
+    constexpr int N = 16 / (int)sizeof(TI);
+    constexpr int NV = NRV + NCV;
+    extern __shared__ uint4 rp_smem[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nvec = p.nvec;
+    uint4* colbuf = rp_smem;                                          // NCV x nvec
+    uint4* wbuf = rp_smem + NCV * nvec + warp * (2 * NRV * nvec);     // 2 buffers x NRV x nvec
+    for (int i = threadIdx.x; i < NCV * nvec; i += blockDim.x)
+        colbuf[i] = *reinterpret_cast<const uint4*>(p.cv[i / nvec] + (int64_t)(i % nvec) * 16);
+    __syncthreads();
+
+    const int64_t nw = (int64_t)gridDim.x * (THREADS / 32);
+    int64_t row = (int64_t)blockIdx.x * (THREADS / 32) + warp;
+    auto issue = [&](int64_t r, int b) {
+#pragma unroll
+        for (int k = 0; k < NRV; k++) {
+            const char* src = p.rv[k] + r * p.rv_rs[k];
+            uint4* dst = wbuf + (b * NRV + k) * nvec;
+            for (int c = lane; c < nvec; c += 32) cp_async16(dst + c, src + (int64_t)c * 16);
+        }
+        cp_async_commit();
+    };
+    if (row < p.rows) issue(row, 0);
+    for (int b = 0; row < p.rows; row += nw, b ^= 1) {
+        if (row + nw < p.rows) {
+            issue(row + nw, b ^ 1);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        const uint4* rbuf = wbuf + b * NRV * nvec;
+        // scalar slots: the row scalars, then the stage results
+        float sv[RP_NS];
+#pragma unroll
+        for (int k = 0; k < RP_NS; k++) sv[k] = 0.0f;
+#pragma unroll
+        for (int k = 0; k < RP_MAX_SC; k++)
+            if (p.sc[k]) sv[k] = load_as<float>(p.sc[k], p.sc_dtype[k], row * p.sc_rs[k]);
+
+        // operand values of chunk c
+        auto operands = [&](int c, float (&vv)[NV][N]) {
+#pragma unroll
+            for (int k = 0; k < NRV; k++) cvt16<TI>(rbuf[k * nvec + c], vv[k]);
+#pragma unroll
+            for (int k = 0; k < NCV; k++) cvt16<TI>(colbuf[k * nvec + c], vv[NRV + k]);
+        };
+
+#pragma unroll 1
+        for (int s = 0; s < p.n_stages; s++) {
+            const RowStageParams& st = p.st[s];
+            const int kind = st.kind;
+            float acc_s = kind == K_SUM ? 0.0f : kind == K_MAX ? -INFINITY : INFINITY;
+#pragma unroll 1
+            for (int c = lane; c < nvec; c += 32) {
+                float vv[NV][N];
+                operands(c, vv);
+                float a[N];
+                run_fprog<NV, RP_NS, N, false>(st.fp, a, vv, sv);
+#pragma unroll
+                for (int j = 0; j < N; j++) acc_s = fold(kind, acc_s, a[j]);
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const float t = __shfl_xor_sync(0xffffffffu, acc_s, o);
+                acc_s = (lane & o) ? combine_k(kind, t, acc_s) : combine_k(kind, acc_s, t);
+            }
+            float v = acc_s;
+            if (st.mean) v = v / (float)p.cols;
+            if (st.pc.n) v = apply_post<float>(st.pc, v);
+            v = round_to(v, st.out_dtype);
+            if (lane == 0) store_from(st.out, st.out_dtype, row * st.out_stride, v);
+            if (s == 0) sv[RP_MAX_SC + 0] = v;
+            else if (s == 1) sv[RP_MAX_SC + 1] = v;
+            else sv[RP_MAX_SC + 2] = v;
+        }
+
+        TO* orow = reinterpret_cast<TO*>(p.out) + row * p.out_rs;
+#pragma unroll 1
+        for (int c = lane; c < nvec; c += 32) {
+            float vv[NV][N];
+            operands(c, vv);
+            float a[N];
+            run_fprog<NV, RP_NS, N, FAST>(p.fp, a, vv, sv);
+            if constexpr (sizeof(TO) == 4) {
+#pragma unroll
+                for (int j = 0; j < N; j += 4)
+                    st_stream_v4(orow + c * N + j, make_uint4(__float_as_uint(a[j]), __float_as_uint(a[j + 1]),
+                                                              __float_as_uint(a[j + 2]), __float_as_uint(a[j + 3])));
+            } else if constexpr (N == 8) {
+                st_stream_v4(orow + c * N, pack8(a, std::is_same<TO, __half>::value ? TADMA_F16 : TADMA_BF16));
+            } else {
+                // 16-bit out, fp32 rows: 4 values, 8 bytes
+                const int dt = std::is_same<TO, __half>::value ? TADMA_F16 : TADMA_BF16;
+                float f8[8] = {a[0], a[1], a[2], a[3], 0.0f, 0.0f, 0.0f, 0.0f};
+                const uint4 w = pack8(f8, dt);
+                __stcs(reinterpret_cast<uint2*>(orow + c * N), make_uint2(w.x, w.y));
+            }
+        }
+        __syncwarp();  // every lane is done with buffer b before it is refilled
+    }
+    cp_async_wait<0>();
+}
+
+template <typename TI, typename TO, int NRV, int NCV, bool FAST>
+int launch_rp_k(const RowProgParams& p, cudaStream_t s) {
+    const void* fn = (const void*)rowprog_kernel<TI, TO, NRV, NCV, FAST>;
+    const size_t smem = (size_t)(NCV * p.nvec + (THREADS / 32) * 2 * NRV * p.nvec) * 16;
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return cuda_fail(e, "tadma_b200_row_program smem attribute");
+    }
+    int per_sm = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, THREADS, smem);
+    if (e != cudaSuccess) return cuda_fail(e, "tadma_b200_row_program occupancy");
+    if (per_sm < 1) return fail(TADMA_ERR_UNSUPPORTED, "tadma_b200_row_program: rows do not fit shared memory");
+    const int64_t want = (p.rows + THREADS / 32 - 1) / (THREADS / 32);
+    const int64_t cap = (int64_t)sm_count() * per_sm;
+    const int grid = (int)(want < cap ? want : cap);
+    e = launch_pdl(rowprog_kernel<TI, TO, NRV, NCV, FAST>, dim3(grid), dim3(THREADS), smem, s, p);
+    if (e == cudaSuccess) e = cudaGetLastError();
+    return e == cudaSuccess ? TADMA_OK : cuda_fail(e, "tadma_b200_row_program launch");
+}
+
+template <typename TI, typename TO, bool FAST>
+int launch_rp_v(int nrv, int ncv, const RowProgParams& p, cudaStream_t s) {
+    if (nrv == 1) {
+        if (ncv == 0) return launch_rp_k<TI, TO, 1, 0, FAST>(p, s);
+        if (ncv == 1) return launch_rp_k<TI, TO, 1, 1, FAST>(p, s);
+        return launch_rp_k<TI, TO, 1, 2, FAST>(p, s);
+    }
+    if (ncv == 0) return launch_rp_k<TI, TO, 2, 0, FAST>(p, s);
+    if (ncv == 1) return launch_rp_k<TI, TO, 2, 1, FAST>(p, s);
+    return launch_rp_k<TI, TO, 2, 2, FAST>(p, s);
+}
+
+template <typename TI>
+int launch_rp_i(int odt, bool fast, int nrv, int ncv, const RowProgParams& p, cudaStream_t s) {
+    if (odt == TADMA_F32) return launch_rp_v<TI, float, false>(nrv, ncv, p, s);
+    if (odt == TADMA_F16) return fast ? launch_rp_v<TI, __half, true>(nrv, ncv, p, s) : launch_rp_v<TI, __half, false>(nrv, ncv, p, s);
+    return fast ? launch_rp_v<TI, __nv_bfloat16, true>(nrv, ncv, p, s) : launch_rp_v<TI, __nv_bfloat16, false>(nrv, ncv, p, s);
+}
+
+}  // namespace
+}  // namespace tadma_b200
+
+using namespace tadma_b200;
+
+extern "C" int tadma_b200_row_program(const tadma_row_program* rp, void* stream) {
+    if (!rp) return fail(TADMA_ERR_INVALID, "rp is NULL");
+    const int64_t rows = rp->rows, cols = rp->cols;
+    if (rows < 0 || cols < 1) return fail(TADMA_ERR_INVALID, "rows must be >= 0 and cols >= 1");
+    if (rp->n_ins < 1 || rp->n_ins > TADMA_MAX_INPUTS) return fail(TADMA_ERR_INVALID, "n_ins out of range [1, 6]");
+    if (rp->n_stages < 0 || rp->n_stages > TADMA_ROWPROG_MAX_STAGES) return fail(TADMA_ERR_INVALID, "n_stages out of range [0, 3]");
+    if (rp->n_instr < 0 || rp->n_instr > TADMA_MAX_INSTR) return fail(TADMA_ERR_INVALID, "n_instr out of range [0, 16]");
+    if (rp->compute != TADMA_COMPUTE_F32 && rp->compute != TADMA_COMPUTE_F32_PRECISE)
+        return fail(TADMA_ERR_UNSUPPORTED, "row programs compute in fp32");
+    std::string err = check_tensor(&rp->out, "out");
+    if (!err.empty()) return fail(TADMA_ERR_INVALID, err);
+    const tadma_tensor& o = rp->out;
+    if (o.rank != 2 || o.dims[0] != rows || o.dims[1] != cols || (cols > 1 && o.strides[1] != 1))
+        return fail(TADMA_ERR_INVALID, "out must be a {rows, cols} view with unit column stride");
+    if (o.dtype != TADMA_F32 && o.dtype != TADMA_F16 && o.dtype != TADMA_BF16)
+        return fail(TADMA_ERR_UNSUPPORTED, "out dtype must be F32, F16 or BF16");
+    const int n_ops = rp->n_ins + rp->n_stages;
+    auto valid_prog = [&](const tadma_instr* prog, int n, int avail) -> bool {
+        for (int i = 0; i < n; i++) {
+            const tadma_instr& I = prog[i];
+            const bool needs_b = I.op >= 32 || (I.op == TADMA_OP_COPY && I.b == TADMA_SRC_IMM);
+            if (needs_b && !(I.b == TADMA_SRC_IMM || (I.b >= 0 && I.b < avail))) return false;
+            if (I.op == TADMA_OP_WHERE && !(I.c == TADMA_SRC_IMM || (I.c >= 0 && I.c < avail))) return false;
+            if (I.round_dtype >= 0 && dtype_size(I.round_dtype) == 0) return false;
+        }
+        return true;
+    };
+    if (rp->acc < 0 || rp->acc >= n_ops || !valid_prog(rp->prog, rp->n_instr, n_ops))
+        return fail(TADMA_ERR_INVALID, "prog: operand out of range or bad round_dtype");
+    if (rows == 0) return TADMA_OK;
+
+    // Classify the operands: row (cs = 1), column (rows dim 1 or rs = 0,
+    // cs = 1) or row scalar (cols dim 1 or cs = 0).
+    RowProgParams p{};
+    p.rows = rows;
+    p.cols = (int32_t)cols;
+    int slot_of[TADMA_MAX_INPUTS + TADMA_ROWPROG_MAX_STAGES];
+    int nrv = 0, ncv = 0, nsc = 0, ti = -1;
+    int kind_of[TADMA_MAX_INPUTS];  // 0 row, 1 column, 2 scalar
+    for (int k = 0; k < rp->n_ins; k++) {
+        const tadma_tensor& t = rp->ins[k];
+        err = check_tensor(&t, "ins[k]");
+        if (!err.empty()) return fail(TADMA_ERR_INVALID, err);
+        if (t.rank != 2 || (t.dims[0] != rows && t.dims[0] != 1) || (t.dims[1] != cols && t.dims[1] != 1))
+            return fail(TADMA_ERR_INVALID, "ins[k] must be a rank-2 view of {rows, cols} (dims may be 1)");
+        const int64_t rs = t.dims[0] == 1 ? 0 : t.strides[0];
+        const int64_t cs = t.dims[1] == 1 ? 0 : t.strides[1];
+        if (cs == 1 && cols > 1) {
+            if (t.dtype != TADMA_F32 && t.dtype != TADMA_F16 && t.dtype != TADMA_BF16)
+                return fail(TADMA_ERR_UNSUPPORTED, "row / column operands must be F32, F16 or BF16");
+            if (ti >= 0 && t.dtype != ti) return fail(TADMA_ERR_UNSUPPORTED, "row / column operands must share one dtype");
+            ti = t.dtype;
+            kind_of[k] = (rs == 0 && rows > 1) ? 1 : 0;
+        } else if (cs == 0) {
+            if (t.dtype != TADMA_F32 && t.dtype != TADMA_F16 && t.dtype != TADMA_BF16 && t.dtype != TADMA_F64)
+                return fail(TADMA_ERR_UNSUPPORTED, "row scalars must be float");
+            kind_of[k] = 2;
+        } else {
+            return fail(TADMA_ERR_UNSUPPORTED, "ins[k]: the column stride must be 1 or 0");
+        }
+        if (kind_of[k] == 0 && nrv == RP_MAX_RV) return fail(TADMA_ERR_UNSUPPORTED, "more than 2 row operands");
+        if (kind_of[k] == 1 && ncv == RP_MAX_CV) return fail(TADMA_ERR_UNSUPPORTED, "more than 2 column operands");
+        if (kind_of[k] == 2 && nsc == RP_MAX_SC) return fail(TADMA_ERR_UNSUPPORTED, "more than 2 row scalars");
+        if (kind_of[k] == 0) nrv++;
+        else if (kind_of[k] == 1) ncv++;
+        else nsc++;
+    }
+    if (nrv == 0 || ti < 0) return fail(TADMA_ERR_UNSUPPORTED, "a row program needs a row operand");
+    const int es = dtype_size(ti);
+    const int N = 16 / es;
+    if (cols % N != 0 || cols > 32 * 8 * N) return fail(TADMA_ERR_UNSUPPORTED, "cols must be a multiple of 16 bytes and at most 256 chunks");
+    p.nvec = (int32_t)(cols / N);
+    int irv = 0, icv = 0, isc = 0;
+    for (int k = 0; k < rp->n_ins; k++) {
+        const tadma_tensor& t = rp->ins[k];
+        const int64_t rs = t.dims[0] == 1 ? 0 : t.strides[0];
+        if (kind_of[k] == 0) {
+            if ((uintptr_t)t.data % 16 || (rs * es) % 16) return fail(TADMA_ERR_UNSUPPORTED, "row operands need 16-byte aligned rows");
+            p.rv[irv] = (const char*)t.data;
+            p.rv_rs[irv] = rs * es;
+            slot_of[k] = irv++;
+        } else if (kind_of[k] == 1) {
+            if ((uintptr_t)t.data % 16) return fail(TADMA_ERR_UNSUPPORTED, "column operands must be 16-byte aligned");
+            p.cv[icv] = (const char*)t.data;
+            slot_of[k] = nrv + icv++;
+        } else {
+            p.sc[isc] = (const char*)t.data;
+            p.sc_dtype[isc] = t.dtype;
+            p.sc_rs[isc] = rs;
+            slot_of[k] = nrv + ncv + isc++;
+        }
+    }
+    const int NV = nrv + ncv;
+    for (int s = 0; s < rp->n_stages; s++) slot_of[rp->n_ins + s] = NV + RP_MAX_SC + s;
+
+    p.n_stages = rp->n_stages;
+    for (int s = 0; s < rp->n_stages; s++) {
+        const tadma_row_stage& S = rp->stages[s];
+        RowStageParams& st = p.st[s];
+        const int avail = rp->n_ins + s;  // a stage reads earlier stages only
+        if (S.op != TADMA_REDUCE_SUM && S.op != TADMA_REDUCE_MEAN && S.op != TADMA_REDUCE_MAX && S.op != TADMA_REDUCE_MIN)
+            return fail(TADMA_ERR_UNSUPPORTED, "stage op must be SUM, MEAN, MAX or MIN");
+        if (S.n_instr < 0 || S.n_instr > TADMA_MAX_INSTR || S.n_post < 0 || S.n_post > TADMA_MAX_INSTR)
+            return fail(TADMA_ERR_INVALID, "stage program length out of range [0, 16]");
+        if (S.acc < 0 || S.acc >= avail || !valid_prog(S.prog, S.n_instr, avail))
+            return fail(TADMA_ERR_INVALID, "stage program: operand out of range or bad round_dtype");
+        for (int i = 0; i < S.n_post; i++) {
+            const tadma_instr& I = S.post[i];
+            const bool needs_b = I.op >= 32 || (I.op == TADMA_OP_COPY && I.b == TADMA_SRC_IMM);
+            if (I.op == TADMA_OP_WHERE || (needs_b && I.b != TADMA_SRC_IMM))
+                return fail(TADMA_ERR_INVALID, "stage post: operands must be immediates");
+            if (I.round_dtype >= 0 && dtype_size(I.round_dtype) == 0) return fail(TADMA_ERR_INVALID, "bad round_dtype in post");
+            st.pc.prog[i] = I;
+        }
+        st.pc.n = S.n_post;
+        err = check_tensor(&S.out, "stage out");
+        if (!err.empty()) return fail(TADMA_ERR_INVALID, err);
+        if (S.out.rank != 1 || S.out.dims[0] != rows) return fail(TADMA_ERR_INVALID, "stage out must be a {rows} view");
+        st.out = (char*)S.out.data;
+        st.out_dtype = S.out.dtype;
+        st.out_stride = S.out.strides[0];
+        st.kind = S.op == TADMA_REDUCE_MAX ? K_MAX : S.op == TADMA_REDUCE_MIN ? K_MIN : K_SUM;
+        st.mean = S.op == TADMA_REDUCE_MEAN;
+        if (!decode_fprog(S.prog, S.n_instr, avail, st.fp, slot_of))
+            return fail(TADMA_ERR_UNSUPPORTED, "stage program step has no typed code");
+        st.fp.acc = slot_of[S.acc];
+    }
+    if (!decode_fprog(rp->prog, rp->n_instr, n_ops, p.fp, slot_of))
+        return fail(TADMA_ERR_UNSUPPORTED, "program step has no typed code");
+    p.fp.acc = slot_of[rp->acc];
+    p.out = (char*)o.data;
+    p.out_rs = o.strides[0];
+    if ((uintptr_t)o.data % 16 || (p.out_rs * dtype_size(o.dtype)) % (sizeof(float) == 4 && o.dtype != TADMA_F32 && es == 4 ? 8 : 16))
+        return fail(TADMA_ERR_UNSUPPORTED, "out rows must be aligned for vector stores");
+    // the typed kernels' fast-math rule (tadma_b200_eltwise)
+    bool fast = rp->compute != TADMA_COMPUTE_F32_PRECISE && (o.dtype == TADMA_F16 || o.dtype == TADMA_BF16);
+    for (int i = 0; i < rp->n_instr && fast; i++) {
+        const int rd = rp->prog[i].round_dtype;
+        if (!(rd < 0 || rd == TADMA_F32 || rd == TADMA_F16 || rd == TADMA_BF16)) fast = false;
+    }
+    cudaStream_t s = (cudaStream_t)stream;
+    switch (ti) {
+    case TADMA_F32: return launch_rp_i<float>(o.dtype, fast, nrv, ncv, p, s);
+    case TADMA_F16: return launch_rp_i<__half>(o.dtype, fast, nrv, ncv, p, s);
+    default: return launch_rp_i<__nv_bfloat16>(o.dtype, fast, nrv, ncv, p, s);
+    }
+}
