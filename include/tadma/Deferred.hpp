@@ -148,6 +148,7 @@ struct Deferred {
     int n_instr = 0, n_ins = 0;
     int compute = TADMA_COMPUTE_AUTO;
     bool reduce = false;  // a tadma_b200_reduce_chain_post call
+    bool plain = false;   // a reduction of ins[0] alone: tadma_b200_reduce, as the eager call
     int red_op = 0, axis = 0;
     std::array<tadma_instr, TADMA_MAX_INSTR> post{};
     int n_post = 0;
@@ -184,15 +185,20 @@ inline void sync_write(StorageCtl* c) {
             if (!d->done) run(*d);
 }
 
+inline bool try_row_program(Deferred& d);
+
 inline void run(Deferred& d) {
     if (d.done) return;
+    if (!d.reduce && try_row_program(d)) return;
     d.done = true;  // before the operands' own work runs: no re-entry
     std::array<tadma_tensor, TADMA_MAX_INPUTS> ins{};
     for (int k = 0; k < d.n_ins; k++) {
         sync_read(d.ins[k].ctl);
         ins[k] = d.ins[k].desc;
     }
-    if (d.reduce) {
+    if (d.plain) {
+        check(tadma_b200_reduce(d.red_op, &ins[0], d.axis, TADMA_OP_COPY, &d.out, d.stream), "tadma reduce (deferred)");
+    } else if (d.reduce) {
         check(tadma_b200_reduce_chain_post(d.red_op, ins.data(), d.n_ins, d.prog.data(), d.n_instr, d.post.data(),
                                            d.n_post, d.compute, d.axis, &d.out, d.stream),
               "tadma reduce (deferred)");
@@ -351,7 +357,7 @@ bool defer_eltwise(const Out& out, std::initializer_list<tadma_instr> prog_list,
         if (!desc_contiguous(o) || desc_numel(o) != desc_numel(p.out) || o.dtype != p.out.dtype) return false;
         if (p.compute != cm) return false;
         if (p.reduce) {
-            if (p.red_op == TADMA_REDUCE_ARGMAX || p.red_op == TADMA_REDUCE_ARGMIN) return false;
+            if (p.plain || p.red_op == TADMA_REDUCE_ARGMAX || p.red_op == TADMA_REDUCE_ARGMIN) return false;
             if (p.n_post + n_instr + 1 > TADMA_MAX_INSTR) return false;
             for (int i = 0; i < n_instr; i++)
                 if (!imm_only(prog[i])) return false;
@@ -386,7 +392,7 @@ bool defer_eltwise(const Out& out, std::initializer_list<tadma_instr> prog_list,
             // after a rounding of the reduced value to the result's own type
             // (what storing it would do).
             const bool arg = q.red_op == TADMA_REDUCE_ARGMAX || q.red_op == TADMA_REDUCE_ARGMIN;
-            bool ok = !arg && q.n_post + n_instr + 1 <= TADMA_MAX_INSTR && desc_contiguous(ops[0].desc) &&
+            bool ok = !arg && !q.plain && q.n_post + n_instr + 1 <= TADMA_MAX_INSTR && desc_contiguous(ops[0].desc) &&
                       ops[0].desc.data == q.out.data && ops[0].desc.dtype == q.out.dtype &&
                       desc_numel(ops[0].desc) == desc_numel(q.out);
             for (int i = 0; i < n_instr && ok; i++) ok = imm_only(prog[i]);
@@ -448,6 +454,10 @@ bool defer_eltwise(const Out& out, std::initializer_list<tadma_instr> prog_list,
 // t: one tadma_b200_reduce_chain_post over t's chain, itself deferred so
 // that immediate-operand steps on the result become its post chain.  False
 // when `t` holds no such chain (the caller reduces at once).
+// Reduced extents from this length on may split across CTAs in the eager
+// reduction (another fold order); those reductions are not deferred.
+constexpr int64_t kDeferMaxAxis = 16384;
+
 template <typename Out, typename T>
 bool defer_reduce(int op, int axis, const Out& out, const T& t) {
     if (!defer_enabled) return false;
@@ -455,6 +465,7 @@ bool defer_reduce(int op, int axis, const Out& out, const T& t) {
     StorageCtl* tc = t.data.ctl;
     const tadma_tensor i = t.describe_raw();
     if (!oc || !tc || oc->refs.load() != 1 || oc->pending) return false;
+    if (i.dims[axis] >= kDeferMaxAxis) return false;
     Deferred* q = spliceable(tc, i, true);
     if (!q) return false;
     auto d = std::make_shared<Deferred>(*q);
@@ -467,6 +478,239 @@ bool defer_reduce(int op, int axis, const Out& out, const T& t) {
     d->done = false;
     oc->pending = d;
     register_reader(d);
+    return true;
+}
+
+// out = reduce of t over its last axis (SUM, MEAN, MAX, MIN of a float
+// tensor), t holding no chain to splice: deferred as the eager
+// tadma_b200_reduce call, so that a row program can take it as a stage.
+template <typename Out, typename T>
+bool defer_plain_reduce(int op, int axis, const Out& out, const T& t) {
+    if (!defer_enabled) return false;
+    if (op != TADMA_REDUCE_SUM && op != TADMA_REDUCE_MEAN && op != TADMA_REDUCE_MAX && op != TADMA_REDUCE_MIN) return false;
+    StorageCtl* oc = out.data.ctl;
+    if (!oc || !t.data.ctl || oc->refs.load() != 1 || oc->pending) return false;
+    const tadma_tensor i = t.describe_raw();
+    if (axis != i.rank - 1 || i.dims[axis] >= kDeferMaxAxis) return false;
+    if (i.dtype != TADMA_F32 && i.dtype != TADMA_F16 && i.dtype != TADMA_BF16) return false;
+    auto d = std::make_shared<Deferred>();
+    d->reduce = d->plain = true;
+    d->red_op = op;
+    d->axis = axis;
+    d->ins[0] = make_operand(t);
+    d->n_ins = 1;
+    d->compute = TADMA_COMPUTE_F32;
+    d->out = out.describe_raw();
+    d->stream = stream;
+    oc->pending = d;
+    register_reader(d);
+    return true;
+}
+
+// ------------------------------------------------------------- row program --
+//
+// An element-wise chain whose operands include deferred reductions over the
+// last axis of rows of its own shape (a LayerNorm written out: mean, -, pow,
+// mean, + eps, sqrt, /, *, +) runs as one tadma_b200_row_program: the
+// reductions become its stages (their own deferred reductions first) and
+// the chain its final program.  The row program gives the bits of the
+// separate calls; grids it does not take (TADMA_ERR_UNSUPPORTED) run as
+// before.
+
+// A view of `t` over the {rows, cols} grid of `o`: a row operand (o's dims,
+// contiguous rows), a column operand (leading dims 1) or a row scalar (last
+// dim 1, leading dims o's with uniform row stride, or all 1).  False if none.
+inline bool grid_view(const tadma_tensor& t, const tadma_tensor& o, int64_t rows, int64_t cols, tadma_tensor& v) {
+    if (t.rank != o.rank) return false;
+    const int last = o.rank - 1;
+    bool lead_one = true, lead_same = true;
+    for (int d = 0; d < last; d++) {
+        if (t.dims[d] != 1 && t.strides[d] != 0) lead_one = false;
+        if (t.dims[d] != o.dims[d]) lead_same = false;
+    }
+    // uniform row stride over the leading dims (row-major row index)
+    auto row_stride = [&](int64_t& rs) {
+        rs = 0;
+        int64_t span = 1;
+        bool first = true;
+        for (int d = last - 1; d >= 0; d--) {
+            if (o.dims[d] == 1) continue;
+            if (first) {
+                rs = t.strides[d];
+                first = false;
+            } else if (t.strides[d] != rs * span) {
+                return false;
+            }
+            span *= o.dims[d];
+        }
+        return true;
+    };
+    v = tadma_tensor{};
+    v.data = t.data;
+    v.dtype = t.dtype;
+    v.rank = 2;
+    v.dims[0] = rows;
+    v.dims[1] = cols;
+    const bool vec = t.dims[last] == cols && (cols == 1 || t.strides[last] == 1);
+    const bool scal = t.dims[last] == 1 || t.strides[last] == 0;
+    int64_t rs = 0;
+    if (vec && cols > 1) {
+        if (lead_one) {
+            v.dims[0] = 1;
+            v.strides[0] = 0;
+        } else if (lead_same && row_stride(rs) && rs == cols) {
+            v.strides[0] = rs;
+        } else {
+            return false;
+        }
+        v.strides[1] = 1;
+        return true;
+    }
+    if (scal) {
+        v.dims[1] = 1;
+        v.strides[1] = 0;
+        if (lead_one) {
+            v.dims[0] = 1;
+            v.strides[0] = 0;
+        } else if (lead_same && row_stride(rs)) {
+            v.strides[0] = rs;
+        } else {
+            return false;
+        }
+        return true;
+    }
+    return false;
+}
+
+inline bool try_row_program(Deferred& d) {
+    if (d.reduce || d.compute != TADMA_COMPUTE_F32 || d.n_ins < 1) return false;
+    const tadma_tensor& o = d.out;
+    if (o.rank < 1 || !desc_contiguous(o)) return false;
+    const int last = o.rank - 1;
+    const int64_t cols = o.dims[last];
+    if (cols < 1) return false;
+    const int64_t rows = desc_numel(o) / cols;
+    if (rows < 1) return false;
+
+    // The stages: deferred reductions among the operands, their own first.
+    std::vector<std::shared_ptr<Deferred>> stages;
+    auto stage_of = [&](const DOperand& op) -> std::shared_ptr<Deferred> {
+        if (!op.ctl || !op.ctl->pending || op.ctl->pending->done || !op.ctl->pending->reduce) return nullptr;
+        return op.ctl->pending;
+    };
+    bool ok = true;
+    auto collect = [&](auto&& self, const Deferred& q, int depth) -> void {
+        for (int k = 0; k < q.n_ins && ok; k++) {
+            std::shared_ptr<Deferred> s = stage_of(q.ins[k]);
+            if (!s) continue;
+            if (std::find(stages.begin(), stages.end(), s) != stages.end()) continue;
+            const int op = s->red_op;
+            if (depth > TADMA_ROWPROG_MAX_STAGES || s->compute != TADMA_COMPUTE_F32 || s->axis != last ||
+                !(op == TADMA_REDUCE_SUM || op == TADMA_REDUCE_MEAN || op == TADMA_REDUCE_MAX || op == TADMA_REDUCE_MIN) ||
+                !desc_contiguous(s->out) || desc_numel(s->out) != rows) {
+                ok = false;
+                return;
+            }
+            // the reduced grid is o's: each operand broadcasts to o's dims
+            for (int j = 0; j < s->n_ins && ok; j++) {
+                const tadma_tensor& t = s->ins[j].desc;
+                if (t.rank != o.rank) ok = false;
+                for (int dd = 0; dd < t.rank && ok; dd++)
+                    if (t.dims[dd] != o.dims[dd] && t.dims[dd] != 1) ok = false;
+            }
+            if (!ok) return;
+            self(self, *s, depth + 1);
+            stages.push_back(s);
+        }
+    };
+    collect(collect, d, 0);
+    if (!ok || stages.empty() || (int)stages.size() > TADMA_ROWPROG_MAX_STAGES) return false;
+
+    // Operands: every view that is not a stage result, numbered first.
+    tadma_row_program rp{};
+    rp.rows = rows;
+    rp.cols = cols;
+    std::vector<StorageCtl*> leaf_ctl;
+    auto number = [&](const DOperand& op) -> int {
+        std::shared_ptr<Deferred> s = stage_of(op);
+        if (s) {
+            const int si = (int)(std::find(stages.begin(), stages.end(), s) - stages.begin());
+            // the consumer reads the stage's whole buffer as one value per row
+            tadma_tensor v;
+            if (op.desc.data != s->out.data || !grid_view(op.desc, o, rows, cols, v) || v.dims[1] != 1 ||
+                (rows > 1 && v.strides[0] != 1))
+                return -1;
+            return 1000 + si;  // resolved once the leaves are counted
+        }
+        tadma_tensor v;
+        if (!grid_view(op.desc, o, rows, cols, v)) return -1;
+        for (int k = 0; k < rp.n_ins; k++)
+            if (rp.ins[k].data == v.data && rp.ins[k].dtype == v.dtype && rp.ins[k].dims[0] == v.dims[0] &&
+                rp.ins[k].dims[1] == v.dims[1] && rp.ins[k].strides[0] == v.strides[0] && rp.ins[k].strides[1] == v.strides[1])
+                return k;
+        if (rp.n_ins == TADMA_MAX_INPUTS) return -1;
+        rp.ins[rp.n_ins] = v;
+        leaf_ctl.push_back(op.ctl);
+        return rp.n_ins++;
+    };
+    // operand numbers of each stage's and of the final chain's inputs
+    std::vector<std::array<int, TADMA_MAX_INPUTS>> smap(stages.size());
+    for (size_t si = 0; si < stages.size(); si++)
+        for (int k = 0; k < stages[si]->n_ins; k++)
+            if ((smap[si][k] = number(stages[si]->ins[k])) < 0) return false;
+    std::array<int, TADMA_MAX_INPUTS> dmap{};
+    for (int k = 0; k < d.n_ins; k++)
+        if ((dmap[k] = number(d.ins[k])) < 0) return false;
+    auto resolve = [&](int n) { return n >= 1000 ? rp.n_ins + (n - 1000) : n; };
+    auto remap = [&](const tadma_instr* prog, int n_instr, const std::array<int, TADMA_MAX_INPUTS>& map, tadma_instr* dst) {
+        for (int i = 0; i < n_instr; i++) {
+            tadma_instr I = prog[i];
+            if (I.b >= 0) I.b = resolve(map[I.b]);
+            if (I.c >= 0) I.c = resolve(map[I.c]);
+            dst[i] = I;
+        }
+    };
+    rp.n_stages = (int32_t)stages.size();
+    for (size_t si = 0; si < stages.size(); si++) {
+        const Deferred& s = *stages[si];
+        tadma_row_stage& st = rp.stages[si];
+        st.op = s.red_op;
+        st.n_instr = s.n_instr;
+        st.n_post = s.n_post;
+        st.acc = resolve(smap[si][0]);
+        remap(s.prog.data(), s.n_instr, smap[si], st.prog);
+        for (int i = 0; i < s.n_post; i++) st.post[i] = s.post[i];
+        st.out = tadma_tensor{};
+        st.out.data = s.out.data;
+        st.out.dtype = s.out.dtype;
+        st.out.rank = 1;
+        st.out.dims[0] = rows;
+        st.out.strides[0] = 1;
+    }
+    rp.n_instr = d.n_instr;
+    remap(d.prog.data(), d.n_instr, dmap, rp.prog);
+    rp.acc = resolve(dmap[0]);
+    rp.compute = launch_compute(d);
+    rp.out = tadma_tensor{};
+    rp.out.data = o.data;
+    rp.out.dtype = o.dtype;
+    rp.out.rank = 2;
+    rp.out.dims[0] = rows;
+    rp.out.dims[1] = cols;
+    rp.out.strides[0] = cols;
+    rp.out.strides[1] = 1;
+
+    // the inputs' own deferred work first
+    for (StorageCtl* c : leaf_ctl) sync_read(c);
+    const int rc = tadma_b200_row_program(&rp, d.stream);
+    if (rc == TADMA_ERR_UNSUPPORTED) return false;
+    check(rc, "tadma row program (deferred)");
+    d.done = true;
+    for (auto& s : stages) {
+        s->done = true;
+        for (int k = 0; k < s->n_ins; k++) s->ins[k] = DOperand{};
+    }
+    for (int k = 0; k < d.n_ins; k++) d.ins[k] = DOperand{};
     return true;
 }
 

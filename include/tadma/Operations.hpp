@@ -211,8 +211,12 @@ auto reduce_to(const T& t) {
     static_assert(Ax >= 0 && Ax < T::Rank, "reduction axis out of range");
     using OutDims = std::conditional_t<KeepDims, typename T::Dims::template Set<Ax, 1>, typename T::Dims::template Remove<Ax>>;
     Tensor<R, Allocator<kCUDA>, OutDims> out;
-    // A reduction of a deferred element-wise result: one reduce_chain, deferred.
+    // A reduction of a deferred element-wise result: one reduce_chain, deferred;
+    // a last-axis reduction of anything else: the eager call, deferred, so
+    // that the chain that reads it can take it into one row program.
     if (defer_reduce(OP, Ax, out, t)) return out;
+    if constexpr (std::is_floating_point_v<R> || std::is_same_v<R, __half> || std::is_same_v<R, __nv_bfloat16>)
+        if (defer_plain_reduce(OP, Ax, out, t)) return out;
     tadma_tensor i = t.describe(), o = out.describe();
     check(tadma_b200_reduce(OP, &i, Ax, TADMA_OP_COPY, &o, stream), "tadma reduce");
     return out;

@@ -13,9 +13,9 @@ import ctypes
 import os
 
 from .abi import (  # noqa: F401  (re-exported)
-    MAX_INPUTS, MAX_INSTR, MAX_RANK, SRC_IMM, SRC_NONE, BINARY_OPS, TRANSCENDENTAL, UNARY_OPS,
-    Compute, Dist, DType, LNMode, Op, Reduce, Status, TadmaInstr, TadmaTensor, instr, make_tensor,
-    program,
+    MAX_INPUTS, MAX_INSTR, MAX_RANK, ROWPROG_MAX_STAGES, SRC_IMM, SRC_NONE, BINARY_OPS, TRANSCENDENTAL, UNARY_OPS,
+    Compute, Dist, DType, LNMode, Op, Reduce, Status, TadmaInstr, TadmaRowProgram, TadmaRowStage, TadmaTensor,
+    instr, make_tensor, program,
 )
 
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libtadma_b200.so")
@@ -26,7 +26,7 @@ EXPORTS = (
     "tadma_b200_eltwise", "tadma_b200_reduce", "tadma_b200_softmax", "tadma_b200_layer_norm",
     "tadma_b200_rms_norm", "tadma_b200_gather", "tadma_b200_fill", "tadma_b200_last_error",
     "tadma_b200_version", "tadma_b200_error_flags", "tadma_b200_dtype_size", "tadma_b200_reduce_noalloc",
-    "tadma_b200_reduce_chain", "tadma_b200_reduce_chain_post",
+    "tadma_b200_reduce_chain", "tadma_b200_reduce_chain_post", "tadma_b200_row_program",
 )
 
 
@@ -55,6 +55,7 @@ def lib() -> ctypes.CDLL:
     L.tadma_b200_reduce_chain.argtypes = [c_int, P(T), c_int, P(I), c_int, c_int, c_int, P(T), c_void]
     L.tadma_b200_reduce_chain_post.argtypes = [c_int, P(T), c_int, P(I), c_int, P(I), c_int, c_int, c_int, P(T),
                                                c_void]
+    L.tadma_b200_row_program.argtypes = [P(TadmaRowProgram), c_void]
     L.tadma_b200_softmax.argtypes = [P(T), c_int, P(T), c_void]
     L.tadma_b200_layer_norm.argtypes = [P(T), c_int, P(T), P(T), c_double, c_int, P(T), c_void]
     L.tadma_b200_rms_norm.argtypes = [P(T), c_int, c_double, P(T), c_void]
@@ -212,6 +213,33 @@ def reduce(op, x, axis, out, pre_op=Op.COPY, stream=None) -> None:
 
 def reduce_chain(op, ins, prog, axis, out, compute=Compute.AUTO, stream=None, post=None) -> None:
     prepare_reduce_chain(op, ins, prog, axis, out, compute, stream, post)()
+
+
+def row_program(rows, cols, ins, stages, prog, out, acc=0, compute=Compute.F32, stream=None) -> None:
+    """tadma_b200_row_program.  ins: descriptors (or torch tensors) viewed as
+    {rows, cols}; stages: (op, chain, post, out, acc) tuples, out a {rows}
+    descriptor or tensor; prog: the final chain; out: {rows, cols}."""
+    rp = TadmaRowProgram()
+    rp.rows, rp.cols = int(rows), int(cols)
+    rp.n_ins = len(ins)
+    for k, t in enumerate(ins):
+        rp.ins[k] = _d(t)
+    rp.n_stages = len(stages)
+    for s, (op, chain, post, sout, sacc) in enumerate(stages):
+        st = rp.stages[s]
+        st.op, st.n_instr, st.n_post, st.acc = int(op), len(chain), len(post), int(sacc)
+        for i, I in enumerate(chain):
+            st.prog[i] = I
+        for i, I in enumerate(post):
+            st.post[i] = I
+        st.out = _d(sout)
+    rp.n_instr = len(prog)
+    for i, I in enumerate(prog):
+        rp.prog[i] = I
+    rp.acc = int(acc)
+    rp.compute = int(compute)
+    rp.out = _d(out)
+    check(lib().tadma_b200_row_program(ctypes.byref(rp), _stream(stream)))
 
 
 def softmax(x, axis, out, stream=None) -> None:

@@ -142,6 +142,40 @@ class TadmaInstr(ctypes.Structure):
     ]
 
 
+ROWPROG_MAX_STAGES = 3
+
+
+class TadmaRowStage(ctypes.Structure):
+    """tadma_row_stage: one per-row reduction of an element chain."""
+    _fields_ = [
+        ("op", ctypes.c_int32),
+        ("n_instr", ctypes.c_int32),
+        ("n_post", ctypes.c_int32),
+        ("acc", ctypes.c_int32),
+        ("prog", TadmaInstr * MAX_INSTR),
+        ("post", TadmaInstr * MAX_INSTR),
+        ("out", TadmaTensor),
+    ]
+
+
+class TadmaRowProgram(ctypes.Structure):
+    """tadma_row_program: stages, then the final chain, over a row grid."""
+    _fields_ = [
+        ("rows", ctypes.c_int64),
+        ("cols", ctypes.c_int64),
+        ("n_ins", ctypes.c_int32),
+        ("n_stages", ctypes.c_int32),
+        ("n_instr", ctypes.c_int32),
+        ("compute", ctypes.c_int32),
+        ("acc", ctypes.c_int32),
+        ("pad", ctypes.c_int32),
+        ("ins", TadmaTensor * MAX_INPUTS),
+        ("stages", TadmaRowStage * ROWPROG_MAX_STAGES),
+        ("prog", TadmaInstr * MAX_INSTR),
+        ("out", TadmaTensor),
+    ]
+
+
 def make_tensor(ptr: int | None, dtype: int, shape, strides=None) -> TadmaTensor:
     """Descriptor for a strided view; strides in ELEMENTS (default row-major)."""
     shape = [int(s) for s in shape]

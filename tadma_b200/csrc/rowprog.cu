@@ -285,7 +285,8 @@ extern "C" int tadma_b200_row_program(const tadma_row_program* rp, void* stream)
                 return fail(TADMA_ERR_UNSUPPORTED, "row / column operands must be F32, F16 or BF16");
             if (ti >= 0 && t.dtype != ti) return fail(TADMA_ERR_UNSUPPORTED, "row / column operands must share one dtype");
             ti = t.dtype;
-            kind_of[k] = (rs == 0 && rows > 1) ? 1 : 0;
+            // a column operand repeats one row: stride 0, or a single row over several
+            kind_of[k] = (t.strides[0] == 0 || (t.dims[0] == 1 && rows > 1)) ? 1 : 0;
         } else if (cs == 0) {
             if (t.dtype != TADMA_F32 && t.dtype != TADMA_F16 && t.dtype != TADMA_BF16 && t.dtype != TADMA_F64)
                 return fail(TADMA_ERR_UNSUPPORTED, "row scalars must be float");

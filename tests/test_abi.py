@@ -46,8 +46,41 @@ def test_enums_match_header():
     assert defines["TADMA_MAX_INPUTS"] == abi.MAX_INPUTS
     assert defines["TADMA_MAX_INSTR"] == abi.MAX_INSTR
     assert defines["TADMA_SRC_IMM"] == abi.SRC_IMM
+    assert defines["TADMA_ROWPROG_MAX_STAGES"] == abi.ROWPROG_MAX_STAGES
     assert ctypes.sizeof(abi.TadmaTensor) == 8 + 4 + 4 + 8 * 8 * 2
     assert ctypes.sizeof(abi.TadmaInstr) == 24
+    # tadma_row_stage / tadma_row_program: natural alignment, no padding beyond the declared fields
+    assert ctypes.sizeof(abi.TadmaRowStage) == 16 + 2 * 16 * 24 + 144
+    assert ctypes.sizeof(abi.TadmaRowProgram) == 16 + 24 + 6 * 144 + 3 * ctypes.sizeof(abi.TadmaRowStage) + 16 * 24 + 144
+
+
+def test_row_program_validation_needs_no_gpu():
+    L = tb.lib()
+    fake = 0x1000
+    rp = abi.TadmaRowProgram()
+    rp.rows, rp.cols, rp.n_ins, rp.n_stages, rp.n_instr, rp.compute = 8, 64, 1, 0, 0, int(abi.Compute.F32)
+    rp.ins[0] = abi.make_tensor(fake, abi.DType.F32, [8, 64])
+    rp.out = abi.make_tensor(fake, abi.DType.F32, [8, 64])
+    rp.compute = int(abi.Compute.F64)
+    assert L.tadma_b200_row_program(ctypes.byref(rp), None) == abi.Status.ERR_UNSUPPORTED
+    rp.compute = int(abi.Compute.F32)
+    rp.n_stages = 4
+    assert L.tadma_b200_row_program(ctypes.byref(rp), None) == abi.Status.ERR_INVALID
+    rp.n_stages = 1
+    rp.stages[0].op = int(abi.Reduce.ARGMAX)
+    rp.stages[0].out = abi.make_tensor(fake, abi.DType.F32, [8])
+    assert L.tadma_b200_row_program(ctypes.byref(rp), None) == abi.Status.ERR_UNSUPPORTED
+    rp.stages[0].op = int(abi.Reduce.MEAN)
+    rp.stages[0].n_instr = 1
+    rp.stages[0].prog[0] = abi.instr(abi.Op.SUB, b=1)  # a stage reads earlier stages only
+    assert L.tadma_b200_row_program(ctypes.byref(rp), None) == abi.Status.ERR_INVALID
+    rp.stages[0].n_instr = 0
+    rp.ins[0] = abi.make_tensor(fake, abi.DType.F32, [8, 64], [64, 2])  # column stride 2
+    assert L.tadma_b200_row_program(ctypes.byref(rp), None) == abi.Status.ERR_UNSUPPORTED
+    rp.ins[0] = abi.make_tensor(fake, abi.DType.F32, [8, 66])
+    rp.cols = 66
+    rp.out = abi.make_tensor(fake, abi.DType.F32, [8, 66])
+    assert L.tadma_b200_row_program(ctypes.byref(rp), None) == abi.Status.ERR_UNSUPPORTED  # 66 fp32: not 16-byte rows
 
 
 def test_dtype_sizes():
