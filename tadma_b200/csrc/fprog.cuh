@@ -24,7 +24,8 @@ constexpr int FC_BI = 21;    // FC_BI + (op - 32): binary op, imm second argumen
 constexpr int FC_BV = 41;    // FC_BV + (op - 32): binary op, operand `b` second argument
 constexpr int FC_WHERE = 61; // acc = acc != 0 ? b : c (operands, or the imm where b / c < 0)
 constexpr int FC_RND = 62;   // FC_RND + k: round to the k-th of F16, BF16, I64, I32, U8, BOOL, I8
-constexpr int FC_COUNT = 69;
+constexpr int FC_SQR = 69;   // pow(acc, 2) with the immediate 2: one rounded multiply, as binary(POW) gives it
+constexpr int FC_COUNT = 70;
 
 struct FInstr {
     uint8_t code;
@@ -68,7 +69,8 @@ inline bool decode_fprog(const tadma_instr* prog, int n_instr, int nin, FProg& f
             }
         } else if (I.op >= TADMA_OP_ADD && I.op <= TADMA_OP_LOR) {
             const int s = slot(I.b);
-            emit(s >= 0 ? FC_BV + (I.op - TADMA_OP_ADD) : FC_BI + (I.op - TADMA_OP_ADD), s, -1, I.imm);
+            if (I.op == TADMA_OP_POW && s < 0 && (float)I.imm == 2.0f) emit(FC_SQR, -1, -1, 0.0);
+            else emit(s >= 0 ? FC_BV + (I.op - TADMA_OP_ADD) : FC_BI + (I.op - TADMA_OP_ADD), s, -1, I.imm);
         } else if (I.op == TADMA_OP_WHERE) {
             emit(FC_WHERE, slot(I.b), slot(I.c), I.imm);
         } else {
@@ -215,6 +217,10 @@ __device__ __forceinline__ void run_fprog(const FProg& fp, float (&acc)[W], cons
             // c is chosen per element, so no second W-wide temporary is live
 #pragma unroll
             for (int j = 0; j < W; j++) acc[j] = acc[j] != 0.0f ? bsel[j] : operand_at<NV, NS, W>(I.c, I.imm, vv, sv, j);
+        } break;
+        case FC_SQR: {
+#pragma unroll
+            for (int j = 0; j < W; j++) acc[j] = __fmul_rn(acc[j], acc[j]);
         } break;
             TADMA_FR(0, TADMA_F16)
             TADMA_FR(1, TADMA_BF16)

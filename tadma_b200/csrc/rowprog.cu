@@ -39,7 +39,9 @@ struct RowStageParams {
 struct RowProgParams {
     int64_t rows;
     int32_t cols, nvec;  // nvec: 16-byte chunks per row
-    int32_t n_stages, pad;
+    int32_t n_stages;
+    int32_t n_rv, n_cv;  // row / column operands
+    int32_t fast;        // the final chain's fast-math bodies (16-bit out)
     const char* rv[RP_MAX_RV];
     int64_t rv_rs[RP_MAX_RV];  // row strides in bytes
     const char* cv[RP_MAX_CV];
@@ -74,40 +76,215 @@ __device__ __forceinline__ void cvt16(uint4 r, float (&f)[16 / sizeof(TI)]) {
     }
 }
 
-// The row reductions' fold (reduce_state.cuh update / combine) with the kind
+// The row reductions' lane combine (reduce_state.cuh combine) with the kind
 // known at run time.
-__device__ __forceinline__ float fold(int kind, float s, float v) {
-    return kind == K_SUM ? s + v : kind == K_MAX ? fmax_nan(s, v) : fmin_nan(s, v);
-}
 __device__ __forceinline__ float combine_k(int kind, float a, float b) {
     return kind == K_SUM ? a + b : kind == K_MAX ? ((b > a || b != b) ? b : a) : ((b < a || b != b) ? b : a);
 }
 
-template <typename TI, typename TO, int NRV, int NCV, bool FAST>
-__global__ void __launch_bounds__(THREADS) rowprog_kernel(const __grid_constant__ RowProgParams p) {
+// The pre-decoded program of one pass (a stage's chain or the final chain)
+// on a group of G chunks of the lane: step-major, so each step is
+// dispatched once per G x N values and reads its operand straight from
+// shared memory.  The op bodies and roundings are those of run_fprog.
+// Operand slots of the kernel: row operands 0-1, column operands 2-3, row
+// scalars 4-5, stage results 6-8 (RP_VEC vector slots, then RP_NS scalars).
+constexpr int RP_VEC = RP_MAX_RV + RP_MAX_CV;
+
+template <typename TI, int G>
+struct RowGroup {
+    static constexpr int N = 16 / (int)sizeof(TI);
+    const uint4* rbuf;
+    const uint4* cbuf;
+    int stride, c0;  // chunks per (padded) operand buffer; chunk of u: c0 + 32 u
+    __device__ __forceinline__ const uint4* base(int slot) const {
+        return slot < RP_MAX_RV ? rbuf + slot * stride : cbuf + (slot - RP_MAX_RV) * stride;
+    }
+    // The buffers are padded to whole groups: a chunk past the row reads
+    // padding, computes on it and is neither folded nor stored.
+    __device__ __forceinline__ void load(int slot, int u, float (&f)[N]) const { cvt16<TI>(base(slot)[c0 + 32 * u], f); }
+};
+
+template <int NS>
+__device__ __forceinline__ float scalar_slot(const float (&sv)[NS], int q) {
+    float s = 0.0f;
+#pragma unroll
+    for (int k = 0; k < NS; k++)
+        if (q == k) s = sv[k];
+    return s;
+}
+
+#define TADMA_RU(OP)                                                                   \
+    case OP: {                                                                         \
+        _Pragma("unroll") for (int u = 0; u < G; u++)                                  \
+            _Pragma("unroll") for (int j = 0; j < N; j++) acc[u][j] = funary<OP, false>(acc[u][j]); \
+    } break;
+#define TADMA_RUF(OP)                                                                  \
+    case OP: {                                                                         \
+        if (fast) {                                                                    \
+            _Pragma("unroll") for (int u = 0; u < G; u++)                              \
+                _Pragma("unroll") for (int j = 0; j < N; j++) acc[u][j] = funary<OP, true>(acc[u][j]); \
+        } else {                                                                       \
+            _Pragma("unroll") for (int u = 0; u < G; u++)                              \
+                _Pragma("unroll") for (int j = 0; j < N; j++) acc[u][j] = funary<OP, false>(acc[u][j]); \
+        }                                                                              \
+    } break;
+#define TADMA_RB(OP)                                                                   \
+    case FC_BI + (OP - TADMA_OP_ADD): {                                                \
+        _Pragma("unroll") for (int u = 0; u < G; u++)                                  \
+            _Pragma("unroll") for (int j = 0; j < N; j++) acc[u][j] = binary(OP, acc[u][j], bs, bs); \
+    } break;                                                                           \
+    case FC_BV + (OP - TADMA_OP_ADD): {                                                \
+        if (bvec) {                                                                    \
+            _Pragma("unroll") for (int u = 0; u < G; u++) {                            \
+                float b[N];                                                            \
+                grp.load(I.b, u, b);                                                   \
+                _Pragma("unroll") for (int j = 0; j < N; j++) acc[u][j] = binary(OP, acc[u][j], b[j], b[j]); \
+            }                                                                          \
+        } else {                                                                       \
+            _Pragma("unroll") for (int u = 0; u < G; u++)                              \
+                _Pragma("unroll") for (int j = 0; j < N; j++) acc[u][j] = binary(OP, acc[u][j], bs, bs); \
+        }                                                                              \
+    } break;
+#define TADMA_RR(K, DT)                                                                \
+    case FC_RND + K: {                                                                 \
+        _Pragma("unroll") for (int u = 0; u < G; u++)                                  \
+            _Pragma("unroll") for (int j = 0; j < N; j++) acc[u][j] = round_to(acc[u][j], DT); \
+    } break;
+
+template <typename TI, int G, int NS>
+__device__ __forceinline__ void run_group(const FProg& fp, bool fast, const RowGroup<TI, G>& grp,
+                                          const float (&sv)[NS], float (&acc)[G][16 / sizeof(TI)]) {
+    constexpr int N = 16 / (int)sizeof(TI);
+    constexpr int NV = RP_VEC;
+    if (fp.acc < NV) {
+#pragma unroll
+        for (int u = 0; u < G; u++) grp.load(fp.acc, u, acc[u]);
+    } else {
+        const float s = scalar_slot<NS>(sv, fp.acc - NV);
+#pragma unroll
+        for (int u = 0; u < G; u++)
+#pragma unroll
+            for (int j = 0; j < N; j++) acc[u][j] = s;
+    }
+    for (int i = 0; i < fp.n; i++) {
+        const FInstr I = fp.ins[i];
+        const bool bvec = I.b >= 0 && I.b < NV;
+        const float bs = I.b >= NV ? scalar_slot<NS>(sv, I.b - NV) : I.imm;
+        switch (I.code) {
+        case FC_FILL: {
+#pragma unroll
+            for (int u = 0; u < G; u++)
+#pragma unroll
+                for (int j = 0; j < N; j++) acc[u][j] = I.imm;
+        } break;
+            TADMA_RU(TADMA_OP_NEG)
+            TADMA_RU(TADMA_OP_ABS)
+            TADMA_RUF(TADMA_OP_EXP)
+            TADMA_RU(TADMA_OP_LOG)
+            TADMA_RU(TADMA_OP_SQRT)
+            TADMA_RU(TADMA_OP_SIN)
+            TADMA_RU(TADMA_OP_COS)
+            TADMA_RU(TADMA_OP_TAN)
+            TADMA_RU(TADMA_OP_ASIN)
+            TADMA_RU(TADMA_OP_ACOS)
+            TADMA_RU(TADMA_OP_ATAN)
+            TADMA_RU(TADMA_OP_ASINH)
+            TADMA_RU(TADMA_OP_ACOSH)
+            TADMA_RU(TADMA_OP_ATANH)
+            TADMA_RU(TADMA_OP_ERF)
+            TADMA_RU(TADMA_OP_RELU)
+            TADMA_RUF(TADMA_OP_SIGMOID)
+            TADMA_RU(TADMA_OP_TANH)
+            TADMA_RUF(TADMA_OP_GELU)
+            TADMA_RU(TADMA_OP_NOT)
+            TADMA_RB(TADMA_OP_ADD)
+            TADMA_RB(TADMA_OP_SUB)
+            TADMA_RB(TADMA_OP_MUL)
+            TADMA_RB(TADMA_OP_DIV)
+            TADMA_RB(TADMA_OP_POW)
+            TADMA_RB(TADMA_OP_RSUB)
+            TADMA_RB(TADMA_OP_RDIV)
+            TADMA_RB(TADMA_OP_MAX)
+            TADMA_RB(TADMA_OP_MIN)
+            TADMA_RB(TADMA_OP_EQ)
+            TADMA_RB(TADMA_OP_NE)
+            TADMA_RB(TADMA_OP_LT)
+            TADMA_RB(TADMA_OP_GT)
+            TADMA_RB(TADMA_OP_LE)
+            TADMA_RB(TADMA_OP_GE)
+            TADMA_RB(TADMA_OP_AND)
+            TADMA_RB(TADMA_OP_OR)
+            TADMA_RB(TADMA_OP_XOR)
+            TADMA_RB(TADMA_OP_LAND)
+            TADMA_RB(TADMA_OP_LOR)
+        case FC_WHERE: {
+            const bool cvec = I.c >= 0 && I.c < NV;
+            const float cs = I.c >= NV ? scalar_slot<NS>(sv, I.c - NV) : I.imm;
+#pragma unroll
+            for (int u = 0; u < G; u++) {
+                float b[N], c[N];
+                if (bvec) grp.load(I.b, u, b);
+                if (cvec) grp.load(I.c, u, c);
+#pragma unroll
+                for (int j = 0; j < N; j++) acc[u][j] = acc[u][j] != 0.0f ? (bvec ? b[j] : bs) : (cvec ? c[j] : cs);
+            }
+        } break;
+        case FC_SQR: {
+#pragma unroll
+            for (int u = 0; u < G; u++)
+#pragma unroll
+                for (int j = 0; j < N; j++) acc[u][j] = __fmul_rn(acc[u][j], acc[u][j]);
+        } break;
+            TADMA_RR(0, TADMA_F16)
+            TADMA_RR(1, TADMA_BF16)
+            TADMA_RR(2, TADMA_I64)
+            TADMA_RR(3, TADMA_I32)
+            TADMA_RR(4, TADMA_U8)
+            TADMA_RR(5, TADMA_BOOL)
+            TADMA_RR(6, TADMA_I8)
+        default:
+            break;
+        }
+    }
+}
+
+#undef TADMA_RU
+#undef TADMA_RUF
+#undef TADMA_RB
+#undef TADMA_RR
+
+// Chunks of one operand buffer in shared memory: the row's, padded to whole
+// groups of G chunks per lane.
+__host__ __device__ constexpr int rp_stride(int nvec, int G) { return (nvec + 32 * G - 1) / (32 * G) * (32 * G); }
+
+template <typename TI, typename TO, int G>
+__global__ void __launch_bounds__(THREADS, 2) rowprog_kernel(const __grid_constant__ RowProgParams p) {
     pdl_begin();
     constexpr int N = 16 / (int)sizeof(TI);
-    constexpr int NV = NRV + NCV;
     extern __shared__ uint4 rp_smem[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int nvec = p.nvec;
-    uint4* colbuf = rp_smem;                                          // NCV x nvec
-    uint4* wbuf = rp_smem + NCV * nvec + warp * (2 * NRV * nvec);     // 2 buffers x NRV x nvec
-    for (int i = threadIdx.x; i < NCV * nvec; i += blockDim.x)
-        colbuf[i] = *reinterpret_cast<const uint4*>(p.cv[i / nvec] + (int64_t)(i % nvec) * 16);
+    const int stride = rp_stride(nvec, G);
+    const int nrv = p.n_rv, ncv = p.n_cv;
+    uint4* colbuf = rp_smem;                                           // ncv x stride
+    uint4* wbuf = rp_smem + ncv * stride + warp * (2 * nrv * stride);  // 2 buffers x nrv x stride
+    for (int i = threadIdx.x; i < ncv * nvec; i += blockDim.x)
+        colbuf[(i / nvec) * stride + i % nvec] = *reinterpret_cast<const uint4*>(p.cv[i / nvec] + (int64_t)(i % nvec) * 16);
     __syncthreads();
 
     const int64_t nw = (int64_t)gridDim.x * (THREADS / 32);
     int64_t row = (int64_t)blockIdx.x * (THREADS / 32) + warp;
     auto issue = [&](int64_t r, int b) {
-#pragma unroll
-        for (int k = 0; k < NRV; k++) {
+        for (int k = 0; k < nrv; k++) {
             const char* src = p.rv[k] + r * p.rv_rs[k];
-            uint4* dst = wbuf + (b * NRV + k) * nvec;
+            uint4* dst = wbuf + (b * nrv + k) * stride;
             for (int c = lane; c < nvec; c += 32) cp_async16(dst + c, src + (int64_t)c * 16);
         }
         cp_async_commit();
     };
+    // chunks of this lane: lane, lane + 32, ...; groups of G of them
+    const int nchunk = lane < nvec ? (nvec - lane + 31) / 32 : 0;
+    const int ngroups = stride / (32 * G);
     if (row < p.rows) issue(row, 0);
     for (int b = 0; row < p.rows; row += nw, b ^= 1) {
         if (row + nw < p.rows) {
@@ -116,7 +293,7 @@ __global__ void __launch_bounds__(THREADS) rowprog_kernel(const __grid_constant_
         } else {
             cp_async_wait<0>();
         }
-        const uint4* rbuf = wbuf + b * NRV * nvec;
+        RowGroup<TI, G> grp{wbuf + b * nrv * stride, colbuf, stride, 0};
         // scalar slots: the row scalars, then the stage results
         float sv[RP_NS];
 #pragma unroll
@@ -125,28 +302,65 @@ __global__ void __launch_bounds__(THREADS) rowprog_kernel(const __grid_constant_
         for (int k = 0; k < RP_MAX_SC; k++)
             if (p.sc[k]) sv[k] = load_as<float>(p.sc[k], p.sc_dtype[k], row * p.sc_rs[k]);
 
-        // operand values of chunk c
-        auto operands = [&](int c, float (&vv)[NV][N]) {
-#pragma unroll
-            for (int k = 0; k < NRV; k++) cvt16<TI>(rbuf[k * nvec + c], vv[k]);
-#pragma unroll
-            for (int k = 0; k < NCV; k++) cvt16<TI>(colbuf[k * nvec + c], vv[NRV + k]);
-        };
-
+        // passes 0 .. n_stages - 1: the stages; pass n_stages: the final chain
 #pragma unroll 1
-        for (int s = 0; s < p.n_stages; s++) {
-            const RowStageParams& st = p.st[s];
-            const int kind = st.kind;
+        for (int s = 0; s <= p.n_stages; s++) {
+            const bool final_pass = s == p.n_stages;
+            const FProg& fp = final_pass ? p.fp : p.st[s].fp;
+            const int kind = final_pass ? K_SUM : p.st[s].kind;
             float acc_s = kind == K_SUM ? 0.0f : kind == K_MAX ? -INFINITY : INFINITY;
+            TO* orow = reinterpret_cast<TO*>(p.out) + row * p.out_rs;
 #pragma unroll 1
-            for (int c = lane; c < nvec; c += 32) {
-                float vv[NV][N];
-                operands(c, vv);
-                float a[N];
-                run_fprog<NV, RP_NS, N, false>(st.fp, a, vv, sv);
+            for (int g = 0; g < ngroups; g++) {
+                grp.c0 = lane + 32 * G * g;
+                const int nval = nchunk - G * g;  // chunks of this group inside the row (may be <= 0 or > G)
+                float a[G][N];
+                run_group<TI, G, RP_NS>(fp, final_pass && p.fast, grp, sv, a);
+                if (!final_pass) {
+                    // the row reductions' per-element fold, in chunk order
+                    if (kind == K_SUM) {
 #pragma unroll
-                for (int j = 0; j < N; j++) acc_s = fold(kind, acc_s, a[j]);
+                        for (int u = 0; u < G; u++)
+                            if (u < nval)
+#pragma unroll
+                                for (int j = 0; j < N; j++) acc_s = acc_s + a[u][j];
+                    } else if (kind == K_MAX) {
+#pragma unroll
+                        for (int u = 0; u < G; u++)
+                            if (u < nval)
+#pragma unroll
+                                for (int j = 0; j < N; j++) acc_s = fmax_nan(acc_s, a[u][j]);
+                    } else {
+#pragma unroll
+                        for (int u = 0; u < G; u++)
+                            if (u < nval)
+#pragma unroll
+                                for (int j = 0; j < N; j++) acc_s = fmin_nan(acc_s, a[u][j]);
+                    }
+                } else {
+#pragma unroll
+                    for (int u = 0; u < G; u++) {
+                        if (u >= nval) continue;
+                        const int c = grp.c0 + 32 * u;
+                        if constexpr (sizeof(TO) == 4) {
+#pragma unroll
+                            for (int j = 0; j < N; j += 4)
+                                st_stream_v4(orow + c * N + j, make_uint4(__float_as_uint(a[u][j]), __float_as_uint(a[u][j + 1]),
+                                                                          __float_as_uint(a[u][j + 2]), __float_as_uint(a[u][j + 3])));
+                        } else if constexpr (N == 8) {
+                            st_stream_v4(orow + c * N, pack8(a[u], std::is_same<TO, __half>::value ? TADMA_F16 : TADMA_BF16));
+                        } else {
+                            // 16-bit out, fp32 rows: 4 values, 8 bytes
+                            const int dt = std::is_same<TO, __half>::value ? TADMA_F16 : TADMA_BF16;
+                            float f8[8] = {a[u][0], a[u][1], a[u][2], a[u][3], 0.0f, 0.0f, 0.0f, 0.0f};
+                            const uint4 w = pack8(f8, dt);
+                            __stcs(reinterpret_cast<uint2*>(orow + c * N), make_uint2(w.x, w.y));
+                        }
+                    }
+                }
             }
+            if (final_pass) break;
+            const RowStageParams& st = p.st[s];
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) {
                 const float t = __shfl_xor_sync(0xffffffffu, acc_s, o);
@@ -161,38 +375,16 @@ __global__ void __launch_bounds__(THREADS) rowprog_kernel(const __grid_constant_
             else if (s == 1) sv[RP_MAX_SC + 1] = v;
             else sv[RP_MAX_SC + 2] = v;
         }
-
-        TO* orow = reinterpret_cast<TO*>(p.out) + row * p.out_rs;
-#pragma unroll 1
-        for (int c = lane; c < nvec; c += 32) {
-            float vv[NV][N];
-            operands(c, vv);
-            float a[N];
-            run_fprog<NV, RP_NS, N, FAST>(p.fp, a, vv, sv);
-            if constexpr (sizeof(TO) == 4) {
-#pragma unroll
-                for (int j = 0; j < N; j += 4)
-                    st_stream_v4(orow + c * N + j, make_uint4(__float_as_uint(a[j]), __float_as_uint(a[j + 1]),
-                                                              __float_as_uint(a[j + 2]), __float_as_uint(a[j + 3])));
-            } else if constexpr (N == 8) {
-                st_stream_v4(orow + c * N, pack8(a, std::is_same<TO, __half>::value ? TADMA_F16 : TADMA_BF16));
-            } else {
-                // 16-bit out, fp32 rows: 4 values, 8 bytes
-                const int dt = std::is_same<TO, __half>::value ? TADMA_F16 : TADMA_BF16;
-                float f8[8] = {a[0], a[1], a[2], a[3], 0.0f, 0.0f, 0.0f, 0.0f};
-                const uint4 w = pack8(f8, dt);
-                __stcs(reinterpret_cast<uint2*>(orow + c * N), make_uint2(w.x, w.y));
-            }
-        }
         __syncwarp();  // every lane is done with buffer b before it is refilled
     }
     cp_async_wait<0>();
 }
 
-template <typename TI, typename TO, int NRV, int NCV, bool FAST>
-int launch_rp_k(const RowProgParams& p, cudaStream_t s) {
-    const void* fn = (const void*)rowprog_kernel<TI, TO, NRV, NCV, FAST>;
-    const size_t smem = (size_t)(NCV * p.nvec + (THREADS / 32) * 2 * NRV * p.nvec) * 16;
+template <typename TI, typename TO, int G>
+int launch_rp_g(const RowProgParams& p, cudaStream_t s) {
+    const void* fn = (const void*)rowprog_kernel<TI, TO, G>;
+    const int stride = rp_stride(p.nvec, G);
+    const size_t smem = (size_t)(p.n_cv * stride + (THREADS / 32) * 2 * p.n_rv * stride) * 16;
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return cuda_fail(e, "tadma_b200_row_program smem attribute");
@@ -204,28 +396,28 @@ int launch_rp_k(const RowProgParams& p, cudaStream_t s) {
     const int64_t want = (p.rows + THREADS / 32 - 1) / (THREADS / 32);
     const int64_t cap = (int64_t)sm_count() * per_sm;
     const int grid = (int)(want < cap ? want : cap);
-    e = launch_pdl(rowprog_kernel<TI, TO, NRV, NCV, FAST>, dim3(grid), dim3(THREADS), smem, s, p);
+    e = launch_pdl(rowprog_kernel<TI, TO, G>, dim3(grid), dim3(THREADS), smem, s, p);
     if (e == cudaSuccess) e = cudaGetLastError();
     return e == cudaSuccess ? TADMA_OK : cuda_fail(e, "tadma_b200_row_program launch");
 }
 
-template <typename TI, typename TO, bool FAST>
-int launch_rp_v(int nrv, int ncv, const RowProgParams& p, cudaStream_t s) {
-    if (nrv == 1) {
-        if (ncv == 0) return launch_rp_k<TI, TO, 1, 0, FAST>(p, s);
-        if (ncv == 1) return launch_rp_k<TI, TO, 1, 1, FAST>(p, s);
-        return launch_rp_k<TI, TO, 1, 2, FAST>(p, s);
+// Chunks per program run: 16-bit rows 2 (16 values); fp32 rows 4 (16
+// values) when that pads the lane's chunks no more than 2 (8 values) does.
+template <typename TI, typename TO>
+int launch_rp_t(const RowProgParams& p, cudaStream_t s) {
+    if constexpr (sizeof(TI) == 4) {
+        const int per_lane = (p.nvec + 31) / 32;
+        auto waste = [&](int g) { return (per_lane + g - 1) / g * g - per_lane; };
+        if (waste(4) <= waste(2)) return launch_rp_g<TI, TO, 4>(p, s);
     }
-    if (ncv == 0) return launch_rp_k<TI, TO, 2, 0, FAST>(p, s);
-    if (ncv == 1) return launch_rp_k<TI, TO, 2, 1, FAST>(p, s);
-    return launch_rp_k<TI, TO, 2, 2, FAST>(p, s);
+    return launch_rp_g<TI, TO, 2>(p, s);
 }
 
 template <typename TI>
-int launch_rp_i(int odt, bool fast, int nrv, int ncv, const RowProgParams& p, cudaStream_t s) {
-    if (odt == TADMA_F32) return launch_rp_v<TI, float, false>(nrv, ncv, p, s);
-    if (odt == TADMA_F16) return fast ? launch_rp_v<TI, __half, true>(nrv, ncv, p, s) : launch_rp_v<TI, __half, false>(nrv, ncv, p, s);
-    return fast ? launch_rp_v<TI, __nv_bfloat16, true>(nrv, ncv, p, s) : launch_rp_v<TI, __nv_bfloat16, false>(nrv, ncv, p, s);
+int launch_rp_i(int odt, const RowProgParams& p, cudaStream_t s) {
+    if (odt == TADMA_F32) return launch_rp_t<TI, float>(p, s);
+    if (odt == TADMA_F16) return launch_rp_t<TI, __half>(p, s);
+    return launch_rp_t<TI, __nv_bfloat16>(p, s);
 }
 
 }  // namespace
@@ -278,7 +470,6 @@ extern "C" int tadma_b200_row_program(const tadma_row_program* rp, void* stream)
         if (!err.empty()) return fail(TADMA_ERR_INVALID, err);
         if (t.rank != 2 || (t.dims[0] != rows && t.dims[0] != 1) || (t.dims[1] != cols && t.dims[1] != 1))
             return fail(TADMA_ERR_INVALID, "ins[k] must be a rank-2 view of {rows, cols} (dims may be 1)");
-        const int64_t rs = t.dims[0] == 1 ? 0 : t.strides[0];
         const int64_t cs = t.dims[1] == 1 ? 0 : t.strides[1];
         if (cs == 1 && cols > 1) {
             if (t.dtype != TADMA_F32 && t.dtype != TADMA_F16 && t.dtype != TADMA_BF16)
@@ -318,16 +509,17 @@ extern "C" int tadma_b200_row_program(const tadma_row_program* rp, void* stream)
         } else if (kind_of[k] == 1) {
             if ((uintptr_t)t.data % 16) return fail(TADMA_ERR_UNSUPPORTED, "column operands must be 16-byte aligned");
             p.cv[icv] = (const char*)t.data;
-            slot_of[k] = nrv + icv++;
+            slot_of[k] = RP_MAX_RV + icv++;
         } else {
             p.sc[isc] = (const char*)t.data;
             p.sc_dtype[isc] = t.dtype;
             p.sc_rs[isc] = rs;
-            slot_of[k] = nrv + ncv + isc++;
+            slot_of[k] = RP_VEC + isc++;
         }
     }
-    const int NV = nrv + ncv;
-    for (int s = 0; s < rp->n_stages; s++) slot_of[rp->n_ins + s] = NV + RP_MAX_SC + s;
+    for (int s = 0; s < rp->n_stages; s++) slot_of[rp->n_ins + s] = RP_VEC + RP_MAX_SC + s;
+    p.n_rv = nrv;
+    p.n_cv = ncv;
 
     p.n_stages = rp->n_stages;
     for (int s = 0; s < rp->n_stages; s++) {
@@ -374,10 +566,11 @@ extern "C" int tadma_b200_row_program(const tadma_row_program* rp, void* stream)
         const int rd = rp->prog[i].round_dtype;
         if (!(rd < 0 || rd == TADMA_F32 || rd == TADMA_F16 || rd == TADMA_BF16)) fast = false;
     }
+    p.fast = fast ? 1 : 0;
     cudaStream_t s = (cudaStream_t)stream;
     switch (ti) {
-    case TADMA_F32: return launch_rp_i<float>(o.dtype, fast, nrv, ncv, p, s);
-    case TADMA_F16: return launch_rp_i<__half>(o.dtype, fast, nrv, ncv, p, s);
-    default: return launch_rp_i<__nv_bfloat16>(o.dtype, fast, nrv, ncv, p, s);
+    case TADMA_F32: return launch_rp_i<float>(o.dtype, p, s);
+    case TADMA_F16: return launch_rp_i<__half>(o.dtype, p, s);
+    default: return launch_rp_i<__nv_bfloat16>(o.dtype, p, s);
     }
 }
