@@ -26,7 +26,22 @@ namespace tadma_b200 {
 constexpr int RP_MAX_RV = 2, RP_MAX_CV = 2, RP_MAX_SC = 2;
 constexpr int RP_NS = RP_MAX_SC + TADMA_ROWPROG_MAX_STAGES;  // scalar slots
 
+// A pass whose decoded program is one of the shapes a LayerNorm written out
+// as separate ops produces runs as straight-line code instead of through
+// the step loop (the same op bodies and roundings, so the same bits):
+//   RC_COPY    x                                   (a plain mean's elements)
+//   RC_SQDIFF  rnd(sqr(rnd(x - s1)))               (the variance's elements)
+//   RC_LNTAIL  rnd(rnd(rnd(rnd(x - s1) / s2) * c1) + c2), the affine part
+//              optional                            (the normalised output)
+// rnd: none, or the rounding to fp16 / bf16 of 16-bit generated code.
+constexpr int RC_GENERIC = 0, RC_COPY = 1, RC_SQDIFF = 2, RC_LNTAIL = 3, RC_LNTAIL_PLAIN = 4;
+struct PassRecipe {
+    int8_t kind, rnd;   // rnd: -1 none, else TADMA_F16 / TADMA_BF16
+    int8_t x, s1, s2, c1, c2, pad;  // operand slots
+};
+
 struct RowStageParams {
+    PassRecipe rc;
     int32_t kind;  // K_SUM, K_MAX, K_MIN
     int32_t mean;  // divide by cols
     char* out;
@@ -49,6 +64,7 @@ struct RowProgParams {
     int32_t sc_dtype[RP_MAX_SC];
     int64_t sc_rs[RP_MAX_SC];  // row strides in elements
     RowStageParams st[TADMA_ROWPROG_MAX_STAGES];
+    PassRecipe rc;  // the final pass's
     FProg fp;
     char* out;
     int64_t out_rs;  // row stride in elements
@@ -253,12 +269,65 @@ __device__ __forceinline__ void run_group(const FProg& fp, bool fast, const RowG
 #undef TADMA_RB
 #undef TADMA_RR
 
+template <int RD>
+__device__ __forceinline__ float rc_rnd(float v) {
+    if constexpr (RD < 0) return v;
+    else return round_to(v, RD);
+}
+
+template <typename TI, int G, int RD, int NS>
+__device__ __forceinline__ void run_recipe_r(const PassRecipe& rc, const RowGroup<TI, G>& grp, const float (&sv)[NS],
+                                             float (&acc)[G][16 / sizeof(TI)]) {
+    constexpr int N = 16 / (int)sizeof(TI);
+#pragma unroll
+    for (int u = 0; u < G; u++) grp.load(rc.x, u, acc[u]);
+    if (rc.kind == RC_COPY) return;
+    const float s1 = scalar_slot<NS>(sv, rc.s1 - RP_VEC);
+    if (rc.kind == RC_SQDIFF) {
+#pragma unroll
+        for (int u = 0; u < G; u++)
+#pragma unroll
+            for (int j = 0; j < N; j++) {
+                const float d = rc_rnd<RD>(binary(TADMA_OP_SUB, acc[u][j], s1, s1));
+                acc[u][j] = rc_rnd<RD>(__fmul_rn(d, d));
+            }
+        return;
+    }
+    const float s2 = scalar_slot<NS>(sv, rc.s2 - RP_VEC);
+#pragma unroll
+    for (int u = 0; u < G; u++) {
+#pragma unroll
+        for (int j = 0; j < N; j++) {
+            const float d = rc_rnd<RD>(binary(TADMA_OP_SUB, acc[u][j], s1, s1));
+            acc[u][j] = rc_rnd<RD>(binary(TADMA_OP_DIV, d, s2, s2));
+        }
+        if (rc.kind == RC_LNTAIL) {
+            float g[N], b[N];
+            grp.load(rc.c1, u, g);
+            grp.load(rc.c2, u, b);
+#pragma unroll
+            for (int j = 0; j < N; j++) {
+                const float t = rc_rnd<RD>(binary(TADMA_OP_MUL, acc[u][j], g[j], g[j]));
+                acc[u][j] = rc_rnd<RD>(binary(TADMA_OP_ADD, t, b[j], b[j]));
+            }
+        }
+    }
+}
+
+template <typename TI, int G, int NS>
+__device__ __forceinline__ void run_recipe(const PassRecipe& rc, const RowGroup<TI, G>& grp, const float (&sv)[NS],
+                                           float (&acc)[G][16 / sizeof(TI)]) {
+    if (rc.rnd == TADMA_F16) run_recipe_r<TI, G, TADMA_F16, NS>(rc, grp, sv, acc);
+    else if (rc.rnd == TADMA_BF16) run_recipe_r<TI, G, TADMA_BF16, NS>(rc, grp, sv, acc);
+    else run_recipe_r<TI, G, -1, NS>(rc, grp, sv, acc);
+}
+
 // Chunks of one operand buffer in shared memory: the row's, padded to whole
 // groups of G chunks per lane.
 __host__ __device__ constexpr int rp_stride(int nvec, int G) { return (nvec + 32 * G - 1) / (32 * G) * (32 * G); }
 
 template <typename TI, typename TO, int G>
-__global__ void __launch_bounds__(THREADS, 2) rowprog_kernel(const __grid_constant__ RowProgParams p) {
+__global__ void __launch_bounds__(THREADS, 3) rowprog_kernel(const __grid_constant__ RowProgParams p) {
     pdl_begin();
     constexpr int N = 16 / (int)sizeof(TI);
     extern __shared__ uint4 rp_smem[];
@@ -307,6 +376,7 @@ __global__ void __launch_bounds__(THREADS, 2) rowprog_kernel(const __grid_consta
         for (int s = 0; s <= p.n_stages; s++) {
             const bool final_pass = s == p.n_stages;
             const FProg& fp = final_pass ? p.fp : p.st[s].fp;
+            const PassRecipe& rc = final_pass ? p.rc : p.st[s].rc;
             const int kind = final_pass ? K_SUM : p.st[s].kind;
             float acc_s = kind == K_SUM ? 0.0f : kind == K_MAX ? -INFINITY : INFINITY;
             TO* orow = reinterpret_cast<TO*>(p.out) + row * p.out_rs;
@@ -315,7 +385,8 @@ __global__ void __launch_bounds__(THREADS, 2) rowprog_kernel(const __grid_consta
                 grp.c0 = lane + 32 * G * g;
                 const int nval = nchunk - G * g;  // chunks of this group inside the row (may be <= 0 or > G)
                 float a[G][N];
-                run_group<TI, G, RP_NS>(fp, final_pass && p.fast, grp, sv, a);
+                if (rc.kind != RC_GENERIC) run_recipe<TI, G, RP_NS>(rc, grp, sv, a);
+                else run_group<TI, G, RP_NS>(fp, final_pass && p.fast, grp, sv, a);
                 if (!final_pass) {
                     // the row reductions' per-element fold, in chunk order
                     if (kind == K_SUM) {
@@ -418,6 +489,59 @@ int launch_rp_i(int odt, const RowProgParams& p, cudaStream_t s) {
     if (odt == TADMA_F32) return launch_rp_t<TI, float>(p, s);
     if (odt == TADMA_F16) return launch_rp_t<TI, __half>(p, s);
     return launch_rp_t<TI, __nv_bfloat16>(p, s);
+}
+
+// The recipe of a decoded pass program (RC_GENERIC when none fits).  Slots:
+// 0-1 row operands, 2-3 column operands, 4+ scalars.
+PassRecipe match_recipe(const FProg& fp) {
+    PassRecipe rc{};
+    rc.kind = RC_GENERIC;
+    rc.rnd = -1;
+    if (fp.acc < 0 || fp.acc >= RP_MAX_RV) return rc;
+    rc.x = (int8_t)fp.acc;
+    int i = 0, rnd = -2;  // -2: not yet seen
+    // one step of code `code` (operand class checked by the caller), then an
+    // optional rounding, the same for every step
+    auto step = [&](int code) -> const FInstr* {
+        if (i >= fp.n || fp.ins[i].code != code) return nullptr;
+        const FInstr* f = &fp.ins[i++];
+        int r = -1;
+        if (i < fp.n && fp.ins[i].code >= FC_RND && fp.ins[i].code <= FC_RND + 1) r = fp.ins[i++].code == FC_RND ? TADMA_F16 : TADMA_BF16;
+        if (rnd == -2) rnd = r;
+        return r == rnd ? f : nullptr;
+    };
+    auto scalar = [](const FInstr* f) { return f && f->b >= RP_VEC; };
+    auto column = [](const FInstr* f) { return f && f->b >= RP_MAX_RV && f->b < RP_VEC; };
+    if (fp.n == 0) {
+        rc.kind = RC_COPY;
+        return rc;
+    }
+    const FInstr* sub = step(FC_BV + (TADMA_OP_SUB - TADMA_OP_ADD));
+    if (!scalar(sub)) return rc;
+    rc.s1 = sub->b;
+    if (i < fp.n && fp.ins[i].code == FC_SQR) {
+        if (step(FC_SQR) && i == fp.n) {
+            rc.kind = RC_SQDIFF;
+            rc.rnd = (int8_t)rnd;
+        }
+        return rc;
+    }
+    const FInstr* div = step(FC_BV + (TADMA_OP_DIV - TADMA_OP_ADD));
+    if (!scalar(div)) return rc;
+    rc.s2 = div->b;
+    if (i == fp.n) {
+        rc.kind = RC_LNTAIL_PLAIN;
+        rc.rnd = (int8_t)rnd;
+        return rc;
+    }
+    const FInstr* mul = step(FC_BV + (TADMA_OP_MUL - TADMA_OP_ADD));
+    const FInstr* add = column(mul) ? step(FC_BV + (TADMA_OP_ADD - TADMA_OP_ADD)) : nullptr;
+    if (!column(mul) || !column(add) || i != fp.n) return rc;
+    rc.c1 = mul->b;
+    rc.c2 = add->b;
+    rc.kind = RC_LNTAIL;
+    rc.rnd = (int8_t)rnd;
+    return rc;
 }
 
 }  // namespace
@@ -552,10 +676,12 @@ extern "C" int tadma_b200_row_program(const tadma_row_program* rp, void* stream)
         if (!decode_fprog(S.prog, S.n_instr, avail, st.fp, slot_of))
             return fail(TADMA_ERR_UNSUPPORTED, "stage program step has no typed code");
         st.fp.acc = slot_of[S.acc];
+        st.rc = match_recipe(st.fp);
     }
     if (!decode_fprog(rp->prog, rp->n_instr, n_ops, p.fp, slot_of))
         return fail(TADMA_ERR_UNSUPPORTED, "program step has no typed code");
     p.fp.acc = slot_of[rp->acc];
+    p.rc = match_recipe(p.fp);
     p.out = (char*)o.data;
     p.out_rs = o.strides[0];
     if ((uintptr_t)o.data % 16 || (p.out_rs * dtype_size(o.dtype)) % (sizeof(float) == 4 && o.dtype != TADMA_F32 && es == 4 ? 8 : 16))
