@@ -171,11 +171,13 @@ __device__ __forceinline__ void cvt_typed(uint4 r, float* f) {
 }
 
 template <typename T, int K, int NIN>
-__global__ void __launch_bounds__(THREADS, NIN == 1 ? 3 : 2) chain_reduce_typed_kernel(const __grid_constant__ ChainReduceParams p) {
+__global__ void __launch_bounds__(THREADS, NIN <= 2 ? 3 : 2) chain_reduce_typed_kernel(const __grid_constant__ ChainReduceParams p) {
     pdl_begin();
     using S = TypedShape<T, NIN>;
     constexpr int N = S::N, UNR = S::UNR, G = S::G, W = S::W;
     const int lane = threadIdx.x & 31;
+    extern __shared__ uint4 cr_ring[];
+    uint4* ring = cr_ring + (threadIdx.x >> 5) * (2 * NIN * UNR * 32);  // 2 stages x NIN x UNR x 32 lanes
     const int64_t gw = ((int64_t)blockIdx.x * THREADS + threadIdx.x) >> 5;
     const int64_t nw = ((int64_t)gridDim.x * THREADS) >> 5;
     for (int64_t row = gw; row < p.nrows; row += nw) {
@@ -205,20 +207,29 @@ __global__ void __launch_bounds__(THREADS, NIN == 1 ? 3 : 2) chain_reduce_typed_
             bc[k] = p.ax[k] == 0 ? load_as<float>(p.chain.in[k].base, p.chain.in[k].dtype, base[k]) : 0.0f;
         State<float> s = init_state<K, float>();
         const int64_t nv = p.R / N;
-        for (int64_t i0 = lane; i0 < nv; i0 += 32 * UNR) {
-            // Vectors i0, i0 + 32, ..., i0 + 32 (UNR - 1) of every streamed
-            // operand (zeros past the row's last vector).
-            uint4 raw[UNR][NIN];
+        // Vectors i0, i0 + 32, ..., i0 + 32 (UNR - 1) of every streamed
+        // operand go into this lane's slots of the warp's two-stage ring
+        // with cp.async; the next group's copies are issued before the
+        // current group is computed.  Each lane reads back only what it
+        // copied, so its own wait_group orders copy and use.  Slots past the
+        // row's last vector keep stale words: computed, never folded.
+        auto issue = [&](int64_t g0, int st) {
 #pragma unroll
             for (int u = 0; u < UNR; u++) {
 #pragma unroll
                 for (int k = 0; k < NIN; k++) {
-                    if (p.ax[k] != 0 && i0 + 32 * u < nv)
-                        raw[u][k] = ld_stream_v4(reinterpret_cast<const T*>(p.chain.in[k].base) + base[k] + (i0 + 32 * u) * N);
-                    else
-                        raw[u][k] = make_uint4(0u, 0u, 0u, 0u);
+                    if (p.ax[k] != 0 && g0 + 32 * u < nv)
+                        cp_async16(ring + ((st * NIN + k) * UNR + u) * 32 + lane,
+                                   reinterpret_cast<const T*>(p.chain.in[k].base) + base[k] + (g0 + 32 * u) * N);
                 }
             }
+            cp_async_commit();
+        };
+        int st = 0;
+        issue(lane, 0);
+        for (int64_t i0 = lane; i0 < nv; i0 += 32 * UNR, st ^= 1) {
+            issue(i0 + 32 * UNR, st ^ 1);
+            cp_async_wait<1>();
 #pragma unroll 1
             for (int h = 0; h < UNR / G; h++) {
                 float val[NIN][W];
@@ -230,7 +241,7 @@ __global__ void __launch_bounds__(THREADS, NIN == 1 ? 3 : 2) chain_reduce_typed_
 #pragma unroll
                             for (int j = 0; j < N; j++) val[k][g * N + j] = bc[k];
                         } else {
-                            cvt_typed<T>(raw[g][k], &val[k][g * N]);
+                            cvt_typed<T>(ring[((st * NIN + k) * UNR + h * G + g) * 32 + lane], &val[k][g * N]);
                         }
                     }
                 }
@@ -249,13 +260,9 @@ __global__ void __launch_bounds__(THREADS, NIN == 1 ? 3 : 2) chain_reduce_typed_
                         }
                     }
                 }
-                // the next G vectors move to the front
-#pragma unroll
-                for (int u = 0; u + G < UNR; u++)
-#pragma unroll
-                    for (int k = 0; k < NIN; k++) raw[u][k] = raw[u + G][k];
             }
         }
+        cp_async_wait<0>();  // the last (empty) group, before the ring's reuse
         for (int64_t r = nv * N + lane; r < p.R; r += 32) {
             float val[NIN][1];
 #pragma unroll
@@ -281,11 +288,28 @@ __global__ void __launch_bounds__(THREADS, NIN == 1 ? 3 : 2) chain_reduce_typed_
 
 template <typename T, int K, int NIN>
 int launch_typed_k(const ChainReduceParams& p, cudaStream_t s) {
+    using S = TypedShape<T, NIN>;
     const void* fn = (const void*)chain_reduce_typed_kernel<T, K, NIN>;
+    const size_t smem = (size_t)(THREADS / 32) * 2 * NIN * S::UNR * 32 * 16;
+    // the shared-memory attribute and the occupancy, once per device (the
+    // attribute belongs to the device's context)
+    static thread_local int occ[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "tadma_b200_reduce_chain cudaGetDevice");
+    int& per_sm = occ[dev & 63];
+    if (per_sm <= 0) {
+        if (smem > 48 * 1024) e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, THREADS, smem);
+        if (e != cudaSuccess) {
+            per_sm = 0;
+            return cuda_fail(e, "tadma_b200_reduce_chain kernel setup");
+        }
+    }
     const int64_t want = (p.nrows + (THREADS / 32) - 1) / (THREADS / 32);
-    const int64_t cap = (int64_t)sm_count() * blocks_per_sm(fn);
+    const int64_t cap = (int64_t)sm_count() * (per_sm > 0 ? per_sm : 1);
     const int grid = (int)(want < cap ? (want > 0 ? want : 1) : cap);
-    cudaError_t e = launch_pdl(chain_reduce_typed_kernel<T, K, NIN>, dim3(grid), dim3(THREADS), 0, s, p);
+    e = launch_pdl(chain_reduce_typed_kernel<T, K, NIN>, dim3(grid), dim3(THREADS), smem, s, p);
     if (e == cudaSuccess) e = cudaGetLastError();
     return e == cudaSuccess ? TADMA_OK : cuda_fail(e, "tadma_b200_reduce_chain launch");
 }

@@ -221,6 +221,108 @@ __global__ void __launch_bounds__(THREADS, 4) transpose16_kernel(const __grid_co
     }
 }
 
+bool identity_chain(const TransposeParams& tp);
+
+// fp32 in: 64 (i) x TJ (j) tiles of 32-bit words, W[i][j].  A warp loads
+// 4 input rows j x 8 consecutive 16-byte chunks of i (four 128-byte runs)
+// and stores each chunk's 4 values as scalar words down rows 4c .. 4c + 3
+// of W; the output side reads 16-byte chunks of 4 words (4 values of j) and
+// stores them along the output's contiguous dim, one W row per warp.  The
+// 4-word chunks of row i sit XOR-swizzled by (i / 4) % 8, so the scalar
+// stores (8 chunks c x 4 rows j per warp) and the 16-byte reads (8
+// consecutive chunks per quarter warp) each cover the 32 banks once; the
+// 64 x 64 fp32 tile of transpose64_kernel, padded rather than swizzled, read
+// its words one at a time with 2-way conflicts.  TJ = 128 keeps 32 KB of
+// loads in flight per CTA.  RAW: an identity chain copies the words.
+template <typename TO, int PROG, int TJ, bool RAW>
+__global__ void __launch_bounds__(THREADS, 4) transpose32_kernel(const __grid_constant__ TransposeParams tp) {
+    pdl_begin();
+    static_assert(TJ == 64 || TJ == 128);
+    constexpr int TI_ = 64;
+    constexpr int NL = (TJ / 4) * 2 / (THREADS / 32);  // load tasks (4 rows x 8 chunks) per warp
+    constexpr int CPR = TJ / 4;                        // 16-byte output chunks per W row
+    constexpr int RPP = THREADS / CPR;                 // W rows per output pass
+    constexpr int NS = TI_ / RPP;                      // output chunks per thread
+    __shared__ __align__(16) uint32_t W[TI_ * TJ];
+    const int t = threadIdx.x, w = t >> 5, lane = t & 31;
+    const int jl = lane & 3, cl = lane >> 2;  // load: row j within the 4, chunk within the 8
+    const int q = t % CPR, r0 = t / CPR;      // output chunk (j = 4q .. 4q + 3), first W row
+    const int64_t i0 = (int64_t)blockIdx.y * TI_, j0 = (int64_t)blockIdx.x * TJ;
+    for (int64_t bz = blockIdx.z; bz < tp.nbatch; bz += gridDim.z) {
+        uint64_t e = (uint64_t)bz;
+        int64_t ib = 0, ob = 0;
+        for (int d = tp.nb - 1; d >= 1; d--) {
+            uint64_t qq, rr;
+            tp.bdm[d].divmod(e, qq, rr);
+            ib += (int64_t)rr * tp.b_in[d];
+            ob += (int64_t)rr * tp.b_out[d];
+            e = qq;
+        }
+        if (tp.nb > 0) {
+            ib += (int64_t)e * tp.b_in[0];
+            ob += (int64_t)e * tp.b_out[0];
+        }
+        const float* in = reinterpret_cast<const float*>(tp.in) + ib;
+        uint4 a[NL];
+#pragma unroll
+        for (int u = 0; u < NL; u++) {
+            const int k = w + (THREADS / 32) * u;  // task: rows 4 (k >> 1) .., chunks 8 (k & 1) ..
+            const int c = 8 * (k & 1) + cl;
+            const int64_t i = i0 + 4 * c, j = j0 + 4 * (k >> 1) + jl;
+            a[u] = (i < tp.n_i && j < tp.n_j) ? ld_stream_v4(in + i + j * tp.in_sj) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int u = 0; u < NL; u++) {
+            const int k = w + (THREADS / 32) * u;
+            const int c = 8 * (k & 1) + cl;
+            const int cj = k >> 1;                                // 4-word chunk of j in W's rows
+            const int col = ((cj ^ (c & 7)) << 2) | jl;           // swizzled word of rows 4c .. 4c + 3
+            const uint32_t av[4] = {a[u].x, a[u].y, a[u].z, a[u].w};
+#pragma unroll
+            for (int h = 0; h < 4; h++) W[(4 * c + h) * TJ + col] = av[h];
+        }
+        __syncthreads();
+        TO* out = reinterpret_cast<TO*>(tp.out) + ob;
+#pragma unroll
+        for (int u = 0; u < NS; u++) {
+            const int row = r0 + RPP * u;
+            const int64_t oi = i0 + row, oj = j0 + 4 * q;
+            if (oi < tp.n_i && oj < tp.n_j) {
+                const uint4 v = *reinterpret_cast<const uint4*>(&W[row * TJ + ((q ^ ((row >> 2) & 7)) << 2)]);
+                if constexpr (RAW) {
+                    st_stream_v4(out + oi * tp.out_si + oj, v);
+                } else {
+                    float val[1][4] = {{__uint_as_float(v.x), __uint_as_float(v.y), __uint_as_float(v.z), __uint_as_float(v.w)}};
+                    float acc[4] = {val[0][0], val[0][1], val[0][2], val[0][3]};
+                    program<float, 1, 4, PROG>(tp.chain, acc, val);
+                    if constexpr (sizeof(TO) == 4) {
+                        st_stream_v4(out + oi * tp.out_si + oj, make_uint4(__float_as_uint(acc[0]), __float_as_uint(acc[1]),
+                                                                           __float_as_uint(acc[2]), __float_as_uint(acc[3])));
+                    } else {
+                        const float f8[8] = {acc[0], acc[1], acc[2], acc[3], 0.0f, 0.0f, 0.0f, 0.0f};
+                        const uint4 p = pack8(f8, std::is_same<TO, __half>::value ? TADMA_F16 : TADMA_BF16);
+                        __stcs(reinterpret_cast<uint2*>(out + oi * tp.out_si + oj), make_uint2(p.x, p.y));
+                    }
+                }
+            }
+        }
+        __syncthreads();
+    }
+}
+
+template <typename TO, int TJ>
+void launch_t32_tj(bool fast, dim3 grid, const TransposeParams& tp, cudaStream_t s) {
+    if (identity_chain(tp)) (void)launch_pdl(transpose32_kernel<TO, PROG_INTERP, TJ, true>, grid, dim3(THREADS), 0, s, tp);
+    else if (fast && sizeof(TO) == 2) (void)launch_pdl(transpose32_kernel<TO, PROG_INTERP_FAST, TJ, false>, grid, dim3(THREADS), 0, s, tp);
+    else (void)launch_pdl(transpose32_kernel<TO, PROG_INTERP, TJ, false>, grid, dim3(THREADS), 0, s, tp);
+}
+template <typename TO>
+void launch_t32_o(bool fast, int64_t gz, const TransposeParams& tp, cudaStream_t s) {
+    const unsigned gy = (unsigned)((tp.n_i + 63) / 64);
+    if (tp.n_j >= 128) launch_t32_tj<TO, 128>(fast, dim3((unsigned)((tp.n_j + 127) / 128), gy, (unsigned)gz), tp, s);
+    else launch_t32_tj<TO, 64>(fast, dim3((unsigned)((tp.n_j + 63) / 64), gy, (unsigned)gz), tp, s);
+}
+
 template <typename TI, typename TO>
 void launch_t64_io(bool fast, dim3 grid, const TransposeParams& tp, cudaStream_t s) {
     if (fast && sizeof(TO) == 2) (void)launch_pdl(transpose64_kernel<TI, TO, PROG_INTERP_FAST>, grid, dim3(THREADS), 0, s, tp);
@@ -290,6 +392,15 @@ int launch_transpose(bool fast, const TransposeParams& tp, cudaStream_t s) {
     if (in16 && out16 && transpose64_ok(tp)) {
         if (tp.in_dtype == TADMA_F16) launch_t16_i<__half>(fast, gz > 0 ? gz : 1, tp, s);
         else launch_t16_i<__nv_bfloat16>(fast, gz > 0 ? gz : 1, tp, s);
+        cudaError_t e = cudaGetLastError();
+        return e == cudaSuccess ? TADMA_OK : cuda_fail(e, "tadma_b200_eltwise launch");
+    }
+    if (tp.in_dtype == TADMA_F32 && transpose64_ok(tp)) {
+        switch (tp.out_dtype) {
+        case TADMA_F32: launch_t32_o<float>(fast, gz > 0 ? gz : 1, tp, s); break;
+        case TADMA_F16: launch_t32_o<__half>(fast, gz > 0 ? gz : 1, tp, s); break;
+        default: launch_t32_o<__nv_bfloat16>(fast, gz > 0 ? gz : 1, tp, s); break;
+        }
         cudaError_t e = cudaGetLastError();
         return e == cudaSuccess ? TADMA_OK : cuda_fail(e, "tadma_b200_eltwise launch");
     }

@@ -45,7 +45,7 @@ def test_config2_reaches_the_row_affine_kernel():
 @pytest.mark.parametrize("case,kernel", [("add", "typed1_kernel"), ("cast", "typed1_kernel"),
                                          ("gt", "typed_cmp_kernel"), ("where", "typed_where_kernel"),
                                          ("chain", "typed_kernel"), ("transpose", "transpose16_kernel"),
-                                         ("transpose32", "transpose64_kernel"),
+                                         ("transpose32", "transpose32_kernel"),
                                          ("gelu_add", "chain_narrow_kernel")])
 def test_eager_calls_reach_their_typed_kernels(case, kernel):
     import torch

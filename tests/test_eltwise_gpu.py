@@ -242,7 +242,7 @@ def test_transpose_copy_and_cast(shape, perm, dt, out_dt):
 
 
 def test_transpose64_with_chain():
-    # aligned rows: the vector-tile kernel runs the chain on the way out
+    # aligned fp32 rows: the swizzled tile kernel runs the chain on the way out
     import torch
     x = gen((6, 136, 72), DType.F32, Dist.NORMAL, 0.0, 1.0, 32)
     xd = to_dev(x)
