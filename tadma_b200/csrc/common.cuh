@@ -239,6 +239,18 @@ struct DivMod {
 // ---------------------------------------------------------- vector memory --
 
 __device__ __forceinline__ uint4 ld_stream_v4(const void* p) { return __ldcs(reinterpret_cast<const uint4*>(p)); }
+
+// Asynchronous 16-byte global -> shared copies (cp.async, L2-only): the
+// issuing thread's groups complete in order; cp.async.wait_group N waits
+// until at most N of its groups are still in flight (a hardware wait).
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
+
 __device__ __forceinline__ uint4 ld_v4(const void* p) { return *reinterpret_cast<const uint4*>(p); }
 __device__ __forceinline__ uint4 ld_nc_v4(const void* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
 __device__ __forceinline__ void st_stream_v4(void* p, uint4 v) { __stcs(reinterpret_cast<uint4*>(p), v); }

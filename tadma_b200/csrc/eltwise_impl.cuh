@@ -162,17 +162,6 @@ int reduce_rowop(int32_t op, const int64_t* shape, int32_t rank, int32_t ax, con
 
 namespace {
 
-// Asynchronous 16-byte global -> shared copies (cp.async, L2-only): the
-// issuing thread's groups complete in order; cp.async.wait_group N waits
-// until at most N of its groups are still in flight (a hardware wait).
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
-    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
-
 template <typename C>
 __device__ __forceinline__ C imm_as(double v);
 template <>

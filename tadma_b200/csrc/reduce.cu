@@ -292,6 +292,8 @@ __global__ void __launch_bounds__(THREADS) reduce_rowop_kernel(const __grid_cons
     const int lane = threadIdx.x & 31;
     const int64_t gw = ((int64_t)blockIdx.x * THREADS + threadIdx.x) >> 5;
     const int64_t nw = ((int64_t)gridDim.x * THREADS) >> 5;
+    __shared__ uint4 ring_s[THREADS / 32][2][UNR][32];  // 32 KB: 2 stages x UNR vectors x 32 lanes per warp
+    uint4 (*ring)[UNR][32] = ring_s[threadIdx.x >> 5];
     for (int64_t row = gw; row < p.nrows; row += nw) {
         const T* x = reinterpret_cast<const T*>(p.in) + row * p.in_row_stride;
         const float m = p.rop ? load_as<float>(p.rop, p.rop_dtype, row * p.rop_row_stride) : __double2float_rn(p.imm1);
@@ -302,22 +304,34 @@ __global__ void __launch_bounds__(THREADS) reduce_rowop_kernel(const __grid_cons
             ArgVec<K, T, N> av;
             if constexpr (ARG) av.init();
             const int64_t nv = p.R / N;
-            for (int64_t i0 = lane; i0 < nv; i0 += 32 * UNR) {
-                uint4 r[UNR];
+            // The lane's vectors i0, i0 + 32, ... go through its slots of the
+            // warp's two-stage ring with cp.async, the next group's copies in
+            // flight while this group runs its chain (exp, division) and
+            // folds; the lane reads back only what it copied.
+            auto issue = [&](int64_t g0, int st) {
 #pragma unroll
                 for (int u = 0; u < UNR; u++)
-                    if (i0 + 32 * u < nv) r[u] = ld_stream_v4(x + (i0 + 32 * u) * N);
+                    if (g0 + 32 * u < nv) cp_async16(&ring[st][u][lane], x + (g0 + 32 * u) * N);
+                cp_async_commit();
+            };
+            int st = 0;
+            issue(lane, 0);
+            for (int64_t i0 = lane; i0 < nv; i0 += 32 * UNR, st ^= 1) {
+                issue(i0 + 32 * UNR, st ^ 1);
+                cp_async_wait<1>();
 #pragma unroll
                 for (int u = 0; u < UNR; u++) {
                     if (i0 + 32 * u < nv) {
+                        const uint4 r = ring[st][u][lane];
                         float f[N];
-                        Vec<T>::cvt(r[u], f);
+                        Vec<T>::cvt(r, f);
                         rowop_vec<N>(p, m, f);
-                        if constexpr (ARG) av.add(r[u], f, i0 + 32 * u);
+                        if constexpr (ARG) av.add(r, f, i0 + 32 * u);
                         else update_vec<K, N>(s, f, (i0 + 32 * u) * N);
                     }
                 }
             }
+            cp_async_wait<0>();  // the last (empty) group, before the ring's reuse
             if constexpr (ARG) s = av.resolve([&](float v) { return rowop_one(p, m, v); });
             done = nv * N;
         }
