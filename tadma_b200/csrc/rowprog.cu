@@ -318,7 +318,9 @@ __device__ __forceinline__ void run_recipe(const PassRecipe& rc, const RowGroup<
 // groups of G chunks per lane.
 __host__ __device__ constexpr int rp_stride(int nvec, int G) { return (nvec + 32 * G - 1) / (32 * G) * (32 * G); }
 
-template <typename TI, typename TO, int G>
+// RONLY: every pass is a recipe (the step loop is not compiled in, so a
+// group can hold the lane's whole row: G = its chunk count).
+template <typename TI, typename TO, int G, bool RONLY>
 __global__ void __launch_bounds__(THREADS, 3) rowprog_kernel(const __grid_constant__ RowProgParams p) {
     pdl_begin();
     constexpr int N = 16 / (int)sizeof(TI);
@@ -377,8 +379,12 @@ __global__ void __launch_bounds__(THREADS, 3) rowprog_kernel(const __grid_consta
                 grp.c0 = lane + 32 * G * g;
                 const int nval = nchunk - G * g;  // chunks of this group inside the row (may be <= 0 or > G)
                 float a[G][N];
-                if (rc.kind != RC_GENERIC) run_recipe<TI, G, RP_NS>(rc, grp, sv, a);
-                else run_group<TI, G, RP_NS>(fp, final_pass && p.fast, grp, sv, a);
+                if constexpr (RONLY) {
+                    run_recipe<TI, G, RP_NS>(rc, grp, sv, a);
+                } else {
+                    if (rc.kind != RC_GENERIC) run_recipe<TI, G, RP_NS>(rc, grp, sv, a);
+                    else run_group<TI, G, RP_NS>(fp, final_pass && p.fast, grp, sv, a);
+                }
                 if (!final_pass) {
                     // the row reductions' per-element fold, in chunk order
                     if (kind == K_SUM) {
@@ -443,9 +449,9 @@ __global__ void __launch_bounds__(THREADS, 3) rowprog_kernel(const __grid_consta
     cp_async_wait<0>();
 }
 
-template <typename TI, typename TO, int G>
+template <typename TI, typename TO, int G, bool RONLY = false>
 int launch_rp_g(const RowProgParams& p, cudaStream_t s) {
-    const void* fn = (const void*)rowprog_kernel<TI, TO, G>;
+    const void* fn = (const void*)rowprog_kernel<TI, TO, G, RONLY>;
     const int stride = rp_stride(p.nvec, G);
     const size_t smem = (size_t)(p.n_cv * stride + (THREADS / 32) * 2 * p.n_rv * stride) * 16;
     if (smem > 48 * 1024) {
@@ -459,7 +465,7 @@ int launch_rp_g(const RowProgParams& p, cudaStream_t s) {
     const int64_t want = (p.rows + THREADS / 32 - 1) / (THREADS / 32);
     const int64_t cap = (int64_t)sm_count() * per_sm;
     const int grid = (int)(want < cap ? want : cap);
-    e = launch_pdl(rowprog_kernel<TI, TO, G>, dim3(grid), dim3(THREADS), smem, s, p);
+    e = launch_pdl(rowprog_kernel<TI, TO, G, RONLY>, dim3(grid), dim3(THREADS), smem, s, p);
     if (e == cudaSuccess) e = cudaGetLastError();
     return e == cudaSuccess ? TADMA_OK : cuda_fail(e, "tadma_b200_row_program launch");
 }
@@ -468,6 +474,17 @@ int launch_rp_g(const RowProgParams& p, cudaStream_t s) {
 // values) when that pads the lane's chunks no more than 2 (8 values) does.
 template <typename TI, typename TO>
 int launch_rp_t(const RowProgParams& p, cudaStream_t s) {
+    // every pass a recipe and every lane the same whole chunks: one group
+    // holds the lane's row (512 / 768 / 1024 values)
+    bool all_rc = p.rc.kind != RC_GENERIC;
+    for (int k = 0; k < p.n_stages; k++) all_rc = all_rc && p.st[k].rc.kind != RC_GENERIC;
+    if (all_rc && p.nvec % 32 == 0) {
+        const int per_lane = p.nvec / 32;
+        constexpr int N = 16 / (int)sizeof(TI);
+        if (per_lane * N == 16) return launch_rp_g<TI, TO, 16 / N, true>(p, s);
+        if (per_lane * N == 24) return launch_rp_g<TI, TO, 24 / N, true>(p, s);
+        if (per_lane * N == 32) return launch_rp_g<TI, TO, 32 / N, true>(p, s);
+    }
     if constexpr (sizeof(TI) == 4) {
         const int per_lane = (p.nvec + 31) / 32;
         auto waste = [&](int g) { return (per_lane + g - 1) / g * g - per_lane; };
