@@ -20,6 +20,7 @@
 //   call stores; the final chain is the typed kernels' pre-decoded program.
 // There is no spin-wait: cp.async.wait_group is the hardware's own wait.
 #include "eltwise_impl.cuh"
+#include "kdiv.cuh"
 
 namespace tadma_b200 {
 
@@ -48,7 +49,7 @@ struct RowStageParams {
     int32_t out_dtype, pad;
     int64_t out_stride;
     FProg fp;
-    PostChain pc;
+    FProg pfp;  // the post chain, pre-decoded (pfp.n == 0: none)
 };
 
 struct RowProgParams {
@@ -286,12 +287,28 @@ __device__ __forceinline__ void run_recipe_r(const PassRecipe& rc, const RowGrou
         return;
     }
     const float s2 = scalar_slot<NS>(sv, rc.s2 - RP_VEC);
+    // The division by the row's s2: its reciprocal once, then the fused
+    // sequence of kdiv.cuh for the group when every dividend is inside its
+    // range (the same bits as the IEEE division, which the group takes
+    // otherwise).
+    const KnownDivisor kd = known_divisor(s2);
+    bool fast = kd.ok;
 #pragma unroll
-    for (int u = 0; u < G; u++) {
+    for (int u = 0; u < G; u++)
 #pragma unroll
         for (int j = 0; j < N; j++) {
-            const float d = rc_rnd<RD>(binary(TADMA_OP_SUB, acc[u][j], s1, s1));
-            acc[u][j] = rc_rnd<RD>(binary(TADMA_OP_DIV, d, s2, s2));
+            acc[u][j] = rc_rnd<RD>(binary(TADMA_OP_SUB, acc[u][j], s1, s1));
+            fast = fast & kdiv_in_range(acc[u][j]);
+        }
+    // chunk by chunk (one chunk's temporaries live at a time)
+#pragma unroll
+    for (int u = 0; u < G; u++) {
+        if (fast) {
+#pragma unroll
+            for (int j = 0; j < N; j++) acc[u][j] = rc_rnd<RD>(kdiv_fast(acc[u][j], kd));
+        } else {
+#pragma unroll
+            for (int j = 0; j < N; j++) acc[u][j] = rc_rnd<RD>(binary(TADMA_OP_DIV, acc[u][j], s2, s2));
         }
         if (rc.kind == RC_LNTAIL) {
             float g[N], b[N];
@@ -314,14 +331,99 @@ __device__ __forceinline__ void run_recipe(const PassRecipe& rc, const RowGroup<
     else run_recipe_r<TI, G, -1, NS>(rc, grp, sv, acc);
 }
 
+// Chunk c of the final pass's output row.
+template <typename TO, int N>
+__device__ __forceinline__ void store_chunk(TO* orow, int c, const float (&a)[N]) {
+    if constexpr (sizeof(TO) == 4) {
+#pragma unroll
+        for (int j = 0; j < N; j += 4)
+            st_stream_v4(orow + c * N + j, make_uint4(__float_as_uint(a[j]), __float_as_uint(a[j + 1]), __float_as_uint(a[j + 2]),
+                                                      __float_as_uint(a[j + 3])));
+    } else if constexpr (N == 8) {
+        st_stream_v4(orow + c * N, pack8(a, std::is_same<TO, __half>::value ? TADMA_F16 : TADMA_BF16));
+    } else {
+        // 16-bit out, fp32 rows: 4 values, 8 bytes
+        const int dt = std::is_same<TO, __half>::value ? TADMA_F16 : TADMA_BF16;
+        float f8[8] = {a[0], a[1], a[2], a[3], 0.0f, 0.0f, 0.0f, 0.0f};
+        const uint4 w = pack8(f8, dt);
+        __stcs(reinterpret_cast<uint2*>(orow + c * N), make_uint2(w.x, w.y));
+    }
+}
+
+// One pass of a recipe-only program over the lane's G chunks, chunk by
+// chunk: chunk u is computed (the op bodies and roundings of run_recipe_r),
+// then folded into acc_s (a stage, in chunk order) or stored (the final
+// pass), so only one chunk's temporaries are live.  RK: the recipe, RD its
+// rounding.
+template <typename TI, typename TO, int G, int RK, int RD>
+__device__ __forceinline__ void recipe_pass(const PassRecipe& rc, const RowGroup<TI, G>& grp, float s1, float s2,
+                                            const KnownDivisor& kd, bool final_pass, int kind, float& acc_s, TO* orow) {
+    constexpr int N = 16 / (int)sizeof(TI);
+#pragma unroll
+    for (int u = 0; u < G; u++) {
+        float a[N];
+        grp.load(rc.x, u, a);
+        if constexpr (RK == RC_SQDIFF) {
+#pragma unroll
+            for (int j = 0; j < N; j++) {
+                const float d = rc_rnd<RD>(binary(TADMA_OP_SUB, a[j], s1, s1));
+                a[j] = rc_rnd<RD>(__fmul_rn(d, d));
+            }
+        } else if constexpr (RK == RC_LNTAIL || RK == RC_LNTAIL_PLAIN) {
+            bool fast = kd.ok;
+#pragma unroll
+            for (int j = 0; j < N; j++) {
+                a[j] = rc_rnd<RD>(binary(TADMA_OP_SUB, a[j], s1, s1));
+                fast = fast & kdiv_in_range(a[j]);
+            }
+            if (fast) {
+#pragma unroll
+                for (int j = 0; j < N; j++) a[j] = rc_rnd<RD>(kdiv_fast(a[j], kd));
+            } else {
+#pragma unroll
+                for (int j = 0; j < N; j++) a[j] = rc_rnd<RD>(binary(TADMA_OP_DIV, a[j], s2, s2));
+            }
+            if constexpr (RK == RC_LNTAIL) {
+                float g[N], b[N];
+                grp.load(rc.c1, u, g);
+                grp.load(rc.c2, u, b);
+#pragma unroll
+                for (int j = 0; j < N; j++) a[j] = rc_rnd<RD>(binary(TADMA_OP_ADD, rc_rnd<RD>(binary(TADMA_OP_MUL, a[j], g[j], g[j])), b[j], b[j]));
+            }
+        }
+        if (final_pass) {
+            store_chunk<TO, N>(orow, grp.c0 + 32 * u, a);
+        } else if (kind == K_SUM) {
+#pragma unroll
+            for (int j = 0; j < N; j++) acc_s = acc_s + a[j];
+        } else if (kind == K_MAX) {
+#pragma unroll
+            for (int j = 0; j < N; j++) acc_s = fmax_nan(acc_s, a[j]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < N; j++) acc_s = fmin_nan(acc_s, a[j]);
+        }
+    }
+}
+
+template <typename TI, typename TO, int G, int RK>
+__device__ __forceinline__ void recipe_pass_r(const PassRecipe& rc, const RowGroup<TI, G>& grp, float s1, float s2,
+                                              const KnownDivisor& kd, bool final_pass, int kind, float& acc_s, TO* orow) {
+    if (rc.rnd == TADMA_F16) recipe_pass<TI, TO, G, RK, TADMA_F16>(rc, grp, s1, s2, kd, final_pass, kind, acc_s, orow);
+    else if (rc.rnd == TADMA_BF16) recipe_pass<TI, TO, G, RK, TADMA_BF16>(rc, grp, s1, s2, kd, final_pass, kind, acc_s, orow);
+    else recipe_pass<TI, TO, G, RK, -1>(rc, grp, s1, s2, kd, final_pass, kind, acc_s, orow);
+}
+
 // Chunks of one operand buffer in shared memory: the row's, padded to whole
 // groups of G chunks per lane.
 __host__ __device__ constexpr int rp_stride(int nvec, int G) { return (nvec + 32 * G - 1) / (32 * G) * (32 * G); }
 
 // RONLY: every pass is a recipe (the step loop is not compiled in, so a
-// group can hold the lane's whole row: G = its chunk count).
+// group can hold the lane's whole row: G = its chunk count; passes run chunk
+// by chunk in at most 64 registers, four CTAs per SM where shared memory
+// allows).
 template <typename TI, typename TO, int G, bool RONLY>
-__global__ void __launch_bounds__(THREADS, 3) rowprog_kernel(const __grid_constant__ RowProgParams p) {
+__global__ void __launch_bounds__(THREADS, RONLY ? 4 : 3) rowprog_kernel(const __grid_constant__ RowProgParams p) {
     pdl_begin();
     constexpr int N = 16 / (int)sizeof(TI);
     extern __shared__ uint4 rp_smem[];
@@ -374,70 +476,77 @@ __global__ void __launch_bounds__(THREADS, 3) rowprog_kernel(const __grid_consta
             const int kind = final_pass ? K_SUM : p.st[s].kind;
             float acc_s = kind == K_SUM ? 0.0f : kind == K_MAX ? -INFINITY : INFINITY;
             TO* orow = reinterpret_cast<TO*>(p.out) + row * p.out_rs;
+            if constexpr (RONLY) {
+                // one group: the lane's G chunks, lane, lane + 32, ...
+                grp.c0 = lane;
+                const float s1 = rc.kind >= RC_SQDIFF ? scalar_slot<RP_NS>(sv, rc.s1 - RP_VEC) : 0.0f;
+                const float s2 = rc.kind >= RC_LNTAIL ? scalar_slot<RP_NS>(sv, rc.s2 - RP_VEC) : 1.0f;
+                KnownDivisor kd{1.0f, 1.0f, true};
+                if (rc.kind >= RC_LNTAIL) kd = known_divisor(s2);
+                switch (rc.kind) {
+                case RC_COPY: recipe_pass<TI, TO, G, RC_COPY, -1>(rc, grp, s1, s2, kd, final_pass, kind, acc_s, orow); break;
+                case RC_SQDIFF: recipe_pass_r<TI, TO, G, RC_SQDIFF>(rc, grp, s1, s2, kd, final_pass, kind, acc_s, orow); break;
+                case RC_LNTAIL: recipe_pass_r<TI, TO, G, RC_LNTAIL>(rc, grp, s1, s2, kd, final_pass, kind, acc_s, orow); break;
+                default: recipe_pass_r<TI, TO, G, RC_LNTAIL_PLAIN>(rc, grp, s1, s2, kd, final_pass, kind, acc_s, orow); break;
+                }
+            } else {
 #pragma unroll 1
-            for (int g = 0; g < ngroups; g++) {
-                grp.c0 = lane + 32 * G * g;
-                const int nval = nchunk - G * g;  // chunks of this group inside the row (may be <= 0 or > G)
-                float a[G][N];
-                if constexpr (RONLY) {
-                    run_recipe<TI, G, RP_NS>(rc, grp, sv, a);
-                } else {
+                for (int g = 0; g < ngroups; g++) {
+                    grp.c0 = lane + 32 * G * g;
+                    const int nval = nchunk - G * g;  // chunks of this group inside the row (may be <= 0 or > G)
+                    float a[G][N];
                     if (rc.kind != RC_GENERIC) run_recipe<TI, G, RP_NS>(rc, grp, sv, a);
                     else run_group<TI, G, RP_NS>(fp, final_pass && p.fast, grp, sv, a);
-                }
-                if (!final_pass) {
-                    // the row reductions' per-element fold, in chunk order
-                    if (kind == K_SUM) {
+                    if (!final_pass) {
+                        // the row reductions' per-element fold, in chunk order
+                        if (kind == K_SUM) {
 #pragma unroll
-                        for (int u = 0; u < G; u++)
-                            if (u < nval)
+                            for (int u = 0; u < G; u++)
+                                if (u < nval)
 #pragma unroll
-                                for (int j = 0; j < N; j++) acc_s = acc_s + a[u][j];
-                    } else if (kind == K_MAX) {
+                                    for (int j = 0; j < N; j++) acc_s = acc_s + a[u][j];
+                        } else if (kind == K_MAX) {
 #pragma unroll
-                        for (int u = 0; u < G; u++)
-                            if (u < nval)
+                            for (int u = 0; u < G; u++)
+                                if (u < nval)
 #pragma unroll
-                                for (int j = 0; j < N; j++) acc_s = fmax_nan(acc_s, a[u][j]);
+                                    for (int j = 0; j < N; j++) acc_s = fmax_nan(acc_s, a[u][j]);
+                        } else {
+#pragma unroll
+                            for (int u = 0; u < G; u++)
+                                if (u < nval)
+#pragma unroll
+                                    for (int j = 0; j < N; j++) acc_s = fmin_nan(acc_s, a[u][j]);
+                        }
                     } else {
 #pragma unroll
                         for (int u = 0; u < G; u++)
-                            if (u < nval)
-#pragma unroll
-                                for (int j = 0; j < N; j++) acc_s = fmin_nan(acc_s, a[u][j]);
-                    }
-                } else {
-#pragma unroll
-                    for (int u = 0; u < G; u++) {
-                        if (u >= nval) continue;
-                        const int c = grp.c0 + 32 * u;
-                        if constexpr (sizeof(TO) == 4) {
-#pragma unroll
-                            for (int j = 0; j < N; j += 4)
-                                st_stream_v4(orow + c * N + j, make_uint4(__float_as_uint(a[u][j]), __float_as_uint(a[u][j + 1]),
-                                                                          __float_as_uint(a[u][j + 2]), __float_as_uint(a[u][j + 3])));
-                        } else if constexpr (N == 8) {
-                            st_stream_v4(orow + c * N, pack8(a[u], std::is_same<TO, __half>::value ? TADMA_F16 : TADMA_BF16));
-                        } else {
-                            // 16-bit out, fp32 rows: 4 values, 8 bytes
-                            const int dt = std::is_same<TO, __half>::value ? TADMA_F16 : TADMA_BF16;
-                            float f8[8] = {a[u][0], a[u][1], a[u][2], a[u][3], 0.0f, 0.0f, 0.0f, 0.0f};
-                            const uint4 w = pack8(f8, dt);
-                            __stcs(reinterpret_cast<uint2*>(orow + c * N), make_uint2(w.x, w.y));
-                        }
+                            if (u < nval) store_chunk<TO, N>(orow, grp.c0 + 32 * u, a[u]);
                     }
                 }
             }
             if (final_pass) break;
             const RowStageParams& st = p.st[s];
+            if (kind == K_SUM) {
+                // the fixed-order butterfly of the row reductions; fp32
+                // addition is commutative, so lane order needs no select
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                const float t = __shfl_xor_sync(0xffffffffu, acc_s, o);
-                acc_s = (lane & o) ? combine_k(kind, t, acc_s) : combine_k(kind, acc_s, t);
+                for (int o = 16; o > 0; o >>= 1) acc_s = acc_s + __shfl_xor_sync(0xffffffffu, acc_s, o);
+            } else {
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    const float t = __shfl_xor_sync(0xffffffffu, acc_s, o);
+                    acc_s = (lane & o) ? combine_k(kind, t, acc_s) : combine_k(kind, acc_s, t);
+                }
             }
             float v = acc_s;
             if (st.mean) v = v / (float)p.cols;
-            if (st.pc.n) v = apply_post<float>(st.pc, v);
+            if (st.pfp.n) {
+                const float in[1][1] = {{v}};
+                float r[1];
+                run_fprog<1, 1, false>(st.pfp, r, in);
+                v = r[0];
+            }
             v = round_to(v, st.out_dtype);
             if (lane == 0) store_from(st.out, st.out_dtype, row * st.out_stride, v);
             if (s == 0) sv[RP_MAX_SC + 0] = v;
@@ -671,9 +780,10 @@ extern "C" int tadma_b200_row_program(const tadma_row_program* rp, void* stream)
             if (I.op == TADMA_OP_WHERE || (needs_b && I.b != TADMA_SRC_IMM))
                 return fail(TADMA_ERR_INVALID, "stage post: operands must be immediates");
             if (I.round_dtype >= 0 && dtype_size(I.round_dtype) == 0) return fail(TADMA_ERR_INVALID, "bad round_dtype in post");
-            st.pc.prog[i] = I;
         }
-        st.pc.n = S.n_post;
+        // the post chain on the stage's value (operand 0), immediates only
+        if (!decode_fprog(S.post, S.n_post, 1, st.pfp))
+            return fail(TADMA_ERR_UNSUPPORTED, "stage post step has no typed code");
         err = check_tensor(&S.out, "stage out");
         if (!err.empty()) return fail(TADMA_ERR_INVALID, err);
         if (S.out.rank != 1 || S.out.dims[0] != rows) return fail(TADMA_ERR_INVALID, "stage out must be a {rows} view");

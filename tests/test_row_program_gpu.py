@@ -45,12 +45,28 @@ def _inputs(dt, rows, cols, seed):
     return x, gamma, beta
 
 
+def _edge_rows(x, dt):
+    """Rows whose quotients leave the fused division's range: a constant row
+    (every x - mean is zero), and for fp32 rows of magnitude 1e20 and 1e-20,
+    a row holding an infinity and one holding a NaN."""
+    x[0] = 0.5
+    if dt == DType.F32 and x.shape[0] >= 6:
+        x[1] *= 1e20
+        x[2] *= 1e-20
+        x[3, 7] = float("inf")
+        x[4, 3] = float("nan")
+        x[5, ::3] = 0.0
+
+
 @pytest.mark.parametrize("dt", [DType.F32, DType.F16, DType.BF16])
-@pytest.mark.parametrize("rows,cols", [(300, 768), (37, 1024), (1, 64), (1000, 128)])
-def test_layer_norm_decomposition_one_pass(dt, rows, cols):
+@pytest.mark.parametrize("rows,cols,edges", [(300, 768, False), (37, 1024, False), (1, 64, False), (1000, 128, False),
+                                             (64, 768, True), (40, 96, True)])
+def test_layer_norm_decomposition_one_pass(dt, rows, cols, edges):
     if dt == DType.F32 and cols > 1024:
         pytest.skip("fp32 rows up to 1024")
     x, gamma, beta = _inputs(dt, rows, cols, rows + cols)
+    if edges:
+        _edge_rows(x, dt)
     eps = 1e-12
     sdt = TDT[dt]
     # separate calls, as deferred evaluation issues them
@@ -84,7 +100,7 @@ def test_layer_norm_decomposition_one_pass(dt, rows, cols):
     assert np.array_equal(_bits(m), _bits(m_sep).reshape(-1))
     assert np.array_equal(_bits(sd), _bits(sd_sep).reshape(-1))
     assert np.array_equal(_bits(y), _bits(y_sep))
-    if dt == DType.F32:
+    if dt == DType.F32 and not edges:
         xn, gn, bn = x.cpu().numpy(), gamma.cpu().numpy(), beta.cpu().numpy()
         ref = np.zeros_like(xn)
         assert O.layer_norm(xn, -1, gn, bn, eps, LNMode.ONNX, ref) == 0
