@@ -18,7 +18,10 @@
 //   shared memory in warp order;
 // * SPLIT (ROW or COL) when few outputs share a long reduced axis: several
 //   CTAs per output reduce fixed chunks into a workspace, a second pass
-//   combines the chunk partials in order;
+//   combines the chunk partials in order; the COL split hands every CTA of
+//   one resident wave the same number of rows (a CTA's share may end in one
+//   column tile and go on in the next), so no SM waits on a second wave or
+//   on a neighbour with one CTA more;
 // * GENERIC path: any other layout / dtype, one warp per output element.
 // Every path assigns elements to lanes and combines partials in a fixed
 // order, so results are deterministic run to run.
@@ -59,8 +62,11 @@ struct RedParams {
     int64_t kin[TADMA_MAX_RANK];
     int64_t kout[TADMA_MAX_RANK];
     // split-R (two-pass) reductions
-    int64_t splits;  // CTAs per row (ROW) / per column tile (COL)
-    int64_t chunk;   // reduced-axis elements per split
+    int64_t splits;  // CTAs per row (ROW) / partial slots per column tile (COL)
+    int64_t chunk;   // ROW: reduced-axis elements per split
+    // COL split: `ctas` CTAs share the `units` = tiles x nrows x R
+    // (tile, row) pairs evenly, in tile-major order
+    int64_t units, tiles, ctas, tile_cols;
     void* partials;  // State<float> workspace
     // row operand (reduce_rowop_kernel): element x of row r becomes
     // op1(x, m_r) before the pre-op, m_r = rop[r * rop_row_stride], or imm1
@@ -343,66 +349,95 @@ __global__ void __launch_bounds__(THREADS) reduce_rowop_kernel(const __grid_cons
 
 // -------------------------------------------------------------- COL path --
 
+// The CTA of a COL split whose share holds (tile, row) pair x: CTA c starts
+// at pair c * units / ctas.
+__host__ __device__ __forceinline__ int64_t col_cta_of(int64_t x, int64_t units, int64_t ctas) {
+    return ((x + 1) * ctas + units - 1) / units - 1;
+}
+
+// Rows [rbeg, rend) of column tile `tile` of outer index o: warps take rows
+// rbeg + w, rbeg + w + 8, ..., lanes 32 x VEC adjacent columns; the warp
+// partials combine in warp order, then go to the output or (SPLIT) to
+// partial slot k of the tile.
+template <typename T, int K, int VEC, bool SPLIT, bool PRE>
+__device__ __forceinline__ void col_segment(const RedParams& p, int64_t o, int64_t tile, int64_t rbeg, int64_t rend, int64_t k,
+                                            State<float> (&part)[WARPS][32 * VEC]) {
+    constexpr int COLS = 32 * VEC;
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int64_t col0 = tile * COLS + lane * VEC;
+    const T* base = reinterpret_cast<const T*>(p.in) + o * p.in_row_stride;
+    State<float> s[VEC];
+#pragma unroll
+    for (int j = 0; j < VEC; j++) s[j] = init_state<K, float>();
+    if (col0 < p.inner) {
+        constexpr int UNR = 4;
+        for (int64_t r0 = rbeg + w; r0 < rend; r0 += WARPS * UNR) {
+            if constexpr (VEC > 1) {
+                uint4 v[UNR];
+#pragma unroll
+                for (int u = 0; u < UNR; u++)
+                    if (r0 + WARPS * u < rend) v[u] = ld_stream_v4(base + (r0 + WARPS * u) * p.r_stride + col0);
+#pragma unroll
+                for (int u = 0; u < UNR; u++) {
+                    if (r0 + WARPS * u < rend) {
+                        float f[Vec<T>::N];
+                        Vec<T>::cvt(v[u], f);
+#pragma unroll
+                        for (int j = 0; j < VEC; j++) update<K, float>(s[j], prep<PRE>(p, f[j]), r0 + WARPS * u);
+                    }
+                }
+            } else {
+                float v[UNR];
+#pragma unroll
+                for (int u = 0; u < UNR; u++)
+                    if (r0 + WARPS * u < rend) v[u] = ld1(base + (r0 + WARPS * u) * p.r_stride + col0);
+#pragma unroll
+                for (int u = 0; u < UNR; u++)
+                    if (r0 + WARPS * u < rend) update<K, float>(s[0], prep<PRE>(p, v[u]), r0 + WARPS * u);
+            }
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < VEC; j++) part[w][lane * VEC + j] = s[j];
+    __syncthreads();
+    for (int c = threadIdx.x; c < COLS; c += THREADS) {
+        const int64_t col = tile * COLS + c;
+        if (col < p.inner) {
+            State<float> t = part[0][c];
+#pragma unroll
+            for (int ww = 1; ww < WARPS; ww++) t = combine<K, float>(t, part[ww][c]);
+            if constexpr (SPLIT) {
+                reinterpret_cast<State<float>*>(p.partials)[(o * p.splits + k) * p.inner + col] = t;
+            } else {
+                finish<K, float>(p, t, o * p.out_row_stride + col);
+            }
+        }
+    }
+    __syncthreads();
+}
+
+// SPLIT: a 1-D grid of p.ctas CTAs; CTA c reduces (tile, row) pairs
+// [c U / P, (c + 1) U / P) of the tile-major sequence (U = p.units, P =
+// p.ctas), one segment per tile its share touches, each into the slot given
+// by its rank among the tile's CTAs.  Otherwise blockIdx.x is the tile and
+// blockIdx.y walks the outer index.
 template <typename T, int K, int VEC, bool SPLIT, bool PRE>
 __global__ void __launch_bounds__(THREADS) reduce_col_kernel(const __grid_constant__ RedParams p) {
     pdl_begin();
-    constexpr int COLS = 32 * VEC;
-    __shared__ State<float> part[WARPS][COLS];
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    const int64_t col0 = (int64_t)blockIdx.x * COLS + lane * VEC;
-    // SPLIT: this CTA covers rows [rbeg, rend) of R and writes a partial state.
-    const int64_t rbeg = SPLIT ? (int64_t)blockIdx.z * p.chunk : 0;
-    const int64_t rend = SPLIT ? (rbeg + p.chunk < p.R ? rbeg + p.chunk : p.R) : p.R;
-    for (int64_t o = blockIdx.y; o < p.nrows; o += gridDim.y) {
-        const T* base = reinterpret_cast<const T*>(p.in) + o * p.in_row_stride;
-        State<float> s[VEC];
-#pragma unroll
-        for (int j = 0; j < VEC; j++) s[j] = init_state<K, float>();
-        if (col0 < p.inner) {
-            constexpr int UNR = 4;
-            for (int64_t r0 = rbeg + w; r0 < rend; r0 += WARPS * UNR) {
-                if constexpr (VEC > 1) {
-                    uint4 v[UNR];
-#pragma unroll
-                    for (int u = 0; u < UNR; u++)
-                        if (r0 + WARPS * u < rend) v[u] = ld_stream_v4(base + (r0 + WARPS * u) * p.r_stride + col0);
-#pragma unroll
-                    for (int u = 0; u < UNR; u++) {
-                        if (r0 + WARPS * u < rend) {
-                            float f[Vec<T>::N];
-                            Vec<T>::cvt(v[u], f);
-#pragma unroll
-                            for (int j = 0; j < VEC; j++) update<K, float>(s[j], prep<PRE>(p, f[j]), r0 + WARPS * u);
-                        }
-                    }
-                } else {
-                    float v[UNR];
-#pragma unroll
-                    for (int u = 0; u < UNR; u++)
-                        if (r0 + WARPS * u < rend) v[u] = ld1(base + (r0 + WARPS * u) * p.r_stride + col0);
-#pragma unroll
-                    for (int u = 0; u < UNR; u++)
-                        if (r0 + WARPS * u < rend) update<K, float>(s[0], prep<PRE>(p, v[u]), r0 + WARPS * u);
-                }
-            }
+    __shared__ State<float> part[WARPS][32 * VEC];
+    if constexpr (SPLIT) {
+        const int64_t U = p.units, P = p.ctas, c = blockIdx.x;
+        const int64_t ue = (c + 1) * U / P;
+        for (int64_t u = c * U / P; u < ue;) {
+            const int64_t tb = u / p.R, rbeg = u - tb * p.R;
+            const int64_t rend = rbeg + (ue - u) < p.R ? rbeg + (ue - u) : p.R;
+            const int64_t o = tb / p.tiles;
+            col_segment<T, K, VEC, true, PRE>(p, o, tb - o * p.tiles, rbeg, rend, c - col_cta_of(tb * p.R, U, P), part);
+            u += rend - rbeg;
         }
-#pragma unroll
-        for (int j = 0; j < VEC; j++) part[w][lane * VEC + j] = s[j];
-        __syncthreads();
-        for (int c = threadIdx.x; c < COLS; c += THREADS) {
-            const int64_t col = (int64_t)blockIdx.x * COLS + c;
-            if (col < p.inner) {
-                State<float> t = part[0][c];
-#pragma unroll
-                for (int ww = 1; ww < WARPS; ww++) t = combine<K, float>(t, part[ww][c]);
-                if constexpr (SPLIT) {
-                    reinterpret_cast<State<float>*>(p.partials)[(o * p.splits + blockIdx.z) * p.inner + col] = t;
-                } else {
-                    finish<K, float>(p, t, o * p.out_row_stride + col);
-                }
-            }
-        }
-        __syncthreads();
+    } else {
+        for (int64_t o = blockIdx.y; o < p.nrows; o += gridDim.y)
+            col_segment<T, K, VEC, false, PRE>(p, o, blockIdx.x, 0, p.R, 0, part);
     }
 }
 
@@ -488,8 +523,11 @@ __global__ void __launch_bounds__(THREADS) reduce_col_finish_kernel(const __grid
     const int64_t total = p.nrows * p.inner;
     for (int64_t idx = (int64_t)blockIdx.x * THREADS + threadIdx.x; idx < total; idx += (int64_t)gridDim.x * THREADS) {
         const int64_t o = idx / p.inner, col = idx - o * p.inner;
+        // the CTAs whose shares cover this column's tile, in row order
+        const int64_t x = (o * p.tiles + col / p.tile_cols) * p.R;
+        const int64_t n = col_cta_of(x + p.R - 1, p.units, p.ctas) - col_cta_of(x, p.units, p.ctas) + 1;
         State<float> t = init_state<K, float>();
-        for (int64_t g = 0; g < p.splits; g++) t = combine<K, float>(t, part[(o * p.splits + g) * p.inner + col]);
+        for (int64_t g = 0; g < n; g++) t = combine<K, float>(t, part[(o * p.splits + g) * p.inner + col]);
         finish<K, float>(p, t, o * p.out_row_stride + col);
     }
 }
@@ -562,10 +600,11 @@ int launch_fast(int path, const RedParams& p, bool vec, cudaStream_t s) {
         constexpr int VEC = Vec<T>::N;
         int64_t tiles = vec ? (p.inner + 32 * VEC - 1) / (32 * VEC) : (p.inner + 31) / 32;
         if (tiles > 0x7fffffff) return fail(TADMA_ERR_UNSUPPORTED, "reduce: too many column tiles");
-        dim3 grid((unsigned)tiles, (unsigned)(p.nrows < 65535 ? p.nrows : 65535), (unsigned)(p.splits > 1 ? p.splits : 1));
+        dim3 grid((unsigned)tiles, (unsigned)(p.nrows < 65535 ? p.nrows : 65535), 1);
         if (p.splits > 1) {
-            if (vec) (void)launch_pdl(reduce_col_kernel<T, K, VEC, true, PRE>, dim3(grid), dim3(THREADS), 0, s, p);
-            else (void)launch_pdl(reduce_col_kernel<T, K, 1, true, PRE>, dim3(grid), dim3(THREADS), 0, s, p);
+            const dim3 g1((unsigned)p.ctas);
+            if (vec) (void)launch_pdl(reduce_col_kernel<T, K, VEC, true, PRE>, g1, dim3(THREADS), 0, s, p);
+            else (void)launch_pdl(reduce_col_kernel<T, K, 1, true, PRE>, g1, dim3(THREADS), 0, s, p);
             const void* fn = (const void*)reduce_col_finish_kernel<K>;
             (void)launch_pdl(reduce_col_finish_kernel<K>, dim3(grid_for(fn, (p.nrows * p.inner + THREADS - 1) / THREADS)), dim3(THREADS), 0, s, p);
         } else {
@@ -592,6 +631,32 @@ template <typename T>
 int launch_fast_kind(int kind, int path, const RedParams& p, bool vec, cudaStream_t s) {
     if (p.pre_op != TADMA_OP_COPY || p.square) return launch_fast_kind_pre<T, true>(kind, path, p, vec, s);
     return launch_fast_kind_pre<T, false>(kind, path, p, vec, s);
+}
+
+// The COL split kernel of (T, kind, vector path, pre-op) and the number of
+// its CTAs resident at once on the device.
+template <typename T, bool PRE>
+const void* col_split_fn(int kind, bool vec) {
+    constexpr int V = Vec<T>::N;
+    switch (kind) {
+    case K_SUM: return vec ? (const void*)reduce_col_kernel<T, K_SUM, V, true, PRE> : (const void*)reduce_col_kernel<T, K_SUM, 1, true, PRE>;
+    case K_MAX: return vec ? (const void*)reduce_col_kernel<T, K_MAX, V, true, PRE> : (const void*)reduce_col_kernel<T, K_MAX, 1, true, PRE>;
+    case K_MIN: return vec ? (const void*)reduce_col_kernel<T, K_MIN, V, true, PRE> : (const void*)reduce_col_kernel<T, K_MIN, 1, true, PRE>;
+    case K_ARGMAX:
+        return vec ? (const void*)reduce_col_kernel<T, K_ARGMAX, V, true, PRE> : (const void*)reduce_col_kernel<T, K_ARGMAX, 1, true, PRE>;
+    default:
+        return vec ? (const void*)reduce_col_kernel<T, K_ARGMIN, V, true, PRE> : (const void*)reduce_col_kernel<T, K_ARGMIN, 1, true, PRE>;
+    }
+}
+
+int64_t col_split_capacity(int dt, int kind, bool vec, bool pre) {
+    const void* fn;
+    switch (dt) {
+    case TADMA_F32: fn = pre ? col_split_fn<float, true>(kind, vec) : col_split_fn<float, false>(kind, vec); break;
+    case TADMA_F16: fn = pre ? col_split_fn<__half, true>(kind, vec) : col_split_fn<__half, false>(kind, vec); break;
+    default: fn = pre ? col_split_fn<__nv_bfloat16, true>(kind, vec) : col_split_fn<__nv_bfloat16, false>(kind, vec); break;
+    }
+    return (int64_t)sm_count() * blocks_per_sm(fn);
 }
 
 template <typename A>
@@ -630,18 +695,24 @@ void plan_row_split(RedParams& p, int64_t R, int64_t sm) {
     p.splits = (R + chunk - 1) / chunk;
 }
 
-// COL: split when fewer than 2 CTAs per SM would be busy and R is long.
-void plan_col_split(RedParams& p, int64_t R, int64_t cols_per_cta, int64_t sm) {
+// COL: split when fewer than 2 CTAs per SM would be busy and R is long:
+// one resident wave of the split kernel (`capacity` CTAs, at least 256 rows
+// each) shares the tiles' rows evenly.  splits: the partial slots per tile,
+// the most CTAs one tile's R rows can span.
+void plan_col_split(RedParams& p, int64_t R, int64_t cols_per_cta, int64_t sm, int64_t capacity) {
     p.splits = 1;
     const int64_t tiles = (p.inner + cols_per_cta - 1) / cols_per_cta;
     const int64_t ctas = tiles * p.nrows;
     if (ctas >= 2 * sm || R < 2048 || p.nrows > 65535) return;
-    int64_t g = (4 * sm + ctas - 1) / ctas;
-    if (g > R / 256) g = R / 256;
-    if (g > 65535) g = 65535;
-    if (g < 2) return;
-    p.chunk = (R + g - 1) / g;
-    p.splits = (R + p.chunk - 1) / p.chunk;
+    const int64_t U = ctas * R;
+    int64_t P = capacity;
+    if (P > U / 256) P = U / 256;
+    if (P <= ctas) return;
+    p.units = U;
+    p.tiles = tiles;
+    p.tile_cols = cols_per_cta;
+    p.ctas = P;
+    p.splits = (P + ctas - 1) / ctas + 1;
 }
 
 int64_t split_workspace_bytes(const RedParams& p, int path) {
@@ -677,13 +748,23 @@ int run_fast(int dt, int kind, int path, RedParams& p, bool vec, cudaStream_t s,
             // for fewer than two, the reduction runs in one pass (no scratch).
             const int64_t per_split = ws / p.splits;
             const int64_t g = fixed.bytes / per_split;
-            if (g < 2) {
-                p.splits = 1;
-                return dispatch_fast(dt, kind, path, p, vec, s);
+            if (path == 1) {
+                // COL: fewer CTAs, so that a tile's rows span at most g of them
+                const int64_t ctas = p.tiles * p.nrows;
+                if (g < 3) {
+                    p.splits = 1;
+                    return dispatch_fast(dt, kind, path, p, vec, s);
+                }
+                if (p.ctas > (g - 1) * ctas) p.ctas = (g - 1) * ctas;
+                p.splits = (p.ctas + ctas - 1) / ctas + 1;
+            } else {
+                if (g < 2) {
+                    p.splits = 1;
+                    return dispatch_fast(dt, kind, path, p, vec, s);
+                }
+                p.chunk = ((p.R + g - 1) / g + 7) / 8 * 8;  // a multiple of every vector width
+                p.splits = (p.R + p.chunk - 1) / p.chunk;
             }
-            p.chunk = (p.R + g - 1) / g;
-            if (path == 0) p.chunk = (p.chunk + 7) / 8 * 8;  // a multiple of every vector width
-            p.splits = (p.R + p.chunk - 1) / p.chunk;
         }
         p.partials = fixed.ptr;
         return dispatch_fast(dt, kind, path, p, vec, s);
@@ -788,7 +869,8 @@ int reduce_impl(int32_t op, const tadma_tensor* in, int32_t axis, int32_t pre_op
         p.out_row_stride = f.rank == 2 ? f.strides[1][0] : 0;
         const int N = 16 / es;
         bool vec = in_aligned && p.inner % N == 0 && (p.r_stride * es) % 16 == 0 && (p.in_row_stride * es) % 16 == 0;
-        plan_col_split(p, R, vec ? 32 * N : 32, sm_count());
+        plan_col_split(p, R, vec ? 32 * N : 32, sm_count(),
+                       col_split_capacity(dt, kind, vec, p.pre_op != TADMA_OP_COPY || p.square));
         return run_fast(dt, kind, 1, p, vec, s, fixed);
     }
     // GENERIC

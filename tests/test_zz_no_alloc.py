@@ -62,7 +62,7 @@ def test_noalloc_matches_reduce_twice(shape, axis, op, dt):
 
 
 @pytest.mark.parametrize("shape", [
-    (1, 4096, 36864),  # 144 column tiles x 5 splits x 36864 columns of 16-byte partials = 2.95 MB: 3 splits fit
+    (1, 4096, 36864),  # 144 column tiles; a wave of CTAs needs 6 partial slots of 36864 x 16 bytes: 3 fit
     (1, 4096, 70000),  # one split's partials (1.1 MB) leave no room for two: one pass, no scratch
 ])
 def test_noalloc_fits_its_split_to_the_static_scratch(shape):
