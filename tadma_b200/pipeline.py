@@ -18,6 +18,22 @@ def chunk_bounds(rows: int, chunks: int):
     return [(lo, min(rows, lo + step)) for lo in range(0, rows, step)]
 
 
+def ramped_bounds(rows: int, chunks: int, part: int = 4):
+    """chunk_bounds with the first and the last chunk each split so that
+    their outer piece holds 1 / `part` of a chunk: the first upload (which
+    nothing overlaps) and the last download (likewise) shrink, the chunks
+    between keep both copy directions busy."""
+    b = chunk_bounds(rows, chunks)
+    if len(b) < 2:
+        return b
+    (lo0, hi0), (lo1, hi1) = b[0], b[-1]
+    q0 = max(1, (hi0 - lo0) // part)
+    q1 = max(1, (hi1 - lo1) // part)
+    head = [(lo0, lo0 + q0), (lo0 + q0, hi0)] if hi0 - lo0 > q0 else [b[0]]
+    tail = [(lo1, hi1 - q1), (hi1 - q1, hi1)] if hi1 - lo1 > q1 else [b[-1]]
+    return head + b[1:-1] + tail
+
+
 class RowPipeline:
     """One step = upload the `uploads` row chunks, run `make_call(lo, hi,
     stream)` per chunk, download the `downloads` row chunks; `once` buffers
@@ -28,12 +44,12 @@ class RowPipeline:
     make_call(lo, hi, stream) returns a callable that launches the op on rows
     [lo, hi) on `stream` (e.g. a tadma_b200.prepare_* call built for views)."""
 
-    def __init__(self, rows, chunks, uploads, downloads, make_call, once=()):
+    def __init__(self, rows, chunks, uploads, downloads, make_call, once=(), bounds=None):
         import torch
         self.rows, self.chunks = rows, max(1, chunks)
         self.uploads, self.downloads, self.once = list(uploads), list(downloads), list(once)
         self.s_in, self.s_run, self.s_out = torch.cuda.Stream(), torch.cuda.Stream(), torch.cuda.Stream()
-        self.bounds = chunk_bounds(rows, self.chunks)
+        self.bounds = list(bounds) if bounds is not None else chunk_bounds(rows, self.chunks)
         self.calls = [make_call(lo, hi, self.s_run) for lo, hi in self.bounds]
         self.ev_in = [torch.cuda.Event() for _ in self.bounds]
         self.ev_run = [torch.cuda.Event() for _ in self.bounds]
