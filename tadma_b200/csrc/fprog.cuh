@@ -13,6 +13,7 @@
 
 #include <cstdint>
 
+#include "kdiv.cuh"
 #include "ops.cuh"
 
 namespace tadma_b200 {
@@ -25,7 +26,8 @@ constexpr int FC_BV = 41;    // FC_BV + (op - 32): binary op, operand `b` second
 constexpr int FC_WHERE = 61; // acc = acc != 0 ? b : c (operands, or the imm where b / c < 0)
 constexpr int FC_RND = 62;   // FC_RND + k: round to the k-th of F16, BF16, I64, I32, U8, BOOL, I8
 constexpr int FC_SQR = 69;   // pow(acc, 2) with the immediate 2: one rounded multiply, as binary(POW) gives it
-constexpr int FC_COUNT = 70;
+constexpr int FC_DIVK = 70;  // acc / imm through imm's reciprocal (kdiv.cuh), which the next step's imm holds
+constexpr int FC_COUNT = 71;
 
 struct FInstr {
     uint8_t code;
@@ -69,8 +71,20 @@ inline bool decode_fprog(const tadma_instr* prog, int n_instr, int nin, FProg& f
             }
         } else if (I.op >= TADMA_OP_ADD && I.op <= TADMA_OP_LOR) {
             const int s = slot(I.b);
-            if (I.op == TADMA_OP_POW && s < 0 && (float)I.imm == 2.0f) emit(FC_SQR, -1, -1, 0.0);
-            else emit(s >= 0 ? FC_BV + (I.op - TADMA_OP_ADD) : FC_BI + (I.op - TADMA_OP_ADD), s, -1, I.imm);
+            // a division by an immediate inside kdiv's range takes a second
+            // step for the reciprocal, while the remaining instructions
+            // still fit at two steps each
+            const bool kdiv = I.op == TADMA_OP_DIV && s < 0 && kdiv_in_range((float)I.imm) &&
+                              2 * TADMA_MAX_INSTR - fp.n - 2 * (n_instr - i) >= 1;
+            if (I.op == TADMA_OP_POW && s < 0 && (float)I.imm == 2.0f) {
+                emit(FC_SQR, -1, -1, 0.0);
+            } else if (kdiv) {
+                const float b = (float)I.imm;
+                emit(FC_DIVK, -1, -1, b);
+                emit(FC_DIVK, -1, -1, 1.0f / b);  // RN(1/b): the host's IEEE single division
+            } else {
+                emit(s >= 0 ? FC_BV + (I.op - TADMA_OP_ADD) : FC_BI + (I.op - TADMA_OP_ADD), s, -1, I.imm);
+            }
         } else if (I.op == TADMA_OP_WHERE) {
             emit(FC_WHERE, slot(I.b), slot(I.c), I.imm);
         } else {
@@ -221,6 +235,20 @@ __device__ __forceinline__ void run_fprog(const FProg& fp, float (&acc)[W], cons
         case FC_SQR: {
 #pragma unroll
             for (int j = 0; j < W; j++) acc[j] = __fmul_rn(acc[j], acc[j]);
+        } break;
+        case FC_DIVK: {
+            const KnownDivisor kd{I.imm, fp.ins[i + 1].imm, true};
+            i++;  // the reciprocal's step
+            bool fast = true;
+#pragma unroll
+            for (int j = 0; j < W; j++) fast = fast & kdiv_in_range(acc[j]);
+            if (fast) {
+#pragma unroll
+                for (int j = 0; j < W; j++) acc[j] = kdiv_fast(acc[j], kd);
+            } else {
+#pragma unroll
+                for (int j = 0; j < W; j++) acc[j] = __fdiv_rn(acc[j], kd.b);
+            }
         } break;
             TADMA_FR(0, TADMA_F16)
             TADMA_FR(1, TADMA_BF16)

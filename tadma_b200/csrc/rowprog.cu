@@ -244,6 +244,23 @@ __device__ __forceinline__ void run_group(const FProg& fp, bool fast, const RowG
 #pragma unroll
                 for (int j = 0; j < N; j++) acc[u][j] = __fmul_rn(acc[u][j], acc[u][j]);
         } break;
+        case FC_DIVK: {
+            const KnownDivisor kd{I.imm, fp.ins[i + 1].imm, true};
+            i++;  // the reciprocal's step
+#pragma unroll
+            for (int u = 0; u < G; u++) {
+                bool fast = true;
+#pragma unroll
+                for (int j = 0; j < N; j++) fast = fast & kdiv_in_range(acc[u][j]);
+                if (fast) {
+#pragma unroll
+                    for (int j = 0; j < N; j++) acc[u][j] = kdiv_fast(acc[u][j], kd);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < N; j++) acc[u][j] = __fdiv_rn(acc[u][j], kd.b);
+                }
+            }
+        } break;
             TADMA_RR(0, TADMA_F16)
             TADMA_RR(1, TADMA_BF16)
             TADMA_RR(2, TADMA_I64)
@@ -359,10 +376,14 @@ template <typename TI, typename TO, int G, int RK, int RD>
 __device__ __forceinline__ void recipe_pass(const PassRecipe& rc, const RowGroup<TI, G>& grp, float s1, float s2,
                                             const KnownDivisor& kd, bool final_pass, int kind, float& acc_s, TO* orow) {
     constexpr int N = 16 / (int)sizeof(TI);
+    // the lane's first chunk of each operand; chunk u is 32 u further
+    const uint4* xb = grp.base(rc.x) + grp.c0;
+    const uint4* gb = grp.base(RK == RC_LNTAIL ? rc.c1 : rc.x) + grp.c0;
+    const uint4* bb = grp.base(RK == RC_LNTAIL ? rc.c2 : rc.x) + grp.c0;
 #pragma unroll
     for (int u = 0; u < G; u++) {
         float a[N];
-        grp.load(rc.x, u, a);
+        cvt16<TI>(xb[32 * u], a);
         if constexpr (RK == RC_SQDIFF) {
 #pragma unroll
             for (int j = 0; j < N; j++) {
@@ -385,8 +406,8 @@ __device__ __forceinline__ void recipe_pass(const PassRecipe& rc, const RowGroup
             }
             if constexpr (RK == RC_LNTAIL) {
                 float g[N], b[N];
-                grp.load(rc.c1, u, g);
-                grp.load(rc.c2, u, b);
+                cvt16<TI>(gb[32 * u], g);
+                cvt16<TI>(bb[32 * u], b);
 #pragma unroll
                 for (int j = 0; j < N; j++) a[j] = rc_rnd<RD>(binary(TADMA_OP_ADD, rc_rnd<RD>(binary(TADMA_OP_MUL, a[j], g[j], g[j])), b[j], b[j]));
             }
@@ -406,12 +427,23 @@ __device__ __forceinline__ void recipe_pass(const PassRecipe& rc, const RowGroup
     }
 }
 
+// The rounding of a recipe-only kernel's passes: none, or (16-bit rows) the
+// rows' own type; the host sends programs with other roundings to the
+// generic kernel (launch_rp_t), so each kernel holds one or two
+// variants of each pass.
+template <typename TI>
+constexpr int rp_own_rnd() { return sizeof(TI) == 4 ? -1 : std::is_same<TI, __half>::value ? TADMA_F16 : TADMA_BF16; }
+
 template <typename TI, typename TO, int G, int RK>
 __device__ __forceinline__ void recipe_pass_r(const PassRecipe& rc, const RowGroup<TI, G>& grp, float s1, float s2,
                                               const KnownDivisor& kd, bool final_pass, int kind, float& acc_s, TO* orow) {
-    if (rc.rnd == TADMA_F16) recipe_pass<TI, TO, G, RK, TADMA_F16>(rc, grp, s1, s2, kd, final_pass, kind, acc_s, orow);
-    else if (rc.rnd == TADMA_BF16) recipe_pass<TI, TO, G, RK, TADMA_BF16>(rc, grp, s1, s2, kd, final_pass, kind, acc_s, orow);
-    else recipe_pass<TI, TO, G, RK, -1>(rc, grp, s1, s2, kd, final_pass, kind, acc_s, orow);
+    if constexpr (rp_own_rnd<TI>() >= 0) {
+        if (rc.rnd >= 0) {
+            recipe_pass<TI, TO, G, RK, rp_own_rnd<TI>()>(rc, grp, s1, s2, kd, final_pass, kind, acc_s, orow);
+            return;
+        }
+    }
+    recipe_pass<TI, TO, G, RK, -1>(rc, grp, s1, s2, kd, final_pass, kind, acc_s, orow);
 }
 
 // Chunks of one operand buffer in shared memory: the row's, padded to whole
@@ -585,8 +617,10 @@ template <typename TI, typename TO>
 int launch_rp_t(const RowProgParams& p, cudaStream_t s) {
     // every pass a recipe and every lane the same whole chunks: one group
     // holds the lane's row (512 / 768 / 1024 values)
-    bool all_rc = p.rc.kind != RC_GENERIC;
-    for (int k = 0; k < p.n_stages; k++) all_rc = all_rc && p.st[k].rc.kind != RC_GENERIC;
+    // (passes rounded, if at all, to the rows' own 16-bit type)
+    auto rnd_ok = [](const PassRecipe& rc) { return rc.kind == RC_COPY || rc.rnd < 0 || rc.rnd == rp_own_rnd<TI>(); };
+    bool all_rc = p.rc.kind != RC_GENERIC && rnd_ok(p.rc);
+    for (int k = 0; k < p.n_stages; k++) all_rc = all_rc && p.st[k].rc.kind != RC_GENERIC && rnd_ok(p.st[k].rc);
     if (all_rc && p.nvec % 32 == 0) {
         const int per_lane = p.nvec / 32;
         constexpr int N = 16 / (int)sizeof(TI);

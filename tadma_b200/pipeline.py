@@ -22,7 +22,11 @@ def ramped_bounds(rows: int, chunks: int, part: int = 4):
     """chunk_bounds with the first and the last chunk each split so that
     their outer piece holds 1 / `part` of a chunk: the first upload (which
     nothing overlaps) and the last download (likewise) shrink, the chunks
-    between keep both copy directions busy."""
+    between keep both copy directions busy.  On config 2 (x[8192, 8192]
+    bf16 in and out over PCIe) 8 chunks ramped by 4 measured 84.9 GB/s
+    against 84.1 for 8 equal chunks: the step is bound by the two copy
+    directions together (99 GB/s for one large copy each way), not by the
+    unoverlapped ends."""
     b = chunk_bounds(rows, chunks)
     if len(b) < 2:
         return b
