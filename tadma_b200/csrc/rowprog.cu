@@ -475,7 +475,13 @@ __global__ void __launch_bounds__(THREADS, RONLY ? 4 : 3) rowprog_kernel(const _
         for (int k = 0; k < nrv; k++) {
             const char* src = p.rv[k] + r * p.rv_rs[k];
             uint4* dst = wbuf + (b * nrv + k) * stride;
-            for (int c = lane; c < nvec; c += 32) cp_async16(dst + c, src + (int64_t)c * 16);
+            if constexpr (RONLY) {
+                // nvec == 32 G: the lane's G chunks at fixed offsets
+#pragma unroll
+                for (int u = 0; u < G; u++) cp_async16(dst + lane + 32 * u, src + (int64_t)(lane + 32 * u) * 16);
+            } else {
+                for (int c = lane; c < nvec; c += 32) cp_async16(dst + c, src + (int64_t)c * 16);
+            }
         }
         cp_async_commit();
     };
