@@ -157,6 +157,42 @@ def test_vector_path_with_ragged_tail(op):
     close(from_dev(out), ref, tmp, op, -1)
 
 
+# Operands that are one row for every output (a bias over the reduced axis),
+# of the rows' dtype (the typed kernel) or another one (the interpreter).
+@pytest.mark.parametrize("op", [Reduce.SUM, Reduce.MEAN, Reduce.MAX, Reduce.ARGMAX])
+@pytest.mark.parametrize("xdt,bdt", [(DType.BF16, DType.F32), (DType.F32, DType.F32), (DType.F16, DType.BF16)])
+def test_column_operand_staged_any_dtype(op, xdt, bdt):
+    x = gen((37, 1000), xdt, Dist.NORMAL, 0.0, 1.0, 30)
+    b = gen((1000,), bdt, Dist.NORMAL, 0.0, 1.0, 31)
+    prog = [instr(Op.ADD, b=1), instr(Op.EXP)]
+    got, ref, tmp = both(op, [x, b], [xdt, bdt], prog, -1)
+    close(got, ref, tmp, op, -1, max_ulp=2)
+
+
+def test_two_column_operands_and_ragged_rows():
+    # rows of 1003 in a [33, 1008] buffer (16-byte aligned rows, a 3-element
+    # tail), two column operands of other dtypes
+    import torch
+    full = gen((33, 1008), DType.F32, Dist.NORMAL, 0, 1, 32)
+    xd = to_dev(full)
+    view = make_tensor(xd.data_ptr(), DType.F32, [33, 1003], [1008, 1])
+    b1 = gen((1003,), DType.F16, Dist.NORMAL, 0, 1, 33)
+    b2 = gen((1003,), DType.BF16, Dist.UNIFORM, 0.5, 1.5, 34)
+    k1, d1 = dev_view(np.broadcast_to(b1, (33, 1003)), DType.F16)
+    k2, d2 = dev_view(np.broadcast_to(b2, (33, 1003)), DType.BF16)
+    prog = [instr(Op.ADD, b=1), instr(Op.MUL, b=2), instr(Op.TANH)]
+    for op in (Reduce.SUM, Reduce.MIN):
+        out = empty_dev((33, 1), DType.F32)
+        tb.reduce_chain(op, [view, d1, d2], prog, -1, out, Compute.F32)
+        shape = (33, 1003)
+        tmp = np.zeros(shape, np.float32)
+        assert O.eltwise(tmp, [full[:, :1003], np.broadcast_to(b1, shape), np.broadcast_to(b2, shape)], prog,
+                         Compute.F32, out_dtype=DType.F32, in_dtypes=[DType.F32, DType.F16, DType.BF16]) == 0
+        ref = np.zeros((33, 1), np.float32)
+        assert O.reduce(op, tmp, -1, ref) == 0
+        close(from_dev(out), ref, tmp, op, -1, max_ulp=2)
+
+
 # Chains of the row-operand form op1(x, m) -> [unary] -> [square], m one value
 # per output row or an immediate: tadma_b200_reduce_chain runs them on the
 # reduction engine's row kernel (reduce_rowop_kernel).
