@@ -221,9 +221,9 @@ class Config1:
             c()
 
     def parts(self):
-        return [("chain_reduce_kernel", "one fused call, CUDA graph replay", self.bytes, self.step),
-                ("chain_reduce_kernel", "compare: one fused call, eager", self.bytes, self.eager),
-                ("chain_vec_kernel + reduce_row_kernel", "compare: two calls (eltwise, reduce), eager", self.bytes,
+        return [("chain_reduce_typed_kernel", "one fused call, CUDA graph replay", self.bytes, self.step),
+                ("chain_reduce_typed_kernel", "compare: one fused call, eager", self.bytes, self.eager),
+                ("affine_rows_kernel + reduce_row_kernel", "compare: two calls (eltwise, reduce), eager", self.bytes,
                  self.two_calls)]
 
     def cpu_sample(self, budget_s):
